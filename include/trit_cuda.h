@@ -1,0 +1,161 @@
+/* trit_cuda: the greedy token loop of Trit's decoder language model
+ * (CausalLm: Qwen3 / Llama / Mistral / Granite) on NVIDIA B200 (sm_100a).
+ * C ABI of libtrit_cuda.so.
+ *
+ * It replaces the CPU decoder behind src/models/parts/causal_lm.rs of
+ * Hi9841/trit; the entry points follow that interface (each cites the
+ * function it stands for) and the rules of include/trit.h:7-18:
+ * - Strings are UTF-8 and NUL-terminated.
+ * - A call that fails returns NULL or -1; trit_last_error() then gives the
+ *   reason, for the calling thread. No C++ exception crosses the ABI.
+ * - One model handle may be used from several threads; calls on it take
+ *   turns (a mutex), as calls on one Trit engine share one worker team.
+ *   Do not free a handle while another thread is in a call on it.
+ * - The caller owns every buffer it passes, for the length of the call;
+ *   the library owns the device memory of a handle until trit_lm_free.
+ * - There is no CPU fallback: without a usable GPU the load fails.
+ *
+ * A model is a folder with config.json (Hugging Face keys, as Config::parse
+ * reads them, causal_lm.rs:41-77) and model.gguf holding the tensors under
+ * their Hugging Face names: Q8_0 matrices (ggml blocks of 32 codes and an
+ * f16 scale), per-row int8 matrices (`.weight` I8 + `.scales` F32 per row),
+ * or ternary matrices (`.qweight`, five base-3 codes a byte, + `.scales`
+ * F32 per 128 inputs, as src/models/parts/fastconformer.rs:440-452 reads
+ * them); norms F32; token tables Q8_0 or int8 with per-32 F32 scales.
+ */
+#ifndef TRIT_CUDA_H
+#define TRIT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct TritLm TritLm;
+typedef struct TritLmPrefix TritLmPrefix;
+typedef struct TritDense TritDense;
+
+/* The library version, for example "0.1.0". Static; do not free.
+ * (trit_version, include/trit.h:41.) */
+const char *trit_cuda_version(void);
+
+/* The error of the last failed call on this thread, or "" after a success.
+ * Valid until the next call on this thread; do not free.
+ * (trit_last_error, include/trit.h:44-46; ffi/src/lib.rs:20-45.) */
+const char *trit_last_error(void);
+
+/* Loads a decoder onto a GPU. `options_json` is NULL, "" or an object;
+ * every key is optional and an unknown key fails (as trit_load_json,
+ * include/trit.h:76-87):
+ *   "device":       CUDA device index (0)
+ *   "kv":           "f16" (default) or "f32": the element type of the paged
+ *                   KV cache; "f32" holds what the reference holds
+ *   "max_context":  positions per stream (4096)
+ *   "max_streams":  stream slots for trit_lm_generate_batch (1)
+ *   "page_tokens":  positions per KV page (64)
+ *   "prefill_rows": prompt rows per prefill pass (512)
+ *   "decode":       "persistent" (default: one kernel runs every greedy
+ *                   step of a batch-1 generation) or "layered" (a kernel
+ *                   per operation and step)
+ * NULL on failure. (CausalLm::load / from_tensors, causal_lm.rs:124-198.) */
+TritLm *trit_lm_load(const char *model_dir, const char *options_json);
+
+/* Frees a model and its device memory. NULL is a no-op. (trit_free,
+ * include/trit.h:115-116.) */
+void trit_lm_free(TritLm *lm);
+
+/* hidden_size, num_hidden_layers, vocab_size; -1 for NULL.
+ * (CausalLm::width / layers, causal_lm.rs:307-313,343-345.) */
+int64_t trit_lm_width(const TritLm *lm);
+int64_t trit_lm_layers(const TritLm *lm);
+int64_t trit_lm_vocab(const TritLm *lm);
+
+/* Runs a prompt start that many calls share (a system prompt) once; a
+ * trit_lm_generate whose prompt begins with it and is longer starts from
+ * its cache. NULL on failure. (CausalLm::prefix, causal_lm.rs:200-215.) */
+TritLmPrefix *trit_lm_prefix(TritLm *lm, const int32_t *ids, size_t n);
+
+/* Frees a prefix. NULL is a no-op. */
+void trit_lm_prefix_free(TritLmPrefix *prefix);
+
+/* Greedy tokens after `prompt` (n ids), until a token of `stop` (nstop ids,
+ * not kept) or `max_new` tokens; writes at most `cap` of them to `out`.
+ * Returns the number of tokens made, or -1. `prefix` may be NULL.
+ * (CausalLm::generate + greedy, causal_lm.rs:217-249,284-302.) */
+int64_t trit_lm_generate(TritLm *lm, const TritLmPrefix *prefix, const int32_t *prompt, size_t n,
+                         int32_t max_new, const int32_t *stop, size_t nstop, int32_t *out, size_t cap);
+
+/* Greedy tokens after a prompt given as embeddings, `nrows` rows of
+ * trit_lm_width() floats (some rows from another model, such as audio
+ * frames). Returns the count, or -1. (CausalLm::generate_rows,
+ * causal_lm.rs:251-262.) */
+int64_t trit_lm_generate_rows(TritLm *lm, const float *rows, size_t nrows, int32_t max_new,
+                              const int32_t *stop, size_t nstop, int32_t *out, size_t cap);
+
+/* generate_rows after the prompt `head` (ids), the rows `audio` (naudio
+ * rows of trit_lm_width() floats) and the prompt `tail` (ids). Returns the
+ * count, or -1. (CausalLm::answer, causal_lm.rs:264-282.) */
+int64_t trit_lm_answer(TritLm *lm, const int32_t *head, size_t nhead, const float *audio, size_t naudio,
+                       const int32_t *tail, size_t ntail, int32_t max_new, const int32_t *stop,
+                       size_t nstop, int32_t *out, size_t cap);
+
+/* The embeddings of `n` ids, n x trit_lm_width() floats, into `out`.
+ * Returns 0, or -1. (CausalLm::embed, causal_lm.rs:347-355.) */
+int trit_lm_embed(TritLm *lm, const int32_t *ids, size_t n, float *out);
+
+/* trit_lm_generate with the logits each token came from: `logits` holds
+ * max_new x trit_lm_vocab() floats; row i is written for every token made
+ * and for a stopping token. For parity checks; slower than
+ * trit_lm_generate. (The logits of forward_rows, causal_lm.rs:366-389.) */
+int64_t trit_lm_generate_traced(TritLm *lm, const TritLmPrefix *prefix, const int32_t *prompt, size_t n,
+                                int32_t max_new, const int32_t *stop, size_t nstop, int32_t *out,
+                                size_t cap, float *logits);
+
+/* trit_lm_answer with the logits trace of trit_lm_generate_traced. */
+int64_t trit_lm_answer_traced(TritLm *lm, const int32_t *head, size_t nhead, const float *audio,
+                              size_t naudio, const int32_t *tail, size_t ntail, int32_t max_new,
+                              const int32_t *stop, size_t nstop, int32_t *out, size_t cap,
+                              float *logits);
+
+/* Independent greedy generations, one per stream (at most "max_streams"),
+ * decoded side by side: stream s starts from prompts[s] (lens[s] ids) and
+ * writes its tokens to out[s * max_new ...] and their count to counts[s].
+ * Returns 0, or -1. (CausalLm::generate for each stream; the streams share
+ * the weights, as the reference's callers share one model.) */
+int trit_lm_generate_batch(TritLm *lm, size_t streams, const int32_t *const *prompts, const size_t *lens,
+                           int32_t max_new, const int32_t *stop, size_t nstop, int32_t *out,
+                           int64_t *counts);
+
+/* The device time of the last generation on this handle, from CUDA events:
+ * the prompt (prefill) and the greedy steps after it, in ms, the number of
+ * decode steps, and the kernel launches it made. Returns 0, or -1. */
+int trit_lm_last_timing(const TritLm *lm, double *prefill_ms, double *decode_ms, int64_t *decode_steps,
+                        int64_t *launches);
+
+/* ---- single product layers (Dense, src/cpu/gemm.rs:14-542) ---- */
+
+/* A layer from ggml Q8_0 blocks of an `n x k` row-major matrix (34 bytes a
+ * block: f16 scale, 32 codes). table = 0: int8 activations in groups of 32
+ * with f16-rounded scales, i8 x i8 products (Dense::q8_0 -> Int8::from_q8_0,
+ * gemm.rs:212-231, int8.rs:234-289); table = 1: a token table, f32 math
+ * (Dense::table -> Weights::Q8, gemm.rs:383-409). NULL on failure. */
+TritDense *trit_dense_q8_0(const void *blocks, size_t n, size_t k, int table, int device);
+
+/* out (rows x n) = x (rows x k) times the layer, both in host memory.
+ * Returns 0, or -1. (Dense::forward, gemm.rs:500-542.) */
+int trit_dense_forward(TritDense *layer, const float *x, size_t rows, float *out);
+
+/* trit_dense_forward on device pointers, queued on `cuda_stream` (a
+ * cudaStream_t, or NULL for the layer's own stream); does not wait. */
+int trit_dense_forward_device(TritDense *layer, const float *x, size_t rows, float *out, void *cuda_stream);
+
+/* Frees a layer. NULL is a no-op. */
+void trit_dense_free(TritDense *layer);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRIT_CUDA_H */

@@ -1,0 +1,85 @@
+"""Parity of the CUDA decoder with the CPU oracle (a restatement of Trit's
+CausalLm, src/models/parts/causal_lm.rs) on seeded small models of each
+weight format: greedy tokens identical for the whole generation, logits
+within max-abs 2e-2 and cosine >= 0.9995 at every step."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from trit_b200 import CausalLm
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+MIN_COS = 0.9995
+FORMATS = ["mini_qwen3_q8_0", "mini_qwen3_int8", "mini_qwen3_ternary", "mini_mistral_q8_0"]
+
+
+def _cos(a, b):
+    return float(np.dot(a, b) / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def _compare(ref, toks, logits):
+    assert toks == ref["tokens"], f"tokens differ: {toks} vs {ref['tokens']} (gaps {ref['gaps']})"
+    for i in range(len(toks)):
+        a, b = logits[i], ref["logits"][i]
+        assert np.abs(a - b).max() <= MAX_ABS, f"step {i}: max abs {np.abs(a - b).max()}"
+        assert _cos(a, b) >= MIN_COS, f"step {i}: cosine {_cos(a, b)}"
+
+
+@pytest.mark.parametrize("name", FORMATS)
+@pytest.mark.parametrize("kv", ["f32", "f16"])
+@pytest.mark.parametrize("decode", ["layered", "persistent"])
+def test_generate_matches_oracle(mini_models, name, kv, decode):
+    path = mini_models[name]
+    rng = np.random.default_rng(3)
+    oracle = O.Oracle(path, kv_f16=(kv == "f16"))
+    prompt = rng.integers(0, oracle.vocab, size=37).tolist()
+    ref = oracle.generate(prompt, 40, trace=True)
+    with CausalLm.load(path, kv=kv, decode=decode, max_context=256) as lm:
+        toks, logits = lm.generate_traced(prompt, max_new=40)
+        _compare(ref, toks, logits)
+        assert lm.generate(prompt, max_new=40) == toks
+
+
+@pytest.mark.parametrize("decode", ["layered", "persistent"])
+def test_stop_tokens_and_prefix(mini_models, decode):
+    path = mini_models["mini_qwen3_q8_0"]
+    oracle = O.Oracle(path)
+    prompt = list(range(100, 160))
+    ref = oracle.generate(prompt, 30)
+    stop = [ref["tokens"][5]]
+    want = oracle.generate(prompt, 30, stop=stop)["tokens"]
+    with CausalLm.load(path, kv="f32", decode=decode, max_context=256) as lm:
+        assert lm.generate(prompt, max_new=30, stop=stop) == want
+        pre = lm.prefix(prompt[:40])
+        assert lm.generate(prompt, prefix=pre, max_new=30) == ref["tokens"]
+        # A prompt that does not start with the prefix ignores it.
+        other = [7] + prompt[1:]
+        assert lm.generate(other, prefix=pre, max_new=12) == oracle.generate(other, 12)["tokens"]
+        assert lm.generate(prompt, max_new=0) == []
+
+
+def test_answer_rows_and_embed(mini_models):
+    path = mini_models["mini_qwen3_q8_0"]
+    oracle = O.Oracle(path)
+    rng = np.random.default_rng(11)
+    audio = rng.standard_normal((23, oracle.width)).astype(np.float32)
+    head, tail = [5, 6, 7], [9, 10]
+    ref = oracle.answer(head, audio, tail, 20, trace=True)
+    with CausalLm.load(path, kv="f32", max_context=256) as lm:
+        toks, logits = lm.answer(head, audio, tail, max_new=20, trace=True)
+        _compare(ref, toks, logits)
+        assert lm.generate_rows(audio, max_new=20) == oracle.generate_rows(audio, 20)["tokens"]
+        assert np.array_equal(lm.embed([1, 2, 3, 4095]), oracle.embed([1, 2, 3, 4095]))
+
+
+def test_long_prompt_in_chunks(mini_models):
+    """A prompt longer than prefill_rows runs in chunks through the cache."""
+    path = mini_models["mini_qwen3_int8"]
+    oracle = O.Oracle(path)
+    prompt = np.random.default_rng(5).integers(0, oracle.vocab, size=150).tolist()
+    ref = oracle.generate(prompt, 16, trace=True)
+    with CausalLm.load(path, kv="f32", prefill_rows=64, max_context=256) as lm:
+        toks, logits = lm.generate_traced(prompt, max_new=16)
+        _compare(ref, toks, logits)

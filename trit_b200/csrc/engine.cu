@@ -1,0 +1,766 @@
+// Loading a decoder into device memory and running CausalLm's generation
+// flows (src/models/parts/causal_lm.rs:141-302) on one GPU.
+#include "engine.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <functional>
+
+namespace trit {
+
+void CudaCheck::ok(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw Error(std::string("CUDA: ") + cudaGetErrorString(e) + " (" + what + ")");
+}
+
+Options Options::parse(const char* text) {
+  Options o;
+  if (!text || !*text) return o;
+  Json j = Json::parse(text);
+  if (j.kind != Json::Object) throw Error("options: not a JSON object");
+  for (auto& f : j.fields) {
+    const std::string& k = f.first;
+    const Json& v = f.second;
+    auto count = [&](int lo, int hi) {
+      if (v.kind != Json::Number || v.num != std::floor(v.num) || v.num < lo || v.num > hi)
+        throw Error("options: " + k + " must be a whole number from " + std::to_string(lo) + " to " + std::to_string(hi));
+      return (int)v.num;
+    };
+    if (k == "device") o.device = count(0, 63);
+    else if (k == "kv") {
+      if (v.kind != Json::String || (v.str != "f16" && v.str != "f32")) throw Error("options: kv is \"f16\" or \"f32\"");
+      o.kv_f16 = v.str == "f16";
+    } else if (k == "max_context") o.max_context = count(1, 1 << 20);
+    else if (k == "max_streams") o.max_streams = count(1, 4096);
+    else if (k == "page_tokens") o.page_tokens = count(1, 4096);
+    else if (k == "prefill_rows") o.prefill_rows = count(1, 65536);
+    else if (k == "decode") {
+      if (v.kind != Json::String || (v.str != "persistent" && v.str != "layered"))
+        throw Error("options: decode is \"persistent\" or \"layered\"");
+      o.decode = v.str;
+    } else {
+      throw Error("options: unknown key " + k);
+    }
+  }
+  return o;
+}
+
+PrefixState::~PrefixState() {
+  if (pages) cudaFree(pages);
+}
+
+namespace {
+
+// Two passes over the weights: the first sizes the arena, the second
+// copies every tensor into it.
+struct Arena {
+  char* base = nullptr;
+  size_t used = 0;
+  bool fill = false;
+  size_t take(size_t n) {
+    size_t at = (used + 255) / 256 * 256;
+    used = at + n;
+    return at;
+  }
+  void put(size_t at, const void* src, size_t n) {
+    if (fill) TRIT_CUDA(cudaMemcpy(base + at, src, n, cudaMemcpyHostToDevice));
+  }
+  const void* ptr(size_t at) const { return base ? base + at : nullptr; }
+};
+
+std::vector<float> f32_of(const GgufFile& g, const std::string& name, size_t len) {
+  const GgufTensor& t = g.at(name);
+  if (t.count() != len) throw Error("tensor " + name + " has " + std::to_string(t.count()) + " values, expected " + std::to_string(len));
+  std::vector<float> out(len);
+  if (t.type == F32) {
+    std::memcpy(out.data(), t.data, len * 4);
+  } else if (t.type == F16) {
+    for (size_t i = 0; i < len; ++i) {
+      uint16_t h;
+      std::memcpy(&h, t.data + 2 * i, 2);
+      out[i] = f16_to_f32(h);
+    }
+  } else {
+    throw Error("tensor " + name + " is not F32 or F16");
+  }
+  return out;
+}
+
+const float* load_vector(const GgufFile& g, Arena& A, const std::string& name, size_t len) {
+  size_t at = A.take(len * 4);
+  if (A.fill) {
+    std::vector<float> v = f32_of(g, name, len);
+    A.put(at, v.data(), len * 4);
+  }
+  return (const float*)A.ptr(at);
+}
+
+// Dense::load (src/cpu/gemm.rs:254-343) of parts stacked by output rows,
+// in the device layout: Q8_0 blocks split into a codes plane and an f16
+// scale plane (34-byte blocks are not 16-byte aligned); per-row int8 codes
+// and row scales; ternary base-3 bytes (src/cpu/kernels.rs:91-130) repacked
+// 16 codes a word in the pack_span order (kernels.rs:618-628).
+DMat load_mat(const GgufFile& g, Arena& A, const std::vector<std::pair<std::string, int>>& parts, int k) {
+  DMat m;
+  m.k = k;
+  for (auto& p : parts) m.n += p.second;
+  const std::string& first = parts[0].first;
+  const GgufTensor* w = g.find(first + ".weight");
+  if (w && w->type == Q8_0) {
+    m.kind = kQ8_0;
+    m.agroup = 32;
+    m.half = 1;
+  } else if (w && w->type == I8 && g.find(first + ".scales")) {
+    m.kind = kInt8Row;
+    m.agroup = 128;
+  } else if (g.find(first + ".qweight")) {
+    m.kind = kTernary;
+    m.agroup = 128;
+  } else {
+    throw Error("model.gguf: no Q8_0, int8 or ternary weights for " + first);
+  }
+  if (k % m.agroup != 0) throw Error(first + ": the input width is not whole groups of " + std::to_string(m.agroup));
+  if (m.n % 32 != 0) throw Error(first + ": the output rows are not a multiple of 32");
+  size_t codes_bytes = (m.kind == kTernary) ? (size_t)m.n * k / 4 : (size_t)m.n * k;
+  size_t scale_bytes = m.kind == kQ8_0 ? (size_t)m.n * (k / 32) * 2 : m.kind == kInt8Row ? (size_t)m.n * 4
+                                                                                         : (size_t)m.n * (k / 128) * 4;
+  size_t co = A.take(codes_bytes), so = A.take(scale_bytes);
+  m.codes = A.ptr(co);
+  m.scales = A.ptr(so);
+  if (!A.fill) return m;
+  std::vector<uint8_t> codes(codes_bytes), scales(scale_bytes);
+  size_t row0 = 0;
+  for (auto& p : parts) {
+    size_t rows = (size_t)p.second;
+    if (m.kind == kQ8_0) {
+      const GgufTensor& t = g.at(p.first + ".weight");
+      if (t.type != Q8_0 || t.count() != rows * k) throw Error("tensor " + p.first + ".weight: expected Q8_0 " + std::to_string(rows) + "x" + std::to_string(k));
+      size_t blocks = rows * k / 32;
+      for (size_t b = 0; b < blocks; ++b) {
+        const uint8_t* blk = t.data + b * 34;
+        std::memcpy(scales.data() + (row0 * (k / 32) + b) * 2, blk, 2);
+        std::memcpy(codes.data() + row0 * k + b * 32, blk + 2, 32);
+      }
+    } else if (m.kind == kInt8Row) {
+      const GgufTensor& t = g.at(p.first + ".weight");
+      if (t.type != I8 || t.count() != rows * k) throw Error("tensor " + p.first + ".weight: expected I8 " + std::to_string(rows) + "x" + std::to_string(k));
+      std::memcpy(codes.data() + row0 * k, t.data, rows * k);
+      std::vector<float> s = f32_of(g, p.first + ".scales", rows);
+      std::memcpy(scales.data() + row0 * 4, s.data(), rows * 4);
+    } else {
+      const GgufTensor& t = g.at(p.first + ".qweight");
+      size_t row_bytes = ((size_t)k + 4) / 5;
+      if (t.count() != rows * row_bytes) throw Error("tensor " + p.first + ".qweight: expected " + std::to_string(rows) + " rows of " + std::to_string(row_bytes) + " bytes");
+      std::vector<uint8_t> digits(k + 5);
+      for (size_t r = 0; r < rows; ++r) {
+        const uint8_t* src = t.data + r * row_bytes;
+        for (size_t b = 0; b < row_bytes; ++b) {
+          unsigned v = src[b];
+          if (v >= 243) throw Error("ternary byte above 242 in row " + std::to_string(row0 + r) + " of " + p.first);
+          for (int dd = 0; dd < 5; ++dd) {
+            digits[b * 5 + dd] = (uint8_t)(v % 3);
+            v /= 3;
+          }
+        }
+        uint32_t* dst = (uint32_t*)(codes.data()) + (row0 + r) * (k / 16);
+        for (int w16 = 0; w16 < k / 16; ++w16) {
+          uint32_t word = 0;
+          for (int s = 0; s < 4; ++s)
+            for (int j = 0; j < 4; ++j) word |= (uint32_t)digits[w16 * 16 + 4 * s + j] << (8 * j + 2 * s);
+          dst[w16] = word;
+        }
+      }
+      std::vector<float> s = f32_of(g, p.first + ".scales", rows * (k / 128));
+      std::memcpy(scales.data() + row0 * (k / 128) * 4, s.data(), s.size() * 4);
+    }
+    row0 += rows;
+  }
+  A.put(co, codes.data(), codes_bytes);
+  A.put(so, scales.data(), scale_bytes);
+  return m;
+}
+
+// Dense::table (src/cpu/gemm.rs:383-409): Q8_0 blocks (f16 scales) or int8
+// codes with one f32 scale per 32 values, f32 math.
+DTable load_table(const GgufFile& g, Arena& A, const std::string& name, int rows, int cols) {
+  DTable t;
+  t.n = rows;
+  t.k = cols;
+  if (cols % 32) throw Error(name + ": the width is not whole blocks of 32");
+  const GgufTensor& w = g.at(name + ".weight");
+  if (w.count() != (uint64_t)rows * cols) throw Error(name + ".weight has the wrong size");
+  t.scale_f16 = w.type == Q8_0;
+  if (w.type != Q8_0 && w.type != I8) throw Error(name + ".weight is neither Q8_0 nor I8");
+  size_t co = A.take((size_t)rows * cols), so = A.take((size_t)rows * (cols / 32) * (t.scale_f16 ? 2 : 4));
+  t.codes = (const int8_t*)A.ptr(co);
+  t.scales = A.ptr(so);
+  if (!A.fill) return t;
+  if (w.type == Q8_0) {
+    std::vector<uint8_t> codes((size_t)rows * cols), scales((size_t)rows * (cols / 32) * 2);
+    for (size_t b = 0; b < (size_t)rows * cols / 32; ++b) {
+      std::memcpy(scales.data() + b * 2, w.data + b * 34, 2);
+      std::memcpy(codes.data() + b * 32, w.data + b * 34 + 2, 32);
+    }
+    A.put(co, codes.data(), codes.size());
+    A.put(so, scales.data(), scales.size());
+  } else {
+    A.put(co, w.data, (size_t)rows * cols);
+    std::vector<float> s = f32_of(g, name + ".scales", (size_t)rows * (cols / 32));
+    A.put(so, s.data(), s.size() * 4);
+  }
+  return t;
+}
+
+}  // namespace
+
+Lm::Lm(const std::string& dir, const Options& o) : opt_(o) {
+  int count = 0;
+  TRIT_CUDA(cudaGetDeviceCount(&count));
+  if (opt_.device >= count) throw Error("options: device " + std::to_string(opt_.device) + " of " + std::to_string(count));
+  TRIT_CUDA(cudaSetDevice(opt_.device));
+  TRIT_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  for (auto& e : ev_) TRIT_CUDA(cudaEventCreate(&e));
+  try {
+    load(dir);
+    alloc_buffers();
+  } catch (...) {
+    release();
+    throw;
+  }
+}
+
+Lm::~Lm() { release(); }
+
+// Frees every device and pinned buffer; safe to call twice.
+void Lm::release() {
+  cudaSetDevice(opt_.device);
+  if (stream_) cudaStreamSynchronize(stream_);
+  void* bufs[] = {arena_, d_layers_, pool_, page_table_, x_, qkv_, att_, h_, part_, xn_, xq_, xs_, row_stream_, row_pos_, ids_,
+                  best_val_, best_idx_, tokens_, logits_, stop_, positions_, dx_, dqkv_, datt_part_, datts_, dh_, dattq_,
+                  dbest_val_, dbest_idx_, dsync_, dstatus_, dcount_, trace_, rope_};
+  for (void* b : bufs)
+    if (b) cudaFree(b);
+  if (host_rows_) cudaFreeHost(host_rows_);
+  for (auto& e : ev_)
+    if (e) cudaEventDestroy(e);
+  if (stream_) cudaStreamDestroy(stream_);
+  arena_ = pool_ = nullptr;
+  d_layers_ = nullptr;
+  page_table_ = nullptr;
+  stream_ = nullptr;
+  host_rows_ = nullptr;
+  for (auto& e : ev_) e = nullptr;
+  x_ = qkv_ = att_ = h_ = part_ = xn_ = nullptr;
+  xq_ = nullptr; xs_ = nullptr; row_stream_ = row_pos_ = ids_ = nullptr; best_val_ = nullptr; best_idx_ = nullptr;
+  tokens_ = nullptr; logits_ = nullptr; stop_ = nullptr; positions_ = nullptr; dx_ = dqkv_ = datt_part_ = datts_ = dh_ = nullptr;
+  dattq_ = nullptr; dbest_val_ = nullptr; dbest_idx_ = nullptr; dsync_ = nullptr; dstatus_ = nullptr;
+  dcount_ = nullptr; trace_ = nullptr; rope_ = nullptr;
+}
+
+// Config::parse (causal_lm.rs:41-77) and CausalLm::from_tensors (:141-198).
+void Lm::load(const std::string& dir) {
+  std::string text;
+  {
+    FILE* f = fopen((dir + "/config.json").c_str(), "rb");
+    if (!f) throw Error("cannot read " + dir + "/config.json");
+    char buf[65536];
+    size_t n;
+    while ((n = fread(buf, 1, sizeof buf, f)) > 0) text.append(buf, n);
+    fclose(f);
+  }
+  Json j = Json::parse(text);
+  std::string type = j.string_or("model_type", "");
+  bool qk_norm;
+  if (type == "qwen3") qk_norm = true;
+  else if (type == "llama" || type == "mistral" || type == "granite") qk_norm = false;
+  else throw Error("config.json does not describe a language model this engine runs");
+  cfg_.heads = (int)j.integer("num_attention_heads");
+  cfg_.kv_heads = (int)j.integer("num_key_value_heads");
+  if (!cfg_.heads || !cfg_.kv_heads || cfg_.heads % cfg_.kv_heads)
+    throw Error("config.json: the query heads do not share the key heads evenly");
+  cfg_.d = (int)j.integer("hidden_size");
+  cfg_.embedding_multiplier = (float)j.number("embedding_multiplier", 1.0);
+  cfg_.has_q_scale = j.has("attention_multiplier");
+  cfg_.residual_multiplier = (float)j.number("residual_multiplier", 1.0);
+  cfg_.logits_scaling = (float)j.number("logits_scaling", 1.0);
+  cfg_.ffn = (int)j.integer("intermediate_size");
+  cfg_.layers = (int)j.integer("num_hidden_layers");
+  cfg_.hd = j.has("head_dim") ? (int)j.integer("head_dim") : cfg_.d / cfg_.heads;
+  cfg_.vocab = (int)j.integer("vocab_size");
+  cfg_.eps = (float)j.number("rms_norm_eps", 1e-6);
+  float rope_base = (float)j.number("rope_theta", 1e6);
+  // `attention` divides by sqrt(head_dim); Granite's multiplier replaces that (causal_lm.rs:416-419).
+  cfg_.q_scale = cfg_.has_q_scale ? (float)j.number("attention_multiplier", 1.0) * std::sqrt((float)cfg_.hd) : 1.0f;
+  tied_ = j.flag("tie_word_embeddings", false);
+  if (cfg_.hd != 128) throw Error("head_dim " + std::to_string(cfg_.hd) + ": the CUDA kernels take head_dim 128");
+  if (cfg_.d % 128 || cfg_.ffn % 128) throw Error("hidden and intermediate sizes must be multiples of 128");
+
+  GgufFile g(dir + "/model.gguf");
+  const int hd = cfg_.hd, qd = cfg_.heads * hd, kvd = cfg_.kv_heads * hd;
+  bool has_head = !tied_ && g.find("lm_head.weight");
+  for (int pass = 0; pass < 2; ++pass) {
+    Arena A;
+    A.fill = pass == 1;
+    A.base = (char*)arena_;
+    layers_.assign(cfg_.layers, DLayer{});
+    for (int l = 0; l < cfg_.layers; ++l) {
+      std::string p = "model.layers." + std::to_string(l);
+      DLayer& L = layers_[l];
+      L.norm_attn = load_vector(g, A, p + ".input_layernorm.weight", cfg_.d);
+      L.qkv = load_mat(g, A, {{p + ".self_attn.q_proj", qd}, {p + ".self_attn.k_proj", kvd}, {p + ".self_attn.v_proj", kvd}}, cfg_.d);
+      if (qk_norm) {
+        L.q_norm = load_vector(g, A, p + ".self_attn.q_norm.weight", hd);
+        L.k_norm = load_vector(g, A, p + ".self_attn.k_norm.weight", hd);
+      }
+      L.out = load_mat(g, A, {{p + ".self_attn.o_proj", cfg_.d}}, qd);
+      L.norm_mlp = load_vector(g, A, p + ".post_attention_layernorm.weight", cfg_.d);
+      L.gate_up = load_mat(g, A, {{p + ".mlp.gate_proj", cfg_.ffn}, {p + ".mlp.up_proj", cfg_.ffn}}, cfg_.d);
+      L.down = load_mat(g, A, {{p + ".mlp.down_proj", cfg_.d}}, cfg_.ffn);
+    }
+    final_norm_ = load_vector(g, A, "model.norm.weight", cfg_.d);
+    embed_ = load_table(g, A, "model.embed_tokens", cfg_.vocab, cfg_.d);
+    head_ = has_head ? load_table(g, A, "lm_head", cfg_.vocab, cfg_.d) : embed_;
+    if (pass == 0) {
+      arena_bytes_ = A.used;
+      TRIT_CUDA(cudaMalloc(&arena_, arena_bytes_));
+    }
+  }
+  TRIT_CUDA(cudaMalloc(&d_layers_, sizeof(DLayer) * cfg_.layers));
+  TRIT_CUDA(cudaMemcpy(d_layers_, layers_.data(), sizeof(DLayer) * cfg_.layers, cudaMemcpyHostToDevice));
+
+  // Rotary::halves (layers.rs:276-300): inv_freq = base^(-2i/hd) in f32, and
+  // (position * f).sin_cos() in f32, here once per position: [pos][sin | cos].
+  std::vector<float> inv(hd / 2);
+  for (int i = 0; i < hd / 2; ++i) inv[i] = powf(rope_base, -((float)(2 * i)) / (float)hd);
+  std::vector<float> table((size_t)opt_.max_context * hd);
+  for (int p = 0; p < opt_.max_context; ++p)
+    for (int i = 0; i < hd / 2; ++i) {
+      float a = (float)p * inv[i];
+      table[(size_t)p * hd + i] = sinf(a);
+      table[(size_t)p * hd + hd / 2 + i] = cosf(a);
+    }
+  TRIT_CUDA(cudaMalloc(&rope_, table.size() * 4));
+  TRIT_CUDA(cudaMemcpy(rope_, table.data(), table.size() * 4, cudaMemcpyHostToDevice));
+}
+
+void Lm::alloc_buffers() {
+  const int d = cfg_.d, hd = cfg_.hd, qd = cfg_.heads * hd, kvd = cfg_.kv_heads * hd;
+  // The paged cache: every stream slot owns pages_per_stream pages.
+  cache_.f16 = opt_.kv_f16;
+  cache_.page_tokens = opt_.page_tokens;
+  cache_.pages_per_stream = (opt_.max_context + opt_.page_tokens - 1) / opt_.page_tokens;
+  page_bytes_ = (size_t)cfg_.layers * 2 * cfg_.kv_heads * opt_.page_tokens * hd * (opt_.kv_f16 ? 2 : 4);
+  size_t pages = (size_t)opt_.max_streams * cache_.pages_per_stream;
+  TRIT_CUDA(cudaMalloc(&pool_, pages * page_bytes_));
+  cache_.pool = pool_;
+  std::vector<int> table(pages);
+  for (size_t i = 0; i < pages; ++i) table[i] = (int)i;
+  TRIT_CUDA(cudaMalloc(&page_table_, pages * sizeof(int)));
+  TRIT_CUDA(cudaMemcpy(page_table_, table.data(), pages * sizeof(int), cudaMemcpyHostToDevice));
+  cache_.page_table = page_table_;
+
+  rows_cap_ = std::max(opt_.prefill_rows, opt_.max_streams);
+  int kmax = std::max(std::max(d, qd), cfg_.ffn);
+  int splits = (opt_.max_context + 255) / 256;
+  part_floats_ = (size_t)rows_cap_ * cfg_.heads * splits * 130;
+  TRIT_CUDA(cudaMalloc(&x_, (size_t)rows_cap_ * d * 4));
+  TRIT_CUDA(cudaMalloc(&qkv_, (size_t)rows_cap_ * (qd + 2 * kvd) * 4));
+  TRIT_CUDA(cudaMalloc(&att_, (size_t)rows_cap_ * qd * 4));
+  TRIT_CUDA(cudaMalloc(&h_, (size_t)rows_cap_ * cfg_.ffn * 4));
+  TRIT_CUDA(cudaMalloc(&part_, part_floats_ * 4));
+  TRIT_CUDA(cudaMalloc(&xq_, (size_t)rows_cap_ * kmax));
+  TRIT_CUDA(cudaMalloc(&xs_, (size_t)rows_cap_ * (kmax / 32) * 4));
+  TRIT_CUDA(cudaMalloc(&row_stream_, (size_t)rows_cap_ * 4));
+  TRIT_CUDA(cudaMalloc(&row_pos_, (size_t)rows_cap_ * 4));
+  TRIT_CUDA(cudaMalloc(&ids_, (size_t)rows_cap_ * 4));
+  TRIT_CUDA(cudaMalloc(&xn_, (size_t)opt_.max_streams * d * 4));
+  TRIT_CUDA(cudaMalloc(&best_val_, (size_t)opt_.max_streams * table_blocks(cfg_.vocab) * 4));
+  TRIT_CUDA(cudaMalloc(&best_idx_, (size_t)opt_.max_streams * table_blocks(cfg_.vocab) * 4));
+  TRIT_CUDA(cudaMalloc(&logits_, (size_t)cfg_.vocab * 4));
+  TRIT_CUDA(cudaMalloc(&stop_, 256 * 4));
+  TRIT_CUDA(cudaMallocHost(&host_rows_, ((size_t)2 * rows_cap_ + opt_.max_context + 16) * 4));
+  TRIT_CUDA(cudaMalloc(&positions_, (size_t)opt_.max_context * std::max(1, opt_.max_streams) * 4));
+}
+
+void Lm::check_ids(const int* ids, size_t n) const {
+  for (size_t i = 0; i < n; ++i)
+    if (ids[i] < 0 || ids[i] >= cfg_.vocab)
+      throw Error("token id " + std::to_string(ids[i]) + " is outside the vocabulary of " + std::to_string(cfg_.vocab));
+}
+
+// CausalLm::hidden (causal_lm.rs:410-481) for the rows in x_, whose stream
+// and position are in row_stream_ / row_pos_.
+void Lm::hidden(int m, int max_tk) {
+  const int d = cfg_.d, qd = cfg_.heads * cfg_.hd, kvd = cfg_.kv_heads * cfg_.hd;
+  cudaStream_t s = stream_;
+  if (cfg_.embedding_multiplier != 1.0f) TRIT_CUDA(launch_scale(x_, (size_t)m * d, cfg_.embedding_multiplier, s));
+  for (int l = 0; l < cfg_.layers; ++l) {
+    const DLayer& L = layers_[l];
+    TRIT_CUDA(launch_norm_quant(x_, m, d, L.norm_attn, cfg_.eps, L.qkv.agroup, L.qkv.half, xq_, xs_, s));
+    TRIT_CUDA(launch_gemv(L.qkv, xq_, xs_, m, kEpOut, qkv_, qd + 2 * kvd, 1.0f, s));
+    TRIT_CUDA(launch_qk_rope_append(qkv_, m, cfg_, L.q_norm, L.k_norm, rope_, opt_.max_context, cache_, row_stream_,
+                                    row_pos_, l, s));
+    TRIT_CUDA(launch_attention(qkv_, m, cfg_, cache_, row_stream_, row_pos_, l, max_tk, part_, part_floats_, att_, s));
+    TRIT_CUDA(launch_norm_quant(att_, m, qd, nullptr, cfg_.eps, L.out.agroup, L.out.half, xq_, xs_, s));
+    TRIT_CUDA(launch_gemv(L.out, xq_, xs_, m, kEpResid, x_, d, cfg_.residual_multiplier, s));
+    TRIT_CUDA(launch_norm_quant(x_, m, d, L.norm_mlp, cfg_.eps, L.gate_up.agroup, L.gate_up.half, xq_, xs_, s));
+    TRIT_CUDA(launch_gemv(L.gate_up, xq_, xs_, m, kEpSilu, h_, cfg_.ffn, 1.0f, s));
+    TRIT_CUDA(launch_norm_quant(h_, m, cfg_.ffn, nullptr, cfg_.eps, L.down.agroup, L.down.half, xq_, xs_, s));
+    TRIT_CUDA(launch_gemv(L.down, xq_, xs_, m, kEpResid, x_, d, cfg_.residual_multiplier, s));
+  }
+  timing_.gpu_launches += cfg_.layers * 10 + (cfg_.embedding_multiplier != 1.0f ? 1 : 0);
+}
+
+// The prompt rows through every layer, prefill_rows at a time (causal
+// attention sees the earlier chunks through the cache). `fill(c0, c1)`
+// writes prompt rows c0..c1 into x_ (embedded, before the embedding
+// multiplier). Leaves the last chunk in x_ and its row count in last_rows_.
+void Lm::run_prompt(size_t m, int slot, int first, const std::function<void(size_t, size_t)>& fill) {
+  int* host = host_rows_;
+  for (size_t c0 = 0; c0 < m; c0 += rows_cap_) {
+    int mc = (int)std::min<size_t>(rows_cap_, m - c0);
+    TRIT_CUDA(cudaStreamSynchronize(stream_));  // the pinned row metadata is reused per chunk
+    for (int r = 0; r < mc; ++r) {
+      host[r] = slot;
+      host[rows_cap_ + r] = first + (int)c0 + r;
+    }
+    TRIT_CUDA(cudaMemcpyAsync(row_stream_, host, mc * 4, cudaMemcpyHostToDevice, stream_));
+    TRIT_CUDA(cudaMemcpyAsync(row_pos_, host + rows_cap_, mc * 4, cudaMemcpyHostToDevice, stream_));
+    fill(c0, c0 + mc);
+    hidden(mc, first + (int)c0 + mc);
+    last_rows_ = mc;
+  }
+}
+
+// Token ids of the prompt, staged once in pinned memory: rows c0..c1 are
+// embedded from there.
+void Lm::embed_rows(const int* ids, size_t c0, size_t c1, float* x) {
+  int* staged = host_rows_ + 2 * rows_cap_;
+  if (ids != staged) throw Error("internal: ids are not staged");
+  TRIT_CUDA(cudaMemcpyAsync(ids_ + c0 % rows_cap_, staged + c0, (c1 - c0) * 4, cudaMemcpyHostToDevice, stream_));
+  TRIT_CUDA(launch_embed(embed_, ids_ + c0 % rows_cap_, (int)(c1 - c0), x, 1.0f, stream_));
+  timing_.gpu_launches += 1;
+}
+
+int* Lm::stage_ids(const int* a, size_t na, const int* b, size_t nb) {
+  if (na + nb > (size_t)opt_.max_context) throw Error("more prompt ids than max_context");
+  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  int* staged = host_rows_ + 2 * rows_cap_;
+  if (na) std::memcpy(staged, a, na * 4);
+  if (nb) std::memcpy(staged + na, b, nb * 4);
+  return staged;
+}
+
+std::vector<int> Lm::generate(const PrefixState* prefix, const int* ids, size_t n, int max_new, const int* stop,
+                              size_t nstop, float* logits) {
+  if (n == 0) throw Error("the prompt is empty");
+  check_ids(ids, n);
+  bool use = prefix && n > prefix->tokens.size() && std::equal(prefix->tokens.begin(), prefix->tokens.end(), ids);
+  size_t done = use ? prefix->tokens.size() : 0;
+  if (n + (size_t)std::max(max_new, 0) > (size_t)opt_.max_context)
+    throw Error("prompt plus max_new (" + std::to_string(n + max_new) + ") exceeds max_context " +
+                std::to_string(opt_.max_context));
+  timing_ = Timing{};
+  TRIT_CUDA(cudaSetDevice(opt_.device));
+  int* staged = stage_ids(ids + done, n - done, nullptr, 0);
+  TRIT_CUDA(cudaEventRecord(ev_[0], stream_));
+  if (use) TRIT_CUDA(cudaMemcpyAsync(pool_, prefix->pages, prefix->bytes, cudaMemcpyDeviceToDevice, stream_));
+  run_prompt(n - done, 0, (int)done, [&](size_t c0, size_t c1) { embed_rows(staged, c0, c1, x_); });
+  return finish(0, (int)n, max_new, stop, nstop, logits);
+}
+
+std::vector<int> Lm::generate_rows(const float* rows, size_t nrows, int max_new, const int* stop, size_t nstop,
+                                   float* logits) {
+  return answer(nullptr, 0, rows, nrows, nullptr, 0, max_new, stop, nstop, logits);
+}
+
+// CausalLm::answer (causal_lm.rs:264-282): [embed(head); audio; embed(tail)]
+// as the prompt rows, then generate_rows (:251-262).
+std::vector<int> Lm::answer(const int* head, size_t nhead, const float* audio, size_t naudio, const int* tail,
+                            size_t ntail, int max_new, const int* stop, size_t nstop, float* logits) {
+  size_t m = nhead + naudio + ntail;
+  if (m == 0) throw Error("no prompt rows");
+  check_ids(head, nhead);
+  check_ids(tail, ntail);
+  if (m + (size_t)std::max(max_new, 0) > (size_t)opt_.max_context)
+    throw Error("prompt plus max_new exceeds max_context " + std::to_string(opt_.max_context));
+  timing_ = Timing{};
+  TRIT_CUDA(cudaSetDevice(opt_.device));
+  int* staged = stage_ids(head, nhead, tail, ntail);  // head ids then tail ids
+  TRIT_CUDA(cudaEventRecord(ev_[0], stream_));
+  const int d = cfg_.d;
+  run_prompt(m, 0, 0, [&](size_t c0, size_t c1) {
+    for (size_t r = c0; r < c1;) {
+      float* dst = x_ + (r - c0) * d;
+      if (r < nhead) {
+        size_t e = std::min(c1, nhead);
+        embed_rows(staged, r, e, dst);
+        r = e;
+      } else if (r < nhead + naudio) {
+        size_t e = std::min(c1, nhead + naudio);
+        TRIT_CUDA(cudaMemcpyAsync(dst, audio + (r - nhead) * d, (e - r) * d * 4, cudaMemcpyHostToDevice, stream_));
+        r = e;
+      } else {
+        // Tail ids sit after the head ids in the staging area.
+        size_t e = c1;
+        size_t s0 = nhead + (r - nhead - naudio), s1 = s0 + (e - r);
+        TRIT_CUDA(cudaMemcpyAsync(ids_, staged + s0, (s1 - s0) * 4, cudaMemcpyHostToDevice, stream_));
+        TRIT_CUDA(launch_embed(embed_, ids_, (int)(s1 - s0), dst, 1.0f, stream_));
+        timing_.gpu_launches += 1;
+        r = e;
+      }
+    }
+  });
+  return finish(0, (int)m, max_new, stop, nstop, logits);
+}
+
+// After a prefill whose last chunk is in x_: the last row's logits, then
+// greedy steps (CausalLm::greedy, causal_lm.rs:284-302). The forward after
+// the last kept token changes no output and is not run.
+std::vector<int> Lm::finish(int slot, int position, int max_new, const int* stop, size_t nstop, float* logits) {
+  std::vector<int> out;
+  if (max_new <= 0) {
+    TRIT_CUDA(cudaStreamSynchronize(stream_));
+    return out;
+  }
+  if (tokens_cap_ < max_new + 1) {
+    if (tokens_) cudaFree(tokens_);
+    tokens_ = nullptr;
+    tokens_cap_ = max_new + 1;
+    TRIT_CUDA(cudaMalloc(&tokens_, (size_t)tokens_cap_ * std::max(1, opt_.max_streams) * 4));
+  }
+  TRIT_CUDA(launch_final(x_ + (size_t)(last_rows_ - 1) * cfg_.d, cfg_.d, 1, final_norm_, cfg_, head_, xn_,
+                         logits ? logits_ : nullptr, best_val_, best_idx_, tokens_, stream_));
+  timing_.gpu_launches += 3;
+  if (logits) TRIT_CUDA(cudaMemcpyAsync(logits, logits_, (size_t)cfg_.vocab * 4, cudaMemcpyDeviceToHost, stream_));
+  TRIT_CUDA(cudaEventRecord(ev_[1], stream_));
+  int steps = max_new - 1;  // forwards after the prompt's
+  if (nstop > 256) throw Error("more than 256 stop ids");
+  nstop_ = (int)nstop;
+  if (nstop) TRIT_CUDA(cudaMemcpyAsync(stop_, stop, nstop * 4, cudaMemcpyHostToDevice, stream_));
+  if (steps > 0) {
+    if (opt_.decode == "persistent") decode_persistent(slot, position, steps, logits);
+    else decode_layered(slot, position, steps, logits);
+  }
+  TRIT_CUDA(cudaEventRecord(ev_[2], stream_));
+  std::vector<int> toks(max_new);
+  TRIT_CUDA(cudaMemcpyAsync(toks.data(), tokens_, (size_t)max_new * 4, cudaMemcpyDeviceToHost, stream_));
+  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  float ms = 0;
+  TRIT_CUDA(cudaEventElapsedTime(&ms, ev_[0], ev_[1]));
+  timing_.prefill_ms = ms;
+  TRIT_CUDA(cudaEventElapsedTime(&ms, ev_[1], ev_[2]));
+  timing_.decode_ms = ms;
+  timing_.decode_tokens = steps;
+  for (int i = 0; i < max_new; ++i) {
+    bool stopped = false;
+    for (size_t s = 0; s < nstop; ++s) stopped |= toks[i] == stop[s];
+    if (stopped) break;
+    out.push_back(toks[i]);
+  }
+  return out;
+}
+
+// Batch-1 decode through the layered kernels: step i feeds tokens_[i] at
+// position + i and writes tokens_[i + 1]; every step's position is in
+// positions_ from the start, so no step waits for the host.
+void Lm::decode_layered(int slot, int position, int steps, float* trace) {
+  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  int* host = host_rows_;
+  host[0] = slot;
+  int* hp = host_rows_ + 2 * rows_cap_;  // free again: the prompt is in
+  for (int i = 0; i < steps; ++i) hp[i] = position + i;
+  TRIT_CUDA(cudaMemcpyAsync(row_stream_, host, 4, cudaMemcpyHostToDevice, stream_));
+  TRIT_CUDA(cudaMemcpyAsync(positions_, hp, (size_t)steps * 4, cudaMemcpyHostToDevice, stream_));
+  int* saved = row_pos_;
+  for (int i = 0; i < steps; ++i) {
+    TRIT_CUDA(launch_embed(embed_, tokens_ + i, 1, x_, 1.0f, stream_));
+    row_pos_ = positions_ + i;
+    hidden(1, position + i + 1);
+    row_pos_ = saved;
+    TRIT_CUDA(launch_final(x_, cfg_.d, 1, final_norm_, cfg_, head_, xn_, trace ? logits_ : nullptr, best_val_,
+                           best_idx_, tokens_ + i + 1, stream_));
+    timing_.gpu_launches += 4;
+    if (trace)
+      TRIT_CUDA(cudaMemcpyAsync(trace + (size_t)(i + 1) * cfg_.vocab, logits_, (size_t)cfg_.vocab * 4,
+                                cudaMemcpyDeviceToHost, stream_));
+  }
+  row_pos_ = saved;
+}
+
+// Batch-1 decode in one cooperative kernel (decode.cu): step i feeds
+// tokens_[i] at position + i; the kernel stops at a stop token.
+void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
+  const int hd = cfg_.hd, qd = cfg_.heads * hd, kvd = cfg_.kv_heads * hd;
+  if (!decode_grid_) {
+    decode_grid_ = decode_grid(opt_.device);
+    if (decode_grid_ < cfg_.kv_heads) throw Error("too few SMs for the persistent decode");
+    int splits = std::max(1, decode_grid_ / cfg_.kv_heads);
+    int qpk = cfg_.heads / cfg_.kv_heads;
+    TRIT_CUDA(cudaMalloc(&dx_, (size_t)cfg_.d * 4));
+    TRIT_CUDA(cudaMalloc(&dqkv_, (size_t)(qd + 2 * kvd) * 4));
+    TRIT_CUDA(cudaMalloc(&datt_part_, (size_t)cfg_.kv_heads * splits * qpk * (hd + 2) * 4));
+    TRIT_CUDA(cudaMalloc(&dattq_, (size_t)qd));
+    TRIT_CUDA(cudaMalloc(&datts_, (size_t)(qd / 32) * 4));
+    TRIT_CUDA(cudaMalloc(&dh_, (size_t)cfg_.ffn * 4));
+    TRIT_CUDA(cudaMalloc(&dbest_val_, (size_t)decode_grid_ * 4));
+    TRIT_CUDA(cudaMalloc(&dbest_idx_, (size_t)decode_grid_ * 4));
+    TRIT_CUDA(cudaMalloc(&dsync_, (size_t)(4 + cfg_.kv_heads) * 4));
+    TRIT_CUDA(cudaMalloc(&dstatus_, 4));
+    TRIT_CUDA(cudaMalloc(&dcount_, 4));
+  }
+  float* dtrace = nullptr;
+  if (trace) {
+    size_t need = (size_t)(steps + 1) * cfg_.vocab;
+    if (trace_cap_ < need) {
+      if (trace_) cudaFree(trace_);
+      trace_ = nullptr;
+      TRIT_CUDA(cudaMalloc(&trace_, need * 4));
+      trace_cap_ = need;
+    }
+    dtrace = trace_;
+  }
+  DecodeArgs a{};
+  a.cfg = cfg_;
+  a.layers = d_layers_;
+  a.final_norm = final_norm_;
+  a.table = head_;
+  a.embed = embed_;
+  a.cache = cache_;
+  a.rope = rope_;
+  a.rope_rows = opt_.max_context;
+  a.stream = slot;
+  a.first_pos = position;
+  a.steps = steps;
+  a.stop = stop_;
+  a.nstop = nstop_;
+  a.tokens = tokens_;
+  a.count = dcount_;
+  a.logits = dtrace;
+  a.x = dx_;
+  a.qkv = dqkv_;
+  a.att_part = datt_part_;
+  a.attq = dattq_;
+  a.atts = datts_;
+  a.h = dh_;
+  a.best_val = dbest_val_;
+  a.best_idx = dbest_idx_;
+  a.sync = dsync_;
+  a.status = dstatus_;
+  TRIT_CUDA(cudaMemsetAsync(dsync_, 0, (size_t)(4 + cfg_.kv_heads) * 4, stream_));
+  TRIT_CUDA(cudaMemsetAsync(dstatus_, 0, 4, stream_));
+  TRIT_CUDA(launch_decode(a, decode_grid_, stream_));
+  timing_.gpu_launches += 1;
+  int status = 0;
+  TRIT_CUDA(cudaMemcpyAsync(&status, dstatus_, 4, cudaMemcpyDeviceToHost, stream_));
+  if (trace)
+    TRIT_CUDA(cudaMemcpyAsync(trace + cfg_.vocab, dtrace + cfg_.vocab, (size_t)steps * cfg_.vocab * 4,
+                              cudaMemcpyDeviceToHost, stream_));
+  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  if (status) throw Error("the persistent decode gave up waiting at a grid barrier (status " + std::to_string(status) + ")");
+}
+
+void Lm::embed(const int* ids, size_t n, float* out) {
+  check_ids(ids, n);
+  TRIT_CUDA(cudaSetDevice(opt_.device));
+  for (size_t c0 = 0; c0 < n; c0 += rows_cap_) {
+    size_t mc = std::min<size_t>(rows_cap_, n - c0);
+    TRIT_CUDA(cudaMemcpyAsync(ids_, ids + c0, mc * 4, cudaMemcpyHostToDevice, stream_));
+    TRIT_CUDA(launch_embed(embed_, ids_, (int)mc, x_, 1.0f, stream_));
+    TRIT_CUDA(cudaMemcpyAsync(out + c0 * cfg_.d, x_, mc * cfg_.d * 4, cudaMemcpyDeviceToHost, stream_));
+    TRIT_CUDA(cudaStreamSynchronize(stream_));
+  }
+}
+
+// CausalLm::prefix (causal_lm.rs:202-215): the prompt start through every
+// layer; its pages are kept.
+std::unique_ptr<PrefixState> Lm::prefix(const int* ids, size_t n) {
+  check_ids(ids, n);
+  if (n > (size_t)opt_.max_context) throw Error("the prefix is longer than max_context");
+  auto p = std::make_unique<PrefixState>();
+  p->tokens.assign(ids, ids + n);
+  if (n == 0) return p;
+  TRIT_CUDA(cudaSetDevice(opt_.device));
+  int* staged = stage_ids(ids, n, nullptr, 0);
+  run_prompt(n, 0, 0, [&](size_t c0, size_t c1) { embed_rows(staged, c0, c1, x_); });
+  size_t pages = (n + opt_.page_tokens - 1) / opt_.page_tokens;
+  p->bytes = pages * page_bytes_;
+  TRIT_CUDA(cudaMalloc(&p->pages, p->bytes));
+  TRIT_CUDA(cudaMemcpyAsync(p->pages, pool_, p->bytes, cudaMemcpyDeviceToDevice, stream_));
+  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  return p;
+}
+
+void Lm::generate_batch(size_t streams, const int* const* prompts, const size_t* lens, int max_new, const int* stop,
+                        size_t nstop, int* out, int64_t* counts) {
+  (void)streams; (void)prompts; (void)lens; (void)max_new; (void)stop; (void)nstop; (void)out; (void)counts;
+  throw Error("generate_batch is not built yet");
+}
+
+
+// ------------------------------------------------------------ DenseOp ----
+DenseOp::~DenseOp() {
+  cudaSetDevice(device);
+  void* bufs[] = {mem, xq, xs, xdev, ydev, best_val, best_idx, token};
+  for (void* b : bufs)
+    if (b) cudaFree(b);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+std::unique_ptr<DenseOp> dense_q8_0(const void* blocks, size_t n, size_t k, int device, bool table) {
+  if (k % 32) throw Error("Q8_0 rows are whole blocks of 32");
+  if (!table && n % 32) throw Error("a W8A8 layer needs a multiple of 32 output rows");
+  auto op = std::make_unique<DenseOp>();
+  op->device = device;
+  op->table = table;
+  TRIT_CUDA(cudaSetDevice(device));
+  TRIT_CUDA(cudaStreamCreateWithFlags(&op->stream, cudaStreamNonBlocking));
+  size_t nb = n * (k / 32);
+  std::vector<uint8_t> codes(n * k), scales(nb * 2);
+  const uint8_t* src = (const uint8_t*)blocks;
+  for (size_t b = 0; b < nb; ++b) {
+    std::memcpy(scales.data() + b * 2, src + b * 34, 2);
+    std::memcpy(codes.data() + b * 32, src + b * 34 + 2, 32);
+  }
+  size_t co = 0, so = (n * k + 255) / 256 * 256;
+  TRIT_CUDA(cudaMalloc(&op->mem, so + scales.size()));
+  TRIT_CUDA(cudaMemcpy(op->mem, codes.data(), codes.size(), cudaMemcpyHostToDevice));
+  TRIT_CUDA(cudaMemcpy((char*)op->mem + so, scales.data(), scales.size(), cudaMemcpyHostToDevice));
+  if (table) {
+    op->tab.n = (int)n; op->tab.k = (int)k; op->tab.scale_f16 = 1;
+    op->tab.codes = (const int8_t*)op->mem + co;
+    op->tab.scales = (char*)op->mem + so;
+  } else {
+    op->mat.kind = kQ8_0; op->mat.n = (int)n; op->mat.k = (int)k; op->mat.agroup = 32; op->mat.half = 1;
+    op->mat.codes = (char*)op->mem + co;
+    op->mat.scales = (char*)op->mem + so;
+  }
+  return op;
+}
+
+void DenseOp::forward_device(const float* x, size_t m, float* y, cudaStream_t s) {
+  if (m > rows_cap) {
+    if (xq) cudaFree(xq);
+    if (xs) cudaFree(xs);
+    if (best_val) cudaFree(best_val);
+    if (best_idx) cudaFree(best_idx);
+    if (token) cudaFree(token);
+    xq = nullptr; xs = nullptr; best_val = nullptr; best_idx = nullptr; token = nullptr;
+    size_t k = table ? tab.k : mat.k;
+    size_t n = table ? tab.n : mat.n;
+    TRIT_CUDA(cudaMalloc(&xq, m * k));
+    TRIT_CUDA(cudaMalloc(&xs, m * (k / 32) * 4));
+    TRIT_CUDA(cudaMalloc(&best_val, m * table_blocks((int)n) * 4));
+    TRIT_CUDA(cudaMalloc(&best_idx, m * table_blocks((int)n) * 4));
+    TRIT_CUDA(cudaMalloc(&token, m * 4));
+    rows_cap = m;
+  }
+  if (table) {
+    TRIT_CUDA(launch_table(tab, x, (int)m, 1.0f, y, best_val, best_idx, s));
+  } else {
+    TRIT_CUDA(launch_norm_quant(x, (int)m, mat.k, nullptr, 0.0f, mat.agroup, mat.half, xq, xs, s));
+    TRIT_CUDA(launch_gemv(mat, xq, xs, (int)m, kEpOut, y, mat.n, 1.0f, s));
+  }
+}
+
+}  // namespace trit

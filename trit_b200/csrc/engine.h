@@ -1,0 +1,169 @@
+// The decoder engine behind the C ABI: one model on one GPU, its paged KV
+// cache, and the generation flows of CausalLm
+// (src/models/parts/causal_lm.rs:200-345).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "host.h"
+#include "kernels.h"
+
+namespace trit {
+
+struct Options {
+  int device = 0;
+  bool kv_f16 = true;            // the paged KV cache in f16 (f32: the reference's cache)
+  int max_context = 4096;        // positions per stream
+  int max_streams = 1;           // stream slots for generate_batch
+  int page_tokens = 64;          // positions per KV page
+  int prefill_rows = 512;        // rows per prefill pass
+  std::string decode = "persistent";  // "persistent" (one kernel per generation) or "layered"
+  static Options parse(const char* json);
+};
+
+struct CudaCheck {
+  static void ok(cudaError_t e, const char* what);
+};
+#define TRIT_CUDA(x) ::trit::CudaCheck::ok((x), #x)
+
+// The KV snapshot of a prompt start that many calls share (Prefix,
+// causal_lm.rs:118-122,202-215): its tokens and a device copy of its pages.
+struct PrefixState {
+  std::vector<int> tokens;
+  void* pages = nullptr;
+  size_t bytes = 0;
+  ~PrefixState();
+};
+
+struct Timing {
+  double prefill_ms = 0, decode_ms = 0;
+  int decode_tokens = 0;
+  int gpu_launches = 0;
+};
+
+class Lm {
+ public:
+  Lm(const std::string& dir, const Options& o);
+  ~Lm();
+  Lm(const Lm&) = delete;
+  Lm& operator=(const Lm&) = delete;
+
+  const DConfig& config() const { return cfg_; }
+  const Options& options() const { return opt_; }
+  std::mutex& mutex() { return mu_; }
+  const Timing& timing() const { return timing_; }
+
+  // CausalLm::generate with an optional prefix; `logits` (host, may be
+  // null) receives the logits of every kept or stopping token, [max_new][vocab].
+  std::vector<int> generate(const PrefixState* prefix, const int* ids, size_t n, int max_new, const int* stop,
+                            size_t nstop, float* logits);
+  // CausalLm::generate_rows: the prompt as embeddings [nrows][d].
+  std::vector<int> generate_rows(const float* rows, size_t nrows, int max_new, const int* stop, size_t nstop,
+                                 float* logits);
+  // CausalLm::answer: head ids, audio rows, tail ids.
+  std::vector<int> answer(const int* head, size_t nhead, const float* audio, size_t naudio, const int* tail,
+                          size_t ntail, int max_new, const int* stop, size_t nstop, float* logits);
+  void embed(const int* ids, size_t n, float* out);
+  std::unique_ptr<PrefixState> prefix(const int* ids, size_t n);
+  // Independent streams, each with its own prompt: out [streams][max_new].
+  void generate_batch(size_t streams, const int* const* prompts, const size_t* lens, int max_new, const int* stop,
+                      size_t nstop, int* out, int64_t* counts);
+
+ private:
+  void load(const std::string& dir);
+  void release();
+  void alloc_buffers();
+  void check_ids(const int* ids, size_t n) const;
+  // Runs rows x (device, [m][d]) through every layer at positions
+  // first.. of stream `slot`; chunks of prefill_rows.
+  void run_prompt(size_t m, int slot, int first, const std::function<void(size_t, size_t)>& fill);
+  void embed_rows(const int* staged, size_t c0, size_t c1, float* x);
+  int* stage_ids(const int* a, size_t na, const int* b, size_t nb);
+  void hidden(int m, int max_tk);
+  // Greedy decode for `slot` after a prefill that left its last row in x.
+  std::vector<int> finish(int slot, int position, int max_new, const int* stop, size_t nstop, float* logits);
+  void decode_layered(int slot, int position, int steps, float* trace);
+  void decode_persistent(int slot, int position, int steps, float* trace);
+
+  Options opt_;
+  DConfig cfg_{};
+  std::mutex mu_;
+  Timing timing_;
+  cudaStream_t stream_ = nullptr;
+  cudaEvent_t ev_[4] = {};
+
+  // weights
+  void* arena_ = nullptr;
+  size_t arena_bytes_ = 0;
+  std::vector<DLayer> layers_;
+  DLayer* d_layers_ = nullptr;
+  const float* final_norm_ = nullptr;
+  DTable embed_{}, head_{};
+  bool tied_ = true;
+  float* rope_ = nullptr;
+
+  // cache
+  DCache cache_{};
+  void* pool_ = nullptr;
+  size_t page_bytes_ = 0;
+  int* page_table_ = nullptr;
+
+  // scratch
+  int rows_cap_ = 0;
+  float *x_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *h_ = nullptr, *part_ = nullptr, *xn_ = nullptr;
+  size_t part_floats_ = 0;
+  int8_t* xq_ = nullptr;
+  float* xs_ = nullptr;
+  int *row_stream_ = nullptr, *row_pos_ = nullptr, *ids_ = nullptr;
+  float* best_val_ = nullptr;
+  int* best_idx_ = nullptr;
+  int* tokens_ = nullptr;       // device [(max_new + 1) * max_streams]
+  int tokens_cap_ = 0;
+  float* logits_ = nullptr;     // device [vocab] trace buffer (one step)
+  int* stop_ = nullptr;
+  int nstop_ = 0;
+  int* host_rows_ = nullptr;    // pinned staging: [rows] streams, [rows] positions, [max_context] ids
+  int* positions_ = nullptr;    // device positions of every decode step
+  int last_rows_ = 0;           // rows of the last prompt chunk (in x_)
+  // persistent decode scratch
+  float *dx_ = nullptr, *dqkv_ = nullptr, *datt_part_ = nullptr, *datts_ = nullptr, *dh_ = nullptr;
+  int8_t* dattq_ = nullptr;
+  float* dbest_val_ = nullptr;
+  int* dbest_idx_ = nullptr;
+  unsigned* dsync_ = nullptr;
+  int* dstatus_ = nullptr;
+  int* dcount_ = nullptr;
+  int decode_grid_ = 0;
+  float* trace_ = nullptr;      // device [max_new][vocab] for traced persistent decode
+  size_t trace_cap_ = 0;
+};
+
+// A lone product layer for the op sweep (Dense::forward, gemm.rs:500-542).
+struct DenseOp {
+  int device = 0;
+  bool table = false;
+  DMat mat{};
+  DTable tab{};
+  void* mem = nullptr;
+  int8_t* xq = nullptr;
+  float *xs = nullptr, *xdev = nullptr, *ydev = nullptr, *best_val = nullptr;
+  int* best_idx = nullptr;
+  int* token = nullptr;
+  size_t rows_cap = 0;
+  cudaStream_t stream = nullptr;
+  ~DenseOp();
+  void forward_device(const float* x, size_t m, float* y, cudaStream_t s);
+};
+
+std::unique_ptr<DenseOp> dense_q8_0(const void* blocks, size_t n, size_t k, int device, bool table);
+
+void synthesize(const std::string& dir, const std::string& spec_json);
+void synth_normal_row(uint64_t seed, const std::string& name, uint64_t row, size_t k, float sd, float* out);
+
+}  // namespace trit

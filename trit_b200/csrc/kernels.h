@@ -1,0 +1,68 @@
+// Launchers of the device kernels (host-callable, no templates).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "types.h"
+
+namespace trit {
+
+enum Epilogue : int { kEpOut = 0, kEpResid = 1, kEpSilu = 2 };
+
+cudaError_t launch_embed(const DTable& T, const int* ids, int m, float* x, float mult, cudaStream_t s);
+cudaError_t launch_scale(float* x, size_t n, float mult, cudaStream_t s);
+cudaError_t launch_norm_quant(const float* x, int m, int d, const float* w, float eps, int group, int half,
+                              int8_t* xq, float* xs, cudaStream_t s);
+cudaError_t launch_gemv(const DMat& W, const int8_t* xq, const float* xs, int m, int mode, float* y, int ldy,
+                        float resid_mult, cudaStream_t s);
+cudaError_t launch_qk_rope_append(float* qkv, int m, const DConfig& cfg, const float* q_norm, const float* k_norm,
+                                  const float* rope, int rope_rows, const DCache& cache, const int* row_stream,
+                                  const int* row_pos, int layer, cudaStream_t s);
+cudaError_t launch_attention(const float* qkv, int m, const DConfig& cfg, const DCache& cache, const int* row_stream,
+                             const int* row_pos, int layer, int max_tk, float* part, size_t part_floats, float* att,
+                             cudaStream_t s);
+// RmsNorm of `nb` rows, the table product and each row's argmax. logits
+// ([nb][vocab]) may be null; best_* hold [nb][table_blocks(vocab)].
+cudaError_t launch_final(const float* x, int ldx, int nb, const float* norm_w, const DConfig& cfg, const DTable& T,
+                         float* xn, float* logits, float* best_val, int* best_idx, int* token, cudaStream_t s);
+// The table product alone for `nb` rows already normed.
+cudaError_t launch_table(const DTable& T, const float* xn, int nb, float mult, float* logits, float* best_val,
+                         int* best_idx, cudaStream_t s);
+int table_blocks(int n);
+int table_max_streams();
+
+// The persistent batch-1 decode (decode.cu).
+struct DecodeArgs {
+  DConfig cfg;
+  const DLayer* layers;  // device array [cfg.layers]
+  const float* final_norm;
+  DTable table;          // the output projection (the embedding when tied)
+  DTable embed;
+  DCache cache;
+  const float* rope;
+  int rope_rows;
+  int stream;            // the stream slot whose pages this decode uses
+  int first_pos;         // position of the first token fed
+  int steps;             // tokens to make (each step feeds the previous one)
+  const int* stop;       // device list of stop ids
+  int nstop;
+  int* tokens;           // [steps + 1]: tokens[0] is the token fed first; the rest are made
+  int* count;            // how many tokens were made before a stop
+  float* logits;         // optional [steps][vocab] trace, or null
+  // scratch (device)
+  float* x;              // [d]
+  float* qkv;            // [qd + 2 kvd]
+  float* att_part;       // [kv_heads][splits][2 q-per-kv][130]
+  int8_t* attq;          // [qd]
+  float* atts;           // [qd / 32]
+  float* h;              // [ffn]
+  float* best_val;       // [grid]
+  int* best_idx;         // [grid]
+  unsigned* sync;        // [4] counters, zeroed before the launch
+  int* status;           // 0 ok; nonzero: a wait ran out (see decode.cu)
+};
+
+cudaError_t launch_decode(const DecodeArgs& a, int grid, cudaStream_t s);
+int decode_grid(int device);
+
+}  // namespace trit

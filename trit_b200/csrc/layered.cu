@@ -1,0 +1,623 @@
+// The layered path: one kernel per step of CausalLm::hidden
+// (src/models/parts/causal_lm.rs:410-481) over `m` rows, each row with its
+// own stream and position. It runs prefill (one stream, many positions),
+// batched decode (many streams, one position each) and, as a fallback,
+// batch-1 decode.
+#include <algorithm>
+#include <cstdio>
+
+#include "device.cuh"
+#include "kernels.h"
+
+namespace trit {
+
+// --------------------------------------------------------- embedding ----
+// Dense::row of a token table (src/cpu/gemm.rs:412-429): code * scale, then
+// the embedding multiplier of CausalLm::hidden (causal_lm.rs:415).
+__global__ void k_embed(DTable T, const int* ids, int m, float* x, float mult) {
+  int r = blockIdx.x;
+  if (r >= m) return;
+  int id = ids[r];
+  if (id < 0 || id >= T.n) id = 0;  // the host checks ids; this keeps the read in bounds
+  for (int kk = threadIdx.x; kk < T.k; kk += blockDim.x) {
+    float v = __fmul_rn((float)T.codes[(size_t)id * T.k + kk], table_scale(T, id, kk / 32));
+    if (mult != 1.0f) v = __fmul_rn(v, mult);
+    x[(size_t)r * T.k + kk] = v;
+  }
+}
+
+__global__ void k_scale(float* x, size_t n, float mult) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    x[i] = __fmul_rn(x[i], mult);
+}
+
+// ------------------------------------------------- norm + quantize ----
+// RmsNorm::apply (src/cpu/layers.rs:135-153) then Quantized::grouped
+// (src/cpu/kernels.rs:661-737) of the normed row. One block per row. The
+// sum of squares is a tree here (the reference sums in order): the only
+// step of this kernel that is not bit-exact.
+template <int G>
+__global__ void __launch_bounds__(256) k_norm_quant(const float* x, int d, const float* w, float eps, int half,
+                                                    int8_t* xq, float* xs) {
+  int r = blockIdx.x;
+  const float* row = x + (size_t)r * d;
+  __shared__ float red[8];
+  __shared__ float s_inv;
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < d; i += 256) s = __fadd_rn(s, __fmul_rn(row[i], row[i]));
+  s = warp_sum(s);
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int i = 0; i < 8; ++i) t = __fadd_rn(t, red[i]);
+    if (w) s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)d), eps)));
+    else s_inv = 1.0f;
+  }
+  __syncthreads();
+  float inv = s_inv;
+  int groups = d / G;
+  for (int g = warp; g < groups; g += 8) {
+    float v[G / 32];
+#pragma unroll
+    for (int i = 0; i < G / 32; ++i) {
+      int kk = g * G + lane * (G / 32) + i;
+      v[i] = w ? __fmul_rn(row[kk], __fmul_rn(inv, w[kk])) : row[kk];
+    }
+    float scale = warp_quantize_group<G>(v, xq + (size_t)r * d + g * G, half);
+    if (lane == 0) xs[(size_t)r * groups + g] = scale;
+  }
+}
+
+// ------------------------------------------------------ W8A8 product ----
+// Int8::forward_biased (src/cpu/int8.rs:425-483), VNNI float order
+// (:560-570): per output and frame, acc = fma(f32(dot_g), ws_g * xs_g, acc)
+// over the groups in order. The i32 group dots come from dp4a over
+// coalesced 16-byte loads (a warp per output row); the group chain runs
+// in order in one thread per (row, frame), so each output is the
+// reference's value bit for bit.
+//
+// Units: OUT/RESID: a unit is one output row. SILU: a unit j is the pair of
+// gate row j and up row ffn + j of a stacked gate_up layer, and the output
+// is h[j] = silu(gate) * up (causal_lm.rs:464-474).
+constexpr int GEMV_THREADS = 256;
+constexpr int GEMV_ROWS = 8;   // output rows per block
+constexpr int GEMV_FRAMES = 8; // frames per pass
+
+__device__ __forceinline__ int4 load_weights16(const DMat& W, int row, int chunk) {
+  if (W.kind == kTernary) {
+    uint32_t word = ((const uint32_t*)W.codes)[(size_t)row * (W.k / 16) + chunk];
+    return make_int4((int)word, 0, 0, 0);
+  }
+  return __ldg((const int4*)((const int8_t*)W.codes + (size_t)row * W.k) + chunk);
+}
+
+__global__ void __launch_bounds__(GEMV_THREADS) k_gemv(DMat W, const int8_t* xq, const float* xs, int m, int mode,
+                                                        float* y, int ldy, float resid_mult, int units) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int k = W.k, groups = k / W.agroup;
+  const int rows_per_unit = (mode == kEpSilu) ? 2 : 1;
+  const int units_per_block = GEMV_ROWS / rows_per_unit;
+  const int unit0 = blockIdx.x * units_per_block;
+  const int nunits = min(units_per_block, units - unit0);
+  int8_t* act = (int8_t*)smem;                                      // [F][k]
+  float* act_s = (float*)(smem + GEMV_FRAMES * k);                  // [F][groups]
+  int* part = (int*)(act_s + GEMV_FRAMES * groups);                 // [ROWS][F][groups]
+  float* res = (float*)(part + GEMV_ROWS * GEMV_FRAMES * groups);   // [ROWS][F]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int chunks = k / 16;            // 16 k-values per lane-load
+  const int lanes_per_group = W.agroup / 16;
+  for (int f0 = 0; f0 < m; f0 += GEMV_FRAMES) {
+    const int nf = min(GEMV_FRAMES, m - f0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nf * k / 16; i += GEMV_THREADS)
+      ((int4*)act)[i] = ((const int4*)(xq + (size_t)f0 * k))[i];
+    for (int i = threadIdx.x; i < nf * groups; i += GEMV_THREADS) act_s[i] = xs[(size_t)f0 * groups + i];
+    __syncthreads();
+    // Group dots: warp w takes local rows w, w + 8, ...
+    for (int lr = warp; lr < nunits * rows_per_unit; lr += GEMV_THREADS / 32) {
+      int u = unit0 + lr / rows_per_unit;
+      int row = (mode == kEpSilu) ? u + (lr % 2) * units : u;
+      for (int c = lane; c < chunks + ((32 - chunks % 32) % 32); c += 32) {
+        bool live = c < chunks;
+        int4 w = live ? load_weights16(W, row, c) : make_int4(0, 0, 0, 0);
+        for (int f = 0; f < nf; ++f) {
+          int dot = 0;
+          if (live) {
+            int4 a = ((const int4*)(act + f * k))[c];
+            dot = (W.kind == kTernary) ? dot16_ternary((uint32_t)w.x, a) : dot16(w, a);
+          }
+          for (int o = 1; o < lanes_per_group; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+          if (live && (lane % lanes_per_group) == 0) part[(lr * GEMV_FRAMES + f) * groups + c / lanes_per_group] = dot;
+        }
+      }
+    }
+    __syncthreads();
+    // Chains: one thread per (local row, frame), groups in order.
+    for (int t = threadIdx.x; t < nunits * rows_per_unit * nf; t += GEMV_THREADS) {
+      int lr = t / nf, f = t % nf;
+      int u = unit0 + lr / rows_per_unit;
+      int row = (mode == kEpSilu) ? u + (lr % 2) * units : u;
+      const int* p = part + (lr * GEMV_FRAMES + f) * groups;
+      const float* sx = act_s + f * groups;
+      float acc = 0.0f;
+      for (int g = 0; g < groups; ++g)
+        acc = __fmaf_rn((float)p[g], __fmul_rn(weight_scale(W, row, g), sx[g]), acc);
+      res[lr * GEMV_FRAMES + f] = acc;
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < nunits * nf; t += GEMV_THREADS) {
+      int lu = t / nf, f = t % nf;
+      int u = unit0 + lu;
+      size_t at = (size_t)(f0 + f) * ldy + u;
+      if (mode == kEpOut) {
+        y[at] = res[lu * GEMV_FRAMES + f];
+      } else if (mode == kEpResid) {
+        float o = res[lu * GEMV_FRAMES + f];
+        y[at] = (resid_mult == 1.0f) ? __fadd_rn(y[at], o) : __fadd_rn(y[at], __fmul_rn(resid_mult, o));
+      } else {
+        float g = res[(2 * lu) * GEMV_FRAMES + f], up = res[(2 * lu + 1) * GEMV_FRAMES + f];
+        y[at] = __fmul_rn(silu(g), up);
+      }
+    }
+  }
+}
+
+size_t gemv_smem(const DMat& W) {
+  size_t groups = W.k / W.agroup;
+  return GEMV_FRAMES * (size_t)W.k + GEMV_FRAMES * groups * 4 + GEMV_ROWS * GEMV_FRAMES * groups * 4 +
+         GEMV_ROWS * GEMV_FRAMES * 4;
+}
+
+// ------------------------------------------- q/k norm, RoPE, KV append ----
+// causal_lm.rs:428-446: per-head RMSNorm of q and k (Qwen3), the halves
+// rotation of layers.rs:317-333 with the host's sin/cos table, Granite's
+// q scale, then K and V appended to the stream's pages. One block per
+// row, one warp per head; lane l holds values 4l..4l+3 of the head, so the
+// rotation partner of value i (i + 64) sits in lane l ^ 16.
+__global__ void k_qk_rope_append(float* qkv, int m, DConfig cfg, const float* q_norm, const float* k_norm,
+                                 const float* rope, int rope_rows, DCache cache, const int* row_stream,
+                                 const int* row_pos, int layer) {
+  int r = blockIdx.x;
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qd = cfg.heads * cfg.hd, kvd = cfg.kv_heads * cfg.hd, stride = qd + 2 * kvd;
+  int pos = row_pos[r], stream = row_stream[r];
+  float* row = qkv + (size_t)r * stride;
+  const int half = cfg.hd / 2;
+  const float* sn = rope + (size_t)min(pos, rope_rows - 1) * cfg.hd;  // [sin(half) | cos(half)]
+  const float* cs = sn + half;
+  for (int h = warp; h < cfg.heads + 2 * cfg.kv_heads; h += blockDim.x / 32) {
+    bool is_q = h < cfg.heads, is_k = !is_q && h < cfg.heads + cfg.kv_heads;
+    float* head = row + h * cfg.hd;  // q heads, then k heads, then v heads
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = head[lane * 4 + i];
+    if (!is_q && !is_k) {
+      // v: append as is
+    } else {
+      const float* nw = is_q ? q_norm : k_norm;
+      if (nw) {
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s = __fadd_rn(s, __fmul_rn(v[i], v[i]));
+        s = warp_sum(s);
+        float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)cfg.hd), cfg.eps)));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], __fmul_rn(inv, nw[lane * 4 + i]));
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float partner = __shfl_xor_sync(0xffffffffu, v[i], 16);
+        int idx = (lane & 15) * 4 + i;  // pair index
+        float c = cs[idx], s = sn[idx];
+        if (lane < 16) v[i] = __fsub_rn(__fmul_rn(v[i], c), __fmul_rn(partner, s));
+        else v[i] = __fadd_rn(__fmul_rn(v[i], c), __fmul_rn(partner, s));
+      }
+      if (is_q && cfg.has_q_scale) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], cfg.q_scale);
+      }
+    }
+    if (is_q) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) head[lane * 4 + i] = v[i];
+    } else {
+      int kvh = is_k ? h - cfg.heads : h - cfg.heads - cfg.kv_heads;
+      int page = cache.page_table[(size_t)stream * cache.pages_per_stream + pos / cache.page_tokens];
+      size_t off = kv_offset(cache, cfg, page, layer, is_k ? 0 : 1, kvh, pos % cache.page_tokens) + lane * 4;
+      if (cache.f16) {
+        __half* dst = (__half*)cache.pool + off;
+        dst[0] = __float2half_rn(v[0]);
+        dst[1] = __float2half_rn(v[1]);
+        dst[2] = __float2half_rn(v[2]);
+        dst[3] = __float2half_rn(v[3]);
+      } else {
+        float* dst = (float*)cache.pool + off;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = v[i];
+      }
+      if (is_k) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) head[lane * 4 + i] = v[i];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------- attention ----
+// Causal GQA softmax attention (layers.rs:343-504) of each row's query over
+// its stream's keys 0..pos, split over key ranges; each split keeps a
+// running maximum, sum and weighted V sum, and k_attention_combine joins
+// the splits. Scores are the reference's sequential fma chains over the
+// head dimension; the softmax sums and the V sums run in another order
+// than the reference's (tolerance, not bit-exact). 128 threads = hd.
+constexpr int ATT_TILE = 128;
+
+// q . key as one fma chain over the head dimension in order (the score of
+// fgemm's nn tile, src/cpu/fgemm.rs:790-800).
+__device__ __forceinline__ float score_chain(const DCache& c, size_t off, const float* q) {
+  float a = 0.0f;
+  if (c.f16) {
+    const int4* p = (const int4*)((const __half*)c.pool + off);
+#pragma unroll 4
+    for (int i = 0; i < 16; ++i) {
+      int4 raw = p[i];
+      const __half2* h = (const __half2*)&raw;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __half22float2(h[j]);
+        a = __fmaf_rn(q[8 * i + 2 * j], f.x, a);
+        a = __fmaf_rn(q[8 * i + 2 * j + 1], f.y, a);
+      }
+    }
+  } else {
+    const float4* p = (const float4*)((const float*)c.pool + off);
+#pragma unroll 4
+    for (int i = 0; i < 32; ++i) {
+      float4 f = p[i];
+      a = __fmaf_rn(q[4 * i], f.x, a);
+      a = __fmaf_rn(q[4 * i + 1], f.y, a);
+      a = __fmaf_rn(q[4 * i + 2], f.z, a);
+      a = __fmaf_rn(q[4 * i + 3], f.w, a);
+    }
+  }
+  return a;
+}
+
+__device__ __forceinline__ float load_value(const DCache& c, size_t off, int f16) {
+  return f16 ? __half2float(((const __half*)c.pool)[off]) : ((const float*)c.pool)[off];
+}
+
+__global__ void __launch_bounds__(128) k_attention(const float* qkv, int m, DConfig cfg, DCache cache,
+                                                   const int* row_stream, const int* row_pos, int layer,
+                                                   int splits, int split_len, float* part) {
+  const int r = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+  const int t = threadIdx.x;
+  const int qd = cfg.heads * cfg.hd, stride = qd + 2 * cfg.kv_heads * cfg.hd;
+  const int g = h / (cfg.heads / cfg.kv_heads);
+  const int pos = row_pos[r], stream = row_stream[r];
+  const int tk = pos + 1;
+  const int j0 = s * split_len, j1 = min(tk, j0 + split_len);
+  __shared__ float q[128];
+  __shared__ float p[ATT_TILE];
+  __shared__ float red[4];
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)cfg.hd));
+  q[t] = __fmul_rn(qkv[(size_t)r * stride + h * cfg.hd + t], scale);
+  __syncthreads();
+  float m_run = -INFINITY, l_run = 0.0f, acc = 0.0f;
+  for (int tile = j0; tile < j1; tile += ATT_TILE) {
+    int j = tile + t;
+    float score = -INFINITY;
+    if (j < j1) {
+      int page = cache.page_table[(size_t)stream * cache.pages_per_stream + j / cache.page_tokens];
+      size_t off = kv_offset(cache, cfg, page, layer, 0, g, j % cache.page_tokens);
+      float a = score_chain(cache, off, q);
+      score = a;
+    }
+    float mx = warp_max(score);
+    if ((t & 31) == 0) red[t >> 5] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    float m_new = fmaxf(m_run, mx);
+    float e = (j < j1) ? cephes_exp(__fsub_rn(score, m_new)) : 0.0f;
+    p[t] = e;
+    float sum = warp_sum(e);
+    if ((t & 31) == 0) red[t >> 5] = sum;
+    __syncthreads();
+    sum = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
+    float corr = (m_run == -INFINITY) ? 0.0f : cephes_exp(__fsub_rn(m_run, m_new));
+    l_run = __fadd_rn(__fmul_rn(l_run, corr), sum);
+    acc = __fmul_rn(acc, corr);
+    int n = min(ATT_TILE, j1 - tile);
+    for (int jj = 0; jj < n; ++jj) {
+      int jk = tile + jj;
+      int page = cache.page_table[(size_t)stream * cache.pages_per_stream + jk / cache.page_tokens];
+      size_t off = kv_offset(cache, cfg, page, layer, 1, g, jk % cache.page_tokens) + t;
+      acc = __fmaf_rn(p[jj], load_value(cache, off, cache.f16), acc);
+    }
+    m_run = m_new;
+    __syncthreads();
+  }
+  float* out = part + (((size_t)r * cfg.heads + h) * splits + s) * (128 + 2);
+  out[2 + t] = acc;
+  if (t == 0) {
+    out[0] = m_run;
+    out[1] = l_run;
+  }
+}
+
+__global__ void k_attention_combine(const float* part, int m, DConfig cfg, int splits, const int* row_pos,
+                                    int split_len, float* att) {
+  const int r = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
+  const int tk = row_pos[r] + 1;
+  const int used = (tk + split_len - 1) / split_len;
+  const float* base = part + ((size_t)r * cfg.heads + h) * splits * 130;
+  float mx = -INFINITY;
+  for (int s = 0; s < used; ++s) mx = fmaxf(mx, base[s * 130]);
+  float l = 0.0f, acc = 0.0f;
+  for (int s = 0; s < used; ++s) {
+    float w = cephes_exp(__fsub_rn(base[s * 130], mx));
+    l = __fmaf_rn(w, base[s * 130 + 1], l);
+    acc = __fmaf_rn(w, base[s * 130 + 2 + t], acc);
+  }
+  att[(size_t)r * cfg.heads * cfg.hd + h * cfg.hd + t] = __fdiv_rn(acc, l);
+}
+
+// ------------------------------------------------ final norm + table ----
+// forward_rows' last step (causal_lm.rs:384-388): RmsNorm of the row, then
+// the token table in f32 math (Q8::matmul -> fgemm::matmul_widened). Each
+// thread owns one vocabulary row and keeps the 16 lanes of the AVX-512 tile
+// (lane l sums k = 16t + l in order with fma) and the _mm512_reduce_add_ps
+// tree (fgemm.rs:380-430), so a logit is the reference's value bit for bit
+// for the same normed row. The block's codes come through shared memory in
+// slabs of 128 bytes a row.
+constexpr int TABLE_ROWS = 64;   // vocabulary rows per block, 4 threads each
+constexpr int TABLE_MAX_B = 16;  // streams per pass
+
+// The token table for `nb` normed rows (streams) at once. Thread q of a
+// vocabulary row holds lanes 4q..4q+3 of the reference's 16-lane
+// accumulator: at step t it reads the 4 code bytes k = 16t + 4q .. +3 (a
+// 32-bit load; the 4 threads of a row read 16 consecutive bytes), widens
+// them (code * scale, exact in f32) and adds x * w into its lanes with
+// fma. The reduce tree then runs across the 4 threads in the order of
+// _mm512_reduce_add_ps.
+template <int B>
+__global__ void __launch_bounds__(256) k_table(DTable T, const float* xn, int nb, float logit_mult, float* logits,
+                                               float* best_val, int* best_idx, int nblocks) {
+  extern __shared__ __align__(16) float xt[];  // [k][B]: the rows side by side
+  const int t = threadIdx.x, q = t & 3;
+  const int row = blockIdx.x * TABLE_ROWS + (t >> 2);
+  for (int i = t; i < T.k * B; i += 256) {
+    int kk = i / B, b = i % B;
+    xt[i] = (b < nb) ? xn[(size_t)b * T.k + kk] : 0.0f;
+  }
+  __syncthreads();
+  float acc[B][4];
+#pragma unroll
+  for (int b = 0; b < B; ++b)
+#pragma unroll
+    for (int l = 0; l < 4; ++l) acc[b][l] = 0.0f;
+  const bool live = row < T.n;
+  if (live) {
+    const uint32_t* codes = (const uint32_t*)(T.codes + (size_t)row * T.k) + q;
+    const int steps = T.k / 16;
+#pragma unroll 4
+    for (int st = 0; st < steps; ++st) {
+      uint32_t word = __ldg(codes + 4 * st) ^ 0x80808080u;
+      float s = table_scale(T, row, st >> 1);
+      int kk = 16 * st + 4 * q;
+#pragma unroll
+      for (int l = 0; l < 4; ++l) {
+        float w = __fmul_rn(byte_to_float(word, l), s);
+#pragma unroll
+        for (int b = 0; b < B; ++b) acc[b][l] = __fmaf_rn(xt[(kk + l) * B + b], w, acc[b][l]);
+      }
+    }
+  }
+  __shared__ float bv[B][8];
+  __shared__ int bi[B][8];
+  const int lane = t & 31, warp = t >> 5;
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    // s8[i] = a[i] + a[i + 8]: threads 0,1 take the lanes of threads 2,3.
+    float s8[4];
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+      float other = __shfl_down_sync(0xffffffffu, acc[b][l], 2);
+      s8[l] = __fadd_rn(acc[b][l], other);
+    }
+    // s4[i] = s8[i] + s8[i + 4]: thread 0 takes thread 1's.
+    float s4[4];
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+      float other = __shfl_down_sync(0xffffffffu, s8[l], 1);
+      s4[l] = __fadd_rn(s8[l], other);
+    }
+    float v = __fadd_rn(__fadd_rn(s4[0], s4[2]), __fadd_rn(s4[1], s4[3]));
+    int idx = 0x7fffffff;
+    if (q == 0 && live && b < nb) {
+      if (logit_mult != 1.0f) v = __fmul_rn(v, logit_mult);
+      if (logits) logits[(size_t)b * T.n + row] = v;
+      idx = row;
+      if (v != v) { v = -INFINITY; idx = 0x7fffffff; }  // a NaN never wins
+    } else {
+      v = -INFINITY;
+    }
+    // The largest value; the lowest index among equals (layers.rs:603-612).
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
+    }
+    if (lane == 0) { bv[b][warp] = v; bi[b][warp] = idx; }
+  }
+  __syncthreads();
+  if (t < nb && t < B) {
+    float v = bv[t][0];
+    int idx = bi[t][0];
+    for (int i = 1; i < 8; ++i)
+      if (bv[t][i] > v || (bv[t][i] == v && bi[t][i] < idx)) { v = bv[t][i]; idx = bi[t][i]; }
+    best_val[(size_t)t * nblocks + blockIdx.x] = v;
+    best_idx[(size_t)t * nblocks + blockIdx.x] = idx;
+  }
+}
+
+__global__ void k_argmax(const float* val, const int* idx, int n, int* token) {
+  // One warp per stream (blockIdx.x): partials [stream][n].
+  val += (size_t)blockIdx.x * n;
+  idx += (size_t)blockIdx.x * n;
+  float v = -INFINITY;
+  int i = 0x7fffffff;
+  for (int p = threadIdx.x; p < n; p += 32) {
+    if (val[p] > v || (val[p] == v && idx[p] < i)) { v = val[p]; i = idx[p]; }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+  }
+  if (threadIdx.x == 0) token[blockIdx.x] = (i == 0x7fffffff) ? 0 : i;
+}
+
+// ------------------------------------------------------------ launch ----
+#define LAUNCH_CHECK()                                   \
+  do {                                                   \
+    cudaError_t e_ = cudaGetLastError();                 \
+    if (e_ != cudaSuccess) return e_;                    \
+  } while (0)
+
+cudaError_t launch_embed(const DTable& T, const int* ids, int m, float* x, float mult, cudaStream_t s) {
+  k_embed<<<m, 256, 0, s>>>(T, ids, m, x, mult);
+  LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
+cudaError_t launch_scale(float* x, size_t n, float mult, cudaStream_t s) {
+  k_scale<<<(unsigned)std::min<size_t>((n + 255) / 256, 4096), 256, 0, s>>>(x, n, mult);
+  LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
+cudaError_t launch_norm_quant(const float* x, int m, int d, const float* w, float eps, int group, int half,
+                              int8_t* xq, float* xs, cudaStream_t s) {
+  if (group == 32) k_norm_quant<32><<<m, 256, 0, s>>>(x, d, w, eps, half, xq, xs);
+  else k_norm_quant<128><<<m, 256, 0, s>>>(x, d, w, eps, half, xq, xs);
+  LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
+cudaError_t launch_gemv(const DMat& W, const int8_t* xq, const float* xs, int m, int mode, float* y, int ldy,
+                        float resid_mult, cudaStream_t s) {
+  int units = (mode == kEpSilu) ? W.n / 2 : W.n;
+  int per_block = (mode == kEpSilu) ? GEMV_ROWS / 2 : GEMV_ROWS;
+  size_t smem = gemv_smem(W);
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    configured = true;
+  }
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  k_gemv<<<(units + per_block - 1) / per_block, GEMV_THREADS, smem, s>>>(W, xq, xs, m, mode, y, ldy, resid_mult,
+                                                                         units);
+  LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
+cudaError_t launch_qk_rope_append(float* qkv, int m, const DConfig& cfg, const float* q_norm, const float* k_norm,
+                                  const float* rope, int rope_rows, const DCache& cache, const int* row_stream,
+                                  const int* row_pos, int layer, cudaStream_t s) {
+  k_qk_rope_append<<<m, 256, 0, s>>>(qkv, m, cfg, q_norm, k_norm, rope, rope_rows, cache, row_stream, row_pos,
+                                     layer);
+  LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
+cudaError_t launch_attention(const float* qkv, int m, const DConfig& cfg, const DCache& cache, const int* row_stream,
+                             const int* row_pos, int layer, int max_tk, float* part, size_t part_floats, float* att,
+                             cudaStream_t s) {
+  int split_len = 256;
+  int splits = (max_tk + split_len - 1) / split_len;
+  if ((size_t)m * cfg.heads * splits * 130 > part_floats) return cudaErrorInvalidValue;
+  dim3 grid(m, cfg.heads, splits);
+  k_attention<<<grid, 128, 0, s>>>(qkv, m, cfg, cache, row_stream, row_pos, layer, splits, split_len, part);
+  LAUNCH_CHECK();
+  k_attention_combine<<<dim3(m, cfg.heads), 128, 0, s>>>(part, m, cfg, splits, row_pos, split_len, att);
+  LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
+// Final RmsNorm of `nb` rows (row stride `ldx`), then the table and the
+// argmax of every row: token[b].
+__global__ void __launch_bounds__(256) k_final_norm_rows(const float* x, int ldx, int d, const float* w, float eps,
+                                                         float* xn) {
+  const float* row = x + (size_t)blockIdx.x * ldx;
+  float* out = xn + (size_t)blockIdx.x * d;
+  __shared__ float red[8];
+  __shared__ float s_inv;
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < d; i += 256) s = __fadd_rn(s, __fmul_rn(row[i], row[i]));
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int i = 0; i < 8; ++i) t = __fadd_rn(t, red[i]);
+    s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)d), eps)));
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < d; i += 256) out[i] = __fmul_rn(row[i], __fmul_rn(s_inv, w[i]));
+}
+
+template <int B>
+static cudaError_t table_pass(const DTable& T, const float* xn, int nb, float mult, float* logits, float* best_val,
+                              int* best_idx, cudaStream_t s) {
+  size_t smem = (size_t)T.k * B * 4;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(k_table<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    configured = true;
+  }
+  int blocks = table_blocks(T.n);
+  k_table<B><<<blocks, 256, smem, s>>>(T, xn, nb, mult, logits, best_val, best_idx, blocks);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_final(const float* x, int ldx, int nb, const float* norm_w, const DConfig& cfg, const DTable& T,
+                         float* xn, float* logits, float* best_val, int* best_idx, int* token, cudaStream_t s) {
+  k_final_norm_rows<<<nb, 256, 0, s>>>(x, ldx, cfg.d, norm_w, cfg.eps, xn);
+  LAUNCH_CHECK();
+  float mult = (cfg.logits_scaling == 1.0f) ? 1.0f : 1.0f / cfg.logits_scaling;
+  int blocks = table_blocks(T.n);
+  cudaError_t e = launch_table(T, xn, nb, mult, logits, best_val, best_idx, s);
+  if (e != cudaSuccess) return e;
+  k_argmax<<<nb, 32, 0, s>>>(best_val, best_idx, blocks, token);
+  LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
+cudaError_t launch_table(const DTable& T, const float* xn, int nb, float mult, float* logits, float* best_val,
+                         int* best_idx, cudaStream_t s) {
+  int blocks = table_blocks(T.n);
+  for (int b0 = 0; b0 < nb; b0 += TABLE_MAX_B) {
+    int n = std::min(TABLE_MAX_B, nb - b0);
+    const float* xb = xn + (size_t)b0 * T.k;
+    float* lg = logits ? logits + (size_t)b0 * T.n : nullptr;
+    float* bv = best_val + (size_t)b0 * blocks;
+    int* bi = best_idx + (size_t)b0 * blocks;
+    cudaError_t e;
+    if (n == 1) e = table_pass<1>(T, xb, n, mult, lg, bv, bi, s);
+    else if (n <= 4) e = table_pass<4>(T, xb, n, mult, lg, bv, bi, s);
+    else e = table_pass<16>(T, xb, n, mult, lg, bv, bi, s);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+int table_blocks(int n) { return (n + TABLE_ROWS - 1) / TABLE_ROWS; }
+int table_max_streams() { return TABLE_MAX_B; }
+
+}  // namespace trit
