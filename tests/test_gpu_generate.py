@@ -1,7 +1,9 @@
 """Parity of the CUDA decoder with the CPU oracle (a restatement of Trit's
 CausalLm, src/models/parts/causal_lm.rs) on seeded small models of each
-weight format: greedy tokens identical for the whole generation, logits
-within max-abs 2e-2 and cosine >= 0.9995 at every step."""
+weight format: greedy tokens identical for the whole generation and the
+logits of every step bit for bit equal to the oracle's (the oracle keeps an
+f16 cache when the decoder does). The north star's tolerance (max-abs 2e-2,
+cosine >= 0.9995) is checked as well."""
 import numpy as np
 import pytest
 
@@ -19,12 +21,14 @@ def _cos(a, b):
     return float(np.dot(a, b) / (np.linalg.norm(a) * np.linalg.norm(b)))
 
 
-def _compare(ref, toks, logits):
+def _compare(ref, toks, logits, exact=True):
     assert toks == ref["tokens"], f"tokens differ: {toks} vs {ref['tokens']} (gaps {ref['gaps']})"
     for i in range(len(toks)):
         a, b = logits[i], ref["logits"][i]
         assert np.abs(a - b).max() <= MAX_ABS, f"step {i}: max abs {np.abs(a - b).max()}"
         assert _cos(a, b) >= MIN_COS, f"step {i}: cosine {_cos(a, b)}"
+        if exact:
+            assert np.array_equal(a, b), f"step {i}: {int((a != b).sum())} logits differ, max {np.abs(a - b).max()}"
 
 
 @pytest.mark.parametrize("name", FORMATS)

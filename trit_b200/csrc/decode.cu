@@ -1,24 +1,34 @@
 // The persistent batch-1 decode: every greedy step of one generation in
 // one cooperative kernel (one block per SM). A step runs the layers of
-// CausalLm::hidden (src/models/parts/causal_lm.rs:410-481) as five phases
-// separated by grid barriers:
+// CausalLm::hidden (src/models/parts/causal_lm.rs:410-481) as five phases:
 //   P1 qkv      every block: RmsNorm + quantize of x (redundant, 4 KB), then
 //               its slice of the stacked q/k/v rows
-//   P2 attend   block (kv head, split): q/k norm, RoPE, K/V append (split 0),
-//               a key range of GQA attention; the last split of a head joins
-//               the splits and quantizes the head's output
-//   P3 o        every block: its rows of o_proj, added to x (residual)
+//   P2 attend   block kvh (one per kv head): q/k norm, RoPE, K/V append,
+//               the exact GQA attention of the kv head's query heads over
+//               every key, and the quantized head outputs
+//   P3 o        every block: its rows of o_proj, added to its residual rows
 //   P4 gate_up  every block: RmsNorm + quantize of x, its units of gate/up,
 //               h = silu(gate) * up
-//   P5 down     every block: quantize h, its rows of down_proj, added to x
+//   P5 down     every block: quantize h, its rows of down_proj, added to its
+//               residual rows
 // then the final RmsNorm, the block's slice of the token table (f32 math),
-// and a per-block argmax that every block reduces to the same token.
-// Weights of the next phases are prefetched into L2 while a block waits.
+// and the argmax, which every block reduces from all blocks' bests.
 //
-// Waits are bounded: a barrier that does not complete within ~2^22 polls
-// sets *status and every block returns; the host reports the error.
+// No grid barrier: a value that one block makes and another needs travels
+// as a 64-bit word {data, tag} (the low-latency protocol of NCCL's LL
+// transfers): the tag names the step and phase, and a consumer polls the
+// words themselves, so the data and the "ready" signal arrive in one round
+// trip. Each buffer is written once per layer; the all-to-all chain of
+// phases guarantees that every reader of a word has read it before its
+// writer can reach the next write of that word. A block issues its weight
+// loads before it waits for its input. Each block keeps the residual rows
+// it owns in shared memory.
+//
+// Waits are bounded: a poll that sees no data within ~2^22 rounds sets
+// *status and every block returns; the host reports the error.
 #include <cuda_runtime.h>
 
+#include "attention.cuh"
 #include "device.cuh"
 #include "kernels.h"
 
@@ -27,106 +37,108 @@ namespace {
 
 constexpr int DT = 512;          // threads per block
 constexpr int DW = DT / 32;      // warps per block
-constexpr int TAB_TILE = 128;    // table rows per tile (4 threads a row)
-constexpr int TAB_SLAB = 128;    // bytes of a row per pipeline stage
-constexpr int TAB_STAGES = 4;
+constexpr int TAB_SLAB = 128;    // bytes of a table row per pipeline stage
+constexpr int TAB_STAGES = 6;
 constexpr int TAB_PITCH = TAB_SLAB + 16;
+constexpr int TAB_ROWS_W = 8;    // table rows per warp group (4 threads a row)
 constexpr long long SPIN_LIMIT = 1ll << 22;
-
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
+constexpr int LLW = 4;           // LL words a thread polls at once
 
 __device__ __forceinline__ int ld_volatile(const int* p) { return *(const volatile int*)p; }
 
-// Grid barrier on a counter that only grows: barrier b of this launch
-// waits for b * gridDim.x arrivals. Returns false when the wait ran out
-// (or another block gave up): the caller returns at once.
-__device__ bool grid_barrier(unsigned* counter, unsigned& target, int* status, volatile int* s_flag) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    target += gridDim.x;
-    __threadfence();
-    atomicAdd(counter, 1u);
-    long long spins = 0;
-    int bad = 0;
-    while (ld_acquire(counter) < target) {
-      if (++spins > SPIN_LIMIT) {
-        atomicCAS(status, 0, 1);
-        bad = 1;
-        break;
-      }
-      if ((spins & 1023) == 0 && ld_volatile(status) != 0) {
-        bad = 1;
-        break;
-      }
-    }
-    __threadfence();
-    *s_flag = bad;
-  }
-  __syncthreads();
-  return *s_flag == 0;
+__device__ __forceinline__ long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return (long long)t;
 }
 
 __device__ __forceinline__ int split_at(int n, int part, int parts) { return (int)((long long)n * part / parts); }
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
-}
 __device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
   unsigned s = (unsigned)__cvta_generic_to_shared(smem);
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(s), "l"(gmem) : "memory");
 }
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-struct Shared {
-  float* xf;       // [d]: x, normed x (final), or h
-  int8_t* xq;      // [kmax]
-  float* xs;       // [kmax / 32]
-  int* part;       // [rows][groups] group dots
-  float* out;      // [rows]
-  float* red;      // [64]
-  float* att;      // attention scratch
-  uint8_t* tab;    // table stages
-  int* flag;       // [4]
-};
-
-// Block reductions over all DT threads.
-__device__ float block_sum(float v, float* red) {
-  v = warp_sum(v);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = 0.0f;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < DW; ++i) t = __fadd_rn(t, red[i]);
-    red[DW] = t;
-  }
-  __syncthreads();
-  return red[DW];
+// ------------------------------------------------------------ LL words --
+__device__ __forceinline__ void ll_put(unsigned long long* p, uint32_t data, uint32_t tag) {
+  unsigned long long v = ((unsigned long long)tag << 32) | data;
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_get(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
-// RmsNorm (layers.rs:135-144) of src (d values) with weight w (null: no
-// norm), then Quantized::grouped of the result into xq / xs.
-__device__ void norm_quant(const float* src, int d, const float* w, float eps, int G, bool half, Shared& S) {
-  if (src != S.xf) {
-    for (int i = threadIdx.x; i < d; i += DT) S.xf[i] = src[i];
+// The block waits until words [0, n) of `src` carry `tag` and hands each
+// word's data to sink(i, data). Thread t polls words t, t + DT, ...: every
+// load of a round goes out before any is checked. False when a wait ran
+// out (the whole block then returns).
+template <class Sink>
+__device__ bool ll_wait(const unsigned long long* src, int n, uint32_t tag, int* status, Sink sink) {
+  bool ok = true;
+  // Passes of LLW words a thread (one pass for n <= LLW * DT).
+  for (int base = 0; base < n && ok; base += LLW * DT) {
+    uint32_t pending = 0;
+#pragma unroll
+    for (int j = 0; j < LLW; ++j)
+      if (base + threadIdx.x + DT * j < n) pending |= 1u << j;
+    long long spins = 0;
+    while (pending) {
+      unsigned long long v[LLW];
+#pragma unroll
+      for (int j = 0; j < LLW; ++j)
+        if (pending & (1u << j)) v[j] = ll_get(src + base + threadIdx.x + DT * j);
+#pragma unroll
+      for (int j = 0; j < LLW; ++j)
+        if ((pending & (1u << j)) && (uint32_t)(v[j] >> 32) == tag) {
+          sink(base + threadIdx.x + DT * j, (uint32_t)v[j]);
+          pending &= ~(1u << j);
+        }
+      if (pending) {
+        if (++spins > SPIN_LIMIT) {
+          atomicCAS(status, 0, 2);
+          ok = false;
+          break;
+        }
+        if ((spins & 255) == 0 && ld_volatile(status) != 0) {
+          ok = false;
+          break;
+        }
+      }
+    }
   }
+  return __syncthreads_and(ok) != 0;
+}
+
+struct Shared {
+  float* xf;       // [kmax]: the phase's f32 input (x or h), normed x for the table
+  int8_t* xq;      // [kmax]
+  float* xs;       // [kmax / 32]
+  float* own;      // [512]: the residual rows this block owns
+  float* out;      // [512]
+  float* red;      // [64]
+  int* part;       // union: GEMV group dots ...
+  float* att;      // ... attention scratch ...
+  uint8_t* tab;    // ... table stages
+  int* flag;       // [16]
+  int gmax;        // the most activation groups of any product
+};
+
+// RmsNorm (layers.rs:135-144) of S.xf (d values) with weight w (null: no
+// norm), then Quantized::grouped of the result into S.xq / S.xs.
+__device__ void norm_quant(int d, const float* w, float eps, int G, bool half, Shared& S) {
   __syncthreads();
   float inv = 1.0f;
   if (w) {
-    float s = 0.0f;
-    for (int i = threadIdx.x; i < d; i += DT) s = __fadd_rn(s, __fmul_rn(S.xf[i], S.xf[i]));
-    float t = block_sum(s, S.red);
-    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)d), eps)));
+    // The sum of squares in the reference's order, by one thread.
+    if (threadIdx.x == 0) S.red[0] = rms_inv(seq_sum_squares(S.xf, d), d, eps);
+    __syncthreads();
+    inv = S.red[0];
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups = d / G;
@@ -151,111 +163,179 @@ __device__ void norm_quant(const float* src, int d, const float* w, float eps, i
   __syncthreads();
 }
 
-__device__ __forceinline__ int4 load16(const DMat& W, int row, int chunk) {
-  if (W.kind == kTernary) {
-    uint32_t word = __ldg((const uint32_t*)W.codes + (size_t)row * (W.k / 16) + chunk);
-    return make_int4((int)word, 0, 0, 0);
-  }
-  return ld_stream((const int8_t*)W.codes + (size_t)row * W.k + (size_t)chunk * 16);
+// ------------------------------------------------------------- products --
+constexpr int WSTAGE = 40 * 1024;  // bytes of one weight staging buffer (two of them)
+
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem) : "memory");
 }
 
-// Group dots of `nrows` rows (row(lr) gives the weight row of local row
-// lr) against the activations in S.xq, into S.part[lr][g]; then one
-// thread per local row runs the group chain of int8.rs:560-570 in order
-// and stores the output in S.out[lr].
-template <class RowOf>
-__device__ void gemv_rows(const DMat& W, int nrows, RowOf row_of, Shared& S) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int k = W.k, chunks = k / 16, groups = k / W.agroup, lpg = W.agroup / 16;
-  constexpr int MAXC = 8;
-  for (int lr = warp; lr < nrows; lr += DW) {
-    const int row = row_of(lr);
-    for (int base = 0; base < chunks; base += 32 * MAXC) {
-      int4 w[MAXC];
-#pragma unroll
-      for (int j = 0; j < MAXC; ++j) {
-        int c = base + lane + 32 * j;
-        w[j] = c < chunks ? load16(W, row, c) : make_int4(0, 0, 0, 0);
+__host__ __device__ inline int code_row_bytes(const DMat& W) { return W.kind == kTernary ? W.k / 4 : W.k; }
+__host__ __device__ inline int scale_row_bytes(const DMat& W) {
+  return W.kind == kQ8_0 ? W.k / 32 * 2 : W.kind == kInt8Row ? 4 : W.k / 128 * 4;
+}
+__host__ __device__ inline int staged_row_bytes(const DMat& W) {
+  return (code_row_bytes(W) + 15) / 16 * 16 + (scale_row_bytes(W) + 15) / 16 * 16;
+}
+
+// Rows of a W8A8 layer for this block (row_of(lr) is the weight row of
+// local row lr). The rows' codes and scales stream into shared memory by
+// cp.async in batches of up to WSTAGE bytes, double-buffered; the first
+// batch is issued before `ready()` (the block's wait for its input and its
+// quantization), so the weights travel while the block waits. Warp w takes
+// local rows w, w + DW, ...: its lanes form the i32 group dots from 16-byte
+// chunks, then lane 0 runs the row's group chain of int8.rs:560-570 in
+// order into S.out[lr].
+template <class RowOf, class Ready>
+__device__ bool gemv(const DMat& W, int nrows, RowOf row_of, Shared& S, Ready ready) {
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int k = W.k, groups = k / W.agroup, lpg = W.agroup / 16, chunks = k / 16;
+  const int crow = code_row_bytes(W), srow = scale_row_bytes(W);
+  const int cpad = (crow + 15) / 16 * 16, rbytes = staged_row_bytes(W);
+  const int per = min(nrows, WSTAGE / rbytes);  // rows a batch (the host checks rbytes <= WSTAGE)
+  const int nbatch = per > 0 ? (nrows + per - 1) / per : 0;
+  uint8_t* buf0 = (uint8_t*)S.part;
+  uint8_t* buf1 = buf0 + WSTAGE;
+  int* wdot = (int*)(buf1 + WSTAGE) + warp * (S.gmax * 2);  // this warp's [groups] dots, then [groups] scales
+  float* wscl = (float*)(wdot + S.gmax);
+  auto issue = [&](int b) {
+    if (b < nbatch) {
+      uint8_t* dst = (b & 1) ? buf1 : buf0;
+      const int lr0 = b * per, n = min(per, nrows - lr0);
+      const int cchunks = crow / 16, swords = srow / 4;
+      for (int i = t; i < n * cchunks; i += DT) {
+        int r = i / cchunks, cc = i % cchunks;
+        cp_async16(dst + r * rbytes + cc * 16, (const uint8_t*)W.codes + (size_t)row_of(lr0 + r) * crow + cc * 16);
       }
-#pragma unroll
-      for (int j = 0; j < MAXC; ++j) {
-        int c = base + lane + 32 * j;
-        if (base + 32 * j >= chunks) break;  // warp-uniform
-        int dot = 0;
-        if (c < chunks) {
-          int4 a = ((const int4*)S.xq)[c];
-          dot = (W.kind == kTernary) ? dot16_ternary((uint32_t)w[j].x, a) : dot16(w[j], a);
-        }
-        for (int o = 1; o < lpg; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-        if (c < chunks && (lane % lpg) == 0) S.part[lr * groups + c / lpg] = dot;
+      for (int i = t; i < n * swords; i += DT) {
+        int r = i / swords, w4 = i % swords;
+        cp_async4(dst + r * rbytes + cpad + w4 * 4, (const uint8_t*)W.scales + (size_t)row_of(lr0 + r) * srow + w4 * 4);
       }
     }
+    cp_commit();
+  };
+  issue(0);
+  if (!ready()) {
+    cp_wait<0>();
+    return false;
   }
-  __syncthreads();
-  for (int lr = threadIdx.x; lr < nrows; lr += DT) {
-    const int row = row_of(lr);
-    const int* p = S.part + lr * groups;
-    float acc = 0.0f;
-    for (int g = 0; g < groups; ++g) acc = __fmaf_rn((float)p[g], __fmul_rn(weight_scale(W, row, g), S.xs[g]), acc);
-    S.out[lr] = acc;
+  for (int b = 0; b < nbatch; ++b) {
+    issue(b + 1);
+    cp_wait<1>();
+    __syncthreads();
+    const uint8_t* src = (b & 1) ? buf1 : buf0;
+    const int lr0 = b * per, n = min(per, nrows - lr0);
+    for (int r = warp; r < n; r += DW) {
+      const uint8_t* rowp = src + r * rbytes;
+      for (int c0 = 0; c0 < chunks; c0 += 32) {
+        const int c = c0 + lane;
+        int dot = 0;
+        if (c < chunks) {
+          int4 act = ((const int4*)S.xq)[c];
+          if (W.kind == kTernary) dot = dot16_ternary(((const uint32_t*)rowp)[c], act);
+          else dot = dot16(((const int4*)rowp)[c], act);
+        }
+        for (int o = 1; o < lpg; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        if (c < chunks && (lane % lpg) == 0) {
+          const int g = c / lpg;
+          float ws = W.kind == kQ8_0 ? f16_bits_to_f32(((const uint16_t*)(rowp + cpad))[g])
+                     : W.kind == kInt8Row ? ((const float*)(rowp + cpad))[0]
+                                          : ((const float*)(rowp + cpad))[g];
+          wdot[g] = dot;
+          wscl[g] = __fmul_rn(ws, S.xs[g]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        float acc = 0.0f;
+        for (int g = 0; g < groups; ++g) acc = __fmaf_rn((float)wdot[g], wscl[g], acc);
+        S.out[lr0 + r] = acc;
+      }
+      __syncwarp();
+    }
+    __syncthreads();  // the buffer is refilled by issue(b + 2)
   }
-  __syncthreads();
-}
-
-__device__ __forceinline__ void prefetch_rows(const DMat& W, int r0, int r1) {
-  if (r1 <= r0) return;
-  size_t code_row = (W.kind == kTernary) ? (size_t)W.k / 4 : (size_t)W.k;
-  prefetch_l2((const int8_t*)W.codes + (size_t)r0 * code_row, (uint32_t)((r1 - r0) * code_row));
-  size_t scale_row = W.kind == kQ8_0 ? (size_t)(W.k / 32) * 2 : W.kind == kInt8Row ? 4 : (size_t)(W.k / 128) * 4;
-  prefetch_l2((const int8_t*)W.scales + (size_t)r0 * scale_row, (uint32_t)((r1 - r0) * scale_row));
-}
-
-// The slices of a layer's weights that block c reads, prefetched into L2.
-__device__ void prefetch_layer(const DLayer& L, const DConfig& cfg, int c, int nb, bool qkv, bool rest) {
-  if (threadIdx.x != 0) return;
-  if (qkv) prefetch_rows(L.qkv, split_at(L.qkv.n, c, nb), split_at(L.qkv.n, c + 1, nb));
-  if (rest) {
-    prefetch_rows(L.out, split_at(L.out.n, c, nb), split_at(L.out.n, c + 1, nb));
-    int u0 = split_at(cfg.ffn, c, nb), u1 = split_at(cfg.ffn, c + 1, nb);
-    prefetch_rows(L.gate_up, u0, u1);
-    prefetch_rows(L.gate_up, cfg.ffn + u0, cfg.ffn + u1);
-    prefetch_rows(L.down, split_at(L.down.n, c, nb), split_at(L.down.n, c + 1, nb));
-  }
+  cp_wait<0>();
+  return true;
 }
 
 // ------------------------------------------------------------ attention --
-// Block (kvh, s) of the P2 phase. Scores are the reference's sequential fma
-// chains; the softmax of the block's keys and the join across blocks run
-// in another order than the reference's (tolerance).
-__device__ void attend(const DecodeArgs& a, const DLayer& L, int layer, int pos, int kvh, int s, int S_splits,
-                       unsigned* counters, Shared& S) {
+// LL word offsets of the decode buffers.
+struct LlLayout {
+  int qkv, attq, attq_scales, xa, h, xb, best, total;
+  __host__ __device__ LlLayout(const DConfig& cfg, int grid) {
+    const int qd = cfg.heads * 128, nqkv = qd + 2 * cfg.kv_heads * 128;
+    qkv = 0;
+    attq = nqkv;
+    attq_scales = attq + qd / 4;
+    xa = attq_scales + qd / 32;
+    h = xa + cfg.d;
+    xb = h + cfg.ffn;
+    best = xb + cfg.d;
+    total = best + 2 * grid;
+  }
+};
+
+__host__ __device__ inline int attend_kt(int f16) { return f16 ? 128 : 64; }
+
+// Shared memory of the attention phase, in floats.
+__host__ __device__ inline size_t attend_smem_floats(int qpk, int tmax, int f16) {
+  return (size_t)(qpk + 2) * 128 + (size_t)qpk * 128 + 2 * 128 + (size_t)qpk * 128 + (size_t)qpk * 4 +
+         (size_t)qpk * 32 + attention_smem_floats(qpk, tmax, attend_kt(f16), f16);
+}
+
+// Block kvh of the P2 phase: the query heads of kv head kvh over keys
+// 0..pos, exact (attention.cuh). Tile 0 of the cached keys and values goes
+// out (cp.async) before the block waits for q, k and v; the block appends
+// the new key and value to the cache and publishes the heads' quantized
+// output as LL words.
+__device__ bool attend(const DecodeArgs& a, const DLayer& L, int layer, int pos, int kvh, int tmax, uint32_t tag_in,
+                       uint32_t tag_out, Shared& S) {
   const DConfig& cfg = a.cfg;
   const int hd = 128, qpk = cfg.heads / cfg.kv_heads, qd = cfg.heads * hd, kvd = cfg.kv_heads * hd;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int T = pos + 1, len = (T + S_splits - 1) / S_splits;
-  const int j0 = min(T, s * len), j1 = min(T, j0 + len), nk = j1 - j0;
-  float* q = S.att;                 // [qpk][128]
-  float* kf = q + qpk * hd;         // [128]
-  float* vf = kf + hd;              // [128]
-  float* sc = vf + hd;              // [qpk][len]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
+  const int T = pos + 1;
   const DCache& cache = a.cache;
+  const LlLayout ll(cfg, gridDim.x);
+  const int nq = qpk * hd;
+  float* raw = S.att;               // [(qpk + 2)][128]: q heads, k, v as P1 made them
+  float* q = raw + nq + 2 * hd;     // [qpk][128]
+  float* kf = q + nq;               // [128]
+  float* vf = kf + hd;              // [128]
+  float* out = vf + hd;             // [qpk][128]
+  float* scales = out + nq;         // [qpk * 4]: one a group of 32 at most
+  int8_t* codes = (int8_t*)(scales + qpk * 4);  // [qpk * 128] bytes
+  float* region = scales + qpk * 4 + qpk * 32;
+  const int kt = attend_kt(cache.f16), row = cache.f16 ? 64 : 128;
+  float* sc = region;
+  float* ktl = sc + qpk * tmax;
+  float* vtl = ktl + kt * (row + 4);
+  float* stat = vtl + kt * row;
+  Attention<DT> A{cache, cfg, a.stream, layer, kvh, qpk, kt, sc, ktl, vtl, stat, tmax};
+  A.preload(T, true);
+  // q heads, k and v of this kv head, as P1 made them.
+  bool ok = ll_wait(a.ll + ll.qkv + kvh * nq, nq, tag_in, a.status, [&](int i, uint32_t v) { raw[i] = __uint_as_float(v); });
+  if (!ok) return false;
+  ok = ll_wait(a.ll + ll.qkv + qd + kvh * hd, hd, tag_in, a.status, [&](int i, uint32_t v) { raw[nq + i] = __uint_as_float(v); });
+  if (!ok) return false;
+  ok = ll_wait(a.ll + ll.qkv + qd + kvd + kvh * hd, hd, tag_in, a.status,
+               [&](int i, uint32_t v) { raw[nq + hd + i] = __uint_as_float(v); });
+  if (!ok) return false;
   const float* sn = a.rope + (size_t)min(pos, a.rope_rows - 1) * hd;
   const float* cs = sn + hd / 2;
-  // Warp 0: k, warp 1: v, warps 2..: q heads.
+  // Warp 0: k, warp 1: v, warps 2..: q heads (causal_lm.rs:428-446).
   for (int h = warp; h < 2 + qpk; h += DW) {
-    const float* src = (h == 0) ? a.qkv + qd + kvh * hd : (h == 1) ? a.qkv + qd + kvd + kvh * hd
-                                                                   : a.qkv + (kvh * qpk + h - 2) * hd;
+    const float* src = (h == 0) ? raw + nq : (h == 1) ? raw + nq + hd : raw + (h - 2) * hd;
     float v[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) v[i] = src[lane * 4 + i];
     if (h != 1) {
       const float* nw = (h == 0) ? L.k_norm : L.q_norm;
       if (nw) {
-        float ss = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
-        ss = warp_sum(ss);
-        float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), cfg.eps)));
+        float inv = 0.0f;
+        if (lane == 0) inv = rms_inv(seq_sum_squares(src, hd), hd, cfg.eps);
+        inv = __shfl_sync(0xffffffffu, inv, 0);
 #pragma unroll
         for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], __fmul_rn(inv, nw[lane * 4 + i]));
       }
@@ -263,9 +343,9 @@ __device__ void attend(const DecodeArgs& a, const DLayer& L, int layer, int pos,
       for (int i = 0; i < 4; ++i) {
         float partner = __shfl_xor_sync(0xffffffffu, v[i], 16);
         int idx = (lane & 15) * 4 + i;
-        float c = cs[idx], sgn = sn[idx];
-        v[i] = (lane < 16) ? __fsub_rn(__fmul_rn(v[i], c), __fmul_rn(partner, sgn))
-                           : __fadd_rn(__fmul_rn(v[i], c), __fmul_rn(partner, sgn));
+        float c = cs[idx], sg = sn[idx];
+        v[i] = (lane < 16) ? __fsub_rn(__fmul_rn(v[i], c), __fmul_rn(partner, sg))
+                           : __fadd_rn(__fmul_rn(v[i], c), __fmul_rn(partner, sg));
       }
     }
     if (h >= 2) {
@@ -278,198 +358,113 @@ __device__ void attend(const DecodeArgs& a, const DLayer& L, int layer, int pos,
     } else {
       float* dst = (h == 0) ? kf : vf;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) dst[lane * 4 + i] = cache.f16 ? round_f16(v[i]) : v[i];
-      if (s == 0) {
-        int page = cache.page_table[(size_t)a.stream * cache.pages_per_stream + pos / cache.page_tokens];
-        size_t off = kv_offset(cache, cfg, page, layer, h, kvh, pos % cache.page_tokens) + lane * 4;
-        if (cache.f16) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) ((__half*)cache.pool)[off + i] = __float2half_rn(v[i]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) ((float*)cache.pool)[off + i] = v[i];
-        }
-      }
-    }
-  }
-  __syncthreads();
-  // Scores: one thread per (q head, key).
-  for (int p = threadIdx.x; p < qpk * nk; p += DT) {
-    int qh = p / nk, jj = p % nk, j = j0 + jj;
-    const float* qv = q + qh * hd;
-    float acc = 0.0f;
-    if (j == pos) {
-      for (int e = 0; e < hd; ++e) acc = __fmaf_rn(qv[e], kf[e], acc);
-    } else {
-      int page = cache.page_table[(size_t)a.stream * cache.pages_per_stream + j / cache.page_tokens];
-      size_t off = kv_offset(cache, cfg, page, layer, 0, kvh, j % cache.page_tokens);
+      for (int i = 0; i < 4; ++i) dst[lane * 4 + i] = v[i];
+      int page = cache.page_table[(size_t)a.stream * cache.pages_per_stream + pos / cache.page_tokens];
+      size_t off = kv_offset(cache, cfg, page, layer, h, kvh, pos % cache.page_tokens) + lane * 4;
       if (cache.f16) {
-        const int4* kp = (const int4*)((const __half*)cache.pool + off);
-        for (int i = 0; i < 16; ++i) {
-          int4 raw = kp[i];
-          const __half2* h2 = (const __half2*)&raw;
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            float2 f = __half22float2(h2[t]);
-            acc = __fmaf_rn(qv[8 * i + 2 * t], f.x, acc);
-            acc = __fmaf_rn(qv[8 * i + 2 * t + 1], f.y, acc);
-          }
-        }
+        for (int i = 0; i < 4; ++i) ((__half*)cache.pool)[off + i] = __float2half_rn(v[i]);
       } else {
-        const float4* kp = (const float4*)((const float*)cache.pool + off);
-        for (int i = 0; i < 32; ++i) {
-          float4 f = kp[i];
-          acc = __fmaf_rn(qv[4 * i], f.x, acc);
-          acc = __fmaf_rn(qv[4 * i + 1], f.y, acc);
-          acc = __fmaf_rn(qv[4 * i + 2], f.z, acc);
-          acc = __fmaf_rn(qv[4 * i + 3], f.w, acc);
-        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ((float*)cache.pool)[off + i] = v[i];
       }
-    }
-    sc[qh * len + jj] = acc;
-  }
-  __syncthreads();
-  // Softmax of the block's keys: warp qh takes head qh.
-  float* stat = sc + qpk * len;  // [qpk][2]: max, sum
-  if (warp < qpk) {
-    float mx = -INFINITY;
-    for (int jj = lane; jj < nk; jj += 32) mx = fmaxf(mx, sc[warp * len + jj]);
-    mx = warp_max(mx);
-    float sum = 0.0f;
-    for (int jj = lane; jj < nk; jj += 32) {
-      float e = cephes_exp(__fsub_rn(sc[warp * len + jj], mx));
-      sc[warp * len + jj] = e;
-      sum = __fadd_rn(sum, e);
-    }
-    sum = warp_sum(sum);
-    if (lane == 0) {
-      stat[2 * warp] = nk ? mx : -INFINITY;
-      stat[2 * warp + 1] = nk ? sum : 0.0f;
+      // Later steps read this row in other blocks after a chain of LL
+      // hand-offs that carry no fence: make the row visible now.
+      __threadfence();
     }
   }
   __syncthreads();
-  // Weighted V sums: one thread per (q head, dimension).
-  float* part = a.att_part + ((size_t)(kvh * S_splits + s) * qpk) * (hd + 2);
-  for (int p = threadIdx.x; p < qpk * hd; p += DT) {
-    int qh = p / hd, e = p % hd;
-    float acc = 0.0f;
-    for (int jj = 0; jj < nk; ++jj) {
-      int j = j0 + jj;
-      float vv;
-      if (j == pos) {
-        vv = vf[e];
-      } else {
-        int page = cache.page_table[(size_t)a.stream * cache.pages_per_stream + j / cache.page_tokens];
-        size_t off = kv_offset(cache, cfg, page, layer, 1, kvh, j % cache.page_tokens) + e;
-        vv = cache.f16 ? __half2float(((const __half*)cache.pool)[off]) : ((const float*)cache.pool)[off];
-      }
-      acc = __fmaf_rn(sc[qh * len + jj], vv, acc);
-    }
-    part[qh * (hd + 2) + 2 + e] = acc;
-    if (e == 0) {
-      part[qh * (hd + 2)] = stat[2 * qh];
-      part[qh * (hd + 2) + 1] = stat[2 * qh + 1];
-    }
-  }
-  // The last block of this kv head to finish joins the splits.
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    unsigned old = atomicAdd(&counters[kvh], 1u);
-    S.flag[1] = (old == (unsigned)S_splits - 1);
-  }
-  __syncthreads();
-  if (!S.flag[1]) return;
-  __threadfence();
-  const float* base = a.att_part + (size_t)kvh * S_splits * qpk * (hd + 2);
-  float* outv = sc;  // [qpk][128], reuse
-  for (int p = threadIdx.x; p < qpk * hd; p += DT) {
-    int qh = p / hd, e = p % hd;
-    float mx = -INFINITY;
-    for (int t = 0; t < S_splits; ++t) {
-      const float* pp = base + ((size_t)t * qpk + qh) * (hd + 2);
-      if (pp[1] > 0.0f) mx = fmaxf(mx, pp[0]);
-    }
-    float l = 0.0f, acc = 0.0f;
-    for (int t = 0; t < S_splits; ++t) {
-      const float* pp = base + ((size_t)t * qpk + qh) * (hd + 2);
-      if (!(pp[1] > 0.0f)) continue;
-      float wgt = cephes_exp(__fsub_rn(pp[0], mx));
-      l = __fmaf_rn(wgt, pp[1], l);
-      acc = __fmaf_rn(wgt, pp[2 + e], acc);
-    }
-    outv[qh * hd + e] = __fdiv_rn(acc, l);
-  }
-  __syncthreads();
-  // Quantize each head's output (groups of 32 or 128 lie inside a head).
+  A.run(q, T, kf, vf, true, out);
+  // Quantize each head's output (groups of 32 or 128 lie inside a head),
+  // then publish codes (4 a word) and scales as LL words.
   const DMat& O = L.out;
   const int G = O.agroup;
-  for (int g = warp; g < qpk * hd / G; g += DW) {
-    int qh0 = kvh * qpk;
-    int8_t* dst = a.attq + qh0 * hd + g * G;
+  for (int g = warp; g < nq / G; g += DW) {
     float sc2;
     if (G == 32) {
-      float v[1] = {outv[g * 32 + lane]};
-      sc2 = warp_quantize_group<32>(v, dst, O.half);
+      float v[1] = {out[g * 32 + lane]};
+      sc2 = warp_quantize_group<32>(v, codes + g * 32, O.half);
     } else {
       float v[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[i] = outv[g * 128 + lane * 4 + i];
-      sc2 = warp_quantize_group<128>(v, dst, O.half);
+      for (int i = 0; i < 4; ++i) v[i] = out[g * 128 + lane * 4 + i];
+      sc2 = warp_quantize_group<128>(v, codes + g * 128, O.half);
     }
-    if (lane == 0) a.atts[(qh0 * hd) / G + g] = sc2;
+    if (lane == 0) scales[g] = sc2;
   }
-  if (threadIdx.x == 0) counters[kvh] = 0;
+  __syncthreads();
+  const int qh0 = kvh * qpk;
+  for (int wd = t; wd < nq / 4; wd += DT) ll_put(a.ll + ll.attq + qh0 * hd / 4 + wd, ((const uint32_t*)codes)[wd], tag_out);
+  for (int g = t; g < nq / G; g += DT) ll_put(a.ll + ll.attq_scales + qh0 * hd / G + g, __float_as_uint(scales[g]), tag_out);
+  __syncthreads();  // the next phase stages weights over this scratch
+  return true;
 }
 
 // ---------------------------------------------------------------- table --
 // The block's slice of the token table (forward_rows' last product,
-// causal_lm.rs:386-388) with f32 math in the lane order of the AVX-512
-// tile, codes streamed through shared memory by cp.async, and the block's
-// best (value, index).
-__device__ void table_slice(const DecodeArgs& a, int v0, int v1, int step, Shared& S, float* best_v, int* best_i) {
+// causal_lm.rs:386-388), f32 math in the lane order of the AVX-512 tile.
+// Each warp streams its own groups of 8 rows through a private cp.async
+// pipeline: a stage holds 128 code bytes of each row and, in the row's
+// padding, the scales of those 4 groups of 32. The first stages are issued
+// before `ready()` (the wait for the final hidden state and its norm).
+template <class Ready>
+__device__ bool table_slice(const DecodeArgs& a, int v0, int v1, int step, Shared& S, float* best_v, int* best_i,
+                            Ready ready) {
   const DTable& T = a.table;
-  const int t = threadIdx.x, q = t & 3, rl = t >> 2;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31, q = lane & 3, rl = lane >> 2;
   const int slabs = T.k / TAB_SLAB;
-  const int tiles = (v1 - v0 + TAB_TILE - 1) / TAB_TILE;
-  const int items = tiles * slabs;
+  const int ngroups = (v1 - v0 + TAB_ROWS_W - 1) / TAB_ROWS_W;
+  const int my_groups = ngroups > warp ? (ngroups - warp + DW - 1) / DW : 0;
+  const int items = my_groups * slabs;
   const float mult = (a.cfg.logits_scaling == 1.0f) ? 1.0f : __fdiv_rn(1.0f, a.cfg.logits_scaling);
+  uint8_t* wstage = S.tab + (size_t)warp * TAB_STAGES * TAB_ROWS_W * TAB_PITCH;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
   auto issue = [&](int item) {
     if (item < items) {
-      int tile = item / slabs, slab = item % slabs;
-      uint8_t* stage = S.tab + (item % TAB_STAGES) * TAB_TILE * TAB_PITCH;
-      // 128 rows x 128 bytes = 1024 chunks of 16 bytes: two a thread.
-      for (int c = t; c < TAB_TILE * (TAB_SLAB / 16); c += DT) {
-        int r = c / (TAB_SLAB / 16), cc = c % (TAB_SLAB / 16);
-        int row = v0 + tile * TAB_TILE + r;
+      int g = warp + DW * (item / slabs), slab = item % slabs;
+      uint8_t* stage = wstage + (item % TAB_STAGES) * TAB_ROWS_W * TAB_PITCH;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        int c = lane + 32 * u, r = c >> 3, cc = c & 7;
+        int row = v0 + g * TAB_ROWS_W + r;
         if (row < v1) cp_async16(stage + r * TAB_PITCH + cc * 16, T.codes + (size_t)row * T.k + slab * TAB_SLAB + cc * 16);
+      }
+      if (lane < TAB_ROWS_W) {
+        int row = v0 + g * TAB_ROWS_W + lane;
+        if (row < v1) {
+          const uint8_t* src = (const uint8_t*)T.scales + ((size_t)row * (T.k / 32) + slab * 4) * (T.scale_f16 ? 2 : 4);
+          if (T.scale_f16) cp_async8(stage + lane * TAB_PITCH + TAB_SLAB, src);
+          else cp_async16(stage + lane * TAB_PITCH + TAB_SLAB, src);
+        }
       }
     }
     cp_commit();
   };
   for (int i = 0; i < TAB_STAGES - 1; ++i) issue(i);
+  if (!ready()) {
+    cp_wait<0>();
+    return false;
+  }
   float lanes[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   for (int item = 0; item < items; ++item) {
     issue(item + TAB_STAGES - 1);
     cp_wait<TAB_STAGES - 1>();
-    __syncthreads();
-    int tile = item / slabs, slab = item % slabs;
-    int row = v0 + tile * TAB_TILE + rl;
-    const uint8_t* stage = S.tab + (item % TAB_STAGES) * TAB_TILE * TAB_PITCH + rl * TAB_PITCH;
-    if (row < v1) {
+    __syncwarp();
+    int g = warp + DW * (item / slabs), slab = item % slabs;
+    int row = v0 + g * TAB_ROWS_W + rl;
+    const uint8_t* srow = wstage + (item % TAB_STAGES) * TAB_ROWS_W * TAB_PITCH + rl * TAB_PITCH;
 #pragma unroll
-      for (int st = 0; st < TAB_SLAB / 16; ++st) {
-        int kk = slab * TAB_SLAB + 16 * st + 4 * q;
-        uint32_t word = *(const uint32_t*)(stage + 16 * st + 4 * q) ^ 0x80808080u;
-        float s = table_scale(T, row, kk / 32);
-        float4 xv = *(const float4*)(S.xf + kk);
-        lanes[0] = __fmaf_rn(xv.x, __fmul_rn(byte_to_float(word, 0), s), lanes[0]);
-        lanes[1] = __fmaf_rn(xv.y, __fmul_rn(byte_to_float(word, 1), s), lanes[1]);
-        lanes[2] = __fmaf_rn(xv.z, __fmul_rn(byte_to_float(word, 2), s), lanes[2]);
-        lanes[3] = __fmaf_rn(xv.w, __fmul_rn(byte_to_float(word, 3), s), lanes[3]);
-      }
+    for (int st = 0; st < TAB_SLAB / 16; ++st) {
+      int kk = slab * TAB_SLAB + 16 * st + 4 * q;
+      uint32_t word = *(const uint32_t*)(srow + 16 * st + 4 * q) ^ 0x80808080u;
+      float s = T.scale_f16 ? f16_bits_to_f32(((const uint16_t*)(srow + TAB_SLAB))[st >> 1])
+                            : ((const float*)(srow + TAB_SLAB))[st >> 1];
+      float4 xv = *(const float4*)(S.xf + kk);
+      lanes[0] = __fmaf_rn(xv.x, __fmul_rn(byte_to_float(word, 0), s), lanes[0]);
+      lanes[1] = __fmaf_rn(xv.y, __fmul_rn(byte_to_float(word, 1), s), lanes[1]);
+      lanes[2] = __fmaf_rn(xv.z, __fmul_rn(byte_to_float(word, 2), s), lanes[2]);
+      lanes[3] = __fmaf_rn(xv.w, __fmul_rn(byte_to_float(word, 3), s), lanes[3]);
     }
     if (slab == slabs - 1) {
       // The row is done: _mm512_reduce_add_ps across the 4 threads.
@@ -482,12 +477,12 @@ __device__ void table_slice(const DecodeArgs& a, int v0, int v1, int step, Share
       if (q == 0 && row < v1) {
         if (mult != 1.0f) v = __fmul_rn(v, mult);
         if (a.logits) a.logits[(size_t)step * T.n + row] = v;
-        if (v > bv) { bv = v; bi = row; }  // rows rise: the first maximum stays
+        if (v > bv || (v == bv && row < bi)) { bv = v; bi = row; }
       }
 #pragma unroll
       for (int l = 0; l < 4; ++l) lanes[l] = 0.0f;
     }
-    __syncthreads();
+    __syncwarp();  // the stage is refilled by the next issue
   }
   cp_wait<0>();
   // Block best: the largest value, the lowest index among equals.
@@ -498,9 +493,9 @@ __device__ void table_slice(const DecodeArgs& a, int v0, int v1, int step, Share
     if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
   }
   __syncthreads();
-  if ((t & 31) == 0) {
-    S.red[t >> 5] = bv;
-    ((int*)S.red)[32 + (t >> 5)] = bi;
+  if (lane == 0) {
+    S.red[warp] = bv;
+    ((int*)S.red)[32 + warp] = bi;
   }
   __syncthreads();
   if (t == 0) {
@@ -512,6 +507,8 @@ __device__ void table_slice(const DecodeArgs& a, int v0, int v1, int step, Share
     *best_v = bv;
     *best_i = bi;
   }
+  __syncthreads();
+  return true;
 }
 
 __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
@@ -520,8 +517,9 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
   const int c = blockIdx.x, nb = gridDim.x;
   const int hd = 128, qd = cfg.heads * hd, kvd = cfg.kv_heads * hd, nqkv = qd + 2 * kvd;
   const int kmax = max(max(cfg.d, qd), cfg.ffn);
-  const int S_splits = max(1, nb / cfg.kv_heads);
-  // Shared memory plan (see decode_smem).
+  const int tmax = (a.first_pos + a.steps + 3) / 4 * 4;  // the most keys a step sees, rounded up
+  const int L = cfg.layers;
+  const LlLayout ll(cfg, nb);
   Shared S;
   uint8_t* p = smem;
   S.flag = (int*)p; p += 64;
@@ -529,19 +527,24 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
   S.xf = (float*)p; p += (size_t)kmax * 4;
   S.xq = (int8_t*)p; p += (size_t)kmax;
   S.xs = (float*)p; p += (size_t)(kmax / 32) * 4;
+  S.own = (float*)p; p += 512 * 4;
   S.out = (float*)p; p += 512 * 4;
-  S.part = (int*)p;          // union with attention and table scratch
+  S.gmax = kmax / 32;
+  S.part = (int*)p;  // union with the attention and table scratch
   S.att = (float*)p;
   S.tab = p;
-  unsigned* counter = a.sync;
-  unsigned* att_counters = a.sync + 4;
-  unsigned target = 0;
-  if (threadIdx.x == 0) S.flag[0] = 0;
-  __syncthreads();
-
+  // The rows this block owns: x rows (o_proj and down_proj), qkv rows, ffn units, table rows.
+  const int r0 = split_at(cfg.d, c, nb), r1 = split_at(cfg.d, c + 1, nb), nown = r1 - r0;
+  const int q0 = split_at(nqkv, c, nb), q1 = split_at(nqkv, c + 1, nb);
+  const int u0 = split_at(cfg.ffn, c, nb), u1 = split_at(cfg.ffn, c + 1, nb), nu = u1 - u0;
+  const int v0 = split_at(a.table.n, c, nb), v1 = split_at(a.table.n, c + 1, nb);
+  int mark_at = 0;
+  auto mark = [&]() {
+    if (a.phase_ns && c == 0 && threadIdx.x == 0) a.phase_ns[mark_at] = gtimer();
+    ++mark_at;
+  };
+  int token = a.tokens[0];
   for (int i = 0; i < a.steps; ++i) {
-    // Every block reduced the same token at the end of the last step.
-    const int token = (i == 0) ? a.tokens[0] : S.flag[2];
     bool stopped = false;
     for (int s = 0; s < a.nstop; ++s) stopped |= a.stop[s] == token;
     if (stopped) {
@@ -549,120 +552,157 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
       return;
     }
     const int pos = a.first_pos + i;
-    // x = the token's embedding (causal_lm.rs:347-355, hidden :414), into
-    // S.xf for layer 0's norm; block 0 also stores it as the residual.
+    const uint32_t base = (uint32_t)i * (uint32_t)(5 * L + 2) + 1;  // tags of this step: base + phase
+    mark_at = i * (5 * L + 2);
+    mark();
+    // x = the token's embedding (causal_lm.rs:347-355, hidden :414).
     const DTable& E = a.embed;
     for (int kk = threadIdx.x; kk < cfg.d; kk += DT) {
       float v = __fmul_rn((float)E.codes[(size_t)token * E.k + kk], table_scale(E, token, kk / 32));
       if (cfg.embedding_multiplier != 1.0f) v = __fmul_rn(v, cfg.embedding_multiplier);
-      if (c == 0) a.x[kk] = v;
       S.xf[kk] = v;
+      if (kk >= r0 && kk < r1) S.own[kk - r0] = v;
     }
-    __syncthreads();
-    for (int l = 0; l < cfg.layers; ++l) {
-      const DLayer& L = a.layers[l];
-      // P1: qkv.
-      prefetch_layer(L, cfg, c, nb, false, true);
-      if (l + 1 < cfg.layers) prefetch_layer(a.layers[l + 1], cfg, c, nb, true, false);
-      norm_quant(l == 0 ? S.xf : a.x, cfg.d, L.norm_attn, cfg.eps, L.qkv.agroup, L.qkv.half, S);
-      {
-        int r0 = split_at(nqkv, c, nb), r1 = split_at(nqkv, c + 1, nb);
-        gemv_rows(L.qkv, r1 - r0, [&](int lr) { return r0 + lr; }, S);
-        for (int lr = threadIdx.x; lr < r1 - r0; lr += DT) a.qkv[r0 + lr] = S.out[lr];
-      }
-      if (!grid_barrier(counter, target, a.status, S.flag)) return;
+    for (int l = 0; l < L; ++l) {
+      const DLayer& Lw = a.layers[l];
+      const uint32_t t_qkv = base + 5 * l, t_att = t_qkv + 1, t_xa = t_qkv + 2, t_h = t_qkv + 3, t_xb = t_qkv + 4;
+      const uint32_t t_x_in = t_qkv - 1;  // xb of the layer before
+      // P1: qkv. Input: x (the embedding, or xb of the layer before).
+      bool ok = gemv(Lw.qkv, q1 - q0, [&](int lr) { return q0 + lr; }, S, [&]() {
+        if (l > 0 && !ll_wait(a.ll + ll.xb, cfg.d, t_x_in, a.status,
+                              [&](int k, uint32_t v) { S.xf[k] = __uint_as_float(v); }))
+          return false;
+        norm_quant(cfg.d, Lw.norm_attn, cfg.eps, Lw.qkv.agroup, Lw.qkv.half, S);
+        return true;
+      });
+      if (!ok) return;
+      for (int lr = threadIdx.x; lr < q1 - q0; lr += DT) ll_put(a.ll + ll.qkv + q0 + lr, __float_as_uint(S.out[lr]), t_qkv);
+      mark();
       // P2: attention.
-      if (c < cfg.kv_heads * S_splits) attend(a, L, l, pos, c / S_splits, c % S_splits, S_splits, att_counters, S);
-      if (!grid_barrier(counter, target, a.status, S.flag)) return;
-      // P3: o_proj + residual.
-      {
-        const int groups = qd / L.out.agroup;
-        for (int j = threadIdx.x; j < qd / 16; j += DT) ((int4*)S.xq)[j] = ((const int4*)a.attq)[j];
-        for (int j = threadIdx.x; j < groups; j += DT) S.xs[j] = a.atts[j];
-        __syncthreads();
-        int r0 = split_at(cfg.d, c, nb), r1 = split_at(cfg.d, c + 1, nb);
-        gemv_rows(L.out, r1 - r0, [&](int lr) { return r0 + lr; }, S);
-        for (int lr = threadIdx.x; lr < r1 - r0; lr += DT) {
-          float o = S.out[lr];
-          float xv = a.x[r0 + lr];
-          a.x[r0 + lr] = (cfg.residual_multiplier == 1.0f) ? __fadd_rn(xv, o)
-                                                           : __fadd_rn(xv, __fmul_rn(cfg.residual_multiplier, o));
-        }
+      if (c < cfg.kv_heads) {
+        if (!attend(a, Lw, l, pos, c, tmax, t_qkv, t_att, S)) return;
       }
-      if (!grid_barrier(counter, target, a.status, S.flag)) return;
-      // P4: gate_up, h = silu(gate) * up.
-      norm_quant(a.x, cfg.d, L.norm_mlp, cfg.eps, L.gate_up.agroup, L.gate_up.half, S);
-      {
-        int u0 = split_at(cfg.ffn, c, nb), u1 = split_at(cfg.ffn, c + 1, nb), nu = u1 - u0;
-        gemv_rows(L.gate_up, 2 * nu, [&](int lr) { return lr < nu ? u0 + lr : cfg.ffn + u0 + lr - nu; }, S);
-        for (int lr = threadIdx.x; lr < nu; lr += DT) a.h[u0 + lr] = __fmul_rn(silu(S.out[lr]), S.out[nu + lr]);
+      mark();
+      // P3: o_proj + residual. Input: the quantized attention output.
+      const int ncode = qd / 4, nsc = qd / Lw.out.agroup;
+      ok = gemv(Lw.out, nown, [&](int lr) { return r0 + lr; }, S, [&]() {
+        if (!ll_wait(a.ll + ll.attq, ncode, t_att, a.status, [&](int k, uint32_t v) { ((uint32_t*)S.xq)[k] = v; }))
+          return false;
+        if (!ll_wait(a.ll + ll.attq_scales, nsc, t_att, a.status, [&](int k, uint32_t v) { S.xs[k] = __uint_as_float(v); }))
+          return false;
+        return true;
+      });
+      if (!ok) return;
+      mark();
+      for (int lr = threadIdx.x; lr < nown; lr += DT) {
+        float o = S.out[lr];
+        float xv = (cfg.residual_multiplier == 1.0f) ? __fadd_rn(S.own[lr], o)
+                                                     : __fadd_rn(S.own[lr], __fmul_rn(cfg.residual_multiplier, o));
+        S.own[lr] = xv;
+        ll_put(a.ll + ll.xa + r0 + lr, __float_as_uint(xv), t_xa);
       }
-      if (!grid_barrier(counter, target, a.status, S.flag)) return;
-      // P5: down + residual.
-      norm_quant(a.h, cfg.ffn, nullptr, cfg.eps, L.down.agroup, L.down.half, S);
-      {
-        int r0 = split_at(cfg.d, c, nb), r1 = split_at(cfg.d, c + 1, nb);
-        gemv_rows(L.down, r1 - r0, [&](int lr) { return r0 + lr; }, S);
-        for (int lr = threadIdx.x; lr < r1 - r0; lr += DT) {
-          float o = S.out[lr];
-          float xv = a.x[r0 + lr];
-          a.x[r0 + lr] = (cfg.residual_multiplier == 1.0f) ? __fadd_rn(xv, o)
-                                                           : __fadd_rn(xv, __fmul_rn(cfg.residual_multiplier, o));
-        }
+      // P4: gate_up, h = silu(gate) * up. Input: xa.
+      ok = gemv(Lw.gate_up, 2 * nu, [&](int lr) { return lr < nu ? u0 + lr : cfg.ffn + u0 + lr - nu; }, S, [&]() {
+        if (!ll_wait(a.ll + ll.xa, cfg.d, t_xa, a.status, [&](int k, uint32_t v) { S.xf[k] = __uint_as_float(v); }))
+          return false;
+        norm_quant(cfg.d, Lw.norm_mlp, cfg.eps, Lw.gate_up.agroup, Lw.gate_up.half, S);
+        return true;
+      });
+      if (!ok) return;
+      mark();
+      for (int lr = threadIdx.x; lr < nu; lr += DT)
+        ll_put(a.ll + ll.h + u0 + lr, __float_as_uint(__fmul_rn(silu(S.out[lr]), S.out[nu + lr])), t_h);
+      // P5: down + residual. Input: h.
+      ok = gemv(Lw.down, nown, [&](int lr) { return r0 + lr; }, S, [&]() {
+        if (!ll_wait(a.ll + ll.h, cfg.ffn, t_h, a.status, [&](int k, uint32_t v) { S.xf[k] = __uint_as_float(v); }))
+          return false;
+        norm_quant(cfg.ffn, nullptr, cfg.eps, Lw.down.agroup, Lw.down.half, S);
+        return true;
+      });
+      if (!ok) return;
+      mark();
+      for (int lr = threadIdx.x; lr < nown; lr += DT) {
+        float o = S.out[lr];
+        float xv = (cfg.residual_multiplier == 1.0f) ? __fadd_rn(S.own[lr], o)
+                                                     : __fadd_rn(S.own[lr], __fmul_rn(cfg.residual_multiplier, o));
+        S.own[lr] = xv;
+        ll_put(a.ll + ll.xb + r0 + lr, __float_as_uint(xv), t_xb);
       }
-      if (!grid_barrier(counter, target, a.status, S.flag)) return;
     }
-    // Final RmsNorm (f32, no quantization) into S.xf, then the table slice.
-    {
-      for (int kk = threadIdx.x; kk < cfg.d; kk += DT) S.xf[kk] = a.x[kk];
+    // The final RmsNorm (f32, no quantization), the table slice, the argmax.
+    const uint32_t t_final = base + 5 * L - 1, t_best = base + 5 * L;
+    bool ok = table_slice(a, v0, v1, i + 1, S, (float*)(S.flag + 4), S.flag + 5, [&]() {
+      if (!ll_wait(a.ll + ll.xb, cfg.d, t_final, a.status, [&](int k, uint32_t v) { S.xf[k] = __uint_as_float(v); }))
+        return false;
+      if (threadIdx.x == 0) S.red[0] = rms_inv(seq_sum_squares(S.xf, cfg.d), cfg.d, cfg.eps);
       __syncthreads();
-      float ss = 0.0f;
-      for (int kk = threadIdx.x; kk < cfg.d; kk += DT) ss = __fadd_rn(ss, __fmul_rn(S.xf[kk], S.xf[kk]));
-      float tsum = block_sum(ss, S.red);
-      float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tsum, (float)cfg.d), cfg.eps)));
+      const float inv = S.red[0];
       for (int kk = threadIdx.x; kk < cfg.d; kk += DT) S.xf[kk] = __fmul_rn(S.xf[kk], __fmul_rn(inv, a.final_norm[kk]));
       __syncthreads();
-      int v0 = split_at(a.table.n, c, nb), v1 = split_at(a.table.n, c + 1, nb);
-      table_slice(a, v0, v1, i + 1, S, a.best_val + c, a.best_idx + c);
+      return true;
+    });
+    if (!ok) return;
+    if (threadIdx.x == 0) {
+      ll_put(a.ll + ll.best + 2 * c, (uint32_t)S.flag[4], t_best);
+      ll_put(a.ll + ll.best + 2 * c + 1, (uint32_t)S.flag[5], t_best);
     }
-    if (!grid_barrier(counter, target, a.status, S.flag)) return;
-    // Every block reduces the per-block bests to the same token.
+    // Every block reduces all blocks' bests to the same token.
+    float* bvals = (float*)S.part;
+    int* bidx = S.part + nb;
+    ok = ll_wait(a.ll + ll.best, 2 * nb, t_best, a.status, [&](int k, uint32_t v) {
+      if (k & 1) bidx[k >> 1] = (int)v;
+      else bvals[k >> 1] = __uint_as_float(v);
+    });
+    if (!ok) return;
+    mark();
     if (threadIdx.x < 32) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-      for (int b = threadIdx.x; b < nb; b += 32) {
-        float v = a.best_val[b];
-        int ix = a.best_idx[b];
-        if (v > bv || (v == bv && ix < bi)) { bv = v; bi = ix; }
-      }
+      float b = -INFINITY;
+      int ix = 0x7fffffff;
+      for (int k = threadIdx.x; k < nb; k += 32)
+        if (bvals[k] > b || (bvals[k] == b && bidx[k] < ix)) { b = bvals[k]; ix = bidx[k]; }
 #pragma unroll
       for (int o = 16; o; o >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        float ob = __shfl_xor_sync(0xffffffffu, b, o);
+        int oi = __shfl_xor_sync(0xffffffffu, ix, o);
+        if (ob > b || (ob == b && oi < ix)) { b = ob; ix = oi; }
       }
-      if (threadIdx.x == 0) {
-        int tok = (bi == 0x7fffffff) ? 0 : bi;
-        S.flag[2] = tok;
-        if (c == 0) a.tokens[i + 1] = tok;
-      }
+      if (threadIdx.x == 0) S.flag[2] = (ix == 0x7fffffff) ? 0 : ix;
     }
     __syncthreads();
-    // Every block has read best_* before any block writes them again: the
-    // next write comes after 5 * layers more barriers.
+    token = S.flag[2];
+    if (c == 0 && threadIdx.x == 0) a.tokens[i + 1] = token;
+    __syncthreads();
   }
   if (c == 0 && threadIdx.x == 0) *a.count = a.steps;
 }
 
-size_t decode_smem(const DConfig& cfg) {
-  const int hd = 128, qd = cfg.heads * hd, kvd = cfg.kv_heads * hd, nqkv = qd + 2 * kvd;
+size_t head_smem(const DConfig& cfg) {
+  const int qd = cfg.heads * 128;
   const int kmax = std::max(std::max(cfg.d, qd), cfg.ffn);
-  size_t head = 64 + 64 * 4 + (size_t)kmax * 4 + kmax + (size_t)(kmax / 32) * 4 + 512 * 4;
-  (void)nqkv;
-  return head;
+  return 64 + 64 * 4 + (size_t)kmax * 4 + kmax + (size_t)(kmax / 32) * 4 + 512 * 4 + 512 * 4;
+}
+
+// The union region: the largest of the GEMV group dots and scales, the
+// attention scratch, the table stages and the argmax partials.
+size_t union_smem(const DConfig& cfg, int grid, int f16, int tmax) {
+  const int qd = cfg.heads * 128;
+  size_t u = 0;
+  const int kmax = std::max(std::max(cfg.d, qd), cfg.ffn);
+  u = std::max(u, (size_t)2 * WSTAGE + (size_t)DW * (kmax / 32) * 8);
+  u = std::max(u, (size_t)DW * TAB_STAGES * TAB_ROWS_W * TAB_PITCH);
+  u = std::max(u, (size_t)grid * 8);
+  u = std::max(u, attend_smem_floats(cfg.heads / cfg.kv_heads, tmax, f16) * 4);
+  return u;
 }
 
 }  // namespace
+
+bool decode_supported(const DConfig& cfg) {
+  auto ok = [](int k) { return k % 128 == 0 && k <= 8192; };
+  int qpk = cfg.heads / cfg.kv_heads;
+  return cfg.hd == 128 && ok(cfg.d) && ok(cfg.heads * 128) && ok(cfg.ffn) && qpk * 128 <= DT &&
+         true;
+}
 
 int decode_grid(int device) {
   cudaDeviceProp prop;
@@ -670,32 +710,21 @@ int decode_grid(int device) {
   return prop.multiProcessorCount;
 }
 
-// Shared memory of the union region: the largest of the GEMV group dots,
-// the attention scratch and the table stages.
-static size_t union_smem(const DConfig& cfg, int grid) {
-  const int hd = 128, qd = cfg.heads * hd, kvd = cfg.kv_heads * hd, nqkv = qd + 2 * kvd;
-  auto rows = [&](int n) { return (n + grid - 1) / grid + 1; };
-  size_t gemv = 0;
-  gemv = std::max(gemv, (size_t)rows(nqkv) * (cfg.d / 32) * 4);
-  gemv = std::max(gemv, (size_t)rows(cfg.d) * (qd / 32) * 4);
-  gemv = std::max(gemv, (size_t)2 * rows(cfg.ffn) * (cfg.d / 32) * 4);
-  gemv = std::max(gemv, (size_t)rows(cfg.d) * (cfg.ffn / 32) * 4);
-  int qpk = cfg.heads / cfg.kv_heads;
-  int splits = std::max(1, grid / cfg.kv_heads);
-  (void)splits;
-  size_t att_cap = 0;  // filled at launch (depends on the position)
-  size_t tab = (size_t)TAB_STAGES * TAB_TILE * TAB_PITCH;
-  (void)qpk;
-  return std::max(std::max(gemv, tab), att_cap);
-}
+size_t decode_ll_words(const DConfig& cfg, int grid) { return (size_t)LlLayout(cfg, grid).total; }
 
 cudaError_t launch_decode(const DecodeArgs& a, int grid, cudaStream_t s) {
-  const int qpk = a.cfg.heads / a.cfg.kv_heads;
-  const int splits = std::max(1, grid / a.cfg.kv_heads);
-  const int max_pos = a.first_pos + a.steps;  // the last position fed
-  const int len = (max_pos + 1 + splits - 1) / splits;
-  size_t att = ((size_t)qpk * 128 + 2 * 128 + (size_t)qpk * len + 2 * qpk + (size_t)qpk * 128) * 4;
-  size_t smem = decode_smem(a.cfg) + std::max(union_smem(a.cfg, grid), att);
+  if (!decode_supported(a.cfg)) return cudaErrorNotSupported;
+  const int tmax = (a.first_pos + a.steps + 3) / 4 * 4;
+  if ((a.cfg.heads / a.cfg.kv_heads) * 128 > 4 * DT || a.cfg.kv_heads > grid) return cudaErrorInvalidValue;
+  // A staged weight row fits a staging buffer.
+  for (int l = 0; l < 1; ++l) {
+    const int kmax = std::max(std::max(a.cfg.d, a.cfg.heads * 128), a.cfg.ffn);
+    if (kmax + kmax / 16 + 32 > WSTAGE) return cudaErrorInvalidValue;
+  }
+  // Per block: at most 512 own rows and 256 ffn units (S.own, S.out).
+  if ((a.cfg.d + grid - 1) / grid > 512 || 2 * ((a.cfg.ffn + grid - 1) / grid) > 512) return cudaErrorInvalidValue;
+  if (((a.cfg.heads * 128 + 2 * a.cfg.kv_heads * 128) + grid - 1) / grid > 512) return cudaErrorInvalidValue;
+  size_t smem = head_smem(a.cfg) + union_smem(a.cfg, grid, a.cache.f16, tmax);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;

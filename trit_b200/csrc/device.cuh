@@ -51,6 +51,20 @@ __device__ __forceinline__ float silu(float v) {
   return __fdiv_rn(v, __fadd_rn(1.0f, cephes_exp(__fsub_rn(0.0f, v))));
 }
 
+// RmsNorm's sum of squares in the reference's order (layers.rs:137): one
+// thread, v[0]^2 + v[1]^2 + ... left to right, each square rounded.
+__device__ __forceinline__ float seq_sum_squares(const float* v, int n) {
+  float s = 0.0f;
+#pragma unroll 8
+  for (int i = 0; i < n; ++i) s = __fadd_rn(s, __fmul_rn(v[i], v[i]));
+  return s;
+}
+
+// inv = 1 / sqrt(sum / d + eps), each step rounded (layers.rs:137).
+__device__ __forceinline__ float rms_inv(float sum, int d, float eps) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)d), eps)));
+}
+
 // ------------------------------------------------------------- warps ----
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -116,6 +130,13 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(at), "r"(n) : "memory");
   }
 }
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 

@@ -3,7 +3,10 @@
 #include "engine.h"
 
 #include <algorithm>
+#include <climits>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 
@@ -235,9 +238,9 @@ Lm::~Lm() { release(); }
 void Lm::release() {
   cudaSetDevice(opt_.device);
   if (stream_) cudaStreamSynchronize(stream_);
-  void* bufs[] = {arena_, d_layers_, pool_, page_table_, x_, qkv_, att_, h_, part_, xn_, xq_, xs_, row_stream_, row_pos_, ids_,
-                  best_val_, best_idx_, tokens_, logits_, stop_, positions_, dx_, dqkv_, datt_part_, datts_, dh_, dattq_,
-                  dbest_val_, dbest_idx_, dsync_, dstatus_, dcount_, trace_, rope_};
+  void* bufs[] = {arena_, d_layers_, pool_, page_table_, x_, qkv_, att_, h_, xn_, xq_, xs_, row_stream_, row_pos_, ids_,
+                  best_val_, best_idx_, tokens_, logits_, stop_, positions_, dll_, dstatus_, dcount_,
+                  trace_, rope_};
   for (void* b : bufs)
     if (b) cudaFree(b);
   if (host_rows_) cudaFreeHost(host_rows_);
@@ -250,10 +253,10 @@ void Lm::release() {
   stream_ = nullptr;
   host_rows_ = nullptr;
   for (auto& e : ev_) e = nullptr;
-  x_ = qkv_ = att_ = h_ = part_ = xn_ = nullptr;
+  x_ = qkv_ = att_ = h_ = xn_ = nullptr;
   xq_ = nullptr; xs_ = nullptr; row_stream_ = row_pos_ = ids_ = nullptr; best_val_ = nullptr; best_idx_ = nullptr;
-  tokens_ = nullptr; logits_ = nullptr; stop_ = nullptr; positions_ = nullptr; dx_ = dqkv_ = datt_part_ = datts_ = dh_ = nullptr;
-  dattq_ = nullptr; dbest_val_ = nullptr; dbest_idx_ = nullptr; dsync_ = nullptr; dstatus_ = nullptr;
+  tokens_ = nullptr; logits_ = nullptr; stop_ = nullptr; positions_ = nullptr; dll_ = nullptr;
+  dstatus_ = nullptr;
   dcount_ = nullptr; trace_ = nullptr; rope_ = nullptr;
 }
 
@@ -361,13 +364,10 @@ void Lm::alloc_buffers() {
 
   rows_cap_ = std::max(opt_.prefill_rows, opt_.max_streams);
   int kmax = std::max(std::max(d, qd), cfg_.ffn);
-  int splits = (opt_.max_context + 255) / 256;
-  part_floats_ = (size_t)rows_cap_ * cfg_.heads * splits * 130;
   TRIT_CUDA(cudaMalloc(&x_, (size_t)rows_cap_ * d * 4));
   TRIT_CUDA(cudaMalloc(&qkv_, (size_t)rows_cap_ * (qd + 2 * kvd) * 4));
   TRIT_CUDA(cudaMalloc(&att_, (size_t)rows_cap_ * qd * 4));
   TRIT_CUDA(cudaMalloc(&h_, (size_t)rows_cap_ * cfg_.ffn * 4));
-  TRIT_CUDA(cudaMalloc(&part_, part_floats_ * 4));
   TRIT_CUDA(cudaMalloc(&xq_, (size_t)rows_cap_ * kmax));
   TRIT_CUDA(cudaMalloc(&xs_, (size_t)rows_cap_ * (kmax / 32) * 4));
   TRIT_CUDA(cudaMalloc(&row_stream_, (size_t)rows_cap_ * 4));
@@ -400,7 +400,7 @@ void Lm::hidden(int m, int max_tk) {
     TRIT_CUDA(launch_gemv(L.qkv, xq_, xs_, m, kEpOut, qkv_, qd + 2 * kvd, 1.0f, s));
     TRIT_CUDA(launch_qk_rope_append(qkv_, m, cfg_, L.q_norm, L.k_norm, rope_, opt_.max_context, cache_, row_stream_,
                                     row_pos_, l, s));
-    TRIT_CUDA(launch_attention(qkv_, m, cfg_, cache_, row_stream_, row_pos_, l, max_tk, part_, part_floats_, att_, s));
+    TRIT_CUDA(launch_attention(qkv_, m, cfg_, cache_, row_stream_, row_pos_, l, max_tk, att_, s));
     TRIT_CUDA(launch_norm_quant(att_, m, qd, nullptr, cfg_.eps, L.out.agroup, L.out.half, xq_, xs_, s));
     TRIT_CUDA(launch_gemv(L.out, xq_, xs_, m, kEpResid, x_, d, cfg_.residual_multiplier, s));
     TRIT_CUDA(launch_norm_quant(x_, m, d, L.norm_mlp, cfg_.eps, L.gate_up.agroup, L.gate_up.half, xq_, xs_, s));
@@ -590,22 +590,16 @@ void Lm::decode_layered(int slot, int position, int steps, float* trace) {
 
 // Batch-1 decode in one cooperative kernel (decode.cu): step i feeds
 // tokens_[i] at position + i; the kernel stops at a stop token.
+// Batch-1 decode in one cooperative kernel (decode.cu): step i feeds
+// tokens_[i] at position + i; the kernel stops at a stop token.
 void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
-  const int hd = cfg_.hd, qd = cfg_.heads * hd, kvd = cfg_.kv_heads * hd;
+  if (!decode_supported(cfg_))
+    throw Error("the persistent decode takes widths up to 8192 in multiples of 128; use {\"decode\": \"layered\"}");
   if (!decode_grid_) {
     decode_grid_ = decode_grid(opt_.device);
     if (decode_grid_ < cfg_.kv_heads) throw Error("too few SMs for the persistent decode");
-    int splits = std::max(1, decode_grid_ / cfg_.kv_heads);
-    int qpk = cfg_.heads / cfg_.kv_heads;
-    TRIT_CUDA(cudaMalloc(&dx_, (size_t)cfg_.d * 4));
-    TRIT_CUDA(cudaMalloc(&dqkv_, (size_t)(qd + 2 * kvd) * 4));
-    TRIT_CUDA(cudaMalloc(&datt_part_, (size_t)cfg_.kv_heads * splits * qpk * (hd + 2) * 4));
-    TRIT_CUDA(cudaMalloc(&dattq_, (size_t)qd));
-    TRIT_CUDA(cudaMalloc(&datts_, (size_t)(qd / 32) * 4));
-    TRIT_CUDA(cudaMalloc(&dh_, (size_t)cfg_.ffn * 4));
-    TRIT_CUDA(cudaMalloc(&dbest_val_, (size_t)decode_grid_ * 4));
-    TRIT_CUDA(cudaMalloc(&dbest_idx_, (size_t)decode_grid_ * 4));
-    TRIT_CUDA(cudaMalloc(&dsync_, (size_t)(4 + cfg_.kv_heads) * 4));
+    ll_words_ = decode_ll_words(cfg_, decode_grid_);
+    TRIT_CUDA(cudaMalloc(&dll_, ll_words_ * 8));
     TRIT_CUDA(cudaMalloc(&dstatus_, 4));
     TRIT_CUDA(cudaMalloc(&dcount_, 4));
   }
@@ -637,17 +631,19 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
   a.tokens = tokens_;
   a.count = dcount_;
   a.logits = dtrace;
-  a.x = dx_;
-  a.qkv = dqkv_;
-  a.att_part = datt_part_;
-  a.attq = dattq_;
-  a.atts = datts_;
-  a.h = dh_;
-  a.best_val = dbest_val_;
-  a.best_idx = dbest_idx_;
-  a.sync = dsync_;
+  a.ll = dll_;
   a.status = dstatus_;
-  TRIT_CUDA(cudaMemsetAsync(dsync_, 0, (size_t)(4 + cfg_.kv_heads) * 4, stream_));
+  // TRIT_PHASE_TRACE=1: stamp every phase of block 0 and print the mean time
+  // of each phase kind to stderr (a measurement aid).
+  static const bool trace_phases = getenv("TRIT_PHASE_TRACE") && *getenv("TRIT_PHASE_TRACE") == '1';
+  const int marks = 5 * cfg_.layers + 2;
+  long long* dphase = nullptr;
+  if (trace_phases) {
+    TRIT_CUDA(cudaMallocAsync(&dphase, (size_t)steps * marks * 8, stream_));
+    TRIT_CUDA(cudaMemsetAsync(dphase, 0, (size_t)steps * marks * 8, stream_));
+  }
+  a.phase_ns = dphase;
+  TRIT_CUDA(cudaMemsetAsync(dll_, 0, ll_words_ * 8, stream_));
   TRIT_CUDA(cudaMemsetAsync(dstatus_, 0, 4, stream_));
   TRIT_CUDA(launch_decode(a, decode_grid_, stream_));
   timing_.gpu_launches += 1;
@@ -657,7 +653,33 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
     TRIT_CUDA(cudaMemcpyAsync(trace + cfg_.vocab, dtrace + cfg_.vocab, (size_t)steps * cfg_.vocab * 4,
                               cudaMemcpyDeviceToHost, stream_));
   TRIT_CUDA(cudaStreamSynchronize(stream_));
-  if (status) throw Error("the persistent decode gave up waiting at a grid barrier (status " + std::to_string(status) + ")");
+  if (dphase) {
+    std::vector<long long> t((size_t)steps * marks);
+    TRIT_CUDA(cudaMemcpy(t.data(), dphase, t.size() * 8, cudaMemcpyDeviceToHost));
+    TRIT_CUDA(cudaFree(dphase));
+    // Stamps per step: start, then per layer the ends of P1 (qkv), P2
+    // (attention), P3 (o), P4 (gate_up), P5 (down, before its hand-off),
+    // then the argmax.
+    double sum[7] = {0};
+    int n[7] = {0};
+    for (int st = 1; st < steps; ++st) {
+      const long long* r = t.data() + (size_t)st * marks;
+      if (!r[marks - 1]) continue;
+      for (int l = 0; l < cfg_.layers; ++l)
+        for (int p = 0; p < 5; ++p) {
+          sum[p] += (double)(r[l * 5 + p + 1] - r[l * 5 + p]);
+          n[p]++;
+        }
+      sum[5] += (double)(r[marks - 1] - r[marks - 2]);
+      n[5]++;
+      sum[6] += (double)(r[marks - 1] - r[0]);
+      n[6]++;
+    }
+    const char* names[7] = {"qkv", "attention", "o", "gate_up", "down", "table", "step"};
+    for (int p = 0; p < 7; ++p)
+      if (n[p]) fprintf(stderr, "phase %-9s %8.2f us\n", names[p], sum[p] / n[p] / 1e3);
+  }
+  if (status) throw Error("the persistent decode gave up waiting for another block (status " + std::to_string(status) + ")");
 }
 
 void Lm::embed(const int* ids, size_t n, float* out) {

@@ -116,8 +116,7 @@ class Lm {
 
   // scratch
   int rows_cap_ = 0;
-  float *x_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *h_ = nullptr, *part_ = nullptr, *xn_ = nullptr;
-  size_t part_floats_ = 0;
+  float *x_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *h_ = nullptr, *xn_ = nullptr;
   int8_t* xq_ = nullptr;
   float* xs_ = nullptr;
   int *row_stream_ = nullptr, *row_pos_ = nullptr, *ids_ = nullptr;
@@ -132,11 +131,8 @@ class Lm {
   int* positions_ = nullptr;    // device positions of every decode step
   int last_rows_ = 0;           // rows of the last prompt chunk (in x_)
   // persistent decode scratch
-  float *dx_ = nullptr, *dqkv_ = nullptr, *datt_part_ = nullptr, *datts_ = nullptr, *dh_ = nullptr;
-  int8_t* dattq_ = nullptr;
-  float* dbest_val_ = nullptr;
-  int* dbest_idx_ = nullptr;
-  unsigned* dsync_ = nullptr;
+  unsigned long long* dll_ = nullptr;
+  size_t ll_words_ = 0;
   int* dstatus_ = nullptr;
   int* dcount_ = nullptr;
   int decode_grid_ = 0;

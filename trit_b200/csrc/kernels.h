@@ -19,8 +19,7 @@ cudaError_t launch_qk_rope_append(float* qkv, int m, const DConfig& cfg, const f
                                   const float* rope, int rope_rows, const DCache& cache, const int* row_stream,
                                   const int* row_pos, int layer, cudaStream_t s);
 cudaError_t launch_attention(const float* qkv, int m, const DConfig& cfg, const DCache& cache, const int* row_stream,
-                             const int* row_pos, int layer, int max_tk, float* part, size_t part_floats, float* att,
-                             cudaStream_t s);
+                             const int* row_pos, int layer, int max_tk, float* att, cudaStream_t s);
 // RmsNorm of `nb` rows, the table product and each row's argmax. logits
 // ([nb][vocab]) may be null; best_* hold [nb][table_blocks(vocab)].
 cudaError_t launch_final(const float* x, int ldx, int nb, const float* norm_w, const DConfig& cfg, const DTable& T,
@@ -43,26 +42,22 @@ struct DecodeArgs {
   int rope_rows;
   int stream;            // the stream slot whose pages this decode uses
   int first_pos;         // position of the first token fed
-  int steps;             // tokens to make (each step feeds the previous one)
+  int steps;             // forwards to run (each feeds the token before)
   const int* stop;       // device list of stop ids
   int nstop;
   int* tokens;           // [steps + 1]: tokens[0] is the token fed first; the rest are made
   int* count;            // how many tokens were made before a stop
-  float* logits;         // optional [steps][vocab] trace, or null
-  // scratch (device)
-  float* x;              // [d]
-  float* qkv;            // [qd + 2 kvd]
-  float* att_part;       // [kv_heads][splits][2 q-per-kv][130]
-  int8_t* attq;          // [qd]
-  float* atts;           // [qd / 32]
-  float* h;              // [ffn]
-  float* best_val;       // [grid]
-  int* best_idx;         // [grid]
-  unsigned* sync;        // [4] counters, zeroed before the launch
+  float* logits;         // optional [steps + 1][vocab] trace (row i + 1 from step i), or null
+  unsigned long long* ll;   // [decode_ll_words] {data, tag} words, zeroed before the launch
   int* status;           // 0 ok; nonzero: a wait ran out (see decode.cu)
+  long long* phase_ns;   // optional [steps][5 * layers + 2] globaltimer stamps of block 0, or null
 };
 
+// Whether the persistent decode takes this model (its product widths).
+bool decode_supported(const DConfig& cfg);
 cudaError_t launch_decode(const DecodeArgs& a, int grid, cudaStream_t s);
 int decode_grid(int device);
+// LL words of the decode's hand-off buffers.
+size_t decode_ll_words(const DConfig& cfg, int grid);
 
 }  // namespace trit

@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <cstdio>
 
+#include "attention.cuh"
 #include "device.cuh"
 #include "kernels.h"
 
@@ -39,31 +40,23 @@ __global__ void k_scale(float* x, size_t n, float mult) {
 template <int G>
 __global__ void __launch_bounds__(256) k_norm_quant(const float* x, int d, const float* w, float eps, int half,
                                                     int8_t* xq, float* xs) {
+  extern __shared__ float rowv[];  // [d]
   int r = blockIdx.x;
   const float* row = x + (size_t)r * d;
-  __shared__ float red[8];
   __shared__ float s_inv;
-  float s = 0.0f;
-  for (int i = threadIdx.x; i < d; i += 256) s = __fadd_rn(s, __fmul_rn(row[i], row[i]));
-  s = warp_sum(s);
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) red[warp] = s;
+  for (int i = threadIdx.x; i < d; i += 256) rowv[i] = row[i];
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.0f;
-    for (int i = 0; i < 8; ++i) t = __fadd_rn(t, red[i]);
-    if (w) s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)d), eps)));
-    else s_inv = 1.0f;
-  }
+  if (threadIdx.x == 0) s_inv = w ? rms_inv(seq_sum_squares(rowv, d), d, eps) : 1.0f;
   __syncthreads();
   float inv = s_inv;
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int groups = d / G;
   for (int g = warp; g < groups; g += 8) {
     float v[G / 32];
 #pragma unroll
     for (int i = 0; i < G / 32; ++i) {
       int kk = g * G + lane * (G / 32) + i;
-      v[i] = w ? __fmul_rn(row[kk], __fmul_rn(inv, w[kk])) : row[kk];
+      v[i] = w ? __fmul_rn(rowv[kk], __fmul_rn(inv, w[kk])) : rowv[kk];
     }
     float scale = warp_quantize_group<G>(v, xq + (size_t)r * d + g * G, half);
     if (lane == 0) xs[(size_t)r * groups + g] = scale;
@@ -105,9 +98,17 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(DMat W, const int8_t* xq,
   float* act_s = (float*)(smem + GEMV_FRAMES * k);                  // [F][groups]
   int* part = (int*)(act_s + GEMV_FRAMES * groups);                 // [ROWS][F][groups]
   float* res = (float*)(part + GEMV_ROWS * GEMV_FRAMES * groups);   // [ROWS][F]
+  float* wsc = res + GEMV_ROWS * GEMV_FRAMES;                        // [ROWS][groups]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int chunks = k / 16;            // 16 k-values per lane-load
   const int lanes_per_group = W.agroup / 16;
+  // The weight scales of the block's rows, once (coalesced per row).
+  for (int i = threadIdx.x; i < nunits * rows_per_unit * groups; i += GEMV_THREADS) {
+    int lr = i / groups, g = i % groups;
+    int u = unit0 + lr / rows_per_unit;
+    int row = (mode == kEpSilu) ? u + (lr % 2) * units : u;
+    wsc[i] = weight_scale(W, row, g);
+  }
   for (int f0 = 0; f0 < m; f0 += GEMV_FRAMES) {
     const int nf = min(GEMV_FRAMES, m - f0);
     __syncthreads();
@@ -137,13 +138,11 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(DMat W, const int8_t* xq,
     // Chains: one thread per (local row, frame), groups in order.
     for (int t = threadIdx.x; t < nunits * rows_per_unit * nf; t += GEMV_THREADS) {
       int lr = t / nf, f = t % nf;
-      int u = unit0 + lr / rows_per_unit;
-      int row = (mode == kEpSilu) ? u + (lr % 2) * units : u;
       const int* p = part + (lr * GEMV_FRAMES + f) * groups;
       const float* sx = act_s + f * groups;
       float acc = 0.0f;
-      for (int g = 0; g < groups; ++g)
-        acc = __fmaf_rn((float)p[g], __fmul_rn(weight_scale(W, row, g), sx[g]), acc);
+      const float* wr = wsc + lr * groups;
+      for (int g = 0; g < groups; ++g) acc = __fmaf_rn((float)p[g], __fmul_rn(wr[g], sx[g]), acc);
       res[lr * GEMV_FRAMES + f] = acc;
     }
     __syncthreads();
@@ -167,7 +166,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(DMat W, const int8_t* xq,
 size_t gemv_smem(const DMat& W) {
   size_t groups = W.k / W.agroup;
   return GEMV_FRAMES * (size_t)W.k + GEMV_FRAMES * groups * 4 + GEMV_ROWS * GEMV_FRAMES * groups * 4 +
-         GEMV_ROWS * GEMV_FRAMES * 4;
+         GEMV_ROWS * GEMV_FRAMES * 4 + GEMV_ROWS * groups * 4;
 }
 
 // ------------------------------------------- q/k norm, RoPE, KV append ----
@@ -176,9 +175,11 @@ size_t gemv_smem(const DMat& W) {
 // q scale, then K and V appended to the stream's pages. One block per
 // row, one warp per head; lane l holds values 4l..4l+3 of the head, so the
 // rotation partner of value i (i + 64) sits in lane l ^ 16.
-__global__ void k_qk_rope_append(float* qkv, int m, DConfig cfg, const float* q_norm, const float* k_norm,
-                                 const float* rope, int rope_rows, DCache cache, const int* row_stream,
-                                 const int* row_pos, int layer) {
+__global__ void __launch_bounds__(256) k_qk_rope_append(float* qkv, int m, DConfig cfg, const float* q_norm,
+                                                        const float* k_norm, const float* rope, int rope_rows,
+                                                        DCache cache, const int* row_stream, const int* row_pos,
+                                                        int layer) {
+  __shared__ float headv[8][128];
   int r = blockIdx.x;
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qd = cfg.heads * cfg.hd, kvd = cfg.kv_heads * cfg.hd, stride = qd + 2 * kvd;
@@ -193,16 +194,17 @@ __global__ void k_qk_rope_append(float* qkv, int m, DConfig cfg, const float* q_
     float v[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) v[i] = head[lane * 4 + i];
-    if (!is_q && !is_k) {
-      // v: append as is
-    } else {
+    if (is_q || is_k) {
       const float* nw = is_q ? q_norm : k_norm;
       if (nw) {
-        float s = 0.0f;
+        // The head's sum of squares in order (layers.rs:137), by lane 0.
 #pragma unroll
-        for (int i = 0; i < 4; ++i) s = __fadd_rn(s, __fmul_rn(v[i], v[i]));
-        s = warp_sum(s);
-        float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)cfg.hd), cfg.eps)));
+        for (int i = 0; i < 4; ++i) headv[warp][lane * 4 + i] = v[i];
+        __syncwarp();
+        float inv = 0.0f;
+        if (lane == 0) inv = rms_inv(seq_sum_squares(headv[warp], cfg.hd), cfg.hd, cfg.eps);
+        inv = __shfl_sync(0xffffffffu, inv, 0);
+        __syncwarp();
 #pragma unroll
         for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], __fmul_rn(inv, nw[lane * 4 + i]));
       }
@@ -228,10 +230,8 @@ __global__ void k_qk_rope_append(float* qkv, int m, DConfig cfg, const float* q_
       size_t off = kv_offset(cache, cfg, page, layer, is_k ? 0 : 1, kvh, pos % cache.page_tokens) + lane * 4;
       if (cache.f16) {
         __half* dst = (__half*)cache.pool + off;
-        dst[0] = __float2half_rn(v[0]);
-        dst[1] = __float2half_rn(v[1]);
-        dst[2] = __float2half_rn(v[2]);
-        dst[3] = __float2half_rn(v[3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = __float2half_rn(v[i]);
       } else {
         float* dst = (float*)cache.pool + off;
 #pragma unroll
@@ -246,123 +246,29 @@ __global__ void k_qk_rope_append(float* qkv, int m, DConfig cfg, const float* q_
 }
 
 // ---------------------------------------------------------- attention ----
-// Causal GQA softmax attention (layers.rs:343-504) of each row's query over
-// its stream's keys 0..pos, split over key ranges; each split keeps a
-// running maximum, sum and weighted V sum, and k_attention_combine joins
-// the splits. Scores are the reference's sequential fma chains over the
-// head dimension; the softmax sums and the V sums run in another order
-// than the reference's (tolerance, not bit-exact). 128 threads = hd.
-constexpr int ATT_TILE = 128;
+// One block per (row, kv head): the exact attention of attention.cuh for
+// the kv head's query heads, over the row's stream's keys 0..pos.
+constexpr int ATT_KT = 64;
 
-// q . key as one fma chain over the head dimension in order (the score of
-// fgemm's nn tile, src/cpu/fgemm.rs:790-800).
-__device__ __forceinline__ float score_chain(const DCache& c, size_t off, const float* q) {
-  float a = 0.0f;
-  if (c.f16) {
-    const int4* p = (const int4*)((const __half*)c.pool + off);
-#pragma unroll 4
-    for (int i = 0; i < 16; ++i) {
-      int4 raw = p[i];
-      const __half2* h = (const __half2*)&raw;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float2 f = __half22float2(h[j]);
-        a = __fmaf_rn(q[8 * i + 2 * j], f.x, a);
-        a = __fmaf_rn(q[8 * i + 2 * j + 1], f.y, a);
-      }
-    }
-  } else {
-    const float4* p = (const float4*)((const float*)c.pool + off);
-#pragma unroll 4
-    for (int i = 0; i < 32; ++i) {
-      float4 f = p[i];
-      a = __fmaf_rn(q[4 * i], f.x, a);
-      a = __fmaf_rn(q[4 * i + 1], f.y, a);
-      a = __fmaf_rn(q[4 * i + 2], f.z, a);
-      a = __fmaf_rn(q[4 * i + 3], f.w, a);
-    }
-  }
-  return a;
-}
-
-__device__ __forceinline__ float load_value(const DCache& c, size_t off, int f16) {
-  return f16 ? __half2float(((const __half*)c.pool)[off]) : ((const float*)c.pool)[off];
-}
-
-__global__ void __launch_bounds__(128) k_attention(const float* qkv, int m, DConfig cfg, DCache cache,
-                                                   const int* row_stream, const int* row_pos, int layer,
-                                                   int splits, int split_len, float* part) {
-  const int r = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
-  const int t = threadIdx.x;
-  const int qd = cfg.heads * cfg.hd, stride = qd + 2 * cfg.kv_heads * cfg.hd;
-  const int g = h / (cfg.heads / cfg.kv_heads);
-  const int pos = row_pos[r], stream = row_stream[r];
-  const int tk = pos + 1;
-  const int j0 = s * split_len, j1 = min(tk, j0 + split_len);
-  __shared__ float q[128];
-  __shared__ float p[ATT_TILE];
-  __shared__ float red[4];
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)cfg.hd));
-  q[t] = __fmul_rn(qkv[(size_t)r * stride + h * cfg.hd + t], scale);
+__global__ void __launch_bounds__(256) k_attention(const float* qkv, int m, DConfig cfg, DCache cache,
+                                                   const int* row_stream, const int* row_pos, int layer, int tmax,
+                                                   float* att) {
+  extern __shared__ __align__(16) float sm[];
+  const int r = blockIdx.x, kvh = blockIdx.y, t = threadIdx.x;
+  const int qpk = cfg.heads / cfg.kv_heads, qd = cfg.heads * 128, stride = qd + 2 * cfg.kv_heads * 128;
+  const int row = cache.f16 ? 64 : 128;
+  float* q = sm;
+  float* out = q + qpk * 128;
+  float* sc = out + qpk * 128;
+  float* ktl = sc + qpk * tmax;
+  float* vtl = ktl + ATT_KT * (row + 4);
+  float* stat = vtl + ATT_KT * row;
+  Attention<256> A{cache, cfg, row_stream[r], layer, kvh, qpk, ATT_KT, sc, ktl, vtl, stat, tmax};
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
+  for (int p = t; p < qpk * 128; p += 256) q[p] = __fmul_rn(qkv[(size_t)r * stride + kvh * qpk * 128 + p], scale);
   __syncthreads();
-  float m_run = -INFINITY, l_run = 0.0f, acc = 0.0f;
-  for (int tile = j0; tile < j1; tile += ATT_TILE) {
-    int j = tile + t;
-    float score = -INFINITY;
-    if (j < j1) {
-      int page = cache.page_table[(size_t)stream * cache.pages_per_stream + j / cache.page_tokens];
-      size_t off = kv_offset(cache, cfg, page, layer, 0, g, j % cache.page_tokens);
-      float a = score_chain(cache, off, q);
-      score = a;
-    }
-    float mx = warp_max(score);
-    if ((t & 31) == 0) red[t >> 5] = mx;
-    __syncthreads();
-    mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    __syncthreads();
-    float m_new = fmaxf(m_run, mx);
-    float e = (j < j1) ? cephes_exp(__fsub_rn(score, m_new)) : 0.0f;
-    p[t] = e;
-    float sum = warp_sum(e);
-    if ((t & 31) == 0) red[t >> 5] = sum;
-    __syncthreads();
-    sum = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
-    float corr = (m_run == -INFINITY) ? 0.0f : cephes_exp(__fsub_rn(m_run, m_new));
-    l_run = __fadd_rn(__fmul_rn(l_run, corr), sum);
-    acc = __fmul_rn(acc, corr);
-    int n = min(ATT_TILE, j1 - tile);
-    for (int jj = 0; jj < n; ++jj) {
-      int jk = tile + jj;
-      int page = cache.page_table[(size_t)stream * cache.pages_per_stream + jk / cache.page_tokens];
-      size_t off = kv_offset(cache, cfg, page, layer, 1, g, jk % cache.page_tokens) + t;
-      acc = __fmaf_rn(p[jj], load_value(cache, off, cache.f16), acc);
-    }
-    m_run = m_new;
-    __syncthreads();
-  }
-  float* out = part + (((size_t)r * cfg.heads + h) * splits + s) * (128 + 2);
-  out[2 + t] = acc;
-  if (t == 0) {
-    out[0] = m_run;
-    out[1] = l_run;
-  }
-}
-
-__global__ void k_attention_combine(const float* part, int m, DConfig cfg, int splits, const int* row_pos,
-                                    int split_len, float* att) {
-  const int r = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
-  const int tk = row_pos[r] + 1;
-  const int used = (tk + split_len - 1) / split_len;
-  const float* base = part + ((size_t)r * cfg.heads + h) * splits * 130;
-  float mx = -INFINITY;
-  for (int s = 0; s < used; ++s) mx = fmaxf(mx, base[s * 130]);
-  float l = 0.0f, acc = 0.0f;
-  for (int s = 0; s < used; ++s) {
-    float w = cephes_exp(__fsub_rn(base[s * 130], mx));
-    l = __fmaf_rn(w, base[s * 130 + 1], l);
-    acc = __fmaf_rn(w, base[s * 130 + 2 + t], acc);
-  }
-  att[(size_t)r * cfg.heads * cfg.hd + h * cfg.hd + t] = __fdiv_rn(acc, l);
+  A.run(q, row_pos[r] + 1, nullptr, nullptr, false, out);
+  for (int p = t; p < qpk * 128; p += 256) att[(size_t)r * qd + kvh * qpk * 128 + p] = out[p];
 }
 
 // ------------------------------------------------ final norm + table ----
@@ -504,8 +410,17 @@ cudaError_t launch_scale(float* x, size_t n, float mult, cudaStream_t s) {
 
 cudaError_t launch_norm_quant(const float* x, int m, int d, const float* w, float eps, int group, int half,
                               int8_t* xq, float* xs, cudaStream_t s) {
-  if (group == 32) k_norm_quant<32><<<m, 256, 0, s>>>(x, d, w, eps, half, xq, xs);
-  else k_norm_quant<128><<<m, 256, 0, s>>>(x, d, w, eps, half, xq, xs);
+  size_t smem = (size_t)d * 4;
+  if (smem > 48 * 1024) {
+    static bool configured = false;
+    if (!configured) {
+      cudaFuncSetAttribute(k_norm_quant<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+      cudaFuncSetAttribute(k_norm_quant<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+      configured = true;
+    }
+  }
+  if (group == 32) k_norm_quant<32><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs);
+  else k_norm_quant<128><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs);
   LAUNCH_CHECK();
   return cudaSuccess;
 }
@@ -537,15 +452,18 @@ cudaError_t launch_qk_rope_append(float* qkv, int m, const DConfig& cfg, const f
 }
 
 cudaError_t launch_attention(const float* qkv, int m, const DConfig& cfg, const DCache& cache, const int* row_stream,
-                             const int* row_pos, int layer, int max_tk, float* part, size_t part_floats, float* att,
-                             cudaStream_t s) {
-  int split_len = 256;
-  int splits = (max_tk + split_len - 1) / split_len;
-  if ((size_t)m * cfg.heads * splits * 130 > part_floats) return cudaErrorInvalidValue;
-  dim3 grid(m, cfg.heads, splits);
-  k_attention<<<grid, 128, 0, s>>>(qkv, m, cfg, cache, row_stream, row_pos, layer, splits, split_len, part);
-  LAUNCH_CHECK();
-  k_attention_combine<<<dim3(m, cfg.heads), 128, 0, s>>>(part, m, cfg, splits, row_pos, split_len, att);
+                             const int* row_pos, int layer, int max_tk, float* att, cudaStream_t s) {
+  const int qpk = cfg.heads / cfg.kv_heads;
+  if (qpk * 128 > 4 * 256) return cudaErrorInvalidValue;
+  const int tmax = (max_tk + 3) / 4 * 4;
+  size_t smem = ((size_t)2 * qpk * 128 + attention_smem_floats(qpk, tmax, ATT_KT, cache.f16)) * 4;
+  if (smem > 220 * 1024) return cudaErrorInvalidValue;
+  static int configured = 0;
+  if (configured < (int)smem) {
+    cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+    configured = 220 * 1024;
+  }
+  k_attention<<<dim3(m, cfg.kv_heads), 256, smem, s>>>(qkv, m, cfg, cache, row_stream, row_pos, layer, tmax, att);
   LAUNCH_CHECK();
   return cudaSuccess;
 }
@@ -554,22 +472,15 @@ cudaError_t launch_attention(const float* qkv, int m, const DConfig& cfg, const 
 // argmax of every row: token[b].
 __global__ void __launch_bounds__(256) k_final_norm_rows(const float* x, int ldx, int d, const float* w, float eps,
                                                          float* xn) {
+  extern __shared__ float rowv[];  // [d]
   const float* row = x + (size_t)blockIdx.x * ldx;
   float* out = xn + (size_t)blockIdx.x * d;
-  __shared__ float red[8];
   __shared__ float s_inv;
-  float s = 0.0f;
-  for (int i = threadIdx.x; i < d; i += 256) s = __fadd_rn(s, __fmul_rn(row[i], row[i]));
-  s = warp_sum(s);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  for (int i = threadIdx.x; i < d; i += 256) rowv[i] = row[i];
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.0f;
-    for (int i = 0; i < 8; ++i) t = __fadd_rn(t, red[i]);
-    s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)d), eps)));
-  }
+  if (threadIdx.x == 0) s_inv = rms_inv(seq_sum_squares(rowv, d), d, eps);
   __syncthreads();
-  for (int i = threadIdx.x; i < d; i += 256) out[i] = __fmul_rn(row[i], __fmul_rn(s_inv, w[i]));
+  for (int i = threadIdx.x; i < d; i += 256) out[i] = __fmul_rn(rowv[i], __fmul_rn(s_inv, w[i]));
 }
 
 template <int B>
@@ -588,7 +499,7 @@ static cudaError_t table_pass(const DTable& T, const float* xn, int nb, float mu
 
 cudaError_t launch_final(const float* x, int ldx, int nb, const float* norm_w, const DConfig& cfg, const DTable& T,
                          float* xn, float* logits, float* best_val, int* best_idx, int* token, cudaStream_t s) {
-  k_final_norm_rows<<<nb, 256, 0, s>>>(x, ldx, cfg.d, norm_w, cfg.eps, xn);
+  k_final_norm_rows<<<nb, 256, (size_t)cfg.d * 4, s>>>(x, ldx, cfg.d, norm_w, cfg.eps, xn);
   LAUNCH_CHECK();
   float mult = (cfg.logits_scaling == 1.0f) ? 1.0f : 1.0f / cfg.logits_scaling;
   int blocks = table_blocks(T.n);
