@@ -117,6 +117,7 @@ __device__ bool ll_wait(const unsigned long long* src, int n, uint32_t tag, int*
 
 struct Shared {
   float* xf;       // [kmax]: the phase's f32 input (x or h), normed x for the table
+  float* sq;       // [kmax]: squares for RmsNorm
   int8_t* xq;      // [kmax]
   float* xs;       // [kmax / 32]
   float* own;      // [512]: the residual rows this block owns
@@ -135,8 +136,12 @@ __device__ void norm_quant(int d, const float* w, float eps, int G, bool half, S
   __syncthreads();
   float inv = 1.0f;
   if (w) {
-    // The sum of squares in the reference's order, by one thread.
-    if (threadIdx.x == 0) S.red[0] = rms_inv(seq_sum_squares(S.xf, d), d, eps);
+    // The sum of squares in the reference's order: the squares in parallel
+    // (each rounded, as the reference rounds them), then one thread adds
+    // them left to right.
+    for (int i = threadIdx.x; i < d; i += DT) S.sq[i] = __fmul_rn(S.xf[i], S.xf[i]);
+    __syncthreads();
+    if (threadIdx.x == 0) S.red[0] = rms_inv(seq_sum(S.sq, d), d, eps);
     __syncthreads();
     inv = S.red[0];
   }
@@ -197,8 +202,10 @@ __device__ bool gemv(const DMat& W, int nrows, RowOf row_of, Shared& S, Ready re
   const int nbatch = per > 0 ? (nrows + per - 1) / per : 0;
   uint8_t* buf0 = (uint8_t*)S.part;
   uint8_t* buf1 = buf0 + WSTAGE;
-  int* wdot = (int*)(buf1 + WSTAGE) + warp * (S.gmax * 2);  // this warp's [groups] dots, then [groups] scales
-  float* wscl = (float*)(wdot + S.gmax);
+  // The batch's group dots and scale products, [group][row]: the chain
+  // threads (one a row) read consecutive words.
+  int* pdot = (int*)(buf1 + WSTAGE);
+  float* pscl = (float*)(pdot + WSTAGE / 32);  // per * groups <= WSTAGE / 32: a row takes >= 32 bytes a group
   auto issue = [&](int b) {
     if (b < nbatch) {
       uint8_t* dst = (b & 1) ? buf1 : buf0;
@@ -242,19 +249,20 @@ __device__ bool gemv(const DMat& W, int nrows, RowOf row_of, Shared& S, Ready re
           float ws = W.kind == kQ8_0 ? f16_bits_to_f32(((const uint16_t*)(rowp + cpad))[g])
                      : W.kind == kInt8Row ? ((const float*)(rowp + cpad))[0]
                                           : ((const float*)(rowp + cpad))[g];
-          wdot[g] = dot;
-          wscl[g] = __fmul_rn(ws, S.xs[g]);
+          pdot[g * per + r] = dot;
+          pscl[g * per + r] = __fmul_rn(ws, S.xs[g]);
         }
       }
-      __syncwarp();
-      if (lane == 0) {
-        float acc = 0.0f;
-        for (int g = 0; g < groups; ++g) acc = __fmaf_rn((float)wdot[g], wscl[g], acc);
-        S.out[lr0 + r] = acc;
-      }
-      __syncwarp();
     }
-    __syncthreads();  // the buffer is refilled by issue(b + 2)
+    __syncthreads();
+    // The group chains of the batch's rows, one thread a row, groups in order.
+    for (int r = t; r < n; r += DT) {
+      float acc = 0.0f;
+#pragma unroll 8
+      for (int g = 0; g < groups; ++g) acc = __fmaf_rn((float)pdot[g * per + r], pscl[g * per + r], acc);
+      S.out[lr0 + r] = acc;
+    }
+    __syncthreads();  // the buffers are refilled by issue(b + 2) and the next batch's dots
   }
   cp_wait<0>();
   return true;
@@ -290,8 +298,9 @@ __host__ __device__ inline size_t attend_smem_floats(int qpk, int tmax, int f16)
 // out (cp.async) before the block waits for q, k and v; the block appends
 // the new key and value to the cache and publishes the heads' quantized
 // output as LL words.
+template <class Ev>
 __device__ bool attend(const DecodeArgs& a, const DLayer& L, int layer, int pos, int kvh, int tmax, uint32_t tag_in,
-                       uint32_t tag_out, Shared& S) {
+                       uint32_t tag_out, Shared& S, Ev ev) {
   const DConfig& cfg = a.cfg;
   const int hd = 128, qpk = cfg.heads / cfg.kv_heads, qd = cfg.heads * hd, kvd = cfg.kv_heads * hd;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
@@ -322,6 +331,7 @@ __device__ bool attend(const DecodeArgs& a, const DLayer& L, int layer, int pos,
   ok = ll_wait(a.ll + ll.qkv + qd + kvd + kvh * hd, hd, tag_in, a.status,
                [&](int i, uint32_t v) { raw[nq + hd + i] = __uint_as_float(v); });
   if (!ok) return false;
+  ev(5);
   const float* sn = a.rope + (size_t)min(pos, a.rope_rows - 1) * hd;
   const float* cs = sn + hd / 2;
   // Warp 0: k, warp 1: v, warps 2..: q heads (causal_lm.rs:428-446).
@@ -375,6 +385,7 @@ __device__ bool attend(const DecodeArgs& a, const DLayer& L, int layer, int pos,
   }
   __syncthreads();
   A.run(q, T, kf, vf, true, out);
+  ev(6);
   // Quantize each head's output (groups of 32 or 128 lie inside a head),
   // then publish codes (4 a word) and scales as LL words.
   const DMat& O = L.out;
@@ -397,6 +408,7 @@ __device__ bool attend(const DecodeArgs& a, const DLayer& L, int layer, int pos,
   for (int wd = t; wd < nq / 4; wd += DT) ll_put(a.ll + ll.attq + qh0 * hd / 4 + wd, ((const uint32_t*)codes)[wd], tag_out);
   for (int g = t; g < nq / G; g += DT) ll_put(a.ll + ll.attq_scales + qh0 * hd / G + g, __float_as_uint(scales[g]), tag_out);
   __syncthreads();  // the next phase stages weights over this scratch
+  ev(7);
   return true;
 }
 
@@ -525,6 +537,7 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
   S.flag = (int*)p; p += 64;
   S.red = (float*)p; p += 64 * 4;
   S.xf = (float*)p; p += (size_t)kmax * 4;
+  S.sq = (float*)p; p += (size_t)kmax * 4;
   S.xq = (int8_t*)p; p += (size_t)kmax;
   S.xs = (float*)p; p += (size_t)(kmax / 32) * 4;
   S.own = (float*)p; p += 512 * 4;
@@ -544,7 +557,14 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
     ++mark_at;
   };
   int token = a.tokens[0];
+  int cur_step = -1, cur_layer = 0;
+  // Optional per-block event stamps of one step: [layer][16][grid].
+  auto ev = [&](int k) {
+    if (a.events && cur_step == a.event_step && threadIdx.x == 0)
+      a.events[((size_t)cur_layer * 16 + k) * nb + c] = gtimer();
+  };
   for (int i = 0; i < a.steps; ++i) {
+    cur_step = i;
     bool stopped = false;
     for (int s = 0; s < a.nstop; ++s) stopped |= a.stop[s] == token;
     if (stopped) {
@@ -564,6 +584,8 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
       if (kk >= r0 && kk < r1) S.own[kk - r0] = v;
     }
     for (int l = 0; l < L; ++l) {
+      cur_layer = l;
+      ev(0);
       const DLayer& Lw = a.layers[l];
       const uint32_t t_qkv = base + 5 * l, t_att = t_qkv + 1, t_xa = t_qkv + 2, t_h = t_qkv + 3, t_xb = t_qkv + 4;
       const uint32_t t_x_in = t_qkv - 1;  // xb of the layer before
@@ -572,15 +594,19 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
         if (l > 0 && !ll_wait(a.ll + ll.xb, cfg.d, t_x_in, a.status,
                               [&](int k, uint32_t v) { S.xf[k] = __uint_as_float(v); }))
           return false;
+        ev(1);
         norm_quant(cfg.d, Lw.norm_attn, cfg.eps, Lw.qkv.agroup, Lw.qkv.half, S);
+        ev(2);
         return true;
       });
       if (!ok) return;
+      ev(3);
       for (int lr = threadIdx.x; lr < q1 - q0; lr += DT) ll_put(a.ll + ll.qkv + q0 + lr, __float_as_uint(S.out[lr]), t_qkv);
+      ev(4);
       mark();
       // P2: attention.
       if (c < cfg.kv_heads) {
-        if (!attend(a, Lw, l, pos, c, tmax, t_qkv, t_att, S)) return;
+        if (!attend(a, Lw, l, pos, c, tmax, t_qkv, t_att, S, ev)) return;
       }
       mark();
       // P3: o_proj + residual. Input: the quantized attention output.
@@ -590,9 +616,11 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
           return false;
         if (!ll_wait(a.ll + ll.attq_scales, nsc, t_att, a.status, [&](int k, uint32_t v) { S.xs[k] = __uint_as_float(v); }))
           return false;
+        ev(8);
         return true;
       });
       if (!ok) return;
+      ev(9);
       mark();
       for (int lr = threadIdx.x; lr < nown; lr += DT) {
         float o = S.out[lr];
@@ -605,10 +633,13 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
       ok = gemv(Lw.gate_up, 2 * nu, [&](int lr) { return lr < nu ? u0 + lr : cfg.ffn + u0 + lr - nu; }, S, [&]() {
         if (!ll_wait(a.ll + ll.xa, cfg.d, t_xa, a.status, [&](int k, uint32_t v) { S.xf[k] = __uint_as_float(v); }))
           return false;
+        ev(10);
         norm_quant(cfg.d, Lw.norm_mlp, cfg.eps, Lw.gate_up.agroup, Lw.gate_up.half, S);
+        ev(11);
         return true;
       });
       if (!ok) return;
+      ev(12);
       mark();
       for (int lr = threadIdx.x; lr < nu; lr += DT)
         ll_put(a.ll + ll.h + u0 + lr, __float_as_uint(__fmul_rn(silu(S.out[lr]), S.out[nu + lr])), t_h);
@@ -616,10 +647,13 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
       ok = gemv(Lw.down, nown, [&](int lr) { return r0 + lr; }, S, [&]() {
         if (!ll_wait(a.ll + ll.h, cfg.ffn, t_h, a.status, [&](int k, uint32_t v) { S.xf[k] = __uint_as_float(v); }))
           return false;
+        ev(13);
         norm_quant(cfg.ffn, nullptr, cfg.eps, Lw.down.agroup, Lw.down.half, S);
+        ev(14);
         return true;
       });
       if (!ok) return;
+      ev(15);
       mark();
       for (int lr = threadIdx.x; lr < nown; lr += DT) {
         float o = S.out[lr];
@@ -634,7 +668,9 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
     bool ok = table_slice(a, v0, v1, i + 1, S, (float*)(S.flag + 4), S.flag + 5, [&]() {
       if (!ll_wait(a.ll + ll.xb, cfg.d, t_final, a.status, [&](int k, uint32_t v) { S.xf[k] = __uint_as_float(v); }))
         return false;
-      if (threadIdx.x == 0) S.red[0] = rms_inv(seq_sum_squares(S.xf, cfg.d), cfg.d, cfg.eps);
+      for (int kk = threadIdx.x; kk < cfg.d; kk += DT) S.sq[kk] = __fmul_rn(S.xf[kk], S.xf[kk]);
+      __syncthreads();
+      if (threadIdx.x == 0) S.red[0] = rms_inv(seq_sum(S.sq, cfg.d), cfg.d, cfg.eps);
       __syncthreads();
       const float inv = S.red[0];
       for (int kk = threadIdx.x; kk < cfg.d; kk += DT) S.xf[kk] = __fmul_rn(S.xf[kk], __fmul_rn(inv, a.final_norm[kk]));
@@ -679,7 +715,7 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
 size_t head_smem(const DConfig& cfg) {
   const int qd = cfg.heads * 128;
   const int kmax = std::max(std::max(cfg.d, qd), cfg.ffn);
-  return 64 + 64 * 4 + (size_t)kmax * 4 + kmax + (size_t)(kmax / 32) * 4 + 512 * 4 + 512 * 4;
+  return 64 + 64 * 4 + (size_t)kmax * 8 + kmax + (size_t)(kmax / 32) * 4 + 512 * 4 + 512 * 4;
 }
 
 // The union region: the largest of the GEMV group dots and scales, the
@@ -688,7 +724,10 @@ size_t union_smem(const DConfig& cfg, int grid, int f16, int tmax) {
   const int qd = cfg.heads * 128;
   size_t u = 0;
   const int kmax = std::max(std::max(cfg.d, qd), cfg.ffn);
-  u = std::max(u, (size_t)2 * WSTAGE + (size_t)DW * (kmax / 32) * 8);
+  // Two staging buffers, then [group][row] dots and scale products for the
+  // rows of a batch (at most WSTAGE / 32 group-row pairs: a staged row
+  // takes at least 32 bytes a group).
+  u = std::max(u, (size_t)2 * WSTAGE + (size_t)(WSTAGE / 32) * 8);
   u = std::max(u, (size_t)DW * TAB_STAGES * TAB_ROWS_W * TAB_PITCH);
   u = std::max(u, (size_t)grid * 8);
   u = std::max(u, attend_smem_floats(cfg.heads / cfg.kv_heads, tmax, f16) * 4);

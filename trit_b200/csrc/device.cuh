@@ -60,6 +60,22 @@ __device__ __forceinline__ float seq_sum_squares(const float* v, int n) {
   return s;
 }
 
+// A sum left to right (the reference's f32 `sum()`), reading 4 values at a
+// time so that only the adds wait on each other. v is 16-byte aligned.
+__device__ __forceinline__ float seq_sum(const float* v, int n) {
+  float s = 0.0f;
+  int i = 0;
+  for (; i + 4 <= n; i += 4) {
+    float4 q = *(const float4*)(v + i);
+    s = __fadd_rn(s, q.x);
+    s = __fadd_rn(s, q.y);
+    s = __fadd_rn(s, q.z);
+    s = __fadd_rn(s, q.w);
+  }
+  for (; i < n; ++i) s = __fadd_rn(s, v[i]);
+  return s;
+}
+
 // inv = 1 / sqrt(sum / d + eps), each step rounded (layers.rs:137).
 __device__ __forceinline__ float rms_inv(float sum, int d, float eps) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)d), eps)));

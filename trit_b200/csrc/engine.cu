@@ -643,6 +643,16 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
     TRIT_CUDA(cudaMemsetAsync(dphase, 0, (size_t)steps * marks * 8, stream_));
   }
   a.phase_ns = dphase;
+  // TRIT_PHASE_TRACE=3: per-block stamps of 16 events a layer for one step.
+  static const bool trace_events = getenv("TRIT_PHASE_TRACE") && *getenv("TRIT_PHASE_TRACE") == '3';
+  long long* devents = nullptr;
+  const size_t nev = (size_t)cfg_.layers * 16 * decode_grid_;
+  if (trace_events && steps > 3) {
+    TRIT_CUDA(cudaMallocAsync(&devents, nev * 8, stream_));
+    TRIT_CUDA(cudaMemsetAsync(devents, 0, nev * 8, stream_));
+  }
+  a.events = devents;
+  a.event_step = 2;
   TRIT_CUDA(cudaMemsetAsync(dll_, 0, ll_words_ * 8, stream_));
   TRIT_CUDA(cudaMemsetAsync(dstatus_, 0, 4, stream_));
   TRIT_CUDA(launch_decode(a, decode_grid_, stream_));
@@ -678,6 +688,34 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
     const char* names[7] = {"qkv", "attention", "o", "gate_up", "down", "table", "step"};
     for (int p = 0; p < 7; ++p)
       if (n[p]) fprintf(stderr, "phase %-9s %8.2f us\n", names[p], sum[p] / n[p] / 1e3);
+  }
+  if (devents) {
+    std::vector<long long> t(nev);
+    TRIT_CUDA(cudaMemcpy(t.data(), devents, nev * 8, cudaMemcpyDeviceToHost));
+    TRIT_CUDA(cudaFree(devents));
+    const char* names[16] = {"layer start", "P1 x arrived", "P1 norm+quant", "P1 qkv rows", "P1 published",
+                             "P2 qkv arrived", "P2 attention", "P2 published", "P3 attq arrived", "P3 o rows",
+                             "P4 xa arrived", "P4 norm+quant", "P4 gate_up rows", "P5 h arrived", "P5 quantize",
+                             "P5 down rows"};
+    const int G = decode_grid_;
+    for (int k = 1; k < 16; ++k) {
+      double sum = 0, mx = 0;
+      long n = 0;
+      for (int l = 1; l < cfg_.layers; ++l)
+        for (int c = 0; c < G; ++c) {
+          long long cur = t[((size_t)l * 16 + k) * G + c];
+          if (!cur) continue;
+          int pk = k - 1;
+          while (pk > 0 && !t[((size_t)l * 16 + pk) * G + c]) --pk;
+          long long prev = t[((size_t)l * 16 + pk) * G + c];
+          if (!prev) continue;
+          double d = (double)(cur - prev) / 1e3;
+          sum += d;
+          mx = std::max(mx, d);
+          ++n;
+        }
+      if (n) fprintf(stderr, "event %-16s mean %7.2f us  max %7.2f us  (%ld)\n", names[k], sum / n, mx, n);
+    }
   }
   if (status) throw Error("the persistent decode gave up waiting for another block (status " + std::to_string(status) + ")");
 }

@@ -51,6 +51,8 @@ struct DecodeArgs {
   unsigned long long* ll;   // [decode_ll_words] {data, tag} words, zeroed before the launch
   int* status;           // 0 ok; nonzero: a wait ran out (see decode.cu)
   long long* phase_ns;   // optional [steps][5 * layers + 2] globaltimer stamps of block 0, or null
+  long long* events;     // optional [layers][16][grid] per-block stamps of step event_step, or null
+  int event_step;
 };
 
 // Whether the persistent decode takes this model (its product widths).
