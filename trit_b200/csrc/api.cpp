@@ -24,8 +24,14 @@ struct TritDense {
 };
 
 namespace {
-
 thread_local std::string g_error;
+}  // namespace
+
+namespace trit {
+void set_last_error(const std::string& text) { g_error = text; }
+}  // namespace trit
+
+namespace {
 
 template <class T, class F>
 T guard(T failed, F body) {

@@ -411,14 +411,7 @@ cudaError_t launch_scale(float* x, size_t n, float mult, cudaStream_t s) {
 cudaError_t launch_norm_quant(const float* x, int m, int d, const float* w, float eps, int group, int half,
                               int8_t* xq, float* xs, cudaStream_t s) {
   size_t smem = (size_t)d * 4;
-  if (smem > 48 * 1024) {
-    static bool configured = false;
-    if (!configured) {
-      cudaFuncSetAttribute(k_norm_quant<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-      cudaFuncSetAttribute(k_norm_quant<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-      configured = true;
-    }
-  }
+  if (smem > 48 * 1024) return cudaErrorInvalidValue;  // d <= 12288
   if (group == 32) k_norm_quant<32><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs);
   else k_norm_quant<128><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs);
   LAUNCH_CHECK();
@@ -430,10 +423,12 @@ cudaError_t launch_gemv(const DMat& W, const int8_t* xq, const float* xs, int m,
   int units = (mode == kEpSilu) ? W.n / 2 : W.n;
   int per_block = (mode == kEpSilu) ? GEMV_ROWS / 2 : GEMV_ROWS;
   size_t smem = gemv_smem(W);
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
     cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    configured = true;
+    configured[dev] = true;
   }
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   k_gemv<<<(units + per_block - 1) / per_block, GEMV_THREADS, smem, s>>>(W, xq, xs, m, mode, y, ldy, resid_mult,
@@ -458,10 +453,12 @@ cudaError_t launch_attention(const float* qkv, int m, const DConfig& cfg, const 
   const int tmax = (max_tk + 3) / 4 * 4;
   size_t smem = ((size_t)2 * qpk * 128 + attention_smem_floats(qpk, tmax, ATT_KT, cache.f16)) * 4;
   if (smem > 220 * 1024) return cudaErrorInvalidValue;
-  static int configured = 0;
-  if (configured < (int)smem) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
     cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-    configured = 220 * 1024;
+    configured[dev] = true;
   }
   k_attention<<<dim3(m, cfg.kv_heads), 256, smem, s>>>(qkv, m, cfg, cache, row_stream, row_pos, layer, tmax, att);
   LAUNCH_CHECK();
@@ -487,10 +484,12 @@ template <int B>
 static cudaError_t table_pass(const DTable& T, const float* xn, int nb, float mult, float* logits, float* best_val,
                               int* best_idx, cudaStream_t s) {
   size_t smem = (size_t)T.k * B * 4;
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
     cudaFuncSetAttribute(k_table<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    configured = true;
+    configured[dev] = true;
   }
   int blocks = table_blocks(T.n);
   k_table<B><<<blocks, 256, smem, s>>>(T, xn, nb, mult, logits, best_val, best_idx, blocks);
