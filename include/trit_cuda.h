@@ -154,6 +154,27 @@ int trit_dense_forward_device(TritDense *layer, const float *x, size_t rows, flo
 /* Frees a layer. NULL is a no-op. */
 void trit_dense_free(TritDense *layer);
 
+/* A Q8_0 W8A8 product that allocates nothing, for callers that cannot
+ * call cudaMalloc when they run it (inside another party's graph capture,
+ * on a real-time thread, or with every byte of device memory owned by
+ * their own pool). No counterpart in the reference: Trit runs on the CPU
+ * and allocates freely. It computes what trit_dense_forward_device
+ * computes, on device pointers: `codes` (n x k int8, row-major) and
+ * `scales` (n x k/32 f16 bits) are the split form of ggml Q8_0 blocks
+ * (block b of row r: scales[r * k/32 + b], codes[r * k + 32 b ...]); x is
+ * rows x k f32; out is rows x n f32. Its scratch (the int8 activations and
+ * their scales) is one 1 MiB device array that the library holds on every
+ * GPU it is loaded on until the process exits, so rows * k * 9 / 8 must stay
+ * within 1 MiB (larger calls fail). All calls share that array and leave
+ * their contents in it: calls that overlap on the GPU (other streams,
+ * other threads) race; order them on one stream. The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture. Returns 0, or -1 with
+ * trit_last_error(). Queued on `cuda_stream` (NULL: the default stream);
+ * does not wait. */
+int trit_dense_q8_0_forward_static(const void *codes, const void *scales, size_t n, size_t k, const float *x,
+                                   size_t rows, float *out, void *cuda_stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -70,6 +70,8 @@ def library() -> ctypes.CDLL:
         "trit_dense_forward_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, _size, ctypes.c_void_p,
                                                      ctypes.c_void_p]),
         "trit_dense_free": (None, [ctypes.c_void_p]),
+        "trit_dense_q8_0_forward_static": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, _size, _size,
+                                                          ctypes.c_void_p, _size, ctypes.c_void_p, ctypes.c_void_p]),
         "trit_synth_model": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p]),
         "trit_synth_normal_row": (None, [ctypes.c_uint64, ctypes.c_char_p, ctypes.c_uint64, _size, ctypes.c_float,
                                          _f32p]),
