@@ -46,6 +46,20 @@ const char *trit_cuda_version(void);
  * (trit_last_error, include/trit.h:44-46; ffi/src/lib.rs:20-45.) */
 const char *trit_last_error(void);
 
+/* A model folder described without a GPU, as JSON text: its settings as
+ * Config::parse reads them (causal_lm.rs:41-77: q/k norms iff model_type
+ * is "qwen3", head_dim defaulting to hidden / heads, eps 1e-6, rope_theta
+ * 1e6, the Granite multipliers, tie_word_embeddings), the storage of its
+ * products and token tables, and the bytes a greedy step reads from device
+ * memory for the products and the output table. `options_json` takes the
+ * "config_at" and "prefix" keys of trit_lm_load (others are ignored).
+ * Free the text with trit_free_text. NULL on failure. */
+char *trit_lm_inspect(const char *model_dir, const char *options_json);
+
+/* Frees text returned by this library. NULL is a no-op. (trit_free_text,
+ * include/trit.h:11.) */
+void trit_free_text(char *text);
+
 /* Loads a decoder onto a GPU. `options_json` is NULL, "" or an object;
  * every key is optional and an unknown key fails (as trit_load_json,
  * include/trit.h:76-87):
@@ -59,6 +73,9 @@ const char *trit_last_error(void);
  *   "decode":       "persistent" (default: one kernel runs every greedy
  *                   step of a batch-1 generation) or "layered" (a kernel
  *                   per operation and step)
+ *   "config_at":    key path of the decoder settings in config.json ("";
+ *                   "thinker_config.text_config." in Qwen3-ASR)
+ *   "prefix":       start of every tensor name ("", "thinker.", "llm.")
  * NULL on failure. (CausalLm::load / from_tensors, causal_lm.rs:124-198.) */
 TritLm *trit_lm_load(const char *model_dir, const char *options_json);
 

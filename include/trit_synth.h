@@ -17,8 +17,12 @@ extern "C" {
  * spec_json: {"config": {Hugging Face config keys: model_type,
  * hidden_size, intermediate_size, num_hidden_layers, num_attention_heads,
  * num_key_value_heads, head_dim, vocab_size, rms_norm_eps, rope_theta,
- * tie_word_embeddings}, "format": "q8_0" | "int8" | "ternary",
- * "seed": N, "std": 0.02}. Returns 0, or -1 (trit_last_error). */
+ * tie_word_embeddings, and Granite's embedding_multiplier,
+ * attention_multiplier, residual_multiplier, logits_scaling},
+ * "format": "q8_0" | "int8" | "ternary", "seed": N, "std": 0.02,
+ * "prefix": start of every tensor name (""), "config_at": key path the
+ * settings are nested under in config.json ("", or for example
+ * "thinker_config.text_config.")}. Returns 0, or -1 (trit_last_error). */
 int trit_synth_model(const char *dir, const char *spec_json);
 
 /* The f32 values of row `row` of tensor `name` (without ".weight") before

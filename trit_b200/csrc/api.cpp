@@ -2,6 +2,7 @@
 // point runs its body under `guard`, which turns a C++ exception into the
 // thread's error text and the failure value, as ffi/src/lib.rs:20-45 does
 // for Rust panics.
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -64,6 +65,20 @@ extern "C" {
 const char* trit_cuda_version(void) { return "0.1.0"; }
 
 const char* trit_last_error(void) { return g_error.c_str(); }
+
+char* trit_lm_inspect(const char* model_dir, const char* options_json) {
+  return guard<char*>(nullptr, [&]() {
+    need(model_dir, "model_dir");
+    trit::Options o = trit::Options::parse(options_json, true);
+    std::string text = trit::describe_model(model_dir, o.config_at, o.prefix);
+    char* out = (char*)std::malloc(text.size() + 1);
+    if (!out) throw trit::Error("out of host memory");
+    std::memcpy(out, text.c_str(), text.size() + 1);
+    return out;
+  });
+}
+
+void trit_free_text(char* text) { std::free(text); }
 
 TritLm* trit_lm_load(const char* model_dir, const char* options_json) {
   return guard<TritLm*>(nullptr, [&]() {

@@ -16,7 +16,7 @@ void CudaCheck::ok(cudaError_t e, const char* what) {
   if (e != cudaSuccess) throw Error(std::string("CUDA: ") + cudaGetErrorString(e) + " (" + what + ")");
 }
 
-Options Options::parse(const char* text) {
+Options Options::parse(const char* text, bool lenient) {
   Options o;
   if (!text || !*text) return o;
   Json j = Json::parse(text);
@@ -24,6 +24,7 @@ Options Options::parse(const char* text) {
   for (auto& f : j.fields) {
     const std::string& k = f.first;
     const Json& v = f.second;
+    if (lenient && k != "config_at" && k != "prefix") continue;
     auto count = [&](int lo, int hi) {
       if (v.kind != Json::Number || v.num != std::floor(v.num) || v.num < lo || v.num > hi)
         throw Error("options: " + k + " must be a whole number from " + std::to_string(lo) + " to " + std::to_string(hi));
@@ -41,6 +42,9 @@ Options Options::parse(const char* text) {
       if (v.kind != Json::String || (v.str != "persistent" && v.str != "layered"))
         throw Error("options: decode is \"persistent\" or \"layered\"");
       o.decode = v.str;
+    } else if (k == "config_at" || k == "prefix") {
+      if (v.kind != Json::String) throw Error("options: " + k + " must be a string");
+      (k == "config_at" ? o.config_at : o.prefix) = v.str;
     } else {
       throw Error("options: unknown key " + k);
     }
@@ -262,52 +266,24 @@ void Lm::release() {
 
 // Config::parse (causal_lm.rs:41-77) and CausalLm::from_tensors (:141-198).
 void Lm::load(const std::string& dir) {
-  std::string text;
-  {
-    FILE* f = fopen((dir + "/config.json").c_str(), "rb");
-    if (!f) throw Error("cannot read " + dir + "/config.json");
-    char buf[65536];
-    size_t n;
-    while ((n = fread(buf, 1, sizeof buf, f)) > 0) text.append(buf, n);
-    fclose(f);
-  }
-  Json j = Json::parse(text);
-  std::string type = j.string_or("model_type", "");
-  bool qk_norm;
-  if (type == "qwen3") qk_norm = true;
-  else if (type == "llama" || type == "mistral" || type == "granite") qk_norm = false;
-  else throw Error("config.json does not describe a language model this engine runs");
-  cfg_.heads = (int)j.integer("num_attention_heads");
-  cfg_.kv_heads = (int)j.integer("num_key_value_heads");
-  if (!cfg_.heads || !cfg_.kv_heads || cfg_.heads % cfg_.kv_heads)
-    throw Error("config.json: the query heads do not share the key heads evenly");
-  cfg_.d = (int)j.integer("hidden_size");
-  cfg_.embedding_multiplier = (float)j.number("embedding_multiplier", 1.0);
-  cfg_.has_q_scale = j.has("attention_multiplier");
-  cfg_.residual_multiplier = (float)j.number("residual_multiplier", 1.0);
-  cfg_.logits_scaling = (float)j.number("logits_scaling", 1.0);
-  cfg_.ffn = (int)j.integer("intermediate_size");
-  cfg_.layers = (int)j.integer("num_hidden_layers");
-  cfg_.hd = j.has("head_dim") ? (int)j.integer("head_dim") : cfg_.d / cfg_.heads;
-  cfg_.vocab = (int)j.integer("vocab_size");
-  cfg_.eps = (float)j.number("rms_norm_eps", 1e-6);
-  float rope_base = (float)j.number("rope_theta", 1e6);
-  // `attention` divides by sqrt(head_dim); Granite's multiplier replaces that (causal_lm.rs:416-419).
-  cfg_.q_scale = cfg_.has_q_scale ? (float)j.number("attention_multiplier", 1.0) * std::sqrt((float)cfg_.hd) : 1.0f;
-  tied_ = j.flag("tie_word_embeddings", false);
+  ModelConfig mc = read_model_config(dir, opt_.config_at);
+  cfg_ = mc.cfg;
+  const bool qk_norm = mc.qk_norm;
+  const float rope_base = mc.rope_base;
+  tied_ = mc.tied;
   if (cfg_.hd != 128) throw Error("head_dim " + std::to_string(cfg_.hd) + ": the CUDA kernels take head_dim 128");
   if (cfg_.d % 128 || cfg_.ffn % 128) throw Error("hidden and intermediate sizes must be multiples of 128");
 
   GgufFile g(dir + "/model.gguf");
   const int hd = cfg_.hd, qd = cfg_.heads * hd, kvd = cfg_.kv_heads * hd;
-  bool has_head = !tied_ && g.find("lm_head.weight");
+  bool has_head = !tied_ && g.find(opt_.prefix + "lm_head.weight");
   for (int pass = 0; pass < 2; ++pass) {
     Arena A;
     A.fill = pass == 1;
     A.base = (char*)arena_;
     layers_.assign(cfg_.layers, DLayer{});
     for (int l = 0; l < cfg_.layers; ++l) {
-      std::string p = "model.layers." + std::to_string(l);
+      std::string p = opt_.prefix + "model.layers." + std::to_string(l);
       DLayer& L = layers_[l];
       L.norm_attn = load_vector(g, A, p + ".input_layernorm.weight", cfg_.d);
       L.qkv = load_mat(g, A, {{p + ".self_attn.q_proj", qd}, {p + ".self_attn.k_proj", kvd}, {p + ".self_attn.v_proj", kvd}}, cfg_.d);
@@ -320,9 +296,9 @@ void Lm::load(const std::string& dir) {
       L.gate_up = load_mat(g, A, {{p + ".mlp.gate_proj", cfg_.ffn}, {p + ".mlp.up_proj", cfg_.ffn}}, cfg_.d);
       L.down = load_mat(g, A, {{p + ".mlp.down_proj", cfg_.d}}, cfg_.ffn);
     }
-    final_norm_ = load_vector(g, A, "model.norm.weight", cfg_.d);
-    embed_ = load_table(g, A, "model.embed_tokens", cfg_.vocab, cfg_.d);
-    head_ = has_head ? load_table(g, A, "lm_head", cfg_.vocab, cfg_.d) : embed_;
+    final_norm_ = load_vector(g, A, opt_.prefix + "model.norm.weight", cfg_.d);
+    embed_ = load_table(g, A, opt_.prefix + "model.embed_tokens", cfg_.vocab, cfg_.d);
+    head_ = has_head ? load_table(g, A, opt_.prefix + "lm_head", cfg_.vocab, cfg_.d) : embed_;
     if (pass == 0) {
       arena_bytes_ = A.used;
       TRIT_CUDA(cudaMalloc(&arena_, arena_bytes_));

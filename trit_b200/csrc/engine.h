@@ -24,7 +24,10 @@ struct Options {
   int page_tokens = 64;          // positions per KV page
   int prefill_rows = 512;        // rows per prefill pass
   std::string decode = "persistent";  // "persistent" (one kernel per generation) or "layered"
-  static Options parse(const char* json);
+  std::string config_at;         // key path of the settings in config.json (from_tensors' config_at)
+  std::string prefix;            // start of every tensor name (from_tensors' prefix)
+  // `lenient`: keys other than config_at and prefix are skipped unchecked.
+  static Options parse(const char* json, bool lenient = false);
 };
 
 struct CudaCheck {

@@ -394,3 +394,128 @@ void GgufWriter::close() {
 }
 
 }  // namespace trit
+
+namespace trit {
+
+ModelConfig parse_model_config(const std::string& text, const std::string& at) {
+  Json j = Json::parse(text);
+  auto key = [&](const char* name) { return at + name; };
+  ModelConfig m;
+  m.type = j.string_or(key("model_type"), "");
+  if (m.type == "qwen3") m.qk_norm = true;
+  else if (m.type == "llama" || m.type == "mistral" || m.type == "granite") m.qk_norm = false;
+  else throw Error("config.json does not describe a language model this engine runs");
+  DConfig& c = m.cfg;
+  c.heads = (int)j.integer(key("num_attention_heads"));
+  c.kv_heads = (int)j.integer(key("num_key_value_heads"));
+  if (c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads)
+    throw Error("config.json: the query heads do not share the key heads evenly");
+  c.d = (int)j.integer(key("hidden_size"));
+  c.embedding_multiplier = (float)j.number(key("embedding_multiplier"), 1.0);
+  c.has_q_scale = j.has(key("attention_multiplier"));
+  c.residual_multiplier = (float)j.number(key("residual_multiplier"), 1.0);
+  c.logits_scaling = (float)j.number(key("logits_scaling"), 1.0);
+  c.ffn = (int)j.integer(key("intermediate_size"));
+  c.layers = (int)j.integer(key("num_hidden_layers"));
+  c.hd = j.has(key("head_dim")) ? (int)j.integer(key("head_dim")) : c.d / c.heads;
+  c.vocab = (int)j.integer(key("vocab_size"));
+  c.eps = (float)j.number(key("rms_norm_eps"), 1e-6);
+  m.rope_base = (float)j.number(key("rope_theta"), 1e6);
+  // `attention` divides by sqrt(head_dim); Granite's multiplier replaces
+  // that (causal_lm.rs:416-419), so the kernels scale q by it times sqrt(hd).
+  m.attention_multiplier = (float)j.number(key("attention_multiplier"), 1.0);
+  c.q_scale = c.has_q_scale ? m.attention_multiplier * std::sqrt((float)c.hd) : 1.0f;
+  m.tied = j.flag(key("tie_word_embeddings"), false);
+  return m;
+}
+
+ModelConfig read_model_config(const std::string& dir, const std::string& at) {
+  std::string text;
+  FILE* f = std::fopen((dir + "/config.json").c_str(), "rb");
+  if (!f) throw Error("cannot read " + dir + "/config.json");
+  char buf[65536];
+  size_t n;
+  while ((n = std::fread(buf, 1, sizeof buf, f)) > 0) text.append(buf, n);
+  std::fclose(f);
+  return parse_model_config(text, at);
+}
+
+namespace {
+
+// The storage of the product `name` (without .weight): its kind and the
+// bytes of its codes and scales as the device holds them.
+std::string product_kind(const GgufFile& g, const std::string& name, uint64_t* bytes) {
+  const GgufTensor* w = g.find(name + ".weight");
+  if (w && w->type == Q8_0) {
+    *bytes = w->count() + w->count() / 32 * 2;
+    return "q8_0";
+  }
+  if (w && w->type == I8 && g.find(name + ".scales")) {
+    *bytes = w->count() + g.at(name + ".scales").count() * 4;
+    return "int8";
+  }
+  const GgufTensor* q = g.find(name + ".qweight");
+  if (q) {
+    const GgufTensor& s = g.at(name + ".scales");
+    // 5 codes a byte in the file, 2 bits a code on the device.
+    *bytes = s.count() * 128 / 4 + s.count() * 4;
+    return "ternary";
+  }
+  throw Error("model.gguf: no Q8_0, int8 or ternary weights for " + name);
+}
+
+}  // namespace
+
+std::string describe_model(const std::string& dir, const std::string& at, const std::string& prefix) {
+  ModelConfig m = read_model_config(dir, at);
+  const DConfig& c = m.cfg;
+  GgufFile g(dir + "/model.gguf");
+  std::map<std::string, int> kinds;
+  uint64_t layer_bytes = 0, b = 0;
+  const char* parts[] = {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
+                         "mlp.gate_proj",    "mlp.up_proj",      "mlp.down_proj"};
+  for (int l = 0; l < c.layers; ++l)
+    for (const char* p : parts) {
+      kinds[product_kind(g, prefix + "model.layers." + std::to_string(l) + "." + p, &b)]++;
+      layer_bytes += b;
+    }
+  auto table_kind = [&](const std::string& name, uint64_t* bytes) -> std::string {
+    const GgufTensor& t = g.at(name);
+    if (t.type == Q8_0) {
+      *bytes = t.count() + t.count() / 32 * 2;
+      return "q8_0";
+    }
+    if (t.type == I8) {
+      *bytes = t.count() + t.count() / 32 * 4;
+      return "int8";
+    }
+    throw Error("model.gguf: " + name + " is neither Q8_0 nor int8 with per-32 scales");
+  };
+  uint64_t embed_bytes = 0, head_bytes = 0;
+  std::string embed = table_kind(prefix + "model.embed_tokens.weight", &embed_bytes);
+  bool has_head = !m.tied && g.find(prefix + "lm_head.weight");
+  std::string head = has_head ? table_kind(prefix + "lm_head.weight", &head_bytes) : embed;
+  if (!has_head) head_bytes = embed_bytes;
+  std::string weights;
+  for (auto& k : kinds) weights += (weights.empty() ? "" : "+") + k.first;
+  char q_mult[64] = "null";
+  if (c.has_q_scale) std::snprintf(q_mult, sizeof q_mult, "%.9g", (double)m.attention_multiplier);
+  char buf[2048];
+  std::snprintf(buf, sizeof buf,
+                "{\"model_type\": \"%s\", \"hidden_size\": %d, \"intermediate_size\": %d, \"num_hidden_layers\": %d, "
+                "\"num_attention_heads\": %d, \"num_key_value_heads\": %d, \"head_dim\": %d, \"vocab_size\": %d, "
+                "\"rms_norm_eps\": %.9g, \"rope_theta\": %.9g, \"qk_norm\": %s, \"tie_word_embeddings\": %s, "
+                "\"embedding_multiplier\": %.9g, \"attention_multiplier\": %s, \"residual_multiplier\": %.9g, "
+                "\"logits_scaling\": %.9g, \"products\": \"%s\", \"token_table\": \"%s\", \"output_table\": \"%s\", "
+                "\"separate_head\": %s, \"product_bytes\": %llu, \"output_table_bytes\": %llu}",
+                m.type.c_str(), c.d, c.ffn, c.layers, c.heads, c.kv_heads, c.hd, c.vocab, (double)c.eps,
+                (double)m.rope_base, m.qk_norm ? "true" : "false", m.tied ? "true" : "false",
+                (double)c.embedding_multiplier,
+                q_mult,
+                (double)c.residual_multiplier, (double)c.logits_scaling, weights.c_str(), embed.c_str(),
+                head.c_str(), has_head ? "true" : "false", (unsigned long long)layer_bytes,
+                (unsigned long long)head_bytes);
+  return buf;
+}
+
+}  // namespace trit

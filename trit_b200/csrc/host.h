@@ -12,6 +12,8 @@
 #include <string>
 #include <vector>
 
+#include "types.h"
+
 namespace trit {
 
 struct Error : std::runtime_error {
@@ -97,5 +99,29 @@ class GgufWriter {
   uint64_t written_ = 0;
   std::FILE* file_ = nullptr;
 };
+
+// The decoder settings of a model folder's config.json, as Config::parse
+// (causal_lm.rs:41-77) reads them: key and value heads, widths, head_dim
+// (default hidden / heads), eps (1e-6), rope_theta (1e6), the Granite
+// multipliers, tie_word_embeddings, and q/k norms iff model_type is
+// "qwen3". Throws for a model this engine does not run.
+struct ModelConfig {
+  DConfig cfg;
+  std::string type;
+  bool qk_norm = false;
+  bool tied = false;
+  float rope_base = 1e6f;
+  float attention_multiplier = 1.0f;  // when cfg.has_q_scale
+};
+// `at` is the key path the settings sit under ("" or, in Qwen3-ASR,
+// "thinker_config.text_config.").
+ModelConfig parse_model_config(const std::string& json_text, const std::string& at = "");
+ModelConfig read_model_config(const std::string& dir, const std::string& at = "");
+
+// A JSON description of a model folder without touching a GPU: its
+// settings, the storage of its products and token tables, and the bytes a
+// greedy step reads from device memory.
+// `prefix` starts every tensor name ("", "thinker.", "llm." ...).
+std::string describe_model(const std::string& dir, const std::string& at = "", const std::string& prefix = "");
 
 }  // namespace trit

@@ -109,6 +109,8 @@ struct Spec {
   float sd = 0.02f;
   size_t d = 0, ffn = 0, layers = 0, heads = 0, kv_heads = 0, hd = 0, vocab = 0;
   bool tied = true;
+  std::string prefix;     // start of every tensor name ("thinker." ...)
+  std::string config_at;  // key path the settings are nested under ("a.b.")
 };
 
 void write_matrix(GgufWriter* w, const Spec& s, const std::string& name, size_t n, size_t k, bool declare) {
@@ -219,7 +221,7 @@ void write_norm(GgufWriter* w, const std::string& name, size_t n, bool declare) 
 void walk(GgufWriter* w, const Spec& s, bool declare) {
   bool qk_norm = s.config.string_or("model_type", "qwen3") == "qwen3";
   for (size_t l = 0; l < s.layers; ++l) {
-    std::string p = "model.layers." + std::to_string(l);
+    std::string p = s.prefix + "model.layers." + std::to_string(l);
     write_norm(w, p + ".input_layernorm.weight", s.d, declare);
     write_matrix(w, s, p + ".self_attn.q_proj", s.heads * s.hd, s.d, declare);
     write_matrix(w, s, p + ".self_attn.k_proj", s.kv_heads * s.hd, s.d, declare);
@@ -234,9 +236,9 @@ void walk(GgufWriter* w, const Spec& s, bool declare) {
     write_matrix(w, s, p + ".mlp.up_proj", s.ffn, s.d, declare);
     write_matrix(w, s, p + ".mlp.down_proj", s.d, s.ffn, declare);
   }
-  write_norm(w, "model.norm.weight", s.d, declare);
-  write_table(w, s, "model.embed_tokens", s.vocab, s.d, declare);
-  if (!s.tied) write_table(w, s, "lm_head", s.vocab, s.d, declare);
+  write_norm(w, s.prefix + "model.norm.weight", s.d, declare);
+  write_table(w, s, s.prefix + "model.embed_tokens", s.vocab, s.d, declare);
+  if (!s.tied) write_table(w, s, s.prefix + "lm_head", s.vocab, s.d, declare);
 }
 
 std::string config_text(const Spec& s) {
@@ -246,11 +248,35 @@ std::string config_text(const Spec& s) {
            "{\n  \"model_type\": \"%s\",\n  \"hidden_size\": %zu,\n  \"intermediate_size\": %zu,\n"
            "  \"num_hidden_layers\": %zu,\n  \"num_attention_heads\": %zu,\n  \"num_key_value_heads\": %zu,\n"
            "  \"head_dim\": %zu,\n  \"vocab_size\": %zu,\n  \"rms_norm_eps\": %.9g,\n  \"rope_theta\": %.9g,\n"
-           "  \"tie_word_embeddings\": %s,\n  \"trit_synthetic\": {\"format\": \"%s\", \"seed\": %llu, \"std\": %.9g}\n}\n",
+           "  \"tie_word_embeddings\": %s",
            c.string_or("model_type", "qwen3").c_str(), s.d, s.ffn, s.layers, s.heads, s.kv_heads, s.hd, s.vocab,
-           c.number("rms_norm_eps", 1e-6), c.number("rope_theta", 1e6), s.tied ? "true" : "false",
+           c.number("rms_norm_eps", 1e-6), c.number("rope_theta", 1e6), s.tied ? "true" : "false");
+  std::string out = buf;
+  // Granite's multipliers, when the spec gives them.
+  for (const char* key : {"embedding_multiplier", "attention_multiplier", "residual_multiplier", "logits_scaling"})
+    if (c.has(key)) {
+      snprintf(buf, sizeof buf, ",\n  \"%s\": %.9g", key, c.number(key, 1.0));
+      out += buf;
+    }
+  out += "\n}";
+  // Nest the settings under config_at ("thinker_config.text_config.").
+  std::vector<std::string> parts;
+  for (size_t from = 0; from < s.config_at.size();) {
+    size_t dot = s.config_at.find('.', from);
+    if (dot == std::string::npos) dot = s.config_at.size();
+    if (dot > from) parts.push_back(s.config_at.substr(from, dot - from));
+    from = dot + 1;
+  }
+  std::string tail;
+  for (size_t i = parts.size(); i-- > 0;) {
+    out = "{\"" + parts[i] + "\": " + out;
+    tail += "}";
+  }
+  snprintf(buf, sizeof buf, "\"trit_synthetic\": {\"format\": \"%s\", \"seed\": %llu, \"std\": %.9g}",
            s.format.c_str(), (unsigned long long)s.seed, (double)s.sd);
-  return buf;
+  if (tail.empty()) out = out.substr(0, out.size() - 2) + ",\n  " + buf + "\n}\n";
+  else out += tail + "\n";
+  return out;
 }
 
 }  // namespace
@@ -272,6 +298,8 @@ void synthesize(const std::string& dir, const std::string& spec_json) {
   s.hd = s.config.has("head_dim") ? s.config.integer("head_dim") : s.d / std::max<size_t>(1, s.heads);
   s.vocab = s.config.integer("vocab_size");
   s.tied = s.config.flag("tie_word_embeddings", true);
+  s.prefix = spec.string_or("prefix", "");
+  s.config_at = spec.string_or("config_at", "");
   if (!s.heads || !s.kv_heads || s.heads % s.kv_heads) throw Error("synthetic spec: heads must share kv heads evenly");
   std::string type = s.config.string_or("model_type", "qwen3");
   if (type != "qwen3" && type != "llama" && type != "mistral" && type != "granite")

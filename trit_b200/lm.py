@@ -43,6 +43,8 @@ def library() -> ctypes.CDLL:
     sig = {
         "trit_cuda_version": (ctypes.c_char_p, []),
         "trit_last_error": (ctypes.c_char_p, []),
+        "trit_lm_inspect": (ctypes.c_void_p, [ctypes.c_char_p, ctypes.c_char_p]),
+        "trit_free_text": (None, [ctypes.c_void_p]),
         "trit_lm_load": (ctypes.c_void_p, [ctypes.c_char_p, ctypes.c_char_p]),
         "trit_lm_free": (None, [ctypes.c_void_p]),
         "trit_lm_width": (ctypes.c_int64, [ctypes.c_void_p]),
@@ -288,10 +290,29 @@ class Dense:
         self.close()
 
 
-def synthesize(model_dir: str, config: dict, fmt: str = "q8_0", seed: int = 0, std: float = 0.02) -> str:
+def inspect(model_dir: str, **options) -> dict:
+    """The settings and weight storage of a model folder, read without a GPU
+    (Config::parse, causal_lm.rs:41-77). Options: config_at, prefix."""
+    lib = library()
+    ptr = lib.trit_lm_inspect(model_dir.encode(), json.dumps(options).encode())
+    if not ptr:
+        raise _error()
+    try:
+        return json.loads(ctypes.string_at(ptr).decode())
+    finally:
+        lib.trit_free_text(ptr)
+
+
+def synthesize(model_dir: str, config: dict, fmt: str = "q8_0", seed: int = 0, std: float = 0.02,
+               prefix: str = "", config_at: str = "") -> str:
     """Writes a seeded synthetic model folder (include/trit_synth.h)."""
     os.makedirs(model_dir, exist_ok=True)
-    spec = json.dumps({"config": config, "format": fmt, "seed": seed, "std": std}).encode()
+    spec = {"config": config, "format": fmt, "seed": seed, "std": std}
+    if prefix:
+        spec["prefix"] = prefix
+    if config_at:
+        spec["config_at"] = config_at
+    spec = json.dumps(spec).encode()
     if library().trit_synth_model(str(model_dir).encode(), spec) != 0:
         raise _error()
     return model_dir

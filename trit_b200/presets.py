@@ -25,6 +25,9 @@ MINI_QWEN3 = dict(QWEN3_06B, hidden_size=256, intermediate_size=768, num_hidden_
 MINI_MISTRAL = dict(MINISTRAL_3B, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
                     num_attention_heads=4, num_key_value_heads=1, vocab_size=2048)
 
+MINI_GRANITE = dict(MINI_QWEN3, model_type="granite", embedding_multiplier=2.0, attention_multiplier=0.0078125,
+                    residual_multiplier=0.8, logits_scaling=4.0)
+
 CONFIGS = {
     # name: (config, format, seed)
     "c1_qwen3_0.6b_q8_0": (QWEN3_06B, "q8_0", 20261201),
@@ -35,7 +38,18 @@ CONFIGS = {
     "mini_qwen3_int8": (MINI_QWEN3, "int8", 8),
     "mini_qwen3_ternary": (MINI_QWEN3, "ternary", 9),
     "mini_mistral_q8_0": (MINI_MISTRAL, "q8_0", 10),
+    "mini_granite_q8_0": (MINI_GRANITE, "q8_0", 11),
 }
+
+
+# The small models draw their weights wider than N(0, 0.02): with tied
+# embeddings a narrow draw leaves the last token's embedding dominant and
+# the greedy loop repeats one token, which tests the loop poorly.
+MINI_STD = 0.15
+
+
+def weight_std(name: str) -> float:
+    return MINI_STD if name.startswith("mini_") else 0.02
 
 
 def cache_dir() -> str:
@@ -47,11 +61,15 @@ def model_path(name: str) -> str:
     from .lm import synthesize
 
     config, fmt, seed = CONFIGS[name]
-    spec = json.dumps({"c": config, "f": fmt, "s": seed}, sort_keys=True).encode()
+    std = weight_std(name)
+    spec = {"c": config, "f": fmt, "s": seed}
+    if std != 0.02:
+        spec["std"] = std
+    spec = json.dumps(spec, sort_keys=True).encode()
     folder = os.path.join(cache_dir(), f"{name}-{hashlib.sha1(spec).hexdigest()[:10]}")
     done = os.path.join(folder, ".complete")
     if not os.path.exists(done):
         os.makedirs(folder, exist_ok=True)
-        synthesize(folder, config, fmt, seed)
+        synthesize(folder, config, fmt, seed, std=std)
         open(done, "w").close()
     return folder
