@@ -1,21 +1,33 @@
-"""Decode throughput of the B200 decoder on the headline configuration.
+"""Decode throughput of the B200 decoder (Trit's CausalLm token loop).
 
 Default workload (the configuration the north
-star's target is quoted on): a Qwen3-0.6B-shaped decoder with seeded
+star's target is quoted on): C1, a Qwen3-0.6B-shaped decoder with seeded
 synthetic Q8_0 weights, batch 1 per GPU, a 64-token prompt of uniform
 random ids, 128 greedy tokens. One step = one generation.
+
+  --config c1   (default) batch 1, Q8_0 0.6B, persistent decode kernel
+  --config c2   16 streams per GPU, per-row int8 0.6B, 256-token prompts,
+                256 greedy steps (trit_lm_generate_batch)
+  --config c3   batch 1, ternary 1.7B, 375 audio-prefix rows + 16 ids,
+                200 greedy steps (trit_lm_answer)
+  --config c5   64 streams per GPU, Q8_0 Ministral-3B shape, 1024-token
+                prompts, 256 greedy steps (trit_lm_generate_batch)
+  --config c4   op sweep: Q8_0 products of five shapes at 1, 4, 16, 64 rows
+
 With --gpus N (torchrun, one process per GPU) every rank runs its own
-independent stream: data parallel over streams, no collective in the data
-path (weak scaling). Timing: a barrier + device synchronize on both sides
-of the K timed steps, the maximum over ranks.
+streams: data parallel over independent streams, no collective on the
+data path (weak scaling). Timing: a barrier + device synchronize on both
+sides of the K timed steps, the maximum over ranks.
 
   value : decode tokens/s of the whole job, from CUDA events around the
-          greedy-step phase inside the library (inputs resident in HBM).
-  e2e   : tokens/s through the public C ABI call trit_lm_generate with the
-          prompt ids in host memory and the tokens copied back, prefill
-          included, wall clock between barriers.
-The weights (633 MB) are larger than the 126 MB L2, so no L2 flush is done
-between steps.
+          greedy steps inside the library (weights and prompts resident).
+  e2e   : tokens/s through the public C ABI call (trit_lm_generate /
+          _generate_batch / _answer) with the prompt in host memory and
+          the tokens copied back, prefill included, wall clock between
+          barriers.
+The weights (0.6-3.8 GB) are larger than the 126 MB L2, so no L2 flush is
+done between steps; the op sweep rotates copies of each matrix so that
+every repetition reads it from HBM.
 
 --impl reference runs the CPU restatement of the reference decoder (the
 oracle, all host threads) on the same workload, rank 0 only.
@@ -36,11 +48,28 @@ sys.path.insert(0, ROOT)
 
 import numpy as np  # noqa: E402
 
-PROMPT = 64
-MAX_NEW = 128
-CONFIG_NAME = "c1_qwen3_0.6b_q8_0"
+from trit_b200 import dp  # noqa: E402
+
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
+SEED = 20261201
+
+WORKLOADS = {
+    "c1": {"model": "c1_qwen3_0.6b_q8_0", "streams": 1, "prompt": 64, "new": 128, "kind": "generate",
+           "metric": "decode tok/s (batch 1 per GPU)",
+           "workload": "C1: Qwen3-0.6B-shaped Q8_0, batch 1 per GPU, 64-token prompt, 128 greedy tokens"},
+    "c2": {"model": "c2_qwen3_0.6b_int8", "streams": 16, "prompt": 256, "new": 256, "kind": "batch",
+           "metric": "decode tok/s (16 streams per GPU)",
+           "workload": "C2: Qwen3-0.6B-shaped per-row int8, 16 streams per GPU, 256-token prompts, 256 greedy steps"},
+    "c3": {"model": "c3_qwen3_1.7b_ternary", "streams": 1, "rows": 375, "prompt": 16, "new": 200, "kind": "answer",
+           "metric": "decode tok/s (batch 1, 391-row prefix)",
+           "workload": "C3: Qwen3-1.7B-shaped ternary, batch 1, 375 audio rows + 16 ids, 200 greedy steps"},
+    "c5": {"model": "c5_ministral_3b_q8_0", "streams": 64, "prompt": 1024, "new": 256, "kind": "batch",
+           "metric": "decode tok/s (64 streams per GPU)",
+           "workload": "C5: Ministral-3B-shaped Q8_0, 64 streams per GPU, 1024-token prompts, 256 greedy steps"},
+}
+SWEEP_SHAPES = [(1024, 3072), (3072, 1024), (2048, 6144), (6144, 2048), (151936, 1024)]
+SWEEP_ROWS = [1, 4, 16, 64]
 
 
 def peaks():
@@ -52,28 +81,17 @@ def peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def algorithmic_bytes(config: dict, fmt: str, positions: list[int], kv_bytes: int) -> dict:
-    """Bytes one greedy step must move: every weight once, the KV cache read
-    up to the step's position, one KV row written."""
-    d, ffn, L = config["hidden_size"], config["intermediate_size"], config["num_hidden_layers"]
-    hd, H, KV, V = config["head_dim"], config["num_attention_heads"], config["num_key_value_heads"], config["vocab_size"]
-    qd, kvd = H * hd, KV * hd
-    mats = [(qd + 2 * kvd, d), (d, qd), (2 * ffn, d), (d, ffn)]
-
-    def mat_bytes(n, k):
-        if fmt == "q8_0":
-            return n * k * 34 // 32
-        if fmt == "int8":
-            return n * k + 4 * n
-        return n * k // 4 + 4 * n * (k // 128)
-
-    layers = L * sum(mat_bytes(n, k) for n, k in mats) + L * 4 * (2 * d + 2 * hd)
-    table = V * d * 34 // 32 if fmt != "int8" else V * d + V * (d // 32) * 4
-    if not config.get("tie_word_embeddings", False):
-        table = table  # the output projection is read; the embedding row is negligible
+def algorithmic_bytes(info: dict, streams: int, positions: list[int], kv_bytes: int) -> dict:
+    """Bytes one greedy step must move: every weight once (products, norms,
+    the output table), each stream's KV cache up to its position, and one
+    new KV row per stream. `positions` are the positions the steps feed."""
+    d, L, hd = info["hidden_size"], info["num_hidden_layers"], info["head_dim"]
+    kvd = info["num_key_value_heads"] * hd
+    norms = L * 4 * (2 * d + (2 * hd if info["qk_norm"] else 0)) + 4 * d
+    weights = info["product_bytes"] + info["output_table_bytes"] + norms
     kv_row = L * 2 * kvd * kv_bytes
-    kv = sum(kv_row * (p + 1) for p in positions) / max(1, len(positions)) + kv_row
-    return {"weights": layers + table, "kv": kv, "total": layers + table + kv}
+    kv = streams * (sum(kv_row * (p + 1) for p in positions) / max(1, len(positions)) + kv_row)
+    return {"weights": weights, "kv": kv, "total": weights + kv}
 
 
 class Clocks:
@@ -129,94 +147,295 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def dist_setup(n_gpus: int):
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import datetime
-
-        import torch
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
-    return rank, world, local
+def audio_rows(width: int, count: int, stream: int) -> np.ndarray:
+    """The seeded N(0, 1) prefix rows of C3 (audio frames in the reference)."""
+    return np.random.default_rng([SEED, 3, stream]).normal(0, 1, (count, width)).astype(np.float32)
 
 
-def barrier_sync(world: int):
-    import torch
-
-    torch.cuda.synchronize()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-    torch.cuda.synchronize()
-
-
-def max_over_ranks(value: float, world: int) -> float:
-    if world == 1:
-        return value
-    import torch
-    import torch.distributed as dist
-
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-
-def prompts(vocab: int, count: int, seed: int) -> list[list[int]]:
-    rng = np.random.default_rng(seed)
-    return [rng.integers(0, vocab, size=PROMPT).tolist() for _ in range(count)]
-
-
-def cpu_baseline(model_dir: str, threads: int | None, decode_tokens: int, reps: int) -> dict:
-    """The oracle (a C++ port of the reference CPU decoder) on the host cores."""
+# ------------------------------------------------------------ CPU legs ----
+def cpu_sample(w: dict, model_dir: str, tokens: int, reps: int, threads: int | None = None) -> dict:
+    """The oracle (a C++ restatement of the reference CPU decoder) on the
+    host cores: the per-token time of `reps` generations of `tokens` greedy
+    tokens after the workload's prompt. Streams are decoded one after
+    another, as calls on one reference engine take turns."""
     from oracle import oracle as O
 
     if threads:
         O.lib().oracle_set_threads(threads)
-    oracle = O.Oracle(model_dir)
-    per_token = []
-    prefill = []
-    for r in range(reps):
-        p = prompts(oracle.vocab, 1, 1000 + r)[0]
-        res = oracle.generate(p, decode_tokens + 1, timing=True)
-        per_token.extend(res["seconds"][1:].tolist())
-        prefill.append(res["prefill_seconds"])
-    med = statistics.median(per_token)
-    return {"value": 1.0 / med, "unit": "tok/s", "cores": int(O.lib().oracle_threads()), "kind": "port",
+    orc = O.Oracle(model_dir, kv_f16=False)
+    if w["kind"] == "answer":
+        # answer() reports no per-token times: the difference of a call with
+        # `tokens` + 1 tokens and one with 1 token, per token.
+        def call(r, n):
+            tail = dp.stream_prompt(SEED, 20_000 + r, w["prompt"], orc.vocab)
+            t0 = time.perf_counter()
+            orc.answer([], audio_rows(orc.width, w["rows"], 20_000 + r), tail, n)
+            return time.perf_counter() - t0
+
+        short = [call(r, 1) for r in range(reps)]
+        full = [call(r, tokens + 1) for r in range(reps)]
+        per = (sum(full) - sum(short)) / (reps * tokens)
+        pre = statistics.median(short)
+    else:
+        per_token, prefill = [], []
+        for r in range(reps):
+            p = dp.stream_prompt(SEED, 10_000 + r, w["prompt"], orc.vocab)
+            res = orc.generate(p, tokens + 1, timing=True)
+            per_token.extend(res["seconds"][1:].tolist())
+            prefill.append(res["prefill_seconds"])
+        per = statistics.median(per_token)
+        pre = statistics.median(prefill)
+    orc.close()
+    return {"value": 1.0 / per, "unit": "tok/s", "cores": int(O.lib().oracle_threads()), "kind": "port",
             "isa": O.lib().oracle_isa().decode(),
-            "sample": f"{reps} x ({PROMPT}-token prompt + {decode_tokens} greedy tokens), median per-token time; "
-                      f"prefill median {statistics.median(prefill) * 1e3:.0f} ms"}
+            "sample": f"{reps} x (the workload's prompt + {tokens} greedy tokens), one stream at a time, "
+                      f"per-token time; prefill {pre * 1e3:.0f} ms"}
 
 
-def run_reference(args, rank: int, world: int) -> None:
-    if rank != 0:
+def cpu_sweep(reps: int) -> dict:
+    """C4 on the host cores: the oracle's W8A8 product (the reference's
+    VNNI tile) for each shape and row count, `reps` repetitions."""
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(SEED + 4)
+    hbm_bytes, seconds, cases = 0.0, 0.0, []
+    for (n, k) in SWEEP_SHAPES:
+        codes = rng.integers(-127, 128, (n, k)).astype(np.int8)
+        scales = rng.uniform(1e-4, 1e-3, (n, k // 32)).astype(np.float32)
+        layer = O.IntLayer(codes, scales, 32, 32, True)
+        for m in SWEEP_ROWS:
+            x = rng.normal(0, 1, (m, k)).astype(np.float32)
+            layer.forward(x)
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                layer.forward(x)
+            s = (time.perf_counter() - t0) / reps
+            b = n * k * 34 / 32 + 4 * m * (k + n)
+            cases.append({"n": n, "k": k, "m": m, "us": s * 1e6, "gbs": b / s / 1e9})
+            hbm_bytes += b
+            seconds += s
+        del layer
+    return {"value": hbm_bytes / seconds / 1e9, "unit": "GB/s", "cores": int(O.lib().oracle_threads()),
+            "kind": "port", "isa": O.lib().oracle_isa().decode(),
+            "sample": f"{reps} repetitions of each of {len(cases)} cases (seeded random codes)", "cases": cases}
+
+
+def run_reference(args, r: dp.Rank) -> None:
+    if r.rank != 0:
         return
     from trit_b200 import presets
 
-    model_dir = presets.model_path(CONFIG_NAME)
-    config, fmt, _ = presets.CONFIGS[CONFIG_NAME]
-    warm = cpu_baseline(model_dir, None, 2, max(1, min(args.warmup, 1)))
-    del warm
-    t0 = time.perf_counter()
-    base = cpu_baseline(model_dir, None, 8, max(1, args.steps))
-    wall = time.perf_counter() - t0
+    if args.config == "c4":
+        t0 = time.perf_counter()
+        base = cpu_sweep(max(1, args.steps))
+        wall = time.perf_counter() - t0
+        w = {"metric": "GEMV HBM GB/s (Q8_0 op sweep)", "model": None,
+             "workload": "C4: Q8_0 products of five shapes at 1, 4, 16, 64 rows"}
+    else:
+        w = WORKLOADS[args.config]
+        model_dir = presets.model_path(w["model"])
+        cpu_sample(w, model_dir, 2, 1)  # warm-up: page in the weights
+        t0 = time.perf_counter()
+        base = cpu_sample(w, model_dir, 8, max(1, args.steps))
+        wall = time.perf_counter() - t0
     line = {
-        "impl": "reference", "metric": "decode tok/s (batch 1 per GPU)", "value": base["value"], "unit": "tok/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall * 1e3 / max(1, args.steps),
+        "impl": "reference", "metric": w["metric"], "value": base["value"], "unit": base["unit"],
+        "n_gpus": r.world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall * 1e3 / max(1, args.steps),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> i32, f32",
-        "data": "synthetic (seeded weights N(0,0.02) -> Q8_0, uniform random prompt ids)",
-        "config": {"workload": "C1: Qwen3-0.6B-shaped Q8_0, batch 1, 64-token prompt, greedy decode",
-                   "model": CONFIG_NAME, "global_batch": world, "seq_len": PROMPT + MAX_NEW,
-                   "parallelism": "cpu (reference arm: the oracle port, all host threads)"},
+        "data": "synthetic (seeded N(0,0.02) weights, uniform random prompt ids)",
+        "config": {"workload": w["workload"], "model": w["model"],
+                   "parallelism": "cpu (reference arm: the oracle port of the reference decoder, all host threads)"},
         "cpu_baseline": base,
-        "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": base["value"], "unit": base["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------ GPU legs ----
+def run_decode(args, r: dp.Rank) -> None:
+    from trit_b200 import CausalLm, lm as lmmod, presets
+
+    w = WORKLOADS[args.config]
+    if r.rank == 0:
+        model_dir = presets.model_path(w["model"])
+    dp.barrier(r)
+    model_dir = presets.model_path(w["model"])
+    info = lmmod.inspect(model_dir)
+    S = w["streams"]
+    prompt_len = w["prompt"] + w.get("rows", 0)
+    opts = {"device": r.local, "kv": args.kv, "max_context": prompt_len + w["new"] + 8}
+    if w["kind"] == "batch":
+        opts.update(max_streams=S, prefill_rows=max(512, S))
+    else:
+        opts.update(decode=args.decode)
+    lm = CausalLm.load(model_dir, **opts)
+    vocab, width = lm.vocab(), lm.width()
+
+    def inputs(step: int):
+        base = (r.rank * 1_000_003 + step) * S
+        prompts = [dp.stream_prompt(SEED, base + s, w["prompt"], vocab) for s in range(S)]
+        rows = audio_rows(width, w["rows"], base) if w["kind"] == "answer" else None
+        return prompts, rows
+
+    def one(step: int):
+        prompts, rows = inputs(step)
+        if w["kind"] == "generate":
+            return len(lm.generate(prompts[0], max_new=w["new"]))
+        if w["kind"] == "answer":
+            return len(lm.answer([], rows, prompts[0], max_new=w["new"]))
+        return sum(len(t) for t in lm.generate_batch(prompts, max_new=w["new"]))
+
+    for i in range(args.warmup):
+        one(i)
+    decode_ms = prefill_ms = 0.0
+    decode_steps = made = launches = 0
+    with Clocks(r.local) as clocks:
+        dp.barrier(r)
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            made += one(args.warmup + i)
+            t = lm.last_timing()
+            decode_ms += t["decode_ms"]
+            prefill_ms += t["prefill_ms"]
+            decode_steps += t["decode_steps"]
+            launches += t["launches"]
+        dp.barrier(r)
+        wall = time.perf_counter() - t0
+    wall_max = dp.reduce(wall, r, "max")
+    decode_max = dp.reduce(decode_ms, r, "max")
+    steps_all = dp.reduce(float(decode_steps), r, "sum")
+    made_all = dp.reduce(float(made), r, "sum")
+    value = steps_all / (decode_max / 1e3)
+    e2e = made_all / wall_max
+    positions = [prompt_len + i for i in range(w["new"] - 1)]
+    alg = algorithmic_bytes(info, S, positions, 2 if args.kv == "f16" else 4)
+    hbm, peak_kind = peaks()
+    greedy_steps = decode_steps / S  # forwards of the whole batch
+    per_step_s = decode_ms / 1e3 / max(1.0, greedy_steps)
+    achieved = alg["total"] / per_step_s / 1e9
+    kernel = {"generate": "decode step (persistent kernel)" if args.decode == "persistent" else "layered step",
+              "answer": "decode step (persistent kernel)" if args.decode == "persistent" else "layered step",
+              "batch": "batched decode step (layered kernels, one CUDA graph)"}[w["kind"]]
+    h2d = S * w["prompt"] * 4 + w.get("rows", 0) * width * 4
+    line = {
+        "metric": w["metric"], "value": value, "unit": "tok/s", "n_gpus": r.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall_max * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> i32, f32",
+        "data": "synthetic (seeded N(0,0.02) weights, uniform random prompt ids"
+                + (", N(0,1) prefix rows)" if w["kind"] == "answer" else ")"),
+        "config": {"workload": w["workload"], "model": w["model"], "global_batch": S * r.world,
+                   "seq_len": prompt_len + w["new"], "parallelism": f"dp{r.world} (independent streams, no collective)",
+                   "decode": args.decode if w["kind"] != "batch" else "batched", "kv_cache": args.kv,
+                   "l2": f"weights {alg['weights'] / 1e6:.0f} MB > 126 MB L2; no flush"},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": S * w["new"] * 4},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": peak_kind, "traffic": TRAFFIC.get(args.config),
+                     "algorithmic_bytes_per_step": alg["total"], "kv_bytes_per_step": alg["kv"], "kernel": kernel},
+        "prefill_ms_per_step": prefill_ms / args.steps,
+        "clocks": clocks.summary(),
+    }
+    if r.rank == 0 and r.world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_sample(w, model_dir, 8, 1)
+    if r.rank == 0:
+        print(json.dumps(line), flush=True)
+    lm.close()
+
+
+# Per-step DRAM bytes (read + write) of the dominant kernel from ncu
+# captures, where one was taken for the workload (see profiles/).
+TRAFFIC: dict = {"c1": (82.304342e9 + 46.220032e6) / 127}  # profiles/k_decode_c1.md
+
+
+def q8_0_blocks(values: np.ndarray) -> np.ndarray:
+    """ggml Q8_0 bytes of a row-major f32 matrix (Blocks::quantize,
+    src/cpu/gemm.rs:53-76): per 32 values d = max|x|/127, codes
+    round-half-away(x * (1/d)), d stored as f16 before the codes."""
+    v = values.astype(np.float32).reshape(-1, 32)
+    d = (np.abs(v).max(axis=1) / np.float32(127.0)).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        inv = np.where(d != 0, np.float32(1.0) / d, np.float32(0.0)).astype(np.float32)
+    prod = (v * inv[:, None]).astype(np.float32)
+    codes = np.clip(np.sign(prod) * np.floor(np.abs(prod) + np.float32(0.5)), -128, 127).astype(np.int8)
+    out = np.empty((v.shape[0], 34), np.uint8)
+    out[:, :2] = d.astype("<f2").view(np.uint8).reshape(-1, 2)
+    out[:, 2:] = codes.view(np.uint8)
+    return out.reshape(-1)
+
+
+def run_sweep(args, r: dp.Rank) -> None:
+    """C4: each Q8_0 product (W8A8, Int8::from_q8_0) at 1, 4, 16, 64 rows,
+    `reps` repetitions through trit_dense_forward_device; copies of the
+    matrix rotate so every repetition reads it from HBM."""
+    import torch
+
+    from trit_b200 import Dense
+
+    torch.cuda.set_device(r.local)
+    hbm, peak_kind = peaks()
+    rng = np.random.default_rng(SEED + 4)
+    cases, total_bytes, total_s = [], 0.0, 0.0
+    launches = 0
+    with Clocks(r.local) as clocks:
+        for (n, k) in SWEEP_SHAPES:
+            blocks = q8_0_blocks(rng.normal(0, 0.02, (n, k)).astype(np.float32))
+            wbytes = n * k * 34 // 32
+            copies = max(1, -(-256 * 2 ** 20 // wbytes))
+            layers = [Dense.q8_0(blocks, n, k, device=r.local) for _ in range(copies)]
+            for m in SWEEP_ROWS:
+                x = torch.from_numpy(rng.normal(0, 1, (m, k)).astype(np.float32)).cuda()
+                y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+                stream = torch.cuda.current_stream().cuda_stream
+                for i in range(3):
+                    layers[i % copies].forward_device(x.data_ptr(), m, y.data_ptr(), stream)
+                reps = args.reps
+                dp.barrier(r)
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+                for i in range(reps):
+                    layers[i % copies].forward_device(x.data_ptr(), m, y.data_ptr(), stream)
+                end.record()
+                torch.cuda.synchronize()
+                s = start.elapsed_time(end) / 1e3 / reps
+                s = dp.reduce(s, r, "max")
+                b = wbytes + 4 * m * (k + n)
+                cases.append({"n": n, "k": k, "m": m, "us": s * 1e6, "gbs": b / s / 1e9, "frac": b / s / 1e9 / hbm,
+                              "tops": 2 * m * n * k / s / 1e12})
+                total_bytes += b * reps
+                total_s += s * reps
+                launches += reps * 2 * r.world
+            del layers
+    value = total_bytes / total_s / 1e9 * r.world
+    best = max(cases, key=lambda c: c["gbs"])
+    # e2e: the largest product at 1 row through host buffers (trit_dense_forward).
+    n, k = SWEEP_SHAPES[-1]
+    layer = Dense.q8_0(q8_0_blocks(rng.normal(0, 0.02, (n, k)).astype(np.float32)), n, k, device=r.local)
+    xh = rng.normal(0, 1, (1, k)).astype(np.float32)
+    layer.forward(xh)
+    t0 = time.perf_counter()
+    for _ in range(20):
+        layer.forward(xh)
+    e2e_s = (time.perf_counter() - t0) / 20
+    layer.close()
+    line = {
+        "metric": "GEMV HBM GB/s (Q8_0 op sweep)", "value": value, "unit": "GB/s", "n_gpus": r.world,
+        "steps": args.reps, "warmup": 3, "ms_per_step": total_s * 1e3 / max(1, len(cases) * args.reps),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> i32, f32",
+        "data": "synthetic (seeded N(0,0.02) weights -> Q8_0, x ~ N(0,1))",
+        "config": {"workload": "C4: Q8_0 products [1024x3072], [3072x1024], [2048x6144], [6144x2048], "
+                               "[151936x1024] (n x k) at 1, 4, 16, 64 rows",
+                   "parallelism": f"dp{r.world}", "l2": "matrix copies rotate past 256 MB per case"},
+        "e2e": {"value": (n * k * 34 / 32 + 4 * (k + n)) / e2e_s / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": 4 * k, "d2h_bytes_per_step": 4 * n},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "achieved": best["gbs"], "peak": hbm, "unit": "GB/s",
+                     "frac": best["gbs"] / hbm, "peak_kind": peak_kind, "traffic": None,
+                     "kernel": f"k_gemv, best case n={best['n']} k={best['k']} m={best['m']}"},
+        "cases": cases,
+        "clocks": clocks.summary(),
+    }
+    if r.rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 def main() -> None:
@@ -225,79 +444,25 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c1", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--decode", default=os.environ.get("TRIT_DECODE", "persistent"))
     ap.add_argument("--kv", default="f16")
+    ap.add_argument("--reps", type=int, default=1000, help="repetitions per case of the op sweep")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    rank, world, local = dist_setup(args.gpus)
+    backend = "nccl"
     if args.impl == "reference":
-        run_reference(args, rank, world)
-        return
-    from trit_b200 import CausalLm, presets
-
-    config, fmt, _ = presets.CONFIGS[CONFIG_NAME]
-    if rank == 0 or world == 1:
-        model_dir = presets.model_path(CONFIG_NAME)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-        model_dir = presets.model_path(CONFIG_NAME)
-    lm = CausalLm.load(model_dir, device=local, kv=args.kv, decode=args.decode, max_context=PROMPT + MAX_NEW + 8)
-    vocab = lm.vocab()
-    ps = prompts(vocab, args.warmup + args.steps, 77 + rank)
-    for i in range(args.warmup):
-        lm.generate(ps[i], max_new=MAX_NEW)
-    decode_ms, decode_steps, made, launches, prefill_ms = 0.0, 0, 0, 0, 0.0
-    with Clocks(local) as clocks:
-        barrier_sync(world)
-        t0 = time.perf_counter()
-        for i in range(args.steps):
-            toks = lm.generate(ps[args.warmup + i], max_new=MAX_NEW)
-            t = lm.last_timing()
-            decode_ms += t["decode_ms"]
-            prefill_ms += t["prefill_ms"]
-            decode_steps += t["decode_steps"]
-            launches += t["launches"]
-            made += len(toks)
-        barrier_sync(world)
-        wall = time.perf_counter() - t0
-    wall_max = max_over_ranks(wall, world)
-    decode_max = max_over_ranks(decode_ms, world)
-    value = world * decode_steps / (decode_max / 1e3)
-    e2e = world * made / wall_max
-    positions = [PROMPT + i for i in range(MAX_NEW - 1)]
-    alg = algorithmic_bytes(config, fmt, positions, 2 if args.kv == "f16" else 4)
-    hbm, peak_kind = peaks()
-    per_step_s = decode_ms / 1e3 / max(1, decode_steps)
-    achieved = alg["total"] / per_step_s / 1e9
-    line = {
-        "metric": "decode tok/s (batch 1 per GPU)", "value": value, "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall_max * 1e3 / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> i32, f32",
-        "data": "synthetic (seeded weights N(0,0.02) -> Q8_0, uniform random prompt ids)",
-        "config": {"workload": "C1: Qwen3-0.6B-shaped Q8_0, batch 1 per GPU, 64-token prompt, 128 greedy tokens",
-                   "model": CONFIG_NAME, "global_batch": world, "seq_len": PROMPT + MAX_NEW,
-                   "parallelism": f"dp{world} (independent streams, no collective)", "decode": args.decode,
-                   "kv_cache": args.kv, "l2": "weights 633 MB > 126 MB L2; no flush"},
-        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4, "d2h_bytes_per_step": MAX_NEW * 4},
-        "gpu_launches": launches,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": peak_kind, "traffic": None,
-                     "algorithmic_bytes_per_token": alg["total"],
-                     "kernel": "decode step (persistent kernel)" if args.decode == "persistent" else "layered step"},
-        "prefill_ms_per_step": prefill_ms / args.steps,
-        "clocks": clocks.summary(),
-    }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(model_dir, None, 8, 1)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    lm.close()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
+        backend = "gloo"
+    r = dp.init(backend, timeout_s=900)
+    try:
+        if args.impl == "reference":
+            run_reference(args, r)
+        elif args.config == "c4":
+            run_sweep(args, r)
+        else:
+            run_decode(args, r)
+    finally:
+        dp.finish(r)
 
 
 if __name__ == "__main__":

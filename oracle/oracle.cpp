@@ -451,7 +451,7 @@ void table_row(const Table& t, size_t index, float* out) {
 }
 
 // ----------------------------------------------------------- layers ----
-// RmsNorm::apply_in_place (src/cpu/layers.rs:135-144): a sequential f32 sum
+// RmsNorm::apply_in_place (src/layers.rs:135-144): a sequential f32 sum
 // of squares, inv = 1 / sqrt(sum / d + eps), v *= inv * w.
 void rms_in_place(float* row, const float* w, size_t d, float eps) {
   float sum = -0.0f;
@@ -466,7 +466,7 @@ void rms_in_place(float* row, const float* w, size_t d, float eps) {
   }
 }
 
-// Rotary::halves + apply (src/cpu/layers.rs:276-335): inv_freq = base^(-2i/dims)
+// Rotary::halves + apply (src/layers.rs:276-335): inv_freq = base^(-2i/dims)
 // in f32, (position * f).sin_cos() in f32, pairs (i, i + dims/2).
 struct Rotary {
   size_t dims = 0;
@@ -500,7 +500,7 @@ struct Rotary {
   }
 };
 
-// attention + HeadMajor + attention_with (src/cpu/layers.rs:343-504) and
+// attention + HeadMajor + attention_with (src/layers.rs:343-504) and
 // softmax_rows (:571-587): q scaled by 1/sqrt(hd); scores as sequential fma
 // chains over the head dimension; keys beyond the causal limit set to -inf
 // before the maximum; exp of (score - max) summed in key order; each
@@ -541,7 +541,7 @@ void attention(const float* q, size_t qs, const float* k, const float* v, size_t
   }
 }
 
-// argmax (src/cpu/layers.rs:603-612): the first strict maximum wins.
+// argmax (src/layers.rs:603-612): the first strict maximum wins.
 size_t argmax(const float* values, size_t n) {
   size_t best = 0;
   for (size_t i = 0; i < n; ++i)

@@ -1,6 +1,6 @@
 """A small GGUF v3 reader for the CPU tests: tensor names, ggml types,
 dimensions and raw bytes, read independently of the library's C++ reader
-(the format the reference parses in src/gguf/mod.rs:147-260)."""
+(the format the reference parses in src/models/gguf/mod.rs)."""
 from __future__ import annotations
 
 import struct

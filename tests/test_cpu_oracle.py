@@ -8,7 +8,7 @@ test; these tests pin each of its parts to the reference's definitions:
                         acc = fma(f32(dot), ws * xs, acc), groups in order)
   token table product   Q8::matmul, src/cpu/gemm.rs:166-187 (f32 math)
   Cephes exp / SiLU     src/cpu/activation.rs:8-38,54-56
-  RmsNorm               src/models/parts/layers.rs:122-153 (sequential sum)
+  RmsNorm               src/layers.rs:122-153 (sequential sum)
   Rotary::halves        layers.rs:276-335
   attention             layers.rs:343-504, softmax_rows :571-587
 The VNNI tile and the scalar path of the oracle must agree bit for bit, as

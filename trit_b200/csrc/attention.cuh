@@ -1,5 +1,5 @@
 // GQA softmax attention of one query position over its stream's keys, in
-// the reference's arithmetic order (src/cpu/layers.rs:343-504 and
+// the reference's arithmetic order (src/layers.rs:343-504 and
 // softmax_rows :571-587, with the nn tiles of src/cpu/fgemm.rs:700-860):
 //   score_j  = fma chain over the head dimension, e = 0..127, of q_e * k_je
 //              (q already times 1/sqrt(hd))

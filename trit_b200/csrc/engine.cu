@@ -248,6 +248,16 @@ void Lm::release() {
   for (void* b : bufs)
     if (b) cudaFree(b);
   if (host_rows_) cudaFreeHost(host_rows_);
+  if (batch_host_) cudaFreeHost(batch_host_);
+  void* batch[] = {batch_last_, batch_cur_, batch_step_, batch_tok_};
+  for (void* b : batch)
+    if (b) cudaFree(b);
+  if (batch_graph_) cudaGraphExecDestroy(batch_graph_);
+  batch_host_ = nullptr;
+  batch_last_ = nullptr;
+  batch_cur_ = batch_step_ = batch_tok_ = nullptr;
+  batch_graph_ = nullptr;
+  batch_ready_ = false;
   for (auto& e : ev_)
     if (e) cudaEventDestroy(e);
   if (stream_) cudaStreamDestroy(stream_);
@@ -727,12 +737,162 @@ std::unique_ptr<PrefixState> Lm::prefix(const int* ids, size_t n) {
   return p;
 }
 
-void Lm::generate_batch(size_t streams, const int* const* prompts, const size_t* lens, int max_new, const int* stop,
+// Independent greedy generations decoded side by side: CausalLm::generate
+// (causal_lm.rs:217-249) and greedy (:284-302) for every stream, each
+// stream in its own KV slot. The prompts of all streams share prefill
+// passes (every row carries its stream and position). Each greedy step runs
+// the rows of all streams through the layered kernels; the step is captured
+// once as a CUDA graph and replayed, since its kernels read the tokens and
+// positions from device buffers that a small kernel advances. Every stream
+// runs max_new steps; the host cuts each at its first stop token.
+void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens, int max_new, const int* stop,
                         size_t nstop, int* out, int64_t* counts) {
-  (void)streams; (void)prompts; (void)lens; (void)max_new; (void)stop; (void)nstop; (void)out; (void)counts;
-  throw Error("generate_batch is not built yet");
+  if (S == 0) return;
+  if (S > (size_t)opt_.max_streams)
+    throw Error(std::to_string(S) + " streams exceed max_streams " + std::to_string(opt_.max_streams));
+  size_t total = 0, longest = 0;
+  for (size_t s = 0; s < S; ++s) {
+    if (!prompts[s]) throw Error("prompt " + std::to_string(s) + " is NULL");
+    if (lens[s] == 0) throw Error("prompt " + std::to_string(s) + " is empty");
+    check_ids(prompts[s], lens[s]);
+    if (lens[s] + (size_t)std::max(max_new, 0) > (size_t)opt_.max_context)
+      throw Error("stream " + std::to_string(s) + ": prompt plus max_new exceeds max_context " +
+                  std::to_string(opt_.max_context));
+    total += lens[s];
+    longest = std::max(longest, lens[s]);
+  }
+  timing_ = Timing{};
+  for (size_t s = 0; s < S; ++s) counts[s] = 0;
+  if (max_new <= 0) return;
+  TRIT_CUDA(cudaSetDevice(opt_.device));
+  const int d = cfg_.d;
+  if (!batch_ready_) {
+    TRIT_CUDA(cudaMallocHost(&batch_host_, (size_t)3 * rows_cap_ * 4));
+    TRIT_CUDA(cudaMalloc(&batch_last_, (size_t)opt_.max_streams * d * 4));
+    TRIT_CUDA(cudaMalloc(&batch_cur_, (size_t)opt_.max_streams * 4));
+    TRIT_CUDA(cudaMalloc(&batch_step_, 4));
+    batch_ready_ = true;
+  }
+  if (batch_tok_cap_ < (size_t)max_new * S) {
+    if (batch_tok_) cudaFree(batch_tok_);
+    batch_tok_ = nullptr;
+    TRIT_CUDA(cudaMalloc(&batch_tok_, (size_t)max_new * S * 4));
+    batch_tok_cap_ = (size_t)max_new * S;
+    if (batch_graph_) cudaGraphExecDestroy(batch_graph_);  // it holds the old buffer's address
+    batch_graph_ = nullptr;
+  }
+  TRIT_CUDA(cudaEventRecord(ev_[0], stream_));
+  // Prefill: rows of every stream in order, rows_cap_ at a time.
+  int* hs = batch_host_;
+  int* hp = batch_host_ + rows_cap_;
+  int* hi = batch_host_ + 2 * rows_cap_;
+  size_t s = 0, p = 0;
+  while (s < S) {
+    TRIT_CUDA(cudaStreamSynchronize(stream_));  // the pinned staging is reused per chunk
+    int mc = 0, top = 0;
+    std::vector<std::pair<int, int>> ends;  // (chunk row, stream) of each stream's last prompt row
+    while (s < S && mc < rows_cap_) {
+      hs[mc] = (int)s;
+      hp[mc] = (int)p;
+      hi[mc] = prompts[s][p];
+      top = std::max(top, (int)p + 1);
+      if (++p == lens[s]) {
+        ends.emplace_back(mc, (int)s);
+        ++s;
+        p = 0;
+      }
+      ++mc;
+    }
+    TRIT_CUDA(cudaMemcpyAsync(row_stream_, hs, (size_t)mc * 4, cudaMemcpyHostToDevice, stream_));
+    TRIT_CUDA(cudaMemcpyAsync(row_pos_, hp, (size_t)mc * 4, cudaMemcpyHostToDevice, stream_));
+    TRIT_CUDA(cudaMemcpyAsync(ids_, hi, (size_t)mc * 4, cudaMemcpyHostToDevice, stream_));
+    TRIT_CUDA(launch_embed(embed_, ids_, mc, x_, 1.0f, stream_));
+    hidden(mc, top);
+    timing_.gpu_launches += 1;
+    for (auto& e : ends)
+      TRIT_CUDA(cudaMemcpyAsync(batch_last_ + (size_t)e.second * d, x_ + (size_t)e.first * d, (size_t)d * 4,
+                                cudaMemcpyDeviceToDevice, stream_));
+  }
+  // The first token of every stream, then the decode state: stream s sits
+  // in slot s at position lens[s] with its last token in batch_cur_.
+  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  for (size_t i = 0; i < S; ++i) {
+    hs[i] = (int)i;
+    hp[i] = (int)lens[i];
+  }
+  TRIT_CUDA(cudaMemcpyAsync(row_stream_, hs, S * 4, cudaMemcpyHostToDevice, stream_));
+  TRIT_CUDA(cudaMemcpyAsync(row_pos_, hp, S * 4, cudaMemcpyHostToDevice, stream_));
+  TRIT_CUDA(cudaMemsetAsync(batch_step_, 0, 4, stream_));
+  TRIT_CUDA(launch_final(batch_last_, d, (int)S, final_norm_, cfg_, head_, xn_, nullptr, best_val_, best_idx_,
+                         batch_cur_, stream_));
+  TRIT_CUDA(launch_batch_advance(batch_cur_, row_pos_, batch_step_, batch_tok_, (int)S, 0, stream_));
+  timing_.gpu_launches += 4;
+  TRIT_CUDA(cudaEventRecord(ev_[1], stream_));
+  const int steps = max_new - 1;
+  const int tmax = (int)(longest + max_new);
+  int per_step = 0;
+  auto step = [&]() {
+    int before = timing_.gpu_launches;
+    TRIT_CUDA(launch_embed(embed_, batch_cur_, (int)S, x_, 1.0f, stream_));
+    hidden((int)S, tmax);
+    TRIT_CUDA(launch_final(x_, d, (int)S, final_norm_, cfg_, head_, xn_, nullptr, best_val_, best_idx_, batch_cur_,
+                           stream_));
+    TRIT_CUDA(launch_batch_advance(batch_cur_, row_pos_, batch_step_, batch_tok_, (int)S, 1, stream_));
+    timing_.gpu_launches += 1 + 3 + 1;
+    per_step = timing_.gpu_launches - before;
+  };
+  if (steps > 0) {
+    step();  // eagerly once: sets up every kernel's attributes before a capture
+    if (steps > 1) {
+      if (!batch_graph_ || batch_graph_streams_ != (int)S || batch_graph_tmax_ < tmax) {
+        if (batch_graph_) cudaGraphExecDestroy(batch_graph_);
+        batch_graph_ = nullptr;
+        int counted = timing_.gpu_launches;
+        cudaGraph_t g = nullptr;
+        TRIT_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+        try {
+          step();
+        } catch (...) {
+          cudaStreamEndCapture(stream_, &g);
+          if (g) cudaGraphDestroy(g);
+          throw;
+        }
+        TRIT_CUDA(cudaStreamEndCapture(stream_, &g));
+        cudaError_t e = cudaGraphInstantiate(&batch_graph_, g, 0);
+        cudaGraphDestroy(g);
+        TRIT_CUDA(e);
+        timing_.gpu_launches = counted;  // captured, not run
+        batch_graph_streams_ = (int)S;
+        batch_graph_tmax_ = tmax;
+      }
+      for (int i = 1; i < steps; ++i) TRIT_CUDA(cudaGraphLaunch(batch_graph_, stream_));
+      timing_.gpu_launches += per_step * (steps - 1);
+    }
+  }
+  TRIT_CUDA(cudaEventRecord(ev_[2], stream_));
+  std::vector<int> toks((size_t)max_new * S);
+  TRIT_CUDA(cudaMemcpyAsync(toks.data(), batch_tok_, toks.size() * 4, cudaMemcpyDeviceToHost, stream_));
+  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  float ms = 0;
+  TRIT_CUDA(cudaEventElapsedTime(&ms, ev_[0], ev_[1]));
+  timing_.prefill_ms = ms;
+  TRIT_CUDA(cudaEventElapsedTime(&ms, ev_[1], ev_[2]));
+  timing_.decode_ms = ms;
+  timing_.decode_tokens = steps * (int)S;
+  (void)total;
+  for (size_t i = 0; i < S; ++i) {
+    int64_t n = 0;
+    for (int t = 0; t < max_new; ++t) {
+      int tok = toks[(size_t)t * S + i];
+      bool stopped = false;
+      for (size_t k = 0; k < nstop; ++k) stopped |= tok == stop[k];
+      if (stopped) break;
+      out[i * (size_t)max_new + t] = tok;
+      ++n;
+    }
+    counts[i] = n;
+  }
 }
-
 
 // ------------------------------------------------------------ DenseOp ----
 DenseOp::~DenseOp() {

@@ -141,6 +141,16 @@ class Lm {
   int decode_grid_ = 0;
   float* trace_ = nullptr;      // device [max_new][vocab] for traced persistent decode
   size_t trace_cap_ = 0;
+  // batched decode state
+  bool batch_ready_ = false;
+  int* batch_host_ = nullptr;   // pinned [3][rows_cap_]: streams, positions, ids of a prefill chunk
+  float* batch_last_ = nullptr; // device [max_streams][d]: each stream's last prompt row
+  int* batch_cur_ = nullptr;    // device [max_streams]: each stream's latest token
+  int* batch_step_ = nullptr;   // device step counter
+  int* batch_tok_ = nullptr;    // device [max_new][streams]
+  size_t batch_tok_cap_ = 0;
+  cudaGraphExec_t batch_graph_ = nullptr;  // one captured greedy step
+  int batch_graph_streams_ = 0, batch_graph_tmax_ = 0;
 };
 
 // A lone product layer for the op sweep (Dense::forward, gemm.rs:500-542).

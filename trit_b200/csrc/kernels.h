@@ -29,6 +29,28 @@ cudaError_t launch_table(const DTable& T, const float* xn, int nb, float mult, f
                          int* best_idx, cudaStream_t s);
 int table_blocks(int n);
 int table_max_streams();
+// After a greedy step of a batch: tokens[step][s] = cur[s] for every stream,
+// positions advance by one when `advance_pos`, and the step counter by one.
+cudaError_t launch_batch_advance(const int* cur, int* pos, int* step, int* tokens, int streams, int advance_pos,
+                                 cudaStream_t s);
+
+// Tensor-core W8A8 products (mma.cu) for prefill and batches. A TcMap is an
+// opaque TMA tensor map (CUtensorMap) of an int8 matrix [rows][k].
+struct alignas(64) TcMap {
+  unsigned long long opaque[16];
+};
+int tc_frames();  // frames (rows of x) per CTA: the frame map's row multiple
+cudaError_t make_tc_weight_map(TcMap* out, const DMat& W, const void* codes8);
+cudaError_t make_tc_frame_map(TcMap* out, const int8_t* xq, size_t rows_cap, size_t k);
+// y (m x ldy) from W times the quantized frames (xq via bmap, scales xs):
+// kEpOut stores, kEpResid adds (times resid_mult). *status is set when a
+// wait inside the kernel ran out.
+cudaError_t launch_gemm_tc(const TcMap& amap, const TcMap& bmap, const DMat& W, const float* xs, int m, int mode,
+                           float* y, int ldy, float resid_mult, int* status, cudaStream_t s);
+// h[m][units] = silu(g[.][u]) * g[.][units + u] for g = [m][2 units].
+cudaError_t launch_silu_pairs(const float* g, int m, int units, float* h, cudaStream_t s);
+// Ternary 2-bit words [n][k/16] -> int8 codes c - 1 in {-1, 0, 1}, [n][k].
+cudaError_t launch_expand_ternary(const DMat& W, int8_t* out, cudaStream_t s);
 
 // The persistent batch-1 decode (decode.cu).
 struct DecodeArgs {

@@ -33,10 +33,10 @@ __global__ void k_scale(float* x, size_t n, float mult) {
 }
 
 // ------------------------------------------------- norm + quantize ----
-// RmsNorm::apply (src/cpu/layers.rs:135-153) then Quantized::grouped
-// (src/cpu/kernels.rs:661-737) of the normed row. One block per row. The
-// sum of squares is a tree here (the reference sums in order): the only
-// step of this kernel that is not bit-exact.
+// RmsNorm::apply (src/layers.rs:135-153) then Quantized::grouped
+// (src/cpu/kernels.rs:661-737) of the normed row. One block per row; one
+// thread sums the squares in order, as the reference does, so the result
+// is the reference's to the bit.
 template <int G>
 __global__ void __launch_bounds__(256) k_norm_quant(const float* x, int d, const float* w, float eps, int half,
                                                     int8_t* xq, float* xs) {
@@ -389,6 +389,17 @@ __global__ void k_argmax(const float* val, const int* idx, int n, int* token) {
   if (threadIdx.x == 0) token[blockIdx.x] = (i == 0x7fffffff) ? 0 : i;
 }
 
+// The bookkeeping between two greedy steps of a batch (one block).
+__global__ void k_batch_advance(const int* cur, int* pos, int* step, int* tokens, int streams, int advance_pos) {
+  const int at = *step;
+  for (int s = threadIdx.x; s < streams; s += blockDim.x) {
+    tokens[(size_t)at * streams + s] = cur[s];
+    if (advance_pos) pos[s] += 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *step = at + 1;
+}
+
 // ------------------------------------------------------------ launch ----
 #define LAUNCH_CHECK()                                   \
   do {                                                   \
@@ -398,6 +409,13 @@ __global__ void k_argmax(const float* val, const int* idx, int n, int* token) {
 
 cudaError_t launch_embed(const DTable& T, const int* ids, int m, float* x, float mult, cudaStream_t s) {
   k_embed<<<m, 256, 0, s>>>(T, ids, m, x, mult);
+  LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
+cudaError_t launch_batch_advance(const int* cur, int* pos, int* step, int* tokens, int streams, int advance_pos,
+                                 cudaStream_t s) {
+  k_batch_advance<<<1, 256, 0, s>>>(cur, pos, step, tokens, streams, advance_pos);
   LAUNCH_CHECK();
   return cudaSuccess;
 }
