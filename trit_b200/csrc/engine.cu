@@ -42,6 +42,11 @@ Options Options::parse(const char* text, bool lenient) {
       if (v.kind != Json::String || (v.str != "persistent" && v.str != "layered"))
         throw Error("options: decode is \"persistent\" or \"layered\"");
       o.decode = v.str;
+    } else if (k == "tensor_cores") {
+      if (v.kind != Json::Bool) throw Error("options: tensor_cores is true or false");
+      o.tensor_cores = v.b;
+    } else if (k == "tc_rows") {
+      o.tc_rows = count(1, 1 << 20);
     } else if (k == "config_at" || k == "prefix") {
       if (v.kind != Json::String) throw Error("options: " + k + " must be a string");
       (k == "config_at" ? o.config_at : o.prefix) = v.str;
@@ -230,6 +235,7 @@ Lm::Lm(const std::string& dir, const Options& o) : opt_(o) {
   try {
     load(dir);
     alloc_buffers();
+    setup_tensor_cores();
   } catch (...) {
     release();
     throw;
@@ -249,13 +255,17 @@ void Lm::release() {
     if (b) cudaFree(b);
   if (host_rows_) cudaFreeHost(host_rows_);
   if (batch_host_) cudaFreeHost(batch_host_);
-  void* batch[] = {batch_last_, batch_cur_, batch_step_, batch_tok_};
+  void* batch[] = {batch_last_, batch_cur_, batch_step_, batch_tok_, tc_expanded_, gu_, tc_status_};
   for (void* b : batch)
     if (b) cudaFree(b);
   if (batch_graph_) cudaGraphExecDestroy(batch_graph_);
   batch_host_ = nullptr;
   batch_last_ = nullptr;
   batch_cur_ = batch_step_ = batch_tok_ = nullptr;
+  tc_expanded_ = nullptr;
+  gu_ = nullptr;
+  tc_status_ = nullptr;
+  tc_ready_ = false;
   batch_graph_ = nullptr;
   batch_ready_ = false;
   for (auto& e : ev_)
@@ -354,7 +364,8 @@ void Lm::alloc_buffers() {
   TRIT_CUDA(cudaMalloc(&qkv_, (size_t)rows_cap_ * (qd + 2 * kvd) * 4));
   TRIT_CUDA(cudaMalloc(&att_, (size_t)rows_cap_ * qd * 4));
   TRIT_CUDA(cudaMalloc(&h_, (size_t)rows_cap_ * cfg_.ffn * 4));
-  TRIT_CUDA(cudaMalloc(&xq_, (size_t)rows_cap_ * kmax));
+  // Whole 64-row tiles: the tensor-core products read frames in tiles.
+  TRIT_CUDA(cudaMalloc(&xq_, (size_t)((rows_cap_ + 63) / 64 * 64) * kmax));
   TRIT_CUDA(cudaMalloc(&xs_, (size_t)rows_cap_ * (kmax / 32) * 4));
   TRIT_CUDA(cudaMalloc(&row_stream_, (size_t)rows_cap_ * 4));
   TRIT_CUDA(cudaMalloc(&row_pos_, (size_t)rows_cap_ * 4));
@@ -379,22 +390,91 @@ void Lm::check_ids(const int* ids, size_t n) const {
 void Lm::hidden(int m, int max_tk) {
   const int d = cfg_.d, qd = cfg_.heads * cfg_.hd, kvd = cfg_.kv_heads * cfg_.hd;
   cudaStream_t s = stream_;
+  const bool tc = tc_ready_ && m >= opt_.tc_rows;
+  // One product: the tensor-core kernel for enough rows, else the GEMV.
+  auto product = [&](int l, int which, const DMat& W, const TcMap& xmap, int mode, float* y, int ldy, float mult) {
+    if (!tc) {
+      TRIT_CUDA(launch_gemv(W, xq_, xs_, m, mode, y, ldy, mult, s));
+      return;
+    }
+    const TcMap& wmap = tc_w_[(size_t)l * 4 + which];
+    if (mode == kEpSilu) {
+      TRIT_CUDA(launch_gemm_tc(wmap, xmap, W, xs_, m, kEpOut, gu_, W.n, 1.0f, tc_status_, s));
+      TRIT_CUDA(launch_silu_pairs(gu_, m, W.n / 2, y, s));
+      timing_.gpu_launches += 1;
+    } else {
+      TRIT_CUDA(launch_gemm_tc(wmap, xmap, W, xs_, m, mode, y, ldy, mult, tc_status_, s));
+    }
+  };
   if (cfg_.embedding_multiplier != 1.0f) TRIT_CUDA(launch_scale(x_, (size_t)m * d, cfg_.embedding_multiplier, s));
   for (int l = 0; l < cfg_.layers; ++l) {
     const DLayer& L = layers_[l];
     TRIT_CUDA(launch_norm_quant(x_, m, d, L.norm_attn, cfg_.eps, L.qkv.agroup, L.qkv.half, xq_, xs_, s));
-    TRIT_CUDA(launch_gemv(L.qkv, xq_, xs_, m, kEpOut, qkv_, qd + 2 * kvd, 1.0f, s));
+    product(l, 0, L.qkv, tc_x_[0], kEpOut, qkv_, qd + 2 * kvd, 1.0f);
     TRIT_CUDA(launch_qk_rope_append(qkv_, m, cfg_, L.q_norm, L.k_norm, rope_, opt_.max_context, cache_, row_stream_,
                                     row_pos_, l, s));
     TRIT_CUDA(launch_attention(qkv_, m, cfg_, cache_, row_stream_, row_pos_, l, max_tk, att_, s));
     TRIT_CUDA(launch_norm_quant(att_, m, qd, nullptr, cfg_.eps, L.out.agroup, L.out.half, xq_, xs_, s));
-    TRIT_CUDA(launch_gemv(L.out, xq_, xs_, m, kEpResid, x_, d, cfg_.residual_multiplier, s));
+    product(l, 1, L.out, tc_x_[1], kEpResid, x_, d, cfg_.residual_multiplier);
     TRIT_CUDA(launch_norm_quant(x_, m, d, L.norm_mlp, cfg_.eps, L.gate_up.agroup, L.gate_up.half, xq_, xs_, s));
-    TRIT_CUDA(launch_gemv(L.gate_up, xq_, xs_, m, kEpSilu, h_, cfg_.ffn, 1.0f, s));
+    product(l, 2, L.gate_up, tc_x_[0], kEpSilu, h_, cfg_.ffn, 1.0f);
     TRIT_CUDA(launch_norm_quant(h_, m, cfg_.ffn, nullptr, cfg_.eps, L.down.agroup, L.down.half, xq_, xs_, s));
-    TRIT_CUDA(launch_gemv(L.down, xq_, xs_, m, kEpResid, x_, d, cfg_.residual_multiplier, s));
+    product(l, 3, L.down, tc_x_[2], kEpResid, x_, d, cfg_.residual_multiplier);
   }
   timing_.gpu_launches += cfg_.layers * 10 + (cfg_.embedding_multiplier != 1.0f ? 1 : 0);
+}
+
+// The tensor-core products (mma.cu) for prefill and batches: TMA maps of
+// every product's int8 codes (ternary layers get an int8 copy of their
+// codes, c - 1, beside the 2-bit one the GEMV reads) and of the quantized
+// frames for each input width. Off on a GPU other than sm_100 or when the
+// "tensor_cores" option is false.
+void Lm::setup_tensor_cores() {
+  if (!opt_.tensor_cores) return;
+  cudaDeviceProp prop;
+  TRIT_CUDA(cudaGetDeviceProperties(&prop, opt_.device));
+  if (prop.major != 10) return;
+  const int d = cfg_.d, qd = cfg_.heads * cfg_.hd;
+  size_t expanded = 0;
+  for (const DLayer& L : layers_)
+    for (const DMat* W : {&L.qkv, &L.out, &L.gate_up, &L.down})
+      if (W->kind == kTernary) expanded += (size_t)W->n * W->k;
+  if (expanded) TRIT_CUDA(cudaMalloc(&tc_expanded_, expanded));
+  size_t at = 0;
+  tc_w_.assign((size_t)cfg_.layers * 4, TcMap{});
+  for (int l = 0; l < cfg_.layers; ++l) {
+    const DLayer& L = layers_[l];
+    const DMat* mats[4] = {&L.qkv, &L.out, &L.gate_up, &L.down};
+    for (int i = 0; i < 4; ++i) {
+      const void* codes = mats[i]->codes;
+      if (mats[i]->kind == kTernary) {
+        int8_t* dst = tc_expanded_ + at;
+        TRIT_CUDA(launch_expand_ternary(*mats[i], dst, stream_));
+        at += (size_t)mats[i]->n * mats[i]->k;
+        codes = dst;
+      }
+      TRIT_CUDA(make_tc_weight_map(&tc_w_[(size_t)l * 4 + i], *mats[i], codes));
+    }
+  }
+  const size_t rows8 = (size_t)(rows_cap_ + 63) / 64 * 64;
+  const int widths[3] = {d, qd, cfg_.ffn};
+  for (int i = 0; i < 3; ++i) TRIT_CUDA(make_tc_frame_map(&tc_x_[i], xq_, rows8, (size_t)widths[i]));
+  TRIT_CUDA(cudaMalloc(&gu_, (size_t)rows_cap_ * 2 * cfg_.ffn * 4));
+  TRIT_CUDA(cudaMalloc(&tc_status_, 4));
+  TRIT_CUDA(cudaMemset(tc_status_, 0, 4));
+  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  tc_ready_ = true;
+}
+
+// Throws if a tensor-core product gave up waiting (its status word).
+void Lm::check_tc_status() {
+  if (!tc_ready_) return;
+  int st = 0;
+  TRIT_CUDA(cudaMemcpy(&st, tc_status_, 4, cudaMemcpyDeviceToHost));
+  if (st) {
+    cudaMemset(tc_status_, 0, 4);
+    throw Error("a tensor-core product gave up waiting for its pipeline (status " + std::to_string(st) + ")");
+  }
 }
 
 // The prompt rows through every layer, prefill_rows at a time (causal
@@ -507,6 +587,7 @@ std::vector<int> Lm::finish(int slot, int position, int max_new, const int* stop
   std::vector<int> out;
   if (max_new <= 0) {
     TRIT_CUDA(cudaStreamSynchronize(stream_));
+    check_tc_status();
     return out;
   }
   if (tokens_cap_ < max_new + 1) {
@@ -532,6 +613,7 @@ std::vector<int> Lm::finish(int slot, int position, int max_new, const int* stop
   std::vector<int> toks(max_new);
   TRIT_CUDA(cudaMemcpyAsync(toks.data(), tokens_, (size_t)max_new * 4, cudaMemcpyDeviceToHost, stream_));
   TRIT_CUDA(cudaStreamSynchronize(stream_));
+  check_tc_status();
   float ms = 0;
   TRIT_CUDA(cudaEventElapsedTime(&ms, ev_[0], ev_[1]));
   timing_.prefill_ms = ms;
@@ -734,6 +816,7 @@ std::unique_ptr<PrefixState> Lm::prefix(const int* ids, size_t n) {
   TRIT_CUDA(cudaMalloc(&p->pages, p->bytes));
   TRIT_CUDA(cudaMemcpyAsync(p->pages, pool_, p->bytes, cudaMemcpyDeviceToDevice, stream_));
   TRIT_CUDA(cudaStreamSynchronize(stream_));
+  check_tc_status();
   return p;
 }
 
@@ -873,6 +956,7 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
   std::vector<int> toks((size_t)max_new * S);
   TRIT_CUDA(cudaMemcpyAsync(toks.data(), batch_tok_, toks.size() * 4, cudaMemcpyDeviceToHost, stream_));
   TRIT_CUDA(cudaStreamSynchronize(stream_));
+  check_tc_status();
   float ms = 0;
   TRIT_CUDA(cudaEventElapsedTime(&ms, ev_[0], ev_[1]));
   timing_.prefill_ms = ms;

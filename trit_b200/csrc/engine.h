@@ -24,6 +24,8 @@ struct Options {
   int page_tokens = 64;          // positions per KV page
   int prefill_rows = 512;        // rows per prefill pass
   std::string decode = "persistent";  // "persistent" (one kernel per generation) or "layered"
+  bool tensor_cores = true;      // tcgen05 products for prefill and batches of >= tc_rows rows
+  int tc_rows = 64;
   std::string config_at;         // key path of the settings in config.json (from_tensors' config_at)
   std::string prefix;            // start of every tensor name (from_tensors' prefix)
   // `lenient`: keys other than config_at and prefix are skipped unchecked.
@@ -89,6 +91,8 @@ class Lm {
   void embed_rows(const int* staged, size_t c0, size_t c1, float* x);
   int* stage_ids(const int* a, size_t na, const int* b, size_t nb);
   void hidden(int m, int max_tk);
+  void setup_tensor_cores();
+  void check_tc_status();
   // Greedy decode for `slot` after a prefill that left its last row in x.
   std::vector<int> finish(int slot, int position, int max_new, const int* stop, size_t nstop, float* logits);
   void decode_layered(int slot, int position, int steps, float* trace);
@@ -151,6 +155,13 @@ class Lm {
   size_t batch_tok_cap_ = 0;
   cudaGraphExec_t batch_graph_ = nullptr;  // one captured greedy step
   int batch_graph_streams_ = 0, batch_graph_tmax_ = 0;
+  // tensor-core products
+  bool tc_ready_ = false;
+  std::vector<TcMap> tc_w_;     // [layer][qkv, out, gate_up, down]
+  TcMap tc_x_[3] = {};          // quantized frames of width d, heads * hd, ffn
+  int8_t* tc_expanded_ = nullptr;  // int8 codes of ternary layers
+  float* gu_ = nullptr;         // [rows][2 ffn] gate|up products before silu * up
+  int* tc_status_ = nullptr;
 };
 
 // A lone product layer for the op sweep (Dense::forward, gemm.rs:500-542).
