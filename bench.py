@@ -255,7 +255,11 @@ def run_reference(args, r: dp.Rank) -> None:
 def run_decode(args, r: dp.Rank) -> None:
     from trit_b200 import CausalLm, lm as lmmod, presets
 
-    w = WORKLOADS[args.config]
+    w = dict(WORKLOADS[args.config])
+    for key in ("streams", "prompt", "new"):
+        if getattr(args, key) is not None:
+            w[key] = getattr(args, key)
+            w["workload"] += f" ({key} set to {getattr(args, key)})"
     if r.rank == 0:
         model_dir = presets.model_path(w["model"])
     dp.barrier(r)
@@ -449,6 +453,9 @@ def main() -> None:
     ap.add_argument("--kv", default="f16")
     ap.add_argument("--reps", type=int, default=1000, help="repetitions per case of the op sweep")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--streams", type=int, help="streams per GPU instead of the workload's (profiling runs)")
+    ap.add_argument("--prompt", type=int, help="prompt ids instead of the workload's")
+    ap.add_argument("--new", type=int, help="greedy tokens instead of the workload's")
     args = ap.parse_args()
     backend = "nccl"
     if args.impl == "reference":

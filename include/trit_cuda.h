@@ -145,6 +145,26 @@ int trit_lm_generate_batch(TritLm *lm, size_t streams, const int32_t *const *pro
                            int32_t max_new, const int32_t *stop, size_t nstop, int32_t *out,
                            int64_t *counts);
 
+/* CausalLm::set_ffn_scales (causal_lm.rs:305-307): the normed MLP input of
+ * layer l is multiplied by scales[l * width ...] (layers x width floats,
+ * copied); NULL clears the scales. Returns 0, or -1. */
+int trit_lm_set_ffn_scales(TritLm *lm, const float *scales, size_t layers, size_t width);
+
+/* CausalLm::generate_additive (causal_lm.rs:317-345), Voxtral Realtime's
+ * loop: the prompt's embeddings plus audio rows 0..n, then each new token's
+ * embedding plus the next row (`audio`: rows x width floats), until a token
+ * of `stop` or the rows end; at most rows - n + 1 tokens, written to `out`
+ * (cap of them). Returns the count, or -1. */
+int64_t trit_lm_generate_additive(TritLm *lm, const int32_t *prompt, size_t n, const float *audio, size_t rows,
+                                  const int32_t *stop, size_t nstop, int32_t *out, size_t cap);
+
+/* CausalLm::bidirectional_tokens (causal_lm.rs:393-408), Granite Speech
+ * NAR's editor: one pass over `m` rows (m x width floats) with no causal
+ * mask, then the best token of each row from `from` on, m - from ids into
+ * `out`. The rows must fit one prefill pass ("prefill_rows"). Returns
+ * m - from, or -1. */
+int64_t trit_lm_bidirectional_tokens(TritLm *lm, const float *rows, size_t m, size_t from, int32_t *out);
+
 /* The device time of the last generation on this handle, from CUDA events:
  * the prompt (prefill) and the greedy steps after it, in ms, the number of
  * decode steps, and the kernel launches it made. Returns 0, or -1. */

@@ -818,6 +818,7 @@ struct Model {
   Table head;
   Rotary rotary;
   bool kv_f16 = false;  // a documented variant: K and V rounded to f16 as stored
+  vector<vector<float>> ffn_scales;  // set_ffn_scales: [layers][d], or empty
 };
 
 const GgufTensor& tensor(const Gguf& g, const string& name) {
@@ -1036,6 +1037,11 @@ void hidden(const Model& M, vector<float>& x, size_t first, Cache& cache, bool c
       x[i] = (c.residual_multiplier == 1.0f) ? x[i] + o[i] : x[i] + c.residual_multiplier * o[i];
     normed = x;
     for (size_t r = 0; r < m; ++r) rms_in_place(normed.data() + r * d, L.norm_mlp.data(), d, c.eps);
+    // set_ffn_scales (causal_lm.rs:305-307,458-463): the normed MLP input
+    // times the layer's scale, element by element.
+    if (!M.ffn_scales.empty())
+      for (size_t r = 0; r < m; ++r)
+        for (size_t i = 0; i < d; ++i) normed[r * d + i] = normed[r * d + i] * M.ffn_scales[l][i];
     vector<float> wide = int_forward(L.gate_up, normed.data(), m);
     vector<float> hbuf(m * c.ffn);
     for (size_t r = 0; r < m; ++r)
@@ -1226,6 +1232,72 @@ int64_t oracle_answer(void* h, const int32_t* head, size_t nhead, const float* a
     vector<float> lg = forward_rows(M, rows, 0, cache);
     return (int64_t)greedy(M, lg, length, cache, (size_t)max_new, stop, nstop, out,
                            Trace{logits, gaps, nullptr}, 0.0);
+  }, -1);
+}
+
+// CausalLm::set_ffn_scales (causal_lm.rs:305-307): [layers][d], or NULL
+// to clear.
+void oracle_set_ffn_scales(void* h, const float* scales) {
+  Model& M = *(Model*)h;
+  M.ffn_scales.clear();
+  if (!scales) return;
+  for (size_t l = 0; l < M.c.layers; ++l) M.ffn_scales.emplace_back(scales + l * M.c.d, scales + (l + 1) * M.c.d);
+}
+
+// CausalLm::generate_additive (causal_lm.rs:317-345): the prompt's
+// embeddings plus audio rows 0..n, then each new token's embedding plus
+// the next row, until a stop token or the rows end.
+int64_t oracle_generate_additive(void* h, const int32_t* prompt, size_t n, const float* audio, size_t rows,
+                                 const int32_t* stop, size_t nstop, int32_t* out, float* logits) {
+  return guarded([&]() -> int64_t {
+    const Model& M = *(Model*)h;
+    const size_t d = M.c.d, V = M.c.vocab;
+    if (n == 0 || rows < n) return (int64_t)0;
+    auto stopped = [&](size_t t) {
+      for (size_t s = 0; s < nstop; ++s)
+        if ((size_t)stop[s] == t) return true;
+      return false;
+    };
+    Cache cache = empty_cache(M);
+    vector<float> x = embed(M, prompt, n);
+    for (size_t i = 0; i < n * d; ++i) x[i] = x[i] + audio[i];
+    vector<float> lg = forward_rows(M, x, 0, cache);
+    size_t token = argmax(lg.data(), V), count = 0;
+    if (logits) memcpy(logits, lg.data(), V * 4);
+    for (size_t position = n; position < rows; ++position) {
+      if (stopped(token)) return (int64_t)count;
+      out[count++] = (int32_t)token;
+      int32_t id = (int32_t)token;
+      vector<float> e = embed(M, &id, 1);
+      for (size_t i = 0; i < d; ++i) e[i] = e[i] + audio[position * d + i];
+      lg = forward_rows(M, e, position, cache);
+      token = argmax(lg.data(), V);
+      if (logits) memcpy(logits + count * V, lg.data(), V * 4);
+    }
+    if (!stopped(token)) out[count++] = (int32_t)token;
+    return (int64_t)count;
+  }, -1);
+}
+
+// CausalLm::bidirectional_tokens (causal_lm.rs:393-408): one pass over all
+// rows without the causal mask, then the best token of each row from
+// `from` on. out: rows - from tokens.
+int64_t oracle_bidirectional_tokens(void* h, const float* rows, size_t m, size_t from, int32_t* out) {
+  return guarded([&]() -> int64_t {
+    const Model& M = *(Model*)h;
+    const size_t d = M.c.d, V = M.c.vocab;
+    if (from > m) throw std::runtime_error("from is past the rows");
+    Cache cache = empty_cache(M);
+    vector<float> x(rows, rows + m * d);
+    hidden(M, x, 0, cache, false);
+    const Table& T = M.has_head ? M.head : M.embed;
+    for (size_t r = from; r < m; ++r) {
+      vector<float> row(x.begin() + r * d, x.begin() + (r + 1) * d);
+      rms_in_place(row.data(), M.norm.data(), d, M.c.eps);
+      vector<float> lg = table_forward(T, row.data(), 1);
+      out[r - from] = (int32_t)argmax(lg.data(), V);
+    }
+    return (int64_t)(m - from);
   }, -1);
 }
 

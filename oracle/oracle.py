@@ -59,6 +59,10 @@ def lib() -> ctypes.CDLL:
         "oracle_answer": (ctypes.c_int64, [ctypes.c_void_p, _i32p, _size, _f32p, _size, _i32p, _size, ctypes.c_int64,
                                            _i32p, _size, _i32p, _f32p, _f32p]),
         "oracle_embed": (ctypes.c_int, [ctypes.c_void_p, _i32p, _size, _f32p]),
+        "oracle_set_ffn_scales": (None, [ctypes.c_void_p, _f32p]),
+        "oracle_generate_additive": (ctypes.c_int64, [ctypes.c_void_p, _i32p, _size, _f32p, _size, _i32p, _size,
+                                                      _i32p, _f32p]),
+        "oracle_bidirectional_tokens": (ctypes.c_int64, [ctypes.c_void_p, _f32p, _size, _size, _i32p]),
         "oracle_f32_to_f16": (ctypes.c_uint16, [ctypes.c_float]),
         "oracle_f16_to_f32": (ctypes.c_float, [ctypes.c_uint16]),
         "oracle_exp": (ctypes.c_float, [ctypes.c_float]),
@@ -167,6 +171,34 @@ class Oracle:
 
     def generate_rows(self, rows: np.ndarray, max_new: int, stop=(), trace: bool = False):
         return self.answer([], rows, [], max_new, stop, trace)
+
+    def set_ffn_scales(self, scales) -> None:
+        """CausalLm::set_ffn_scales: [layers][width] floats, or None."""
+        if scales is None:
+            lib().oracle_set_ffn_scales(self.h, None)
+            return
+        self._ffn = np.ascontiguousarray(scales, dtype=np.float32)
+        lib().oracle_set_ffn_scales(self.h, _p(self._ffn, _f32p))
+
+    def generate_additive(self, prompt, audio: np.ndarray, stop=(), trace: bool = False):
+        ids, st = _ids(prompt), _ids(stop)
+        a = np.ascontiguousarray(audio, dtype=np.float32).reshape(-1, self.width)
+        cap = max(a.shape[0] - ids.size + 1, 1)
+        out = np.zeros(cap, dtype=np.int32)
+        logits = np.zeros((cap, self.vocab), dtype=np.float32) if trace else None
+        n = lib().oracle_generate_additive(self.h, _p(ids, _i32p), ids.size, _p(a, _f32p), a.shape[0],
+                                           _p(st, _i32p), st.size, _p(out, _i32p), _p(logits, _f32p))
+        if n < 0:
+            raise _err()
+        return {"tokens": out[:n].tolist(), "logits": logits}
+
+    def bidirectional_tokens(self, rows: np.ndarray, start: int) -> list:
+        r = np.ascontiguousarray(rows, dtype=np.float32).reshape(-1, self.width)
+        out = np.zeros(max(r.shape[0] - start, 1), dtype=np.int32)
+        n = lib().oracle_bidirectional_tokens(self.h, _p(r, _f32p), r.shape[0], start, _p(out, _i32p))
+        if n < 0:
+            raise _err()
+        return out[:n].tolist()
 
     def embed(self, tokens) -> np.ndarray:
         ids = _ids(tokens)

@@ -190,6 +190,44 @@ int trit_lm_embed(TritLm* lm, const int32_t* ids, size_t n, float* out) {
   });
 }
 
+int trit_lm_set_ffn_scales(TritLm* lm, const float* scales, size_t layers, size_t width) {
+  return guard<int>(-1, [&]() {
+    need(lm, "lm");
+    const trit::DConfig& c = lm->lm->config();
+    if (scales && (layers != (size_t)c.layers || width != (size_t)c.d))
+      throw trit::Error("ffn scales are " + std::to_string(layers) + " x " + std::to_string(width) + ", the model has " +
+                        std::to_string(c.layers) + " layers of width " + std::to_string(c.d));
+    std::lock_guard<std::mutex> lock(lm->lm->mutex());
+    lm->lm->set_ffn_scales(scales);
+    return 0;
+  });
+}
+
+int64_t trit_lm_generate_additive(TritLm* lm, const int32_t* prompt, size_t n, const float* audio, size_t rows,
+                                  const int32_t* stop, size_t nstop, int32_t* out, size_t cap) {
+  return guard<int64_t>(-1, [&]() {
+    need(lm, "lm");
+    if (n) need(prompt, "prompt");
+    if (rows) need(audio, "audio");
+    if (nstop) need(stop, "stop");
+    std::lock_guard<std::mutex> lock(lm->lm->mutex());
+    auto toks = lm->lm->generate_additive(prompt, n, audio, rows, stop, nstop, nullptr);
+    return copy_out(toks, out, cap);
+  });
+}
+
+int64_t trit_lm_bidirectional_tokens(TritLm* lm, const float* rows, size_t m, size_t from, int32_t* out) {
+  return guard<int64_t>(-1, [&]() {
+    need(lm, "lm");
+    if (m) need(rows, "rows");
+    if (m > from) need(out, "out");
+    std::lock_guard<std::mutex> lock(lm->lm->mutex());
+    auto toks = lm->lm->bidirectional_tokens(rows, m, from);
+    for (size_t i = 0; i < toks.size(); ++i) out[i] = toks[i];
+    return (int64_t)toks.size();
+  });
+}
+
 int trit_lm_generate_batch(TritLm* lm, size_t streams, const int32_t* const* prompts, const size_t* lens,
                            int32_t max_new, const int32_t* stop, size_t nstop, int32_t* out, int64_t* counts) {
   return guard<int>(-1, [&]() {

@@ -132,7 +132,8 @@ struct Shared {
 
 // RmsNorm (layers.rs:135-144) of S.xf (d values) with weight w (null: no
 // norm), then Quantized::grouped of the result into S.xq / S.xs.
-__device__ void norm_quant(int d, const float* w, float eps, int G, bool half, Shared& S) {
+__device__ void norm_quant(int d, const float* w, float eps, int G, bool half, Shared& S,
+                           const float* sc = nullptr) {
   __syncthreads();
   float inv = 1.0f;
   if (w) {
@@ -152,6 +153,7 @@ __device__ void norm_quant(int d, const float* w, float eps, int G, bool half, S
       float v[1];
       int kk = g * 32 + lane;
       v[0] = w ? __fmul_rn(S.xf[kk], __fmul_rn(inv, w[kk])) : S.xf[kk];
+      if (sc) v[0] = __fmul_rn(v[0], sc[kk]);
       float sc = warp_quantize_group<32>(v, S.xq + g * 32, half);
       if (lane == 0) S.xs[g] = sc;
     } else {
@@ -160,6 +162,7 @@ __device__ void norm_quant(int d, const float* w, float eps, int G, bool half, S
       for (int i = 0; i < 4; ++i) {
         int kk = g * 128 + lane * 4 + i;
         v[i] = w ? __fmul_rn(S.xf[kk], __fmul_rn(inv, w[kk])) : S.xf[kk];
+        if (sc) v[i] = __fmul_rn(v[i], sc[kk]);
       }
       float sc = warp_quantize_group<128>(v, S.xq + g * 128, half);
       if (lane == 0) S.xs[g] = sc;
@@ -634,7 +637,7 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
         if (!ll_wait(a.ll + ll.xa, cfg.d, t_xa, a.status, [&](int k, uint32_t v) { S.xf[k] = __uint_as_float(v); }))
           return false;
         ev(10);
-        norm_quant(cfg.d, Lw.norm_mlp, cfg.eps, Lw.gate_up.agroup, Lw.gate_up.half, S);
+        norm_quant(cfg.d, Lw.norm_mlp, cfg.eps, Lw.gate_up.agroup, Lw.gate_up.half, S, Lw.ffn_scale);
         ev(11);
         return true;
       });

@@ -255,7 +255,11 @@ void Lm::release() {
     if (b) cudaFree(b);
   if (host_rows_) cudaFreeHost(host_rows_);
   if (batch_host_) cudaFreeHost(batch_host_);
-  void* batch[] = {batch_last_, batch_cur_, batch_step_, batch_tok_, tc_expanded_, gu_, tc_status_};
+  if (tiles_pinned_) cudaFreeHost(tiles_pinned_);
+  if (tiles_dev_) cudaFree(tiles_dev_);
+  tiles_pinned_ = nullptr;
+  tiles_dev_ = nullptr;
+  void* batch[] = {batch_last_, batch_cur_, batch_step_, batch_tok_, tc_expanded_, gu_, tc_status_, ffn_scales_, audio_};
   for (void* b : batch)
     if (b) cudaFree(b);
   if (batch_graph_) cudaGraphExecDestroy(batch_graph_);
@@ -263,6 +267,8 @@ void Lm::release() {
   batch_last_ = nullptr;
   batch_cur_ = batch_step_ = batch_tok_ = nullptr;
   tc_expanded_ = nullptr;
+  ffn_scales_ = nullptr;
+  audio_ = nullptr;
   gu_ = nullptr;
   tc_status_ = nullptr;
   tc_ready_ = false;
@@ -377,6 +383,8 @@ void Lm::alloc_buffers() {
   TRIT_CUDA(cudaMalloc(&stop_, 256 * 4));
   TRIT_CUDA(cudaMallocHost(&host_rows_, ((size_t)2 * rows_cap_ + opt_.max_context + 16) * 4));
   TRIT_CUDA(cudaMalloc(&positions_, (size_t)opt_.max_context * std::max(1, opt_.max_streams) * 4));
+  TRIT_CUDA(cudaMallocHost(&tiles_pinned_, (size_t)rows_cap_ * 8));
+  TRIT_CUDA(cudaMalloc(&tiles_dev_, (size_t)rows_cap_ * 8));
 }
 
 void Lm::check_ids(const int* ids, size_t n) const {
@@ -387,9 +395,20 @@ void Lm::check_ids(const int* ids, size_t n) const {
 
 // CausalLm::hidden (causal_lm.rs:410-481) for the rows in x_, whose stream
 // and position are in row_stream_ / row_pos_.
-void Lm::hidden(int m, int max_tk) {
+void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* tiles) {
   const int d = cfg_.d, qd = cfg_.heads * cfg_.hd, kvd = cfg_.kv_heads * cfg_.hd;
   cudaStream_t s = stream_;
+  // Prompt tiles: attention shares each stream's keys among a tile's rows.
+  int ntiles = 0, rows_max = 0;
+  if (tiles && causal_ && !tiles->empty()) {
+    ntiles = (int)tiles->size();
+    for (int i = 0; i < ntiles; ++i) {
+      tiles_pinned_[2 * i] = (*tiles)[i].first;
+      tiles_pinned_[2 * i + 1] = (*tiles)[i].second;
+      rows_max = std::max(rows_max, (*tiles)[i].second);
+    }
+    TRIT_CUDA(cudaMemcpyAsync(tiles_dev_, tiles_pinned_, (size_t)ntiles * 8, cudaMemcpyHostToDevice, s));
+  }
   const bool tc = tc_ready_ && m >= opt_.tc_rows;
   // One product: the tensor-core kernel for enough rows, else the GEMV.
   auto product = [&](int l, int which, const DMat& W, const TcMap& xmap, int mode, float* y, int ldy, float mult) {
@@ -413,15 +432,172 @@ void Lm::hidden(int m, int max_tk) {
     product(l, 0, L.qkv, tc_x_[0], kEpOut, qkv_, qd + 2 * kvd, 1.0f);
     TRIT_CUDA(launch_qk_rope_append(qkv_, m, cfg_, L.q_norm, L.k_norm, rope_, opt_.max_context, cache_, row_stream_,
                                     row_pos_, l, s));
-    TRIT_CUDA(launch_attention(qkv_, m, cfg_, cache_, row_stream_, row_pos_, l, max_tk, att_, s));
+    if (ntiles)
+      TRIT_CUDA(launch_attention_rows(qkv_, (const int2*)tiles_dev_, ntiles, rows_max, cfg_, cache_, row_stream_,
+                                      row_pos_, l, max_tk, att_, s));
+    else
+      TRIT_CUDA(launch_attention_rows(qkv_, nullptr, m, 1, cfg_, cache_, row_stream_, row_pos_, l, max_tk, att_, s,
+                                      causal_ ? 0 : max_tk));
     TRIT_CUDA(launch_norm_quant(att_, m, qd, nullptr, cfg_.eps, L.out.agroup, L.out.half, xq_, xs_, s));
     product(l, 1, L.out, tc_x_[1], kEpResid, x_, d, cfg_.residual_multiplier);
-    TRIT_CUDA(launch_norm_quant(x_, m, d, L.norm_mlp, cfg_.eps, L.gate_up.agroup, L.gate_up.half, xq_, xs_, s));
+    TRIT_CUDA(launch_norm_quant(x_, m, d, L.norm_mlp, cfg_.eps, L.gate_up.agroup, L.gate_up.half, xq_, xs_, s,
+                                L.ffn_scale));
     product(l, 2, L.gate_up, tc_x_[0], kEpSilu, h_, cfg_.ffn, 1.0f);
     TRIT_CUDA(launch_norm_quant(h_, m, cfg_.ffn, nullptr, cfg_.eps, L.down.agroup, L.down.half, xq_, xs_, s));
     product(l, 3, L.down, tc_x_[2], kEpResid, x_, d, cfg_.residual_multiplier);
   }
   timing_.gpu_launches += cfg_.layers * 10 + (cfg_.embedding_multiplier != 1.0f ? 1 : 0);
+}
+
+// CausalLm::set_ffn_scales (causal_lm.rs:305-307): the normed MLP input of
+// layer l times scales[l] (hidden, :458-463); null clears them.
+void Lm::set_ffn_scales(const float* scales) {
+  TRIT_CUDA(cudaSetDevice(opt_.device));
+  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  if (scales) {
+    if (!ffn_scales_) TRIT_CUDA(cudaMalloc(&ffn_scales_, (size_t)cfg_.layers * cfg_.d * 4));
+    TRIT_CUDA(cudaMemcpy(ffn_scales_, scales, (size_t)cfg_.layers * cfg_.d * 4, cudaMemcpyHostToDevice));
+  }
+  for (int l = 0; l < cfg_.layers; ++l) layers_[l].ffn_scale = scales ? ffn_scales_ + (size_t)l * cfg_.d : nullptr;
+  TRIT_CUDA(cudaMemcpy(d_layers_, layers_.data(), sizeof(DLayer) * cfg_.layers, cudaMemcpyHostToDevice));
+}
+
+// CausalLm::generate_additive (causal_lm.rs:317-345), Voxtral Realtime's
+// loop: the prompt's embeddings plus audio rows [0, n), then each new
+// token's embedding plus the next audio row, until a stop token or the
+// rows run out (at most rows - n + 1 tokens). Decoded with the layered
+// kernels, one added row per step.
+std::vector<int> Lm::generate_additive(const int* ids, size_t n, const float* audio, size_t rows, const int* stop,
+                                       size_t nstop, float* logits) {
+  std::vector<int> out;
+  if (n == 0 || rows < n) return out;
+  check_ids(ids, n);
+  if (rows + 1 > (size_t)opt_.max_context) throw Error("audio rows exceed max_context " + std::to_string(opt_.max_context));
+  timing_ = Timing{};
+  TRIT_CUDA(cudaSetDevice(opt_.device));
+  const int d = cfg_.d;
+  if (audio_cap_ < rows) {
+    if (audio_) cudaFree(audio_);
+    audio_ = nullptr;
+    TRIT_CUDA(cudaMalloc(&audio_, rows * d * 4));
+    audio_cap_ = rows;
+  }
+  int* staged = stage_ids(ids, n, nullptr, 0);
+  TRIT_CUDA(cudaEventRecord(ev_[0], stream_));
+  TRIT_CUDA(cudaMemcpyAsync(audio_, audio, rows * d * 4, cudaMemcpyHostToDevice, stream_));
+  run_prompt(n, 0, 0, [&](size_t c0, size_t c1) {
+    embed_rows(staged, c0, c1, x_);
+    TRIT_CUDA(launch_add(x_, audio_ + c0 * d, (c1 - c0) * d, stream_));
+    timing_.gpu_launches += 1;
+  });
+  const int max_new = (int)(rows - n + 1);
+  if (tokens_cap_ < max_new + 1) {
+    if (tokens_) cudaFree(tokens_);
+    tokens_ = nullptr;
+    tokens_cap_ = max_new + 1;
+    TRIT_CUDA(cudaMalloc(&tokens_, (size_t)tokens_cap_ * std::max(1, opt_.max_streams) * 4));
+  }
+  TRIT_CUDA(launch_final(x_ + (size_t)(last_rows_ - 1) * d, d, 1, final_norm_, cfg_, head_, xn_,
+                         logits ? logits_ : nullptr, best_val_, best_idx_, tokens_, stream_));
+  if (logits) TRIT_CUDA(cudaMemcpyAsync(logits, logits_, (size_t)cfg_.vocab * 4, cudaMemcpyDeviceToHost, stream_));
+  TRIT_CUDA(cudaEventRecord(ev_[1], stream_));
+  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  int* host = host_rows_;
+  host[0] = 0;
+  TRIT_CUDA(cudaMemcpyAsync(row_stream_, host, 4, cudaMemcpyHostToDevice, stream_));
+  int* hp = host_rows_ + 2 * rows_cap_;
+  const int steps = max_new - 1;
+  for (int i = 0; i < steps; ++i) hp[i] = (int)n + i;
+  TRIT_CUDA(cudaMemcpyAsync(positions_, hp, (size_t)steps * 4, cudaMemcpyHostToDevice, stream_));
+  int* saved = row_pos_;
+  for (int i = 0; i < steps; ++i) {
+    TRIT_CUDA(launch_embed(embed_, tokens_ + i, 1, x_, 1.0f, stream_));
+    TRIT_CUDA(launch_add(x_, audio_ + (n + i) * d, d, stream_));
+    row_pos_ = positions_ + i;
+    hidden(1, (int)n + i + 1);
+    row_pos_ = saved;
+    TRIT_CUDA(launch_final(x_, d, 1, final_norm_, cfg_, head_, xn_, logits ? logits_ : nullptr, best_val_, best_idx_,
+                           tokens_ + i + 1, stream_));
+    timing_.gpu_launches += 5;
+    if (logits)
+      TRIT_CUDA(cudaMemcpyAsync(logits + (size_t)(i + 1) * cfg_.vocab, logits_, (size_t)cfg_.vocab * 4,
+                                cudaMemcpyDeviceToHost, stream_));
+  }
+  row_pos_ = saved;
+  TRIT_CUDA(cudaEventRecord(ev_[2], stream_));
+  std::vector<int> toks(max_new);
+  TRIT_CUDA(cudaMemcpyAsync(toks.data(), tokens_, (size_t)max_new * 4, cudaMemcpyDeviceToHost, stream_));
+  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  check_tc_status();
+  float ms = 0;
+  TRIT_CUDA(cudaEventElapsedTime(&ms, ev_[0], ev_[1]));
+  timing_.prefill_ms = ms;
+  TRIT_CUDA(cudaEventElapsedTime(&ms, ev_[1], ev_[2]));
+  timing_.decode_ms = ms;
+  timing_.decode_tokens = steps;
+  for (int t : toks) {
+    bool stopped = false;
+    for (size_t k = 0; k < nstop; ++k) stopped |= t == stop[k];
+    if (stopped) break;
+    out.push_back(t);
+  }
+  return out;
+}
+
+// CausalLm::bidirectional_tokens (causal_lm.rs:393-408), Granite Speech
+// NAR's editor: one pass over all rows with no causal mask (every row sees
+// every key), then the best token of each row from `from` on. The rows
+// must fit one pass (prefill_rows).
+std::vector<int> Lm::bidirectional_tokens(const float* rows, size_t m, size_t from) {
+  if (from > m) throw Error("from (" + std::to_string(from) + ") is past the rows (" + std::to_string(m) + ")");
+  if (m == 0) return {};
+  if (m > (size_t)rows_cap_)
+    throw Error(std::to_string(m) + " rows do not fit one pass of prefill_rows " + std::to_string(rows_cap_));
+  if (m > (size_t)opt_.max_context) throw Error("more rows than max_context");
+  timing_ = Timing{};
+  TRIT_CUDA(cudaSetDevice(opt_.device));
+  const int d = cfg_.d;
+  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  int* host = host_rows_;
+  for (size_t r = 0; r < m; ++r) {
+    host[r] = 0;
+    host[rows_cap_ + r] = (int)r;
+  }
+  TRIT_CUDA(cudaEventRecord(ev_[0], stream_));
+  TRIT_CUDA(cudaMemcpyAsync(row_stream_, host, m * 4, cudaMemcpyHostToDevice, stream_));
+  TRIT_CUDA(cudaMemcpyAsync(row_pos_, host + rows_cap_, m * 4, cudaMemcpyHostToDevice, stream_));
+  TRIT_CUDA(cudaMemcpyAsync(x_, rows, m * d * 4, cudaMemcpyHostToDevice, stream_));
+  causal_ = false;
+  try {
+    hidden((int)m, (int)m);
+  } catch (...) {
+    causal_ = true;
+    throw;
+  }
+  causal_ = true;
+  const size_t nb = m - from;
+  if (tokens_cap_ < (int)nb + 1) {
+    if (tokens_) cudaFree(tokens_);
+    tokens_ = nullptr;
+    tokens_cap_ = (int)nb + 1;
+    TRIT_CUDA(cudaMalloc(&tokens_, (size_t)tokens_cap_ * std::max(1, opt_.max_streams) * 4));
+  }
+  const size_t chunk = (size_t)std::max(1, opt_.max_streams);
+  for (size_t r0 = 0; r0 < nb; r0 += chunk) {
+    int c = (int)std::min(chunk, nb - r0);
+    TRIT_CUDA(launch_final(x_ + (from + r0) * d, d, c, final_norm_, cfg_, head_, xn_, nullptr, best_val_, best_idx_,
+                           tokens_ + r0, stream_));
+    timing_.gpu_launches += 3;
+  }
+  std::vector<int> out(nb);
+  TRIT_CUDA(cudaMemcpyAsync(out.data(), tokens_, nb * 4, cudaMemcpyDeviceToHost, stream_));
+  TRIT_CUDA(cudaEventRecord(ev_[1], stream_));
+  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  check_tc_status();
+  float ms = 0;
+  TRIT_CUDA(cudaEventElapsedTime(&ms, ev_[0], ev_[1]));
+  timing_.prefill_ms = ms;
+  return out;
 }
 
 // The tensor-core products (mma.cu) for prefill and batches: TMA maps of
@@ -493,7 +669,11 @@ void Lm::run_prompt(size_t m, int slot, int first, const std::function<void(size
     TRIT_CUDA(cudaMemcpyAsync(row_stream_, host, mc * 4, cudaMemcpyHostToDevice, stream_));
     TRIT_CUDA(cudaMemcpyAsync(row_pos_, host + rows_cap_, mc * 4, cudaMemcpyHostToDevice, stream_));
     fill(c0, c0 + mc);
-    hidden(mc, first + (int)c0 + mc);
+    const int top = first + (int)c0 + mc;
+    const int R = attention_tile_rows(cfg_, (top + 3) / 4 * 4);
+    std::vector<std::pair<int, int>> tiles;
+    for (int r = 0; r < mc; r += R) tiles.emplace_back(r, std::min(R, mc - r));
+    hidden(mc, top, &tiles);
     last_rows_ = mc;
   }
 }
@@ -890,7 +1070,16 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
     TRIT_CUDA(cudaMemcpyAsync(row_pos_, hp, (size_t)mc * 4, cudaMemcpyHostToDevice, stream_));
     TRIT_CUDA(cudaMemcpyAsync(ids_, hi, (size_t)mc * 4, cudaMemcpyHostToDevice, stream_));
     TRIT_CUDA(launch_embed(embed_, ids_, mc, x_, 1.0f, stream_));
-    hidden(mc, top);
+    // Tiles: runs of rows of one stream, at most R rows each.
+    const int R = attention_tile_rows(cfg_, (top + 3) / 4 * 4);
+    std::vector<std::pair<int, int>> tiles;
+    for (int r = 0; r < mc;) {
+      int e = r + 1;
+      while (e < mc && e - r < R && hs[e] == hs[r]) ++e;
+      tiles.emplace_back(r, e - r);
+      r = e;
+    }
+    hidden(mc, top, &tiles);
     timing_.gpu_launches += 1;
     for (auto& e : ends)
       TRIT_CUDA(cudaMemcpyAsync(batch_last_ + (size_t)e.second * d, x_ + (size_t)e.first * d, (size_t)d * 4,

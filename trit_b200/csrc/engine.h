@@ -76,6 +76,13 @@ class Lm {
                           size_t ntail, int max_new, const int* stop, size_t nstop, float* logits);
   void embed(const int* ids, size_t n, float* out);
   std::unique_ptr<PrefixState> prefix(const int* ids, size_t n);
+  // CausalLm::set_ffn_scales: [layers][d] host floats, or null to clear.
+  void set_ffn_scales(const float* scales);
+  // CausalLm::generate_additive: prompt ids plus audio rows [rows][d].
+  std::vector<int> generate_additive(const int* ids, size_t n, const float* audio, size_t rows, const int* stop,
+                                     size_t nstop, float* logits);
+  // CausalLm::bidirectional_tokens: rows [m][d] without the causal mask.
+  std::vector<int> bidirectional_tokens(const float* rows, size_t m, size_t from);
   // Independent streams, each with its own prompt: out [streams][max_new].
   void generate_batch(size_t streams, const int* const* prompts, const size_t* lens, int max_new, const int* stop,
                       size_t nstop, int* out, int64_t* counts);
@@ -90,7 +97,9 @@ class Lm {
   void run_prompt(size_t m, int slot, int first, const std::function<void(size_t, size_t)>& fill);
   void embed_rows(const int* staged, size_t c0, size_t c1, float* x);
   int* stage_ids(const int* a, size_t na, const int* b, size_t nb);
-  void hidden(int m, int max_tk);
+  // `tiles`: {first row, rows} runs of one stream at consecutive positions
+  // (prompt chunks), or null for one row per attention block.
+  void hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* tiles = nullptr);
   void setup_tensor_cores();
   void check_tc_status();
   // Greedy decode for `slot` after a prefill that left its last row in x.
@@ -162,6 +171,12 @@ class Lm {
   int8_t* tc_expanded_ = nullptr;  // int8 codes of ternary layers
   float* gu_ = nullptr;         // [rows][2 ffn] gate|up products before silu * up
   int* tc_status_ = nullptr;
+  bool causal_ = true;
+  int* tiles_pinned_ = nullptr;  // pinned [rows_cap][2]
+  int* tiles_dev_ = nullptr;     // device copy of the tiles of a prompt chunk          // false: attention sees every key (bidirectional_tokens)
+  float* ffn_scales_ = nullptr; // device [layers][d]
+  float* audio_ = nullptr;      // device rows of generate_additive
+  size_t audio_cap_ = 0;
 };
 
 // A lone product layer for the op sweep (Dense::forward, gemm.rs:500-542).

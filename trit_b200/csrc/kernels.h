@@ -11,15 +11,25 @@ enum Epilogue : int { kEpOut = 0, kEpResid = 1, kEpSilu = 2 };
 
 cudaError_t launch_embed(const DTable& T, const int* ids, int m, float* x, float mult, cudaStream_t s);
 cudaError_t launch_scale(float* x, size_t n, float mult, cudaStream_t s);
+// RmsNorm (weights w; null: none) of m rows, times `scale` (null: none),
+// then the activation quantizer in groups of `group`.
 cudaError_t launch_norm_quant(const float* x, int m, int d, const float* w, float eps, int group, int half,
-                              int8_t* xq, float* xs, cudaStream_t s);
+                              int8_t* xq, float* xs, cudaStream_t s, const float* scale = nullptr);
 cudaError_t launch_gemv(const DMat& W, const int8_t* xq, const float* xs, int m, int mode, float* y, int ldy,
                         float resid_mult, cudaStream_t s);
 cudaError_t launch_qk_rope_append(float* qkv, int m, const DConfig& cfg, const float* q_norm, const float* k_norm,
                                   const float* rope, int rope_rows, const DCache& cache, const int* row_stream,
                                   const int* row_pos, int layer, cudaStream_t s);
-cudaError_t launch_attention(const float* qkv, int m, const DConfig& cfg, const DCache& cache, const int* row_stream,
-                             const int* row_pos, int layer, int max_tk, float* att, cudaStream_t s);
+// Attention of tiles of rows: tiles[b] = {first row, rows} of rows of one
+// stream at consecutive positions, at most rows_max rows a tile
+// (attention_tile_rows); tiles null: one row a block (ntiles rows).
+// all_keys > 0: every row sees keys [0, all_keys) (no causal mask).
+int attention_tile_rows(const DConfig& cfg, int tmax);
+cudaError_t launch_attention_rows(const float* qkv, const int2* tiles, int ntiles, int rows_max, const DConfig& cfg,
+                                  const DCache& cache, const int* row_stream, const int* row_pos, int layer,
+                                  int max_tk, float* att, cudaStream_t s, int all_keys = 0);
+// x[i] += a[i] for i < n.
+cudaError_t launch_add(float* x, const float* a, size_t n, cudaStream_t s);
 // RmsNorm of `nb` rows, the table product and each row's argmax. logits
 // ([nb][vocab]) may be null; best_* hold [nb][table_blocks(vocab)].
 cudaError_t launch_final(const float* x, int ldx, int nb, const float* norm_w, const DConfig& cfg, const DTable& T,

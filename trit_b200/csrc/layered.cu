@@ -39,7 +39,7 @@ __global__ void k_scale(float* x, size_t n, float mult) {
 // is the reference's to the bit.
 template <int G>
 __global__ void __launch_bounds__(256) k_norm_quant(const float* x, int d, const float* w, float eps, int half,
-                                                    int8_t* xq, float* xs) {
+                                                    int8_t* xq, float* xs, const float* sc) {
   extern __shared__ float rowv[];  // [d]
   int r = blockIdx.x;
   const float* row = x + (size_t)r * d;
@@ -57,6 +57,7 @@ __global__ void __launch_bounds__(256) k_norm_quant(const float* x, int d, const
     for (int i = 0; i < G / 32; ++i) {
       int kk = g * G + lane * (G / 32) + i;
       v[i] = w ? __fmul_rn(rowv[kk], __fmul_rn(inv, w[kk])) : rowv[kk];
+      if (sc) v[i] = __fmul_rn(v[i], sc[kk]);
     }
     float scale = warp_quantize_group<G>(v, xq + (size_t)r * d + g * G, half);
     if (lane == 0) xs[(size_t)r * groups + g] = scale;
@@ -246,29 +247,209 @@ __global__ void __launch_bounds__(256) k_qk_rope_append(float* qkv, int m, DConf
 }
 
 // ---------------------------------------------------------- attention ----
-// One block per (row, kv head): the exact attention of attention.cuh for
-// the kv head's query heads, over the row's stream's keys 0..pos.
-constexpr int ATT_KT = 64;
+// Attention of a tile of rows of one stream at consecutive positions (a
+// prompt chunk; a decode step is a tile of one row), every row and query
+// head in the reference's order as Attention::run computes it: row i of the
+// tile (position p0 + i) sees keys [0, p0 + i + 1), or [0, all_keys) when
+// all_keys > 0 (no causal mask). Keys and values are staged once for all
+// the tile's rows, 128 at a time. Scores: a thread keeps a QB x 4 block of
+// (query head, key) chains, each an fma chain over the head dimension in
+// order (keys a quarter tile apart); outputs: a thread keeps 8 (query head, dimension) chains, each an
+// fma chain over the keys in order. The scores of the tile's RQ query heads
+// stay in shared memory, [RQ][tmax]. tiles[b] = {first row, rows}, or
+// null for one row per block.
+constexpr int AR_KT = 128;  // keys staged at a time
 
-__global__ void __launch_bounds__(256) k_attention(const float* qkv, int m, DConfig cfg, DCache cache,
-                                                   const int* row_stream, const int* row_pos, int layer, int tmax,
-                                                   float* att) {
+template <int QB>
+__global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const int2* tiles, DConfig cfg, DCache cache,
+                                                        const int* row_stream, const int* row_pos, int layer, int tmax,
+                                                        int all_keys, float* att) {
   extern __shared__ __align__(16) float sm[];
-  const int r = blockIdx.x, kvh = blockIdx.y, t = threadIdx.x;
+  const int kvh = blockIdx.y, t = threadIdx.x;
+  const int2 tile = tiles ? tiles[blockIdx.x] : make_int2(blockIdx.x, 1);
+  const int r0 = tile.x, R = tile.y;
   const int qpk = cfg.heads / cfg.kv_heads, qd = cfg.heads * 128, stride = qd + 2 * cfg.kv_heads * 128;
-  const int row = cache.f16 ? 64 : 128;
-  float* q = sm;
-  float* out = q + qpk * 128;
-  float* sc = out + qpk * 128;
-  float* ktl = sc + qpk * tmax;
-  float* vtl = ktl + ATT_KT * (row + 4);
-  float* stat = vtl + ATT_KT * row;
-  Attention<256> A{cache, cfg, row_stream[r], layer, kvh, qpk, ATT_KT, sc, ktl, vtl, stat, tmax};
+  const int RQ = R * qpk;
+  const bool f16 = cache.f16;
+  const int pitch = 132;                      // floats a staged row (f32 rows; f16 rows use half of it)
+  float* q = sm;                              // [RQ][128]
+  float* sc = q + RQ * 128;                   // [RQ][tmax]
+  float* kv = sc + (size_t)RQ * tmax;         // [AR_KT][pitch]
+  float* inv = kv + AR_KT * pitch;            // [RQ]
+  const int stream = row_stream[r0];
+  const int p0 = row_pos[r0];
+  const int T = all_keys > 0 ? all_keys : p0 + R;  // keys the last row sees
+  auto visible = [&](int qh) { return all_keys > 0 ? all_keys : p0 + qh / qpk + 1; };
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
-  for (int p = t; p < qpk * 128; p += 256) q[p] = __fmul_rn(qkv[(size_t)r * stride + kvh * qpk * 128 + p], scale);
+  for (int i = t; i < RQ * 128; i += 256) {
+    int qh = i / 128, e = i % 128, r = qh / qpk, h = qh % qpk;
+    q[i] = __fmul_rn(qkv[(size_t)(r0 + r) * stride + (kvh * qpk + h) * 128 + e], scale);
+  }
+  // Keys (which 0) or values (1) [j0, j0 + n) into kv, row pitch `pitch` floats.
+  auto stage = [&](int which, int j0, int n) {
+    const int cpr = f16 ? 16 : 32;  // 16-byte chunks a row
+    for (int ci = t; ci < n * cpr; ci += 256) {
+      int jj = ci / cpr, cc = ci % cpr, j = j0 + jj;
+      int page = cache.page_table[(size_t)stream * cache.pages_per_stream + j / cache.page_tokens];
+      size_t off = kv_offset(cache, cfg, page, layer, which, kvh, j % cache.page_tokens);
+      const int4* src = f16 ? (const int4*)((const __half*)cache.pool + off) : (const int4*)((const float*)cache.pool + off);
+      cp_async16(kv + jj * pitch + cc * 4, src + cc);
+    }
+    cp_commit();
+    cp_wait_all();
+    __syncthreads();
+  };
+  // Four consecutive dimensions of a staged row as floats.
+  auto row4 = [&](int jj, int e) -> float4 {
+    if (f16) {
+      uint2 raw = *(const uint2*)((const __half*)(kv + jj * pitch) + e);
+      float2 a = __half22float2(*(const __half2*)&raw.x), b = __half22float2(*(const __half2*)&raw.y);
+      return make_float4(a.x, a.y, b.x, b.y);
+    }
+    return *(const float4*)(kv + jj * pitch + e);
+  };
+  // Scores.
+  for (int j0 = 0; j0 < T; j0 += AR_KT) {
+    const int n = min(AR_KT, T - j0);
+    __syncthreads();
+    stage(0, j0, n);
+    const int kg = (n + 3) / 4, items = ((RQ + QB - 1) / QB) * kg;
+    for (int it = t; it < items; it += 256) {
+      // Keys jb, jb + kg, jb + 2 kg, jb + 3 kg: neighbouring threads read
+      // neighbouring staged rows (no shared-memory bank conflicts).
+      const int qb = it / kg, jb = it % kg;
+      float acc[QB][4];
+#pragma unroll
+      for (int a = 0; a < QB; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
+      for (int e = 0; e < 128; e += 4) {
+        float4 kk[4], qq[QB];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) kk[b] = row4(min(jb + b * kg, n - 1), e);
+#pragma unroll
+        for (int a = 0; a < QB; ++a) qq[a] = *(const float4*)(q + min(qb * QB + a, RQ - 1) * 128 + e);
+#pragma unroll
+        for (int a = 0; a < QB; ++a)
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            acc[a][b] = __fmaf_rn(qq[a].x, kk[b].x, acc[a][b]);
+            acc[a][b] = __fmaf_rn(qq[a].y, kk[b].y, acc[a][b]);
+            acc[a][b] = __fmaf_rn(qq[a].z, kk[b].z, acc[a][b]);
+            acc[a][b] = __fmaf_rn(qq[a].w, kk[b].w, acc[a][b]);
+          }
+      }
+#pragma unroll
+      for (int a = 0; a < QB; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int qh = qb * QB + a, jj = jb + b * kg, j = j0 + jj;
+          if (qh < RQ && jj < n && j < visible(qh)) sc[(size_t)qh * tmax + j] = acc[a][b];
+        }
+    }
+  }
   __syncthreads();
-  A.run(q, row_pos[r] + 1, nullptr, nullptr, false, out);
-  for (int p = t; p < qpk * 128; p += 256) att[(size_t)r * qd + kvh * qpk * 128 + p] = out[p];
+  // Max, exp, the sum in key order, the probabilities: a warp per query head.
+  const int warp = t >> 5, lane = t & 31;
+  for (int qh = warp; qh < RQ; qh += 8) {
+    const int vis = visible(qh);
+    float* srow = sc + (size_t)qh * tmax;
+    float mx = -INFINITY;
+    for (int j = lane; j < vis; j += 32) mx = fmaxf(mx, srow[j]);
+    mx = warp_max(mx);
+    for (int j = lane; j < vis; j += 32) srow[j] = cephes_exp(__fsub_rn(srow[j], mx));
+    __syncwarp();
+    if (lane == 0) {
+      float sum = 0.0f;
+      for (int j = 0; j < vis; ++j) sum = __fadd_rn(sum, srow[j]);
+      inv[qh] = __fdiv_rn(1.0f, sum);
+    }
+    __syncwarp();
+    const float iv = inv[qh];
+    for (int j = lane; j < vis; j += 32) srow[j] = __fmul_rn(srow[j], iv);
+  }
+  // Values: a thread keeps 8 chains (one query head, 8 dimensions).
+  const int items = RQ * 16;
+  constexpr int MAXI = 64 * 16 / 256;  // items a thread (RQ <= 64)
+  float acc[MAXI][8];
+#pragma unroll
+  for (int u = 0; u < MAXI; ++u)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[u][c] = 0.0f;
+  for (int j0 = 0; j0 < T; j0 += AR_KT) {
+    const int n = min(AR_KT, T - j0);
+    __syncthreads();
+    stage(1, j0, n);
+#pragma unroll
+    for (int u = 0; u < MAXI; ++u) {
+      const int it = t + u * 256;
+      if (it < items) {
+        const int qh = it / 16, e = (it % 16) * 8;
+        const int lim = min(n, visible(qh) - j0);
+        const float* pr = sc + (size_t)qh * tmax + j0;
+        for (int jj = 0; jj < lim; ++jj) {
+          const float p = pr[jj];
+          const float4 v0 = row4(jj, e), v1 = row4(jj, e + 4);
+          acc[u][0] = __fmaf_rn(p, v0.x, acc[u][0]);
+          acc[u][1] = __fmaf_rn(p, v0.y, acc[u][1]);
+          acc[u][2] = __fmaf_rn(p, v0.z, acc[u][2]);
+          acc[u][3] = __fmaf_rn(p, v0.w, acc[u][3]);
+          acc[u][4] = __fmaf_rn(p, v1.x, acc[u][4]);
+          acc[u][5] = __fmaf_rn(p, v1.y, acc[u][5]);
+          acc[u][6] = __fmaf_rn(p, v1.z, acc[u][6]);
+          acc[u][7] = __fmaf_rn(p, v1.w, acc[u][7]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < MAXI; ++u) {
+    const int it = t + u * 256;
+    if (it < items) {
+      const int qh = it / 16, e = (it % 16) * 8, r = qh / qpk, h = qh % qpk;
+      float* dst = att + (size_t)(r0 + r) * qd + (kvh * qpk + h) * 128 + e;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) dst[c] = acc[u][c];
+    }
+  }
+}
+
+int attention_tile_rows(const DConfig& cfg, int tmax) {
+  // Scores of R rows x qpk heads x tmax keys within ~110 KB, at most 64
+  // query heads a block, and whole groups of 4 query heads.
+  const int qpk = cfg.heads / cfg.kv_heads;
+  long cap = 28160L / ((long)qpk * std::max(tmax, 1));
+  int r = (int)std::min<long>(std::min<long>(16, cap), 64 / std::max(qpk, 1));
+  if (r * qpk >= 16) r = r / (4 / std::__gcd(qpk, 4)) * (4 / std::__gcd(qpk, 4));
+  return std::max(r, 1);
+}
+
+cudaError_t launch_attention_rows(const float* qkv, const int2* tiles, int ntiles, int rows_max, const DConfig& cfg,
+                                  const DCache& cache, const int* row_stream, const int* row_pos, int layer,
+                                  int max_tk, float* att, cudaStream_t s, int all_keys) {
+  const int qpk = cfg.heads / cfg.kv_heads;
+  const int RQ = rows_max * qpk;
+  if (RQ > 64 || all_keys > max_tk) return cudaErrorInvalidValue;
+  const int tmax = (max_tk + 3) / 4 * 4;
+  size_t smem = ((size_t)RQ * 128 + (size_t)RQ * tmax + (size_t)AR_KT * 132 + RQ) * 4;
+  if (smem > 220 * 1024) return cudaErrorInvalidValue;
+  // Blocks of 4 query heads for tiles of 16 or more query heads.
+  const bool quad = tiles && RQ >= 16;
+  static bool configured[64][2] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev][quad]) {
+    cudaFuncSetAttribute(quad ? k_attention_rows<4> : k_attention_rows<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         220 * 1024);
+    configured[dev][quad] = true;
+  }
+  if (quad)
+    k_attention_rows<4><<<dim3(ntiles, cfg.kv_heads), 256, smem, s>>>(qkv, tiles, cfg, cache, row_stream, row_pos,
+                                                                      layer, tmax, all_keys, att);
+  else
+    k_attention_rows<1><<<dim3(ntiles, cfg.kv_heads), 256, smem, s>>>(qkv, tiles, cfg, cache, row_stream, row_pos,
+                                                                      layer, tmax, all_keys, att);
+  return cudaGetLastError();
 }
 
 // ------------------------------------------------ final norm + table ----
@@ -389,6 +570,12 @@ __global__ void k_argmax(const float* val, const int* idx, int n, int* token) {
   if (threadIdx.x == 0) token[blockIdx.x] = (i == 0x7fffffff) ? 0 : i;
 }
 
+// add_into (src/layers.rs): x[i] = x[i] + a[i].
+__global__ void k_add(float* x, const float* a, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    x[i] = __fadd_rn(x[i], a[i]);
+}
+
 // The bookkeeping between two greedy steps of a batch (one block).
 __global__ void k_batch_advance(const int* cur, int* pos, int* step, int* tokens, int streams, int advance_pos) {
   const int at = *step;
@@ -420,6 +607,12 @@ cudaError_t launch_batch_advance(const int* cur, int* pos, int* step, int* token
   return cudaSuccess;
 }
 
+cudaError_t launch_add(float* x, const float* a, size_t n, cudaStream_t s) {
+  k_add<<<(unsigned)std::min<size_t>((n + 255) / 256, 4096), 256, 0, s>>>(x, a, n);
+  LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
 cudaError_t launch_scale(float* x, size_t n, float mult, cudaStream_t s) {
   k_scale<<<(unsigned)std::min<size_t>((n + 255) / 256, 4096), 256, 0, s>>>(x, n, mult);
   LAUNCH_CHECK();
@@ -427,11 +620,11 @@ cudaError_t launch_scale(float* x, size_t n, float mult, cudaStream_t s) {
 }
 
 cudaError_t launch_norm_quant(const float* x, int m, int d, const float* w, float eps, int group, int half,
-                              int8_t* xq, float* xs, cudaStream_t s) {
+                              int8_t* xq, float* xs, cudaStream_t s, const float* scale) {
   size_t smem = (size_t)d * 4;
   if (smem > 48 * 1024) return cudaErrorInvalidValue;  // d <= 12288
-  if (group == 32) k_norm_quant<32><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs);
-  else k_norm_quant<128><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs);
+  if (group == 32) k_norm_quant<32><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs, scale);
+  else k_norm_quant<128><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs, scale);
   LAUNCH_CHECK();
   return cudaSuccess;
 }
@@ -464,24 +657,6 @@ cudaError_t launch_qk_rope_append(float* qkv, int m, const DConfig& cfg, const f
   return cudaSuccess;
 }
 
-cudaError_t launch_attention(const float* qkv, int m, const DConfig& cfg, const DCache& cache, const int* row_stream,
-                             const int* row_pos, int layer, int max_tk, float* att, cudaStream_t s) {
-  const int qpk = cfg.heads / cfg.kv_heads;
-  if (qpk * 128 > 4 * 256) return cudaErrorInvalidValue;
-  const int tmax = (max_tk + 3) / 4 * 4;
-  size_t smem = ((size_t)2 * qpk * 128 + attention_smem_floats(qpk, tmax, ATT_KT, cache.f16)) * 4;
-  if (smem > 220 * 1024) return cudaErrorInvalidValue;
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-    configured[dev] = true;
-  }
-  k_attention<<<dim3(m, cfg.kv_heads), 256, smem, s>>>(qkv, m, cfg, cache, row_stream, row_pos, layer, tmax, att);
-  LAUNCH_CHECK();
-  return cudaSuccess;
-}
 
 // Final RmsNorm of `nb` rows (row stride `ldx`), then the table and the
 // argmax of every row: token[b].

@@ -17,8 +17,12 @@
 //              one of two TMEM accumulators and commits it to an mbarrier:
 //              a 32-value group (Q8_0) is one MMA, a 128-value group
 //              (per-row int8, ternary) four MMAs into the same accumulator;
-//   warps 2-5  epilogue: per group, load the 128 x 64 i32 accumulator from
-//              TMEM, free it, and fold it into 64 f32 chains per thread.
+//   warps 2-9  epilogue: per group, load the 128 x 64 i32 accumulator from
+//              TMEM (warp w: lanes 32 (w % 4).., columns 32 ((w - 2) / 4)..),
+//              free it, and fold it into 32 f32 chains per thread with
+//              packed f32x2 arithmetic (each lane rounds as the scalar
+//              instruction does). A dot (|dot| < 2^22) becomes a float
+//              exactly through the 1.5 * 2^23 bias.
 // Every wait is bounded in time; a wait that runs out sets the kernel's
 // status, the CTA waits (bounded) for its copies and MMAs in flight, frees
 // its TMEM and returns.
@@ -38,7 +42,8 @@ constexpr int TC_N = 64;
 constexpr int TC_KT = 128;  // K bytes a stage (four MMA steps of K = 32)
 constexpr int TC_STAGES = 4;
 constexpr int TC_BUFS = 2;
-constexpr int TC_THREADS = 192;
+constexpr int TC_EPI_WARPS = 8;   // two per TMEM lane quarter, 32 columns each
+constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
 constexpr int A_STAGE = TC_M * TC_KT;  // 16 KB
 constexpr int B_STAGE = TC_N * TC_KT;  // 8 KB
 constexpr int TC_TMEM_COLS = TC_BUFS * TC_N;  // 128 (a power of two >= 32)
@@ -139,6 +144,36 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : TC_R8(0), TC_R8(8), TC_R8(16), TC_R8(24)
       : "r"(taddr));
 }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+// Two i32 dots as exact floats: 1.5 * 2^23 + dot has ulp 1 for |dot| < 2^22.
+__device__ __forceinline__ float2 dots_to_float2(uint32_t a, uint32_t b) {
+  return add2(make_float2(__int_as_float(0x4B400000 + (int)a), __int_as_float(0x4B400000 + (int)b)),
+              make_float2(-12582912.0f, -12582912.0f));
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 struct TcSmem {
@@ -157,7 +192,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint8_t* a_st = base;
   uint8_t* b_st = a_st + TC_STAGES * A_STAGE;
   const int G = W.agroup, groups = W.k / G;
-  float* xs_s = (float*)(b_st + TC_STAGES * B_STAGE);  // [TC_N][groups]
+  float* xs_s = (float*)(b_st + TC_STAGES * B_STAGE);  // [groups][TC_N]
   TcSmem* S = (TcSmem*)(xs_s + TC_N * groups);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * TC_M, f0 = blockIdx.y * TC_N;
@@ -171,7 +206,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int b = 0; b < TC_BUFS; ++b) {
       mbar_init(&S->tfull[b], 1);
-      mbar_init(&S->tempty[b], 128);
+      mbar_init(&S->tempty[b], 32 * TC_EPI_WARPS);
     }
     mbar_init(&S->drain, 1);
     S->abort = 0;
@@ -183,9 +218,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // The frames' activation scales, [frame][group] (rows past m read as 0).
+  // The frames' activation scales, [group][frame] (rows past m read as 0).
   for (int i = threadIdx.x; i < TC_N * groups; i += TC_THREADS) {
-    int f = i / groups, g = i % groups;
+    int g = i / TC_N, f = i % TC_N;
     xs_s[i] = (f0 + f < m) ? xs[(size_t)(f0 + f) * groups + g] : 0.0f;
   }
   fence_before();
@@ -247,45 +282,58 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
   } else {
-    // Epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31.
-    const int quarter = warp & 3;
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
     const int lr = quarter * 32 + lane;
     const int row = n0 + lr;
     const bool live = row < W.n;
-    float acc[TC_N];
+    float2 acc[16];  // frames 32 half + 2 i, + 1
 #pragma unroll
-    for (int j = 0; j < TC_N; ++j) acc[j] = 0.0f;
+    for (int i = 0; i < 16; ++i) acc[i] = make_float2(0.0f, 0.0f);
+    // Weight scales 8 groups ahead, so their loads overlap the MMAs.
+    float wcur[8], wnxt[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) wcur[i] = (live && i < groups) ? weight_scale(W, row, i) : 0.0f;
     bool ok = true;
-    for (int g = 0; g < groups; ++g) {
-      const int b = g % TC_BUFS;
-      const float ws = live ? weight_scale(W, row, g) : 0.0f;
-      if (!mbar_wait(&S->tfull[b], (g / TC_BUFS) & 1, abort)) {
-        ok = false;
-        break;
+    for (int gc = 0; gc < groups && ok; gc += 8) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wnxt[i] = (live && gc + 8 + i < groups) ? weight_scale(W, row, gc + 8 + i) : 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int g = gc + i;
+        if (g >= groups) break;
+        const int b = g % TC_BUFS;
+        if (!mbar_wait(&S->tfull[b], (g / TC_BUFS) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + b * TC_N + half * 32, r);
+        tmem_wait_ld();
+        fence_before();
+        mbar_arrive(&S->tempty[b]);
+        const float2 ws2 = make_float2(wcur[i], wcur[i]);
+        const float4* xg = (const float4*)(xs_s + g * TC_N + half * 32);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 xv = xg[q];
+          acc[2 * q] = fma2(dots_to_float2(r[4 * q], r[4 * q + 1]), mul2(ws2, make_float2(xv.x, xv.y)), acc[2 * q]);
+          acc[2 * q + 1] =
+              fma2(dots_to_float2(r[4 * q + 2], r[4 * q + 3]), mul2(ws2, make_float2(xv.z, xv.w)), acc[2 * q + 1]);
+        }
       }
-      fence_after();
-      uint32_t r0[32], r1[32];
-      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + b * TC_N;
-      tmem_ld32(taddr, r0);
-      tmem_ld32(taddr + 32, r1);
-      tmem_wait_ld();
-      fence_before();
-      mbar_arrive(&S->tempty[b]);
-      const float* xg = xs_s + g;
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        acc[j] = __fmaf_rn(__int2float_rn((int)r0[j]), __fmul_rn(ws, xg[j * groups]), acc[j]);
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        acc[32 + j] = __fmaf_rn(__int2float_rn((int)r1[j]), __fmul_rn(ws, xg[(32 + j) * groups]), acc[32 + j]);
+      for (int i = 0; i < 8; ++i) wcur[i] = wnxt[i];
     }
     if (ok && live) {
 #pragma unroll
-      for (int j = 0; j < TC_N; ++j) {
-        if (f0 + j < m) {
-          float* p = y + (size_t)(f0 + j) * ldy + row;
-          if (mode == kEpOut) *p = acc[j];
-          else *p = (resid_mult == 1.0f) ? __fadd_rn(*p, acc[j]) : __fadd_rn(*p, __fmul_rn(resid_mult, acc[j]));
+      for (int j = 0; j < 32; ++j) {
+        const int f = f0 + half * 32 + j;
+        const float v = (j & 1) ? acc[j >> 1].y : acc[j >> 1].x;
+        if (f < m) {
+          float* p = y + (size_t)f * ldy + row;
+          if (mode == kEpOut) *p = v;
+          else *p = (resid_mult == 1.0f) ? __fadd_rn(*p, v) : __fadd_rn(*p, __fmul_rn(resid_mult, v));
         }
       }
     }

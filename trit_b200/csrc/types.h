@@ -37,6 +37,7 @@ struct DLayer {
   const float* q_norm = nullptr;  // null: no qk norm (llama, mistral, granite)
   const float* k_norm = nullptr;
   const float* norm_mlp = nullptr;
+  const float* ffn_scale = nullptr;  // set_ffn_scales: the normed MLP input times this [d], or null
   DMat qkv, out, gate_up, down;
 };
 

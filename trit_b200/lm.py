@@ -67,6 +67,10 @@ def library() -> ctypes.CDLL:
                                                   ctypes.POINTER(_size), ctypes.c_int32, _i32p, _size, _i32p,
                                                   _i64p]),
         "trit_lm_last_timing": (ctypes.c_int, [ctypes.c_void_p, _f64p, _f64p, _i64p, _i64p]),
+        "trit_lm_set_ffn_scales": (ctypes.c_int, [ctypes.c_void_p, _f32p, _size, _size]),
+        "trit_lm_generate_additive": (ctypes.c_int64, [ctypes.c_void_p, _i32p, _size, _f32p, _size, _i32p, _size,
+                                                       _i32p, _size]),
+        "trit_lm_bidirectional_tokens": (ctypes.c_int64, [ctypes.c_void_p, _f32p, _size, _size, _i32p]),
         "trit_dense_q8_0": (ctypes.c_void_p, [ctypes.c_void_p, _size, _size, ctypes.c_int, ctypes.c_int]),
         "trit_dense_forward": (ctypes.c_int, [ctypes.c_void_p, _f32p, _size, _f32p]),
         "trit_dense_forward_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, _size, ctypes.c_void_p,
@@ -241,6 +245,36 @@ class CausalLm:
         if rc != 0:
             raise _error()
         return [out[s, :counts[s]].tolist() for s in range(len(arrays))]
+
+    def set_ffn_scales(self, scales: np.ndarray | None) -> None:
+        """CausalLm::set_ffn_scales (causal_lm.rs:305-307): [layers][width], or None."""
+        if scales is None:
+            rc = library().trit_lm_set_ffn_scales(self._handle, None, 0, 0)
+        else:
+            s = np.ascontiguousarray(scales, dtype=np.float32)
+            rc = library().trit_lm_set_ffn_scales(self._handle, _ptr(s, _f32p), s.shape[0], s.shape[1])
+        if rc != 0:
+            raise _error()
+
+    def generate_additive(self, prompt: Sequence[int], audio: np.ndarray, stop: Sequence[int] = ()) -> list[int]:
+        """CausalLm::generate_additive (causal_lm.rs:317-345)."""
+        ids, st = _ids(prompt), _ids(stop)
+        a = np.ascontiguousarray(audio, dtype=np.float32).reshape(-1, self.width())
+        out = np.zeros(max(a.shape[0] - ids.size + 1, 1), dtype=np.int32)
+        n = library().trit_lm_generate_additive(self._handle, _ptr(ids, _i32p), ids.size, _ptr(a, _f32p), a.shape[0],
+                                                _ptr(st, _i32p), st.size, _ptr(out, _i32p), out.size)
+        if n < 0:
+            raise _error()
+        return out[:n].tolist()
+
+    def bidirectional_tokens(self, rows: np.ndarray, start: int) -> list[int]:
+        """CausalLm::bidirectional_tokens (causal_lm.rs:393-408)."""
+        r = np.ascontiguousarray(rows, dtype=np.float32).reshape(-1, self.width())
+        out = np.zeros(max(r.shape[0] - start, 1), dtype=np.int32)
+        n = library().trit_lm_bidirectional_tokens(self._handle, _ptr(r, _f32p), r.shape[0], start, _ptr(out, _i32p))
+        if n < 0:
+            raise _error()
+        return out[:n].tolist()
 
     def last_timing(self) -> dict:
         """Device time of the last generation (CUDA events)."""
