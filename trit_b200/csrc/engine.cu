@@ -244,6 +244,49 @@ Lm::Lm(const std::string& dir, const Options& o) : opt_(o) {
 
 Lm::~Lm() { release(); }
 
+// TRIT_KERNEL_CLOCK=1: CUDA events between the steps of hidden() and the
+// table; report() prints each step's total device time to stderr (a
+// measurement aid; the batched decode then runs without its graph).
+KernelClock::KernelClock() {
+  const char* v = getenv("TRIT_KERNEL_CLOCK");
+  on = v && *v == '1';
+}
+KernelClock::~KernelClock() {
+  for (auto& e : pool) cudaEventDestroy(e);
+}
+void KernelClock::mark(const char* name, cudaStream_t s) {
+  if (!on) return;
+  if (used == pool.size()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return;
+    pool.push_back(e);
+  }
+  cudaEventRecord(pool[used], s);
+  names.push_back(name);
+  ++used;
+}
+void KernelClock::report(const char* what) {
+  if (!on || used < 2) {
+    used = 0;
+    names.clear();
+    return;
+  }
+  cudaEventSynchronize(pool[used - 1]);
+  std::map<std::string, double> total;
+  double all = 0;
+  for (size_t i = 0; i + 1 < used; ++i) {
+    if (!names[i]) continue;
+    float ms = 0;
+    cudaEventElapsedTime(&ms, pool[i], pool[i + 1]);
+    total[names[i]] += ms;
+    all += ms;
+  }
+  fprintf(stderr, "kernel clock (%s): %.3f ms in marked steps\n", what, all);
+  for (auto& kv : total) fprintf(stderr, "  %-26s %9.3f ms  %5.1f%%\n", kv.first.c_str(), kv.second, 100 * kv.second / all);
+  used = 0;
+  names.clear();
+}
+
 // Frees every device and pinned buffer; safe to call twice.
 void Lm::release() {
   cudaSetDevice(opt_.device);
@@ -428,23 +471,34 @@ void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* tiles
   if (cfg_.embedding_multiplier != 1.0f) TRIT_CUDA(launch_scale(x_, (size_t)m * d, cfg_.embedding_multiplier, s));
   for (int l = 0; l < cfg_.layers; ++l) {
     const DLayer& L = layers_[l];
+    clock_.mark("norm+quant", s);
     TRIT_CUDA(launch_norm_quant(x_, m, d, L.norm_attn, cfg_.eps, L.qkv.agroup, L.qkv.half, xq_, xs_, s));
+    clock_.mark("qkv", s);
     product(l, 0, L.qkv, tc_x_[0], kEpOut, qkv_, qd + 2 * kvd, 1.0f);
+    clock_.mark("qk norm+rope+append", s);
     TRIT_CUDA(launch_qk_rope_append(qkv_, m, cfg_, L.q_norm, L.k_norm, rope_, opt_.max_context, cache_, row_stream_,
                                     row_pos_, l, s));
+    clock_.mark("attention", s);
     if (ntiles)
       TRIT_CUDA(launch_attention_rows(qkv_, (const int2*)tiles_dev_, ntiles, rows_max, cfg_, cache_, row_stream_,
                                       row_pos_, l, max_tk, att_, s));
     else
       TRIT_CUDA(launch_attention_rows(qkv_, nullptr, m, 1, cfg_, cache_, row_stream_, row_pos_, l, max_tk, att_, s,
                                       causal_ ? 0 : max_tk));
+    clock_.mark("norm+quant", s);
     TRIT_CUDA(launch_norm_quant(att_, m, qd, nullptr, cfg_.eps, L.out.agroup, L.out.half, xq_, xs_, s));
+    clock_.mark("o", s);
     product(l, 1, L.out, tc_x_[1], kEpResid, x_, d, cfg_.residual_multiplier);
+    clock_.mark("norm+quant", s);
     TRIT_CUDA(launch_norm_quant(x_, m, d, L.norm_mlp, cfg_.eps, L.gate_up.agroup, L.gate_up.half, xq_, xs_, s,
                                 L.ffn_scale));
+    clock_.mark("gate_up", s);
     product(l, 2, L.gate_up, tc_x_[0], kEpSilu, h_, cfg_.ffn, 1.0f);
+    clock_.mark("norm+quant", s);
     TRIT_CUDA(launch_norm_quant(h_, m, cfg_.ffn, nullptr, cfg_.eps, L.down.agroup, L.down.half, xq_, xs_, s));
+    clock_.mark("down", s);
     product(l, 3, L.down, tc_x_[2], kEpResid, x_, d, cfg_.residual_multiplier);
+    clock_.mark(nullptr, s);
   }
   timing_.gpu_launches += cfg_.layers * 10 + (cfg_.embedding_multiplier != 1.0f ? 1 : 0);
 }
@@ -765,6 +819,7 @@ std::vector<int> Lm::answer(const int* head, size_t nhead, const float* audio, s
 // the last kept token changes no output and is not run.
 std::vector<int> Lm::finish(int slot, int position, int max_new, const int* stop, size_t nstop, float* logits) {
   std::vector<int> out;
+  clock_.report("prefill");
   if (max_new <= 0) {
     TRIT_CUDA(cudaStreamSynchronize(stream_));
     check_tc_status();
@@ -790,6 +845,7 @@ std::vector<int> Lm::finish(int slot, int position, int max_new, const int* stop
     else decode_layered(slot, position, steps, logits);
   }
   TRIT_CUDA(cudaEventRecord(ev_[2], stream_));
+  clock_.report("generate");
   std::vector<int> toks(max_new);
   TRIT_CUDA(cudaMemcpyAsync(toks.data(), tokens_, (size_t)max_new * 4, cudaMemcpyDeviceToHost, stream_));
   TRIT_CUDA(cudaStreamSynchronize(stream_));
@@ -1087,6 +1143,7 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
   }
   // The first token of every stream, then the decode state: stream s sits
   // in slot s at position lens[s] with its last token in batch_cur_.
+  clock_.report("batch prefill");
   TRIT_CUDA(cudaStreamSynchronize(stream_));
   for (size_t i = 0; i < S; ++i) {
     hs[i] = (int)i;
@@ -1107,15 +1164,19 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
     int before = timing_.gpu_launches;
     TRIT_CUDA(launch_embed(embed_, batch_cur_, (int)S, x_, 1.0f, stream_));
     hidden((int)S, tmax);
+    clock_.mark("final norm+table+argmax", stream_);
     TRIT_CUDA(launch_final(x_, d, (int)S, final_norm_, cfg_, head_, xn_, nullptr, best_val_, best_idx_, batch_cur_,
                            stream_));
+    clock_.mark(nullptr, stream_);
     TRIT_CUDA(launch_batch_advance(batch_cur_, row_pos_, batch_step_, batch_tok_, (int)S, 1, stream_));
     timing_.gpu_launches += 1 + 3 + 1;
     per_step = timing_.gpu_launches - before;
   };
   if (steps > 0) {
     step();  // eagerly once: sets up every kernel's attributes before a capture
-    if (steps > 1) {
+    if (steps > 1 && clock_.on) {
+      for (int i = 1; i < steps; ++i) step();  // per-kernel clocks: no graph
+    } else if (steps > 1) {
       if (!batch_graph_ || batch_graph_streams_ != (int)S || batch_graph_tmax_ < tmax) {
         if (batch_graph_) cudaGraphExecDestroy(batch_graph_);
         batch_graph_ = nullptr;
@@ -1142,6 +1203,7 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
     }
   }
   TRIT_CUDA(cudaEventRecord(ev_[2], stream_));
+  clock_.report("generate_batch");
   std::vector<int> toks((size_t)max_new * S);
   TRIT_CUDA(cudaMemcpyAsync(toks.data(), batch_tok_, toks.size() * 4, cudaMemcpyDeviceToHost, stream_));
   TRIT_CUDA(cudaStreamSynchronize(stream_));

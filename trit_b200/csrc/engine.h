@@ -52,6 +52,18 @@ struct Timing {
   int gpu_launches = 0;
 };
 
+// Device time per step kind (TRIT_KERNEL_CLOCK=1), a measurement aid.
+struct KernelClock {
+  bool on = false;
+  std::vector<cudaEvent_t> pool;
+  std::vector<const char*> names;  // the step that starts at each mark (null: none)
+  size_t used = 0;
+  KernelClock();
+  ~KernelClock();
+  void mark(const char* name, cudaStream_t s);
+  void report(const char* what);
+};
+
 class Lm {
  public:
   Lm(const std::string& dir, const Options& o);
@@ -172,6 +184,7 @@ class Lm {
   float* gu_ = nullptr;         // [rows][2 ffn] gate|up products before silu * up
   int* tc_status_ = nullptr;
   bool causal_ = true;
+  KernelClock clock_;
   int* tiles_pinned_ = nullptr;  // pinned [rows_cap][2]
   int* tiles_dev_ = nullptr;     // device copy of the tiles of a prompt chunk          // false: attention sees every key (bidirectional_tokens)
   float* ffn_scales_ = nullptr; // device [layers][d]

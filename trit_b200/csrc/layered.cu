@@ -252,15 +252,15 @@ __global__ void __launch_bounds__(256) k_qk_rope_append(float* qkv, int m, DConf
 // head in the reference's order as Attention::run computes it: row i of the
 // tile (position p0 + i) sees keys [0, p0 + i + 1), or [0, all_keys) when
 // all_keys > 0 (no causal mask). Keys and values are staged once for all
-// the tile's rows, 128 at a time. Scores: a thread keeps a QB x 4 block of
+// the tile's rows, 128 at a time. Scores: a thread keeps a QB x KB block of
 // (query head, key) chains, each an fma chain over the head dimension in
-// order (keys a quarter tile apart); outputs: a thread keeps 8 (query head, dimension) chains, each an
+// order; outputs: a thread keeps DW (query head, dimension) chains, each an
 // fma chain over the keys in order. The scores of the tile's RQ query heads
 // stay in shared memory, [RQ][tmax]. tiles[b] = {first row, rows}, or
 // null for one row per block.
 constexpr int AR_KT = 128;  // keys staged at a time
 
-template <int QB>
+template <int QB, int KB, int DW>
 __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const int2* tiles, DConfig cfg, DCache cache,
                                                         const int* row_stream, const int* row_pos, int layer, int tmax,
                                                         int all_keys, float* att) {
@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
   const int qpk = cfg.heads / cfg.kv_heads, qd = cfg.heads * 128, stride = qd + 2 * cfg.kv_heads * 128;
   const int RQ = R * qpk;
   const bool f16 = cache.f16;
-  const int pitch = 132;                      // floats a staged row (f32 rows; f16 rows use half of it)
+  const int pitch = f16 ? 68 : 132;           // floats a staged row (16-byte aligned, banks staggered)
   float* q = sm;                              // [RQ][128]
   float* sc = q + RQ * 128;                   // [RQ][tmax]
   float* kv = sc + (size_t)RQ * tmax;         // [AR_KT][pitch]
@@ -299,57 +299,69 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
     cp_wait_all();
     __syncthreads();
   };
-  // Four consecutive dimensions of a staged row as floats.
-  auto row4 = [&](int jj, int e) -> float4 {
+  // Eight consecutive dimensions of a staged row as floats (one 16-byte
+  // load for f16 rows).
+  auto row8 = [&](int jj, int e, float (&o)[8]) {
     if (f16) {
-      uint2 raw = *(const uint2*)((const __half*)(kv + jj * pitch) + e);
-      float2 a = __half22float2(*(const __half2*)&raw.x), b = __half22float2(*(const __half2*)&raw.y);
-      return make_float4(a.x, a.y, b.x, b.y);
+      const uint4 raw = *(const uint4*)((const __half*)(kv + jj * pitch) + e);
+      const __half2* h = (const __half2*)&raw;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        o[2 * i] = f.x;
+        o[2 * i + 1] = f.y;
+      }
+    } else {
+      const float4 a = *(const float4*)(kv + jj * pitch + e), b = *(const float4*)(kv + jj * pitch + e + 4);
+      o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+      o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
     }
-    return *(const float4*)(kv + jj * pitch + e);
   };
   // Scores.
   for (int j0 = 0; j0 < T; j0 += AR_KT) {
     const int n = min(AR_KT, T - j0);
     __syncthreads();
     stage(0, j0, n);
-    const int kg = (n + 3) / 4, items = ((RQ + QB - 1) / QB) * kg;
+    const int kg = (n + KB - 1) / KB, items = ((RQ + QB - 1) / QB) * kg;
     for (int it = t; it < items; it += 256) {
-      // Keys jb, jb + kg, jb + 2 kg, jb + 3 kg: neighbouring threads read
-      // neighbouring staged rows (no shared-memory bank conflicts).
+      // Keys jb, jb + kg, ...: neighbouring threads read neighbouring
+      // staged rows (no shared-memory bank conflicts).
       const int qb = it / kg, jb = it % kg;
-      float acc[QB][4];
+      float acc[QB][KB];
 #pragma unroll
       for (int a = 0; a < QB; ++a)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
-      for (int e = 0; e < 128; e += 4) {
-        float4 kk[4], qq[QB];
+        for (int b = 0; b < KB; ++b) acc[a][b] = 0.0f;
+      for (int e = 0; e < 128; e += 8) {
+        float kk[KB][8], qq[QB][8];
 #pragma unroll
-        for (int b = 0; b < 4; ++b) kk[b] = row4(min(jb + b * kg, n - 1), e);
+        for (int b = 0; b < KB; ++b) row8(min(jb + b * kg, n - 1), e, kk[b]);
 #pragma unroll
-        for (int a = 0; a < QB; ++a) qq[a] = *(const float4*)(q + min(qb * QB + a, RQ - 1) * 128 + e);
+        for (int a = 0; a < QB; ++a) {
+          const float* qr = q + min(qb * QB + a, RQ - 1) * 128 + e;
+          const float4 lo = *(const float4*)qr, hi = *(const float4*)(qr + 4);
+          qq[a][0] = lo.x; qq[a][1] = lo.y; qq[a][2] = lo.z; qq[a][3] = lo.w;
+          qq[a][4] = hi.x; qq[a][5] = hi.y; qq[a][6] = hi.z; qq[a][7] = hi.w;
+        }
 #pragma unroll
         for (int a = 0; a < QB; ++a)
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            acc[a][b] = __fmaf_rn(qq[a].x, kk[b].x, acc[a][b]);
-            acc[a][b] = __fmaf_rn(qq[a].y, kk[b].y, acc[a][b]);
-            acc[a][b] = __fmaf_rn(qq[a].z, kk[b].z, acc[a][b]);
-            acc[a][b] = __fmaf_rn(qq[a].w, kk[b].w, acc[a][b]);
-          }
+          for (int b = 0; b < KB; ++b)
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc[a][b] = __fmaf_rn(qq[a][c], kk[b][c], acc[a][b]);
       }
 #pragma unroll
       for (int a = 0; a < QB; ++a)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
+        for (int b = 0; b < KB; ++b) {
           const int qh = qb * QB + a, jj = jb + b * kg, j = j0 + jj;
           if (qh < RQ && jj < n && j < visible(qh)) sc[(size_t)qh * tmax + j] = acc[a][b];
         }
     }
   }
   __syncthreads();
-  // Max, exp, the sum in key order, the probabilities: a warp per query head.
+  // Max and exp: a warp per query head; then the sums in key order, one
+  // thread per query head (all heads at once); then the probabilities.
   const int warp = t >> 5, lane = t & 31;
   for (int qh = warp; qh < RQ; qh += 8) {
     const int vis = visible(qh);
@@ -358,24 +370,31 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
     for (int j = lane; j < vis; j += 32) mx = fmaxf(mx, srow[j]);
     mx = warp_max(mx);
     for (int j = lane; j < vis; j += 32) srow[j] = cephes_exp(__fsub_rn(srow[j], mx));
-    __syncwarp();
-    if (lane == 0) {
-      float sum = 0.0f;
-      for (int j = 0; j < vis; ++j) sum = __fadd_rn(sum, srow[j]);
-      inv[qh] = __fdiv_rn(1.0f, sum);
-    }
-    __syncwarp();
+  }
+  __syncthreads();
+  if (t < RQ) {
+    const int vis = visible(t);
+    const float* srow = sc + (size_t)t * tmax;
+    float sum = 0.0f;
+    for (int j = 0; j < vis; ++j) sum = __fadd_rn(sum, srow[j]);
+    inv[t] = __fdiv_rn(1.0f, sum);
+  }
+  __syncthreads();
+  for (int qh = warp; qh < RQ; qh += 8) {
+    const int vis = visible(qh);
+    float* srow = sc + (size_t)qh * tmax;
     const float iv = inv[qh];
     for (int j = lane; j < vis; j += 32) srow[j] = __fmul_rn(srow[j], iv);
   }
-  // Values: a thread keeps 8 chains (one query head, 8 dimensions).
-  const int items = RQ * 16;
-  constexpr int MAXI = 64 * 16 / 256;  // items a thread (RQ <= 64)
-  float acc[MAXI][8];
+  // Values: a thread keeps DW chains (one query head, DW dimensions).
+  constexpr int PER_HEAD = 128 / DW;
+  const int items = RQ * PER_HEAD;
+  constexpr int MAXI = 64 * PER_HEAD / 256;  // items a thread (RQ <= 64)
+  float acc[MAXI][DW];
 #pragma unroll
   for (int u = 0; u < MAXI; ++u)
 #pragma unroll
-    for (int c = 0; c < 8; ++c) acc[u][c] = 0.0f;
+    for (int c = 0; c < DW; ++c) acc[u][c] = 0.0f;
   for (int j0 = 0; j0 < T; j0 += AR_KT) {
     const int n = min(AR_KT, T - j0);
     __syncthreads();
@@ -384,20 +403,28 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
     for (int u = 0; u < MAXI; ++u) {
       const int it = t + u * 256;
       if (it < items) {
-        const int qh = it / 16, e = (it % 16) * 8;
+        const int qh = it / PER_HEAD, e = (it % PER_HEAD) * DW;
         const int lim = min(n, visible(qh) - j0);
         const float* pr = sc + (size_t)qh * tmax + j0;
         for (int jj = 0; jj < lim; ++jj) {
           const float p = pr[jj];
-          const float4 v0 = row4(jj, e), v1 = row4(jj, e + 4);
-          acc[u][0] = __fmaf_rn(p, v0.x, acc[u][0]);
-          acc[u][1] = __fmaf_rn(p, v0.y, acc[u][1]);
-          acc[u][2] = __fmaf_rn(p, v0.z, acc[u][2]);
-          acc[u][3] = __fmaf_rn(p, v0.w, acc[u][3]);
-          acc[u][4] = __fmaf_rn(p, v1.x, acc[u][4]);
-          acc[u][5] = __fmaf_rn(p, v1.y, acc[u][5]);
-          acc[u][6] = __fmaf_rn(p, v1.z, acc[u][6]);
-          acc[u][7] = __fmaf_rn(p, v1.w, acc[u][7]);
+          float v[DW];
+          if (DW == 2) {
+            float2 f = f16 ? __half22float2(*((const __half2*)(kv + jj * pitch) + e / 2))
+                           : *(const float2*)(kv + jj * pitch + e);
+            v[0] = f.x;
+            v[DW - 1] = f.y;
+          } else {
+#pragma unroll
+            for (int c = 0; c < DW; c += 8) {
+              float f[8];
+              row8(jj, e + c, f);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) v[c + i] = f[i];
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < DW; ++c) acc[u][c] = __fmaf_rn(p, v[c], acc[u][c]);
         }
       }
     }
@@ -406,10 +433,10 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
   for (int u = 0; u < MAXI; ++u) {
     const int it = t + u * 256;
     if (it < items) {
-      const int qh = it / 16, e = (it % 16) * 8, r = qh / qpk, h = qh % qpk;
+      const int qh = it / PER_HEAD, e = (it % PER_HEAD) * DW, r = qh / qpk, h = qh % qpk;
       float* dst = att + (size_t)(r0 + r) * qd + (kvh * qpk + h) * 128 + e;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) dst[c] = acc[u][c];
+      for (int c = 0; c < DW; ++c) dst[c] = acc[u][c];
     }
   }
 }
@@ -431,7 +458,7 @@ cudaError_t launch_attention_rows(const float* qkv, const int2* tiles, int ntile
   const int RQ = rows_max * qpk;
   if (RQ > 64 || all_keys > max_tk) return cudaErrorInvalidValue;
   const int tmax = (max_tk + 3) / 4 * 4;
-  size_t smem = ((size_t)RQ * 128 + (size_t)RQ * tmax + (size_t)AR_KT * 132 + RQ) * 4;
+  size_t smem = ((size_t)RQ * 128 + (size_t)RQ * tmax + (size_t)AR_KT * (cache.f16 ? 68 : 132) + RQ) * 4;
   if (smem > 220 * 1024) return cudaErrorInvalidValue;
   // Blocks of 4 query heads for tiles of 16 or more query heads.
   const bool quad = tiles && RQ >= 16;
@@ -439,15 +466,15 @@ cudaError_t launch_attention_rows(const float* qkv, const int2* tiles, int ntile
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev][quad]) {
-    cudaFuncSetAttribute(quad ? k_attention_rows<4> : k_attention_rows<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         220 * 1024);
+    cudaFuncSetAttribute(quad ? k_attention_rows<4, 4, 8> : k_attention_rows<1, 2, 2>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
     configured[dev][quad] = true;
   }
   if (quad)
-    k_attention_rows<4><<<dim3(ntiles, cfg.kv_heads), 256, smem, s>>>(qkv, tiles, cfg, cache, row_stream, row_pos,
+    k_attention_rows<4, 4, 8><<<dim3(ntiles, cfg.kv_heads), 256, smem, s>>>(qkv, tiles, cfg, cache, row_stream, row_pos,
                                                                       layer, tmax, all_keys, att);
   else
-    k_attention_rows<1><<<dim3(ntiles, cfg.kv_heads), 256, smem, s>>>(qkv, tiles, cfg, cache, row_stream, row_pos,
+    k_attention_rows<1, 2, 2><<<dim3(ntiles, cfg.kv_heads), 256, smem, s>>>(qkv, tiles, cfg, cache, row_stream, row_pos,
                                                                       layer, tmax, all_keys, att);
   return cudaGetLastError();
 }
@@ -549,6 +576,111 @@ __global__ void __launch_bounds__(256) k_table(DTable T, const float* xn, int nb
       if (bv[t][i] > v || (bv[t][i] == v && bi[t][i] < idx)) { v = bv[t][i]; idx = bi[t][i]; }
     best_val[(size_t)t * nblocks + blockIdx.x] = v;
     best_idx[(size_t)t * nblocks + blockIdx.x] = idx;
+  }
+}
+
+// The token table for batches of streams: each thread keeps lane l of the
+// reference's 16-lane accumulator (k = l mod 16) for 4 vocabulary rows and
+// B streams, so every x value read from shared memory feeds 4 fma and
+// every widened weight B of them. A block owns TABLE_ROWS rows: 16 row
+// groups x 16 lanes. The streams' rows come through shared memory in
+// chunks of TB_KC values (cp.async, double-buffered); codes and scales
+// are read from global memory one k step ahead. The 16 lanes of a row then
+// reduce in the order of _mm512_reduce_add_ps, as k_table does.
+constexpr int TB_KC = 256;
+
+template <int B>
+__global__ void __launch_bounds__(256) k_table_rows(DTable T, const float* xn, int nb, float logit_mult,
+                                                    float* logits, float* best_val, int* best_idx, int nblocks) {
+  extern __shared__ __align__(16) float xb[];  // [2][B][TB_KC]
+  __shared__ float fin[B][TABLE_ROWS];
+  const int t = threadIdx.x, l = t & 15, rg = t >> 4;
+  const int row0 = blockIdx.x * TABLE_ROWS + rg * 4;
+  const int k = T.k;
+  auto stage = [&](int buf, int k0) {
+    float* dst = xb + (size_t)buf * B * TB_KC;
+    const int per = TB_KC / 4;  // 16-byte chunks a stream
+    for (int i = t; i < B * per; i += 256) {
+      int b = i / per, c = i % per;
+      if (b < nb) cp_async16(dst + b * TB_KC + c * 4, xn + (size_t)b * k + k0 + c * 4);
+      else *(float4*)(dst + b * TB_KC + c * 4) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    cp_commit();
+  };
+  float acc[4][B];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[a][b] = 0.0f;
+  bool live[4];
+  const int8_t* crow[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    live[a] = row0 + a < T.n;
+    crow[a] = T.codes + (size_t)(live[a] ? row0 + a : 0) * k;
+  }
+  const int chunks = k / TB_KC;
+  stage(0, 0);
+  for (int c = 0; c < chunks; ++c) {
+    if (c + 1 < chunks) stage((c + 1) & 1, (c + 1) * TB_KC);
+    if (c + 1 < chunks) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else cp_wait_all();
+    __syncthreads();
+    const float* xc = xb + (size_t)(c & 1) * B * TB_KC;
+    int code[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) code[a] = crow[a][c * TB_KC + l];
+    for (int st = 0; st < TB_KC / 16; ++st) {
+      const int kk = st * 16 + l, kg = c * TB_KC + kk;
+      int next[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) next[a] = (st + 1 < TB_KC / 16) ? crow[a][kg + 16] : 0;
+      float w[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) w[a] = __fmul_rn((float)code[a], table_scale(T, live[a] ? row0 + a : 0, kg / 32));
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const float xv = xc[b * TB_KC + kk];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) acc[a][b] = __fmaf_rn(xv, w[a], acc[a][b]);
+      }
+#pragma unroll
+      for (int a = 0; a < 4; ++a) code[a] = next[a];
+    }
+    __syncthreads();
+  }
+  // Reduce the 16 lanes of each row: s8[i] = a[i] + a[i + 8], s4[i] =
+  // s8[i] + s8[i + 4], then (s4[0] + s4[2]) + (s4[1] + s4[3]).
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      float v = acc[a][b];
+      v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 8, 16));
+      v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4, 16));
+      v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2, 16));
+      v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1, 16));
+      if (l == 0) {
+        if (logit_mult != 1.0f) v = __fmul_rn(v, logit_mult);
+        if (logits && live[a] && b < nb) logits[(size_t)b * T.n + row0 + a] = v;
+        fin[b][rg * 4 + a] = (live[a] && v == v) ? v : -INFINITY;  // a NaN never wins
+      }
+    }
+  __syncthreads();
+  // The block's best row per stream: the largest value, the lowest index
+  // among equals (layers.rs:603-612).
+  if (t < B && t < nb) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int r = 0; r < TABLE_ROWS; ++r) {
+      const int row = blockIdx.x * TABLE_ROWS + r;
+      if (row < T.n && fin[t][r] > bv) {
+        bv = fin[t][r];
+        bi = row;
+      }
+    }
+    best_val[(size_t)t * nblocks + blockIdx.x] = bv;
+    best_idx[(size_t)t * nblocks + blockIdx.x] = bi;
   }
 }
 
@@ -689,6 +821,22 @@ static cudaError_t table_pass(const DTable& T, const float* xn, int nb, float mu
   return cudaGetLastError();
 }
 
+template <int B>
+static cudaError_t table_rows_pass(const DTable& T, const float* xn, int nb, float mult, float* logits,
+                                   float* best_val, int* best_idx, cudaStream_t s) {
+  size_t smem = (size_t)2 * B * TB_KC * 4;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    cudaFuncSetAttribute(k_table_rows<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    configured[dev] = true;
+  }
+  int blocks = table_blocks(T.n);
+  k_table_rows<B><<<blocks, 256, smem, s>>>(T, xn, nb, mult, logits, best_val, best_idx, blocks);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_final(const float* x, int ldx, int nb, const float* norm_w, const DConfig& cfg, const DTable& T,
                          float* xn, float* logits, float* best_val, int* best_idx, int* token, cudaStream_t s) {
   k_final_norm_rows<<<nb, 256, (size_t)cfg.d * 4, s>>>(x, ldx, cfg.d, norm_w, cfg.eps, xn);
@@ -705,8 +853,10 @@ cudaError_t launch_final(const float* x, int ldx, int nb, const float* norm_w, c
 cudaError_t launch_table(const DTable& T, const float* xn, int nb, float mult, float* logits, float* best_val,
                          int* best_idx, cudaStream_t s) {
   int blocks = table_blocks(T.n);
-  for (int b0 = 0; b0 < nb; b0 += TABLE_MAX_B) {
-    int n = std::min(TABLE_MAX_B, nb - b0);
+  // Passes of up to 32 streams (16 when the width is not whole chunks).
+  const int pass = (T.k % TB_KC) ? TABLE_MAX_B : 32;
+  for (int b0 = 0; b0 < nb; b0 += pass) {
+    int n = std::min(pass, nb - b0);
     const float* xb = xn + (size_t)b0 * T.k;
     float* lg = logits ? logits + (size_t)b0 * T.n : nullptr;
     float* bv = best_val + (size_t)b0 * blocks;
@@ -714,7 +864,9 @@ cudaError_t launch_table(const DTable& T, const float* xn, int nb, float mult, f
     cudaError_t e;
     if (n == 1) e = table_pass<1>(T, xb, n, mult, lg, bv, bi, s);
     else if (n <= 4) e = table_pass<4>(T, xb, n, mult, lg, bv, bi, s);
-    else e = table_pass<16>(T, xb, n, mult, lg, bv, bi, s);
+    else if (T.k % TB_KC) e = table_pass<16>(T, xb, n, mult, lg, bv, bi, s);
+    else if (n <= 16) e = table_rows_pass<16>(T, xb, n, mult, lg, bv, bi, s);
+    else e = table_rows_pass<32>(T, xb, n, mult, lg, bv, bi, s);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

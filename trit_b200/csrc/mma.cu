@@ -14,7 +14,7 @@
 //              (the no-swizzle K-major canonical layout of the tcgen05
 //              shared-memory descriptor) by one 4-D tensor copy each;
 //   warp 1     allocates TMEM; lane 0 issues one MMA (K = 32) per step into
-//              one of two TMEM accumulators and commits it to an mbarrier:
+//              one of four TMEM accumulators and commits it to an mbarrier:
 //              a 32-value group (Q8_0) is one MMA, a 128-value group
 //              (per-row int8, ternary) four MMAs into the same accumulator;
 //   warps 2-9  epilogue: per group, load the 128 x 64 i32 accumulator from
@@ -41,12 +41,12 @@ constexpr int TC_M = 128;
 constexpr int TC_N = 64;
 constexpr int TC_KT = 128;  // K bytes a stage (four MMA steps of K = 32)
 constexpr int TC_STAGES = 4;
-constexpr int TC_BUFS = 2;
+constexpr int TC_BUFS = 4;
 constexpr int TC_EPI_WARPS = 8;   // two per TMEM lane quarter, 32 columns each
 constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
 constexpr int A_STAGE = TC_M * TC_KT;  // 16 KB
 constexpr int B_STAGE = TC_N * TC_KT;  // 8 KB
-constexpr int TC_TMEM_COLS = TC_BUFS * TC_N;  // 128 (a power of two >= 32)
+constexpr int TC_TMEM_COLS = TC_BUFS * TC_N;  // 256 (a power of two >= 32)
 constexpr long long TC_WAIT_NS = 2000000000ll;  // 2 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -293,7 +293,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     float wcur[8], wnxt[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) wcur[i] = (live && i < groups) ? weight_scale(W, row, i) : 0.0f;
+    // The next group's accumulator is loaded from TMEM while this group's
+    // chains run (tcgen05.wait::ld waits for both at the end).
     bool ok = true;
+    uint32_t rc[32], rn[32];
+    auto fetch = [&](int g, uint32_t (&r)[32]) -> bool {
+      const int b = g % TC_BUFS;
+      if (!mbar_wait(&S->tfull[b], (g / TC_BUFS) & 1, abort)) return false;
+      fence_after();
+      tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + b * TC_N + half * 32, r);
+      return true;
+    };
+    ok = fetch(0, rc);
+    if (ok) {
+      tmem_wait_ld();
+      fence_before();
+      mbar_arrive(&S->tempty[0]);
+    }
     for (int gc = 0; gc < groups && ok; gc += 8) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) wnxt[i] = (live && gc + 8 + i < groups) ? weight_scale(W, row, gc + 8 + i) : 0.0f;
@@ -301,25 +317,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int i = 0; i < 8; ++i) {
         const int g = gc + i;
         if (g >= groups) break;
-        const int b = g % TC_BUFS;
-        if (!mbar_wait(&S->tfull[b], (g / TC_BUFS) & 1, abort)) {
+        const bool more = g + 1 < groups;
+        if (more && !fetch(g + 1, rn)) {
           ok = false;
           break;
         }
-        fence_after();
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + b * TC_N + half * 32, r);
-        tmem_wait_ld();
-        fence_before();
-        mbar_arrive(&S->tempty[b]);
         const float2 ws2 = make_float2(wcur[i], wcur[i]);
         const float4* xg = (const float4*)(xs_s + g * TC_N + half * 32);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const float4 xv = xg[q];
-          acc[2 * q] = fma2(dots_to_float2(r[4 * q], r[4 * q + 1]), mul2(ws2, make_float2(xv.x, xv.y)), acc[2 * q]);
+          acc[2 * q] = fma2(dots_to_float2(rc[4 * q], rc[4 * q + 1]), mul2(ws2, make_float2(xv.x, xv.y)), acc[2 * q]);
           acc[2 * q + 1] =
-              fma2(dots_to_float2(r[4 * q + 2], r[4 * q + 3]), mul2(ws2, make_float2(xv.z, xv.w)), acc[2 * q + 1]);
+              fma2(dots_to_float2(rc[4 * q + 2], rc[4 * q + 3]), mul2(ws2, make_float2(xv.z, xv.w)), acc[2 * q + 1]);
+        }
+        if (more) {
+          tmem_wait_ld();
+          fence_before();
+          mbar_arrive(&S->tempty[(g + 1) % TC_BUFS]);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) rc[c] = rn[c];
         }
       }
 #pragma unroll
