@@ -132,8 +132,23 @@ struct Shared {
 
 // RmsNorm (layers.rs:135-144) of S.xf (d values) with weight w (null: no
 // norm), then Quantized::grouped of the result into S.xq / S.xs.
-__device__ void norm_quant(int d, const float* w, float eps, int G, bool half, Shared& S,
-                           const float* sc = nullptr) {
+// Groups a warp quantizes at once in norm_quant.
+constexpr int NQ_AT_ONCE = 4;
+
+template <int G>
+__device__ void norm_quant_g(int d, const float* w, float eps, bool half, Shared& S, const float* sc) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = d / G;
+  constexpr int PL = G / 32;  // values a lane holds of a group
+  // The norm weights of this warp's first groups, loaded before the sum so
+  // that their latency overlaps it.
+  float wv[NQ_AT_ONCE][PL];
+#pragma unroll
+  for (int q = 0; q < NQ_AT_ONCE; ++q) {
+    const int g = warp + q * DW;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) wv[q][i] = (g < groups && w) ? w[g * G + lane * PL + i] : 1.0f;
+  }
   __syncthreads();
   float inv = 1.0f;
   if (w) {
@@ -146,29 +161,37 @@ __device__ void norm_quant(int d, const float* w, float eps, int G, bool half, S
     __syncthreads();
     inv = S.red[0];
   }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int groups = d / G;
-  for (int g = warp; g < groups; g += DW) {
-    if (G == 32) {
-      float v[1];
-      int kk = g * 32 + lane;
-      v[0] = w ? __fmul_rn(S.xf[kk], __fmul_rn(inv, w[kk])) : S.xf[kk];
-      if (sc) v[0] = __fmul_rn(v[0], sc[kk]);
-      float sc = warp_quantize_group<32>(v, S.xq + g * 32, half);
-      if (lane == 0) S.xs[g] = sc;
-    } else {
-      float v[4];
+  for (int g0 = warp; g0 < groups; g0 += DW * NQ_AT_ONCE) {
+    float v[NQ_AT_ONCE][PL];
+    int8_t* codes[NQ_AT_ONCE];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        int kk = g * 128 + lane * 4 + i;
-        v[i] = w ? __fmul_rn(S.xf[kk], __fmul_rn(inv, w[kk])) : S.xf[kk];
-        if (sc) v[i] = __fmul_rn(v[i], sc[kk]);
+    for (int q = 0; q < NQ_AT_ONCE; ++q) {
+      const int g = g0 + q * DW;
+      codes[q] = g < groups ? S.xq + g * G : nullptr;
+#pragma unroll
+      for (int i = 0; i < PL; ++i) {
+        const int kk = min(g, groups - 1) * G + lane * PL + i;
+        const float wk = (g0 == warp) ? wv[q][i] : (w ? w[kk] : 1.0f);
+        float x = w ? __fmul_rn(S.xf[kk], __fmul_rn(inv, wk)) : S.xf[kk];
+        if (sc) x = __fmul_rn(x, sc[kk]);
+        v[q][i] = x;
       }
-      float sc = warp_quantize_group<128>(v, S.xq + g * 128, half);
-      if (lane == 0) S.xs[g] = sc;
+    }
+    float scale[NQ_AT_ONCE];
+    warp_quantize_groups<G, NQ_AT_ONCE>(v, codes, half, scale);
+    if (lane == 0) {
+#pragma unroll
+      for (int q = 0; q < NQ_AT_ONCE; ++q)
+        if (g0 + q * DW < groups) S.xs[g0 + q * DW] = scale[q];
     }
   }
   __syncthreads();
+}
+
+__device__ void norm_quant(int d, const float* w, float eps, int G, bool half, Shared& S,
+                           const float* sc = nullptr) {
+  if (G == 32) norm_quant_g<32>(d, w, eps, half, S, sc);
+  else norm_quant_g<128>(d, w, eps, half, S, sc);
 }
 
 // ------------------------------------------------------------- products --
@@ -195,32 +218,38 @@ __host__ __device__ inline int staged_row_bytes(const DMat& W) {
 // local rows w, w + DW, ...: its lanes form the i32 group dots from 16-byte
 // chunks, then lane 0 runs the row's group chain of int8.rs:560-570 in
 // order into S.out[lr].
-template <class RowOf, class Ready>
-__device__ bool gemv(const DMat& W, int nrows, RowOf row_of, Shared& S, Ready ready) {
+// ev(evbase + 0..2): the first batch's weights in shared memory, its group
+// dots, its chains (event trace only).
+template <class RowOf, class Ready, class Ev>
+__device__ bool gemv(const DMat& Wg, int nrows, RowOf row_of, Shared& S, Ready ready, Ev ev, int evbase) {
+  const DMat W = Wg;  // in registers: the loops below store to shared memory, which would force reloads
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int k = W.k, groups = k / W.agroup, lpg = W.agroup / 16, chunks = k / 16;
+  const int lpg_shift = lpg == 2 ? 1 : 3;  // lanes a group: 2 (groups of 32) or 8 (groups of 128)
   const int crow = code_row_bytes(W), srow = scale_row_bytes(W);
   const int cpad = (crow + 15) / 16 * 16, rbytes = staged_row_bytes(W);
   const int per = min(nrows, WSTAGE / rbytes);  // rows a batch (the host checks rbytes <= WSTAGE)
   const int nbatch = per > 0 ? (nrows + per - 1) / per : 0;
   uint8_t* buf0 = (uint8_t*)S.part;
   uint8_t* buf1 = buf0 + WSTAGE;
-  // The batch's group dots and scale products, [group][row]: the chain
-  // threads (one a row) read consecutive words.
-  int* pdot = (int*)(buf1 + WSTAGE);
-  float* pscl = (float*)(pdot + WSTAGE / 32);  // per * groups <= WSTAGE / 32: a row takes >= 32 bytes a group
+  // The batch's group dots (exact i32 values as f32, |dot| < 2^24) and
+  // scale products, [group][row]: the chain threads (one a row) read
+  // consecutive words.
+  float* pdot = (float*)(buf1 + WSTAGE);
+  float* pscl = pdot + WSTAGE / 32;  // per * groups <= WSTAGE / 32: a row takes >= 32 bytes a group
+  // A warp per row: lanes take the row's 16-byte code chunks and 4-byte
+  // scale words (no integer division in these loops).
   auto issue = [&](int b) {
     if (b < nbatch) {
       uint8_t* dst = (b & 1) ? buf1 : buf0;
       const int lr0 = b * per, n = min(per, nrows - lr0);
       const int cchunks = crow / 16, swords = srow / 4;
-      for (int i = t; i < n * cchunks; i += DT) {
-        int r = i / cchunks, cc = i % cchunks;
-        cp_async16(dst + r * rbytes + cc * 16, (const uint8_t*)W.codes + (size_t)row_of(lr0 + r) * crow + cc * 16);
-      }
-      for (int i = t; i < n * swords; i += DT) {
-        int r = i / swords, w4 = i % swords;
-        cp_async4(dst + r * rbytes + cpad + w4 * 4, (const uint8_t*)W.scales + (size_t)row_of(lr0 + r) * srow + w4 * 4);
+      for (int r = warp; r < n; r += DW) {
+        const uint8_t* codes = (const uint8_t*)W.codes + (size_t)row_of(lr0 + r) * crow;
+        const uint8_t* scales = (const uint8_t*)W.scales + (size_t)row_of(lr0 + r) * srow;
+        uint8_t* d = dst + r * rbytes;
+        for (int cc = lane; cc < cchunks; cc += 32) cp_async16(d + cc * 16, codes + cc * 16);
+        for (int w4 = lane; w4 < swords; w4 += 32) cp_async4(d + cpad + w4 * 4, scales + w4 * 4);
       }
     }
     cp_commit();
@@ -234,38 +263,72 @@ __device__ bool gemv(const DMat& W, int nrows, RowOf row_of, Shared& S, Ready re
     issue(b + 1);
     cp_wait<1>();
     __syncthreads();
+    if (b == 0) ev(evbase);
     const uint8_t* src = (b & 1) ? buf1 : buf0;
     const int lr0 = b * per, n = min(per, nrows - lr0);
-    for (int r = warp; r < n; r += DW) {
-      const uint8_t* rowp = src + r * rbytes;
-      for (int c0 = 0; c0 < chunks; c0 += 32) {
-        const int c = c0 + lane;
+    // The batch's (row, chunk) dots. With at least a row per warp, a warp
+    // takes whole rows; with fewer rows, the dots spread over all threads:
+    // thread t takes flat indices t, t + DT, ... Either way the lpg lanes of
+    // a group are adjacent (chunks and DT are multiples of lpg), so a
+    // shuffle sums the group.
+    auto group_dot = [&](int r, int c, int dot) {
+      if ((lane & (lpg - 1)) == 0) {
+        const uint8_t* rowp = src + r * rbytes;
+        const int g = c >> lpg_shift;
+        float ws = W.kind == kQ8_0 ? f16_bits_to_f32(((const uint16_t*)(rowp + cpad))[g])
+                   : W.kind == kInt8Row ? ((const float*)(rowp + cpad))[0]
+                                        : ((const float*)(rowp + cpad))[g];
+        pdot[g * per + r] = __int2float_rn(dot);
+        pscl[g * per + r] = __fmul_rn(ws, S.xs[g]);
+      }
+    };
+    if (n >= DW) {
+      for (int r = warp; r < n; r += DW) {
+        const uint8_t* rowp = src + r * rbytes;
+        for (int c0 = 0; c0 < chunks; c0 += 32) {
+          const int c = c0 + lane;
+          int dot = 0;
+          if (c < chunks) {
+            int4 act = ((const int4*)S.xq)[c];
+            if (W.kind == kTernary) dot = dot16_ternary(((const uint32_t*)rowp)[c], act);
+            else dot = dot16(((const int4*)rowp)[c], act);
+          }
+          for (int o = 1; o < lpg; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+          if (c < chunks) group_dot(r, c, dot);
+        }
+      }
+    } else {
+      int r = t / chunks, c = t - r * chunks;
+      const int steps = (n * chunks + DT - 1) / DT;
+      for (int it = 0; it < steps; ++it) {
+        const bool live = r < n;
         int dot = 0;
-        if (c < chunks) {
+        if (live) {
+          const uint8_t* rowp = src + r * rbytes;
           int4 act = ((const int4*)S.xq)[c];
           if (W.kind == kTernary) dot = dot16_ternary(((const uint32_t*)rowp)[c], act);
           else dot = dot16(((const int4*)rowp)[c], act);
         }
         for (int o = 1; o < lpg; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-        if (c < chunks && (lane % lpg) == 0) {
-          const int g = c / lpg;
-          float ws = W.kind == kQ8_0 ? f16_bits_to_f32(((const uint16_t*)(rowp + cpad))[g])
-                     : W.kind == kInt8Row ? ((const float*)(rowp + cpad))[0]
-                                          : ((const float*)(rowp + cpad))[g];
-          pdot[g * per + r] = dot;
-          pscl[g * per + r] = __fmul_rn(ws, S.xs[g]);
+        if (live) group_dot(r, c, dot);
+        c += DT;
+        while (c >= chunks) {
+          c -= chunks;
+          ++r;
         }
       }
     }
     __syncthreads();
+    if (b == 0) ev(evbase + 1);
     // The group chains of the batch's rows, one thread a row, groups in order.
     for (int r = t; r < n; r += DT) {
       float acc = 0.0f;
 #pragma unroll 8
-      for (int g = 0; g < groups; ++g) acc = __fmaf_rn((float)pdot[g * per + r], pscl[g * per + r], acc);
+      for (int g = 0; g < groups; ++g) acc = __fmaf_rn(pdot[g * per + r], pscl[g * per + r], acc);
       S.out[lr0 + r] = acc;
     }
     __syncthreads();  // the buffers are refilled by issue(b + 2) and the next batch's dots
+    if (b == 0) ev(evbase + 2);
   }
   cp_wait<0>();
   return true;
@@ -381,12 +444,13 @@ __device__ bool attend(const DecodeArgs& a, const DLayer& L, int layer, int pos,
 #pragma unroll
         for (int i = 0; i < 4; ++i) ((float*)cache.pool)[off + i] = v[i];
       }
-      // Later steps read this row in other blocks after a chain of LL
-      // hand-offs that carry no fence: make the row visible now.
-      __threadfence();
+      // Only this block (the one of kv head kvh) reads the row in later
+      // steps, after the __syncthreads below and its own later barriers;
+      // other kernels read it after this kernel ends.
     }
   }
   __syncthreads();
+  ev(28);
   A.run(q, T, kf, vf, true, out);
   ev(6);
   // Quantize each head's output (groups of 32 or 128 lie inside a head),
@@ -564,7 +628,7 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
   // Optional per-block event stamps of one step: [layer][16][grid].
   auto ev = [&](int k) {
     if (a.events && cur_step == a.event_step && threadIdx.x == 0)
-      a.events[((size_t)cur_layer * 16 + k) * nb + c] = gtimer();
+      a.events[((size_t)cur_layer * kEventSlots + k) * nb + c] = gtimer();
   };
   for (int i = 0; i < a.steps; ++i) {
     cur_step = i;
@@ -601,7 +665,7 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
         norm_quant(cfg.d, Lw.norm_attn, cfg.eps, Lw.qkv.agroup, Lw.qkv.half, S);
         ev(2);
         return true;
-      });
+      }, ev, 16);
       if (!ok) return;
       ev(3);
       for (int lr = threadIdx.x; lr < q1 - q0; lr += DT) ll_put(a.ll + ll.qkv + q0 + lr, __float_as_uint(S.out[lr]), t_qkv);
@@ -621,7 +685,7 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
           return false;
         ev(8);
         return true;
-      });
+      }, ev, 19);
       if (!ok) return;
       ev(9);
       mark();
@@ -640,7 +704,7 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
         norm_quant(cfg.d, Lw.norm_mlp, cfg.eps, Lw.gate_up.agroup, Lw.gate_up.half, S, Lw.ffn_scale);
         ev(11);
         return true;
-      });
+      }, ev, 22);
       if (!ok) return;
       ev(12);
       mark();
@@ -654,7 +718,7 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
         norm_quant(cfg.ffn, nullptr, cfg.eps, Lw.down.agroup, Lw.down.half, S);
         ev(14);
         return true;
-      });
+      }, ev, 25);
       if (!ok) return;
       ev(15);
       mark();

@@ -947,10 +947,10 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
     TRIT_CUDA(cudaMemsetAsync(dphase, 0, (size_t)steps * marks * 8, stream_));
   }
   a.phase_ns = dphase;
-  // TRIT_PHASE_TRACE=3: per-block stamps of 16 events a layer for one step.
+  // TRIT_PHASE_TRACE=3: per-block stamps of kEventSlots events a layer for one step.
   static const bool trace_events = getenv("TRIT_PHASE_TRACE") && *getenv("TRIT_PHASE_TRACE") == '3';
   long long* devents = nullptr;
-  const size_t nev = (size_t)cfg_.layers * 16 * decode_grid_;
+  const size_t nev = (size_t)cfg_.layers * kEventSlots * decode_grid_;
   if (trace_events && steps > 3) {
     TRIT_CUDA(cudaMallocAsync(&devents, nev * 8, stream_));
     TRIT_CUDA(cudaMemsetAsync(devents, 0, nev * 8, stream_));
@@ -997,29 +997,36 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
     std::vector<long long> t(nev);
     TRIT_CUDA(cudaMemcpy(t.data(), devents, nev * 8, cudaMemcpyDeviceToHost));
     TRIT_CUDA(cudaFree(devents));
-    const char* names[16] = {"layer start", "P1 x arrived", "P1 norm+quant", "P1 qkv rows", "P1 published",
-                             "P2 qkv arrived", "P2 attention", "P2 published", "P3 attq arrived", "P3 o rows",
-                             "P4 xa arrived", "P4 norm+quant", "P4 gate_up rows", "P5 h arrived", "P5 quantize",
-                             "P5 down rows"};
+    const char* names[kEventSlots] = {"layer start", "P1 x arrived", "P1 norm+quant", "P1 qkv rows", "P1 published",
+                                      "P2 qkv arrived", "P2 attention", "P2 published", "P3 attq arrived", "P3 o rows",
+                                      "P4 xa arrived", "P4 norm+quant", "P4 gate_up rows", "P5 h arrived",
+                                      "P5 quantize", "P5 down rows", "P1 weights in smem", "P1 dots", "P1 chains",
+                                      "P3 weights in smem", "P3 dots", "P3 chains", "P4 weights in smem", "P4 dots",
+                                      "P4 chains", "P5 weights in smem", "P5 dots", "P5 chains", "P2 qk norm+rope",
+                                      "", "", ""};
+    // Per block and layer: the stamps in time order; each interval is
+    // charged to the stamp that ends it.
     const int G = decode_grid_;
-    for (int k = 1; k < 16; ++k) {
-      double sum = 0, mx = 0;
-      long n = 0;
-      for (int l = 1; l < cfg_.layers; ++l)
-        for (int c = 0; c < G; ++c) {
-          long long cur = t[((size_t)l * 16 + k) * G + c];
-          if (!cur) continue;
-          int pk = k - 1;
-          while (pk > 0 && !t[((size_t)l * 16 + pk) * G + c]) --pk;
-          long long prev = t[((size_t)l * 16 + pk) * G + c];
-          if (!prev) continue;
-          double d = (double)(cur - prev) / 1e3;
-          sum += d;
-          mx = std::max(mx, d);
-          ++n;
+    double sum[kEventSlots] = {0}, mx[kEventSlots] = {0};
+    long cnt[kEventSlots] = {0};
+    for (int l = 1; l < cfg_.layers; ++l)
+      for (int c = 0; c < G; ++c) {
+        std::vector<std::pair<long long, int>> st;
+        for (int k = 0; k < kEventSlots; ++k) {
+          long long v = t[((size_t)l * kEventSlots + k) * G + c];
+          if (v) st.emplace_back(v, k);
         }
-      if (n) fprintf(stderr, "event %-16s mean %7.2f us  max %7.2f us  (%ld)\n", names[k], sum / n, mx, n);
-    }
+        std::sort(st.begin(), st.end());
+        for (size_t i2 = 1; i2 < st.size(); ++i2) {
+          double d = (double)(st[i2].first - st[i2 - 1].first) / 1e3;
+          sum[st[i2].second] += d;
+          mx[st[i2].second] = std::max(mx[st[i2].second], d);
+          ++cnt[st[i2].second];
+        }
+      }
+    for (int k = 1; k < kEventSlots; ++k)
+      if (cnt[k])
+        fprintf(stderr, "event %-20s mean %7.2f us  max %7.2f us  (%ld)\n", names[k], sum[k] / cnt[k], mx[k], cnt[k]);
   }
   if (status) throw Error("the persistent decode gave up waiting for another block (status " + std::to_string(status) + ")");
 }

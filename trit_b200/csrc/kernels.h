@@ -63,6 +63,7 @@ cudaError_t launch_silu_pairs(const float* g, int m, int units, float* h, cudaSt
 cudaError_t launch_expand_ternary(const DMat& W, int8_t* out, cudaStream_t s);
 
 // The persistent batch-1 decode (decode.cu).
+constexpr int kEventSlots = 32;  // event stamps a layer (TRIT_PHASE_TRACE=3)
 struct DecodeArgs {
   DConfig cfg;
   const DLayer* layers;  // device array [cfg.layers]
@@ -83,7 +84,7 @@ struct DecodeArgs {
   unsigned long long* ll;   // [decode_ll_words] {data, tag} words, zeroed before the launch
   int* status;           // 0 ok; nonzero: a wait ran out (see decode.cu)
   long long* phase_ns;   // optional [steps][5 * layers + 2] globaltimer stamps of block 0, or null
-  long long* events;     // optional [layers][16][grid] per-block stamps of step event_step, or null
+  long long* events;     // optional [layers][kEventSlots][grid] per-block stamps of step event_step, or null
   int event_step;
 };
 

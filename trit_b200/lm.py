@@ -16,7 +16,8 @@ from typing import Iterable, Sequence
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIBRARY = os.path.join(_HERE, "libtrit_cuda.so")
+# TRIT_CUDA_LIBRARY names another build of the library (a user's own).
+LIBRARY = os.environ.get("TRIT_CUDA_LIBRARY") or os.path.join(_HERE, "libtrit_cuda.so")
 
 _i32p = ctypes.POINTER(ctypes.c_int32)
 _f32p = ctypes.POINTER(ctypes.c_float)
