@@ -223,8 +223,12 @@ def cpu_sweep(reps: int) -> dict:
 def run_reference(args, r: dp.Rank) -> None:
     if r.rank != 0:
         return
+    from oracle import oracle as O
     from trit_b200 import presets
 
+    # Every host thread this process may use: torchrun sets OMP_NUM_THREADS=1
+    # for multi-rank runs, which would leave the reference arm one core.
+    O.lib().oracle_set_threads(len(os.sched_getaffinity(0)))
     if args.config == "c4":
         t0 = time.perf_counter()
         base = cpu_sweep(max(1, args.steps))

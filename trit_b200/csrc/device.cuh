@@ -126,40 +126,6 @@ __device__ __forceinline__ float warp_quantize_group(const float (&v)[G / 32], i
   return half ? round_f16(scale) : scale;
 }
 
-// NG groups at once, interleaved so that their shuffles and divisions
-// overlap (each group exactly as warp_quantize_group computes it).
-// codes[q] may be null for a group the caller skips.
-template <int G, int NG>
-__device__ __forceinline__ void warp_quantize_groups(const float (&v)[NG][G / 32], int8_t* const (&codes)[NG],
-                                                     bool half, float (&scale)[NG]) {
-  float m[NG];
-#pragma unroll
-  for (int q = 0; q < NG; ++q) {
-    m[q] = 0.0f;
-#pragma unroll
-    for (int i = 0; i < G / 32; ++i) m[q] = fmaxf(m[q], fabsf(v[q][i]));
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1)
-#pragma unroll
-    for (int q = 0; q < NG; ++q) m[q] = fmaxf(m[q], __shfl_xor_sync(0xffffffffu, m[q], o));
-  float inv[NG];
-#pragma unroll
-  for (int q = 0; q < NG; ++q) {
-    scale[q] = group_scale(m[q]);
-    inv[q] = __fdiv_rn(1.0f, scale[q]);
-  }
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int q = 0; q < NG; ++q) {
-    if (codes[q]) {
-#pragma unroll
-      for (int i = 0; i < G / 32; ++i) codes[q][lane * (G / 32) + i] = (int8_t)quantize_value(v[q][i], inv[q]);
-    }
-    if (half) scale[q] = round_f16(scale[q]);
-  }
-}
-
 // ------------------------------------------------------------ loads ----
 __device__ __forceinline__ int4 ld_stream(const void* p) {
   int4 r;
