@@ -380,6 +380,7 @@ def run_sweep(args, r: dp.Rank) -> None:
     from trit_b200 import Dense
 
     torch.cuda.set_device(r.local)
+    timing_stream = torch.cuda.Stream()
     hbm, peak_kind = peaks()
     rng = np.random.default_rng(SEED + 4)
     cases, total_bytes, total_s = [], 0.0, 0.0
@@ -393,16 +394,22 @@ def run_sweep(args, r: dp.Rank) -> None:
             for m in SWEEP_ROWS:
                 x = torch.from_numpy(rng.normal(0, 1, (m, k)).astype(np.float32)).cuda()
                 y = torch.empty((m, n), dtype=torch.float32, device="cuda")
-                stream = torch.cuda.current_stream().cuda_stream
-                for i in range(3):
+                # A stream of our own: its handle is never 0, which the C ABI
+                # reads as "the layer's own stream", so the events below see
+                # the products they bracket.
+                stream = timing_stream.cuda_stream
+                torch.cuda.synchronize()
+                # Every copy once first: a copy's first call at a new row
+                # count sizes its buffers (a device allocation).
+                for i in range(copies + 2):
                     layers[i % copies].forward_device(x.data_ptr(), m, y.data_ptr(), stream)
                 reps = args.reps
                 dp.barrier(r)
                 start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                start.record()
+                start.record(timing_stream)
                 for i in range(reps):
                     layers[i % copies].forward_device(x.data_ptr(), m, y.data_ptr(), stream)
-                end.record()
+                end.record(timing_stream)
                 torch.cuda.synchronize()
                 s = start.elapsed_time(end) / 1e3 / reps
                 s = dp.reduce(s, r, "max")

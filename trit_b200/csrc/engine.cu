@@ -1239,7 +1239,7 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
 // ------------------------------------------------------------ DenseOp ----
 DenseOp::~DenseOp() {
   cudaSetDevice(device);
-  void* bufs[] = {mem, xq, xs, xdev, ydev, best_val, best_idx, token};
+  void* bufs[] = {mem, xq, xs, xdev, ydev, best_val, best_idx, token, tc_status};
   for (void* b : bufs)
     if (b) cudaFree(b);
   if (stream) cudaStreamDestroy(stream);
@@ -1272,6 +1272,14 @@ std::unique_ptr<DenseOp> dense_q8_0(const void* blocks, size_t n, size_t k, int 
     op->mat.kind = kQ8_0; op->mat.n = (int)n; op->mat.k = (int)k; op->mat.agroup = 32; op->mat.half = 1;
     op->mat.codes = (char*)op->mem + co;
     op->mat.scales = (char*)op->mem + so;
+    // The tensor-core product (64 rows or more) on sm_100.
+    int major = 0;
+    TRIT_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+    if (major == 10 && k % 128 == 0 && make_tc_weight_map(&op->tc_w, op->mat, op->mat.codes) == cudaSuccess) {
+      TRIT_CUDA(cudaMalloc(&op->tc_status, 4));
+      TRIT_CUDA(cudaMemset(op->tc_status, 0, 4));
+      op->tc_ok = true;
+    }
   }
   return op;
 }
@@ -1286,7 +1294,9 @@ void DenseOp::forward_device(const float* x, size_t m, float* y, cudaStream_t s)
     xq = nullptr; xs = nullptr; best_val = nullptr; best_idx = nullptr; token = nullptr;
     size_t k = table ? tab.k : mat.k;
     size_t n = table ? tab.n : mat.n;
-    TRIT_CUDA(cudaMalloc(&xq, m * k));
+    // Whole 64-row tiles: the tensor-core product reads frames in tiles.
+    TRIT_CUDA(cudaMalloc(&xq, (m + 63) / 64 * 64 * k));
+    tc_tried = false;  // the frame map names the old buffer
     TRIT_CUDA(cudaMalloc(&xs, m * (k / 32) * 4));
     TRIT_CUDA(cudaMalloc(&best_val, m * table_blocks((int)n) * 4));
     TRIT_CUDA(cudaMalloc(&best_idx, m * table_blocks((int)n) * 4));
@@ -1297,7 +1307,14 @@ void DenseOp::forward_device(const float* x, size_t m, float* y, cudaStream_t s)
     TRIT_CUDA(launch_table(tab, x, (int)m, 1.0f, y, best_val, best_idx, s));
   } else {
     TRIT_CUDA(launch_norm_quant(x, (int)m, mat.k, nullptr, 0.0f, mat.agroup, mat.half, xq, xs, s));
-    TRIT_CUDA(launch_gemv(mat, xq, xs, (int)m, kEpOut, y, mat.n, 1.0f, s));
+    if (m >= 64 && tc_ok && !tc_tried) {
+      // The frame map of the current activation buffer (made again after
+      // the buffer grows).
+      tc_tried = true;
+      tc_ok = make_tc_frame_map(&tc_x, xq, (rows_cap + 63) / 64 * 64, (size_t)mat.k) == cudaSuccess;
+    }
+    if (m >= 64 && tc_ok) TRIT_CUDA(launch_gemm_tc(tc_w, tc_x, mat, xs, (int)m, kEpOut, y, mat.n, 1.0f, tc_status, s));
+    else TRIT_CUDA(launch_gemv(mat, xq, xs, (int)m, kEpOut, y, mat.n, 1.0f, s));
   }
 }
 

@@ -205,6 +205,10 @@ struct DenseOp {
   int* token = nullptr;
   size_t rows_cap = 0;
   cudaStream_t stream = nullptr;
+  // The tensor-core product for 64 rows or more (sm_100 only).
+  bool tc_tried = false, tc_ok = false;
+  TcMap tc_w{}, tc_x{};
+  int* tc_status = nullptr;
   ~DenseOp();
   void forward_device(const float* x, size_t m, float* y, cudaStream_t s);
 };

@@ -164,6 +164,130 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(DMat W, const int8_t* xq,
   }
 }
 
+// The W8A8 product for decode-size batches (Int8::forward_biased,
+// src/cpu/int8.rs:425-483, VNNI float order :560-570). A warp owns one
+// output row; a row is cut into 32-byte slots (32 int8 codes, or 32
+// two-bit ternary codes in two words), lane l taking slots l, l + 32, ...
+// Each weight slot is loaded once and multiplied with the codes of every
+// frame of the pass (FR frames, staged in shared memory). A Q8_0 group is
+// one slot; a 128-value group is four slots of neighbouring lanes, summed
+// with two shuffles. The exact i32 group dots go to shared memory as f32;
+// then one thread per (row, frame) runs the chain acc = fma(f32(dot_g),
+// ws_g * xs_g, acc) over the groups in order, so each output is the
+// reference's value bit for bit.
+constexpr int GS_WARPS = 8;
+
+template <int FR>
+__global__ void __launch_bounds__(GS_WARPS * 32) k_gemv_slots(DMat W, const int8_t* xq, const float* xs, int m,
+                                                            int mode, float* y, int ldy, float resid_mult,
+                                                            int units) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int k = W.k, G = W.agroup, groups = k / G, slots = k / 32;
+  const int rows_per_unit = (mode == kEpSilu) ? 2 : 1;
+  const int units_per_block = GS_WARPS / rows_per_unit;
+  const int unit0 = blockIdx.x * units_per_block;
+  const int nunits = min(units_per_block, units - unit0);
+  const int nrows = nunits * rows_per_unit;
+  int8_t* act = (int8_t*)smem;                             // [FR][k]
+  float* axs = (float*)(smem + (size_t)FR * k);            // [FR][groups]
+  float* pdot = axs + FR * groups;                         // [GS_WARPS][groups][FR]
+  float* wsc = pdot + GS_WARPS * groups * FR;              // [GS_WARPS][groups]
+  float* res = wsc + GS_WARPS * groups;                    // [GS_WARPS][FR]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto row_of = [&](int lr) {
+    const int u = unit0 + lr / rows_per_unit;
+    return (mode == kEpSilu) ? u + (lr % 2) * units : u;
+  };
+  for (int i = threadIdx.x; i < nrows * groups; i += GS_WARPS * 32)
+    wsc[i] = weight_scale(W, row_of(i / groups), i % groups);
+  const bool live_row = warp < nrows;
+  const int row = live_row ? row_of(warp) : 0;
+  const bool ternary = W.kind == kTernary;
+  const int8_t* wrow = (const int8_t*)W.codes + (size_t)row * k;          // int8 codes
+  const uint2* trow = (const uint2*)W.codes + (size_t)row * (k / 32);      // ternary: two words a slot
+  for (int f0 = 0; f0 < m; f0 += FR) {
+    const int nf = min(FR, m - f0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nf * k / 16; i += GS_WARPS * 32)
+      ((int4*)act)[i] = ((const int4*)(xq + (size_t)f0 * k))[i];
+    for (int i = threadIdx.x; i < nf * groups; i += GS_WARPS * 32) axs[i] = xs[(size_t)f0 * groups + i];
+    __syncthreads();
+    if (live_row) {
+#pragma unroll 2
+      for (int s0 = 0; s0 < slots; s0 += 32) {
+        const int sl = s0 + lane;
+        const bool live = sl < slots;
+        int4 w0 = make_int4(0, 0, 0, 0), w1 = make_int4(0, 0, 0, 0);
+        uint2 tw = make_uint2(0, 0);
+        if (live) {
+          if (ternary) tw = __ldg(trow + sl);
+          else {
+            w0 = __ldg((const int4*)(wrow + sl * 32));
+            w1 = __ldg((const int4*)(wrow + sl * 32 + 16));
+          }
+        }
+        int dot[FR];
+#pragma unroll
+        for (int f = 0; f < FR; ++f) {
+          dot[f] = 0;
+          if (live && f < nf) {
+            const int4 a0 = *(const int4*)(act + (size_t)f * k + sl * 32);
+            const int4 a1 = *(const int4*)(act + (size_t)f * k + sl * 32 + 16);
+            dot[f] = ternary ? dot16_ternary(tw.x, a0) + dot16_ternary(tw.y, a1) : dot16(w0, a0) + dot16(w1, a1);
+          }
+        }
+        if (G == 128) {
+#pragma unroll
+          for (int f = 0; f < FR; ++f) {
+            dot[f] += __shfl_xor_sync(0xffffffffu, dot[f], 1);
+            dot[f] += __shfl_xor_sync(0xffffffffu, dot[f], 2);
+          }
+        }
+        if (live && (G == 32 || (lane & 3) == 0)) {
+          const int g = (sl * 32) / G;
+          float* pd = pdot + ((size_t)warp * groups + g) * FR;
+#pragma unroll
+          for (int f = 0; f < FR; ++f)
+            if (f < nf) pd[f] = __int2float_rn(dot[f]);
+        }
+      }
+    }
+    __syncthreads();
+    // The chains: one thread per (row, frame), groups in order.
+    for (int t = threadIdx.x; t < nrows * nf; t += GS_WARPS * 32) {
+      const int lr = t / nf, f = t - lr * nf;
+      const float* pd = pdot + (size_t)lr * groups * FR + f;
+      const float* ws = wsc + lr * groups;
+      const float* sx = axs + f * groups;
+      float acc = 0.0f;
+#pragma unroll 8
+      for (int g = 0; g < groups; ++g) acc = __fmaf_rn(pd[g * FR], __fmul_rn(ws[g], sx[g]), acc);
+      res[lr * FR + f] = acc;
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < nunits * nf; t += GS_WARPS * 32) {
+      const int lu = t / nf, f = t - lu * nf;
+      const int u = unit0 + lu;
+      const size_t at = (size_t)(f0 + f) * ldy + u;
+      if (mode == kEpOut) {
+        y[at] = res[lu * FR + f];
+      } else if (mode == kEpResid) {
+        const float o = res[lu * FR + f];
+        y[at] = (resid_mult == 1.0f) ? __fadd_rn(y[at], o) : __fadd_rn(y[at], __fmul_rn(resid_mult, o));
+      } else {
+        const float g = res[(2 * lu) * FR + f], up = res[(2 * lu + 1) * FR + f];
+        y[at] = __fmul_rn(silu(g), up);
+      }
+    }
+  }
+}
+
+size_t gemv_slots_smem(const DMat& W, int fr) {
+  const size_t groups = W.k / W.agroup;
+  return (size_t)fr * W.k + (size_t)fr * groups * 4 + (size_t)GS_WARPS * groups * fr * 4 + GS_WARPS * groups * 4 +
+         GS_WARPS * fr * 4;
+}
+
 size_t gemv_smem(const DMat& W) {
   size_t groups = W.k / W.agroup;
   return GEMV_FRAMES * (size_t)W.k + GEMV_FRAMES * groups * 4 + GEMV_ROWS * GEMV_FRAMES * groups * 4 +
@@ -761,23 +885,34 @@ cudaError_t launch_norm_quant(const float* x, int m, int d, const float* w, floa
   return cudaSuccess;
 }
 
-cudaError_t launch_gemv(const DMat& W, const int8_t* xq, const float* xs, int m, int mode, float* y, int ldy,
-                        float resid_mult, cudaStream_t s) {
-  int units = (mode == kEpSilu) ? W.n / 2 : W.n;
-  int per_block = (mode == kEpSilu) ? GEMV_ROWS / 2 : GEMV_ROWS;
-  size_t smem = gemv_smem(W);
+template <int FR>
+static cudaError_t gemv_slots_pass(const DMat& W, const int8_t* xq, const float* xs, int m, int mode, float* y,
+                                   int ldy, float resid_mult, cudaStream_t s) {
+  const int units = (mode == kEpSilu) ? W.n / 2 : W.n;
+  const int per_block = (mode == kEpSilu) ? GS_WARPS / 2 : GS_WARPS;
+  const size_t smem = gemv_slots_smem(W, FR);
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
-    cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(k_gemv_slots<FR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     configured[dev] = true;
   }
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  k_gemv<<<(units + per_block - 1) / per_block, GEMV_THREADS, smem, s>>>(W, xq, xs, m, mode, y, ldy, resid_mult,
-                                                                         units);
-  LAUNCH_CHECK();
-  return cudaSuccess;
+  k_gemv_slots<FR><<<(units + per_block - 1) / per_block, GS_WARPS * 32, smem, s>>>(W, xq, xs, m, mode, y, ldy,
+                                                                                   resid_mult, units);
+  return cudaGetLastError();
+}
+
+// Frames a pass: as many as the batch needs, up to 16, fewer when the
+// shared memory of a wide input would not fit.
+cudaError_t launch_gemv(const DMat& W, const int8_t* xq, const float* xs, int m, int mode, float* y, int ldy,
+                        float resid_mult, cudaStream_t s) {
+  if (W.k % 128) return cudaErrorInvalidValue;
+  if (m <= 1) return gemv_slots_pass<1>(W, xq, xs, m, mode, y, ldy, resid_mult, s);
+  if (m <= 4) return gemv_slots_pass<4>(W, xq, xs, m, mode, y, ldy, resid_mult, s);
+  if (gemv_slots_smem(W, 16) <= 100 * 1024) return gemv_slots_pass<16>(W, xq, xs, m, mode, y, ldy, resid_mult, s);
+  return gemv_slots_pass<8>(W, xq, xs, m, mode, y, ldy, resid_mult, s);
 }
 
 cudaError_t launch_qk_rope_append(float* qkv, int m, const DConfig& cfg, const float* q_norm, const float* k_norm,
