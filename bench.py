@@ -449,6 +449,8 @@ def run_sweep(args, r: dp.Rank) -> None:
         "cases": cases,
         "clocks": clocks.summary(),
     }
+    if r.rank == 0 and r.world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_sweep(1)
     if r.rank == 0:
         print(json.dumps(line), flush=True)
 

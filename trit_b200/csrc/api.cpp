@@ -284,7 +284,7 @@ int trit_dense_forward(TritDense* layer, const float* x, size_t rows, float* out
     TRIT_CUDA(cudaFreeAsync(dx, op.stream));
     TRIT_CUDA(cudaFreeAsync(dy, op.stream));
     TRIT_CUDA(cudaStreamSynchronize(op.stream));
-    if (op.tc_status && rows >= 64) {  // the tensor-core product ran: did a wait in it run out?
+    if (op.tc_status) {  // did a wait in a tensor-core product run out?
       int st = 0;
       TRIT_CUDA(cudaMemcpyAsync(&st, op.tc_status, 4, cudaMemcpyDeviceToHost, op.stream));
       TRIT_CUDA(cudaStreamSynchronize(op.stream));

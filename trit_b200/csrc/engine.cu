@@ -1275,6 +1275,7 @@ std::unique_ptr<DenseOp> dense_q8_0(const void* blocks, size_t n, size_t k, int 
     // The tensor-core product (64 rows or more) on sm_100.
     int major = 0;
     TRIT_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+    TRIT_CUDA(cudaDeviceGetAttribute(&op->sm_count, cudaDevAttrMultiProcessorCount, device));
     if (major == 10 && k % 128 == 0 && make_tc_weight_map(&op->tc_w, op->mat, op->mat.codes) == cudaSuccess) {
       TRIT_CUDA(cudaMalloc(&op->tc_status, 4));
       TRIT_CUDA(cudaMemset(op->tc_status, 0, 4));
@@ -1307,13 +1308,17 @@ void DenseOp::forward_device(const float* x, size_t m, float* y, cudaStream_t s)
     TRIT_CUDA(launch_table(tab, x, (int)m, 1.0f, y, best_val, best_idx, s));
   } else {
     TRIT_CUDA(launch_norm_quant(x, (int)m, mat.k, nullptr, 0.0f, mat.agroup, mat.half, xq, xs, s));
-    if (m >= 64 && tc_ok && !tc_tried) {
+    // The tensor cores from 64 rows, or from 16 rows when the matrix is
+    // wide enough to give every SM two 128-row tiles (the dp4a GEMV then
+    // spends its time on the dot products).
+    const bool use_tc = tc_ok && (m >= 64 || (m >= 16 && (size_t)mat.n >= (size_t)2 * 128 * sm_count));
+    if (use_tc && !tc_tried) {
       // The frame map of the current activation buffer (made again after
       // the buffer grows).
       tc_tried = true;
       tc_ok = make_tc_frame_map(&tc_x, xq, (rows_cap + 63) / 64 * 64, (size_t)mat.k) == cudaSuccess;
     }
-    if (m >= 64 && tc_ok) TRIT_CUDA(launch_gemm_tc(tc_w, tc_x, mat, xs, (int)m, kEpOut, y, mat.n, 1.0f, tc_status, s));
+    if (use_tc && tc_ok) TRIT_CUDA(launch_gemm_tc(tc_w, tc_x, mat, xs, (int)m, kEpOut, y, mat.n, 1.0f, tc_status, s));
     else TRIT_CUDA(launch_gemv(mat, xq, xs, (int)m, kEpOut, y, mat.n, 1.0f, s));
   }
 }

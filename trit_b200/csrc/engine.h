@@ -207,6 +207,7 @@ struct DenseOp {
   cudaStream_t stream = nullptr;
   // The tensor-core product for 64 rows or more (sm_100 only).
   bool tc_tried = false, tc_ok = false;
+  int sm_count = 148;
   TcMap tc_w{}, tc_x{};
   int* tc_status = nullptr;
   ~DenseOp();

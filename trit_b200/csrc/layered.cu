@@ -185,98 +185,108 @@ __global__ void __launch_bounds__(GS_WARPS * 32) k_gemv_slots(DMat W, const int8
   const int k = W.k, G = W.agroup, groups = k / G, slots = k / 32;
   const int rows_per_unit = (mode == kEpSilu) ? 2 : 1;
   const int units_per_block = GS_WARPS / rows_per_unit;
-  const int unit0 = blockIdx.x * units_per_block;
-  const int nunits = min(units_per_block, units - unit0);
-  const int nrows = nunits * rows_per_unit;
-  int8_t* act = (int8_t*)smem;                             // [FR][k]
+  const int ntiles = (units + units_per_block - 1) / units_per_block;
+  // Frames' codes as [FR][2][slots] 16-byte halves: the lanes of a warp
+  // read consecutive 16-byte words (no bank conflicts). Group dots as
+  // [GS_WARPS][FR][groups + 1]: the padding keeps both the writes (lanes
+  // by group) and the chain reads (threads by frame) conflict-free.
+  const int gp = groups + 1;
+  int4* act = (int4*)smem;                                 // [FR][2][slots]
   float* axs = (float*)(smem + (size_t)FR * k);            // [FR][groups]
-  float* pdot = axs + FR * groups;                         // [GS_WARPS][groups][FR]
-  float* wsc = pdot + GS_WARPS * groups * FR;              // [GS_WARPS][groups]
+  float* pdot = axs + FR * groups;                         // [GS_WARPS][FR][gp]
+  float* wsc = pdot + GS_WARPS * FR * gp;                  // [GS_WARPS][groups]
   float* res = wsc + GS_WARPS * groups;                    // [GS_WARPS][FR]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  auto row_of = [&](int lr) {
-    const int u = unit0 + lr / rows_per_unit;
-    return (mode == kEpSilu) ? u + (lr % 2) * units : u;
-  };
-  for (int i = threadIdx.x; i < nrows * groups; i += GS_WARPS * 32)
-    wsc[i] = weight_scale(W, row_of(i / groups), i % groups);
-  const bool live_row = warp < nrows;
-  const int row = live_row ? row_of(warp) : 0;
   const bool ternary = W.kind == kTernary;
-  const int8_t* wrow = (const int8_t*)W.codes + (size_t)row * k;          // int8 codes
-  const uint2* trow = (const uint2*)W.codes + (size_t)row * (k / 32);      // ternary: two words a slot
   for (int f0 = 0; f0 < m; f0 += FR) {
     const int nf = min(FR, m - f0);
     __syncthreads();
-    for (int i = threadIdx.x; i < nf * k / 16; i += GS_WARPS * 32)
-      ((int4*)act)[i] = ((const int4*)(xq + (size_t)f0 * k))[i];
+    for (int i = threadIdx.x; i < nf * k / 16; i += GS_WARPS * 32) {
+      const int f = i / (k / 16), c = i - f * (k / 16);
+      act[(f * 2 + (c & 1)) * slots + (c >> 1)] = ((const int4*)(xq + (size_t)f0 * k))[i];
+    }
     for (int i = threadIdx.x; i < nf * groups; i += GS_WARPS * 32) axs[i] = xs[(size_t)f0 * groups + i];
-    __syncthreads();
-    if (live_row) {
+    // The block's row tiles, the frames staged once for all of them.
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const int unit0 = tile * units_per_block;
+      const int nunits = min(units_per_block, units - unit0);
+      const int nrows = nunits * rows_per_unit;
+      auto row_of = [&](int lr) {
+        const int u = unit0 + lr / rows_per_unit;
+        return (mode == kEpSilu) ? u + (lr % 2) * units : u;
+      };
+      __syncthreads();  // the tile before is done with wsc, pdot and res
+      for (int i = threadIdx.x; i < nrows * groups; i += GS_WARPS * 32)
+        wsc[i] = weight_scale(W, row_of(i / groups), i % groups);
+      if (warp < nrows) {
+        const int row = row_of(warp);
+        const int8_t* wrow = (const int8_t*)W.codes + (size_t)row * k;      // int8 codes
+        const uint2* trow = (const uint2*)W.codes + (size_t)row * (k / 32);  // ternary: two words a slot
 #pragma unroll 2
-      for (int s0 = 0; s0 < slots; s0 += 32) {
-        const int sl = s0 + lane;
-        const bool live = sl < slots;
-        int4 w0 = make_int4(0, 0, 0, 0), w1 = make_int4(0, 0, 0, 0);
-        uint2 tw = make_uint2(0, 0);
-        if (live) {
-          if (ternary) tw = __ldg(trow + sl);
-          else {
-            w0 = __ldg((const int4*)(wrow + sl * 32));
-            w1 = __ldg((const int4*)(wrow + sl * 32 + 16));
+        for (int s0 = 0; s0 < slots; s0 += 32) {
+          const int sl = s0 + lane;
+          const bool live = sl < slots;
+          int4 w0 = make_int4(0, 0, 0, 0), w1 = make_int4(0, 0, 0, 0);
+          uint2 tw = make_uint2(0, 0);
+          if (live) {
+            if (ternary) tw = __ldg(trow + sl);
+            else {
+              w0 = __ldg((const int4*)(wrow + sl * 32));
+              w1 = __ldg((const int4*)(wrow + sl * 32 + 16));
+            }
           }
-        }
-        int dot[FR];
-#pragma unroll
-        for (int f = 0; f < FR; ++f) {
-          dot[f] = 0;
-          if (live && f < nf) {
-            const int4 a0 = *(const int4*)(act + (size_t)f * k + sl * 32);
-            const int4 a1 = *(const int4*)(act + (size_t)f * k + sl * 32 + 16);
-            dot[f] = ternary ? dot16_ternary(tw.x, a0) + dot16_ternary(tw.y, a1) : dot16(w0, a0) + dot16(w1, a1);
-          }
-        }
-        if (G == 128) {
+          int dot[FR];
 #pragma unroll
           for (int f = 0; f < FR; ++f) {
-            dot[f] += __shfl_xor_sync(0xffffffffu, dot[f], 1);
-            dot[f] += __shfl_xor_sync(0xffffffffu, dot[f], 2);
+            dot[f] = 0;
+            if (live && f < nf) {
+              const int4 a0 = act[(f * 2) * slots + sl];
+              const int4 a1 = act[(f * 2 + 1) * slots + sl];
+              dot[f] = ternary ? dot16_ternary(tw.x, a0) + dot16_ternary(tw.y, a1) : dot16(w0, a0) + dot16(w1, a1);
+            }
+          }
+          if (G == 128) {
+#pragma unroll
+            for (int f = 0; f < FR; ++f) {
+              dot[f] += __shfl_xor_sync(0xffffffffu, dot[f], 1);
+              dot[f] += __shfl_xor_sync(0xffffffffu, dot[f], 2);
+            }
+          }
+          if (live && (G == 32 || (lane & 3) == 0)) {
+            const int g = (sl * 32) / G;
+            float* pd = pdot + (size_t)warp * FR * gp + g;
+#pragma unroll
+            for (int f = 0; f < FR; ++f)
+              if (f < nf) pd[f * gp] = __int2float_rn(dot[f]);
           }
         }
-        if (live && (G == 32 || (lane & 3) == 0)) {
-          const int g = (sl * 32) / G;
-          float* pd = pdot + ((size_t)warp * groups + g) * FR;
-#pragma unroll
-          for (int f = 0; f < FR; ++f)
-            if (f < nf) pd[f] = __int2float_rn(dot[f]);
-        }
       }
-    }
-    __syncthreads();
-    // The chains: one thread per (row, frame), groups in order.
-    for (int t = threadIdx.x; t < nrows * nf; t += GS_WARPS * 32) {
-      const int lr = t / nf, f = t - lr * nf;
-      const float* pd = pdot + (size_t)lr * groups * FR + f;
-      const float* ws = wsc + lr * groups;
-      const float* sx = axs + f * groups;
-      float acc = 0.0f;
+      __syncthreads();
+      // The chains: one thread per (row, frame), groups in order.
+      for (int t = threadIdx.x; t < nrows * nf; t += GS_WARPS * 32) {
+        const int lr = t / nf, f = t - lr * nf;
+        const float* pd = pdot + ((size_t)lr * FR + f) * gp;
+        const float* ws = wsc + lr * groups;
+        const float* sx = axs + f * groups;
+        float acc = 0.0f;
 #pragma unroll 8
-      for (int g = 0; g < groups; ++g) acc = __fmaf_rn(pd[g * FR], __fmul_rn(ws[g], sx[g]), acc);
-      res[lr * FR + f] = acc;
-    }
-    __syncthreads();
-    for (int t = threadIdx.x; t < nunits * nf; t += GS_WARPS * 32) {
-      const int lu = t / nf, f = t - lu * nf;
-      const int u = unit0 + lu;
-      const size_t at = (size_t)(f0 + f) * ldy + u;
-      if (mode == kEpOut) {
-        y[at] = res[lu * FR + f];
-      } else if (mode == kEpResid) {
-        const float o = res[lu * FR + f];
-        y[at] = (resid_mult == 1.0f) ? __fadd_rn(y[at], o) : __fadd_rn(y[at], __fmul_rn(resid_mult, o));
-      } else {
-        const float g = res[(2 * lu) * FR + f], up = res[(2 * lu + 1) * FR + f];
-        y[at] = __fmul_rn(silu(g), up);
+        for (int g = 0; g < groups; ++g) acc = __fmaf_rn(pd[g], __fmul_rn(ws[g], sx[g]), acc);
+        res[lr * FR + f] = acc;
+      }
+      __syncthreads();
+      for (int t = threadIdx.x; t < nunits * nf; t += GS_WARPS * 32) {
+        const int lu = t / nf, f = t - lu * nf;
+        const int u = unit0 + lu;
+        const size_t at = (size_t)(f0 + f) * ldy + u;
+        if (mode == kEpOut) {
+          y[at] = res[lu * FR + f];
+        } else if (mode == kEpResid) {
+          const float o = res[lu * FR + f];
+          y[at] = (resid_mult == 1.0f) ? __fadd_rn(y[at], o) : __fadd_rn(y[at], __fmul_rn(resid_mult, o));
+        } else {
+          const float g = res[(2 * lu) * FR + f], up = res[(2 * lu + 1) * FR + f];
+          y[at] = __fmul_rn(silu(g), up);
+        }
       }
     }
   }
@@ -284,8 +294,8 @@ __global__ void __launch_bounds__(GS_WARPS * 32) k_gemv_slots(DMat W, const int8
 
 size_t gemv_slots_smem(const DMat& W, int fr) {
   const size_t groups = W.k / W.agroup;
-  return (size_t)fr * W.k + (size_t)fr * groups * 4 + (size_t)GS_WARPS * groups * fr * 4 + GS_WARPS * groups * 4 +
-         GS_WARPS * fr * 4;
+  return (size_t)fr * W.k + (size_t)fr * groups * 4 + (size_t)GS_WARPS * (groups + 1) * fr * 4 +
+         GS_WARPS * groups * 4 + GS_WARPS * fr * 4;
 }
 
 size_t gemv_smem(const DMat& W) {
@@ -899,8 +909,12 @@ static cudaError_t gemv_slots_pass(const DMat& W, const int8_t* xq, const float*
     configured[dev] = true;
   }
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  k_gemv_slots<FR><<<(units + per_block - 1) / per_block, GS_WARPS * 32, smem, s>>>(W, xq, xs, m, mode, y, ldy,
-                                                                                   resid_mult, units);
+  // At most 8 blocks an SM; each loops over row tiles.
+  static int sms[64] = {};
+  if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int ntiles = (units + per_block - 1) / per_block;
+  const int grid = std::min(ntiles, 8 * std::max(dev < 64 ? sms[dev] : 148, 1));
+  k_gemv_slots<FR><<<grid, GS_WARPS * 32, smem, s>>>(W, xq, xs, m, mode, y, ldy, resid_mult, units);
   return cudaGetLastError();
 }
 
