@@ -128,7 +128,9 @@ struct Attention {
       for (int j = lane; j < T; j += 32) sc[qh * tmax + j] = cephes_exp(__fsub_rn(sc[qh * tmax + j], mx));
       __syncwarp();
       if (lane == 0) {
+        // In key order; unrolled so that the loads run ahead of the adds.
         float sum = 0.0f;
+#pragma unroll 8
         for (int j = 0; j < T; ++j) sum = __fadd_rn(sum, sc[qh * tmax + j]);
         stat[qh] = __fdiv_rn(1.0f, sum);
       }
@@ -155,8 +157,10 @@ struct Attention {
         float x = acc[u];
         if (cache.f16) {
           const __half* vp = (const __half*)vtl;
+#pragma unroll 8
           for (int jj = 0; jj < n; ++jj) x = __fmaf_rn(pr[jj], __half2float(vp[jj * 2 * row + e]), x);
         } else {
+#pragma unroll 8
           for (int jj = 0; jj < n; ++jj) x = __fmaf_rn(pr[jj], vtl[jj * row + e], x);
         }
         acc[u] = x;

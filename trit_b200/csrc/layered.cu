@@ -510,6 +510,7 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
     const int vis = visible(t);
     const float* srow = sc + (size_t)t * tmax;
     float sum = 0.0f;
+#pragma unroll 8
     for (int j = 0; j < vis; ++j) sum = __fadd_rn(sum, srow[j]);
     inv[t] = __fdiv_rn(1.0f, sum);
   }
@@ -540,6 +541,7 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
         const int qh = it / PER_HEAD, e = (it % PER_HEAD) * DW;
         const int lim = min(n, visible(qh) - j0);
         const float* pr = sc + (size_t)qh * tmax + j0;
+#pragma unroll 4
         for (int jj = 0; jj < lim; ++jj) {
           const float p = pr[jj];
           float v[DW];
