@@ -724,7 +724,7 @@ void Lm::run_prompt(size_t m, int slot, int first, const std::function<void(size
     TRIT_CUDA(cudaMemcpyAsync(row_pos_, host + rows_cap_, mc * 4, cudaMemcpyHostToDevice, stream_));
     fill(c0, c0 + mc);
     const int top = first + (int)c0 + mc;
-    const int R = attention_tile_rows(cfg_, (top + 3) / 4 * 4);
+    const int R = attention_tile_rows(cfg_, (top + 3) / 4 * 4, cache_.f16);
     std::vector<std::pair<int, int>> tiles;
     for (int r = 0; r < mc; r += R) tiles.emplace_back(r, std::min(R, mc - r));
     hidden(mc, top, &tiles);
@@ -1134,7 +1134,7 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
     TRIT_CUDA(cudaMemcpyAsync(ids_, hi, (size_t)mc * 4, cudaMemcpyHostToDevice, stream_));
     TRIT_CUDA(launch_embed(embed_, ids_, mc, x_, 1.0f, stream_));
     // Tiles: runs of rows of one stream, at most R rows each.
-    const int R = attention_tile_rows(cfg_, (top + 3) / 4 * 4);
+    const int R = attention_tile_rows(cfg_, (top + 3) / 4 * 4, cache_.f16);
     std::vector<std::pair<int, int>> tiles;
     for (int r = 0; r < mc;) {
       int e = r + 1;

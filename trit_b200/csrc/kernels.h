@@ -24,7 +24,7 @@ cudaError_t launch_qk_rope_append(float* qkv, int m, const DConfig& cfg, const f
 // stream at consecutive positions, at most rows_max rows a tile
 // (attention_tile_rows); tiles null: one row a block (ntiles rows).
 // all_keys > 0: every row sees keys [0, all_keys) (no causal mask).
-int attention_tile_rows(const DConfig& cfg, int tmax);
+int attention_tile_rows(const DConfig& cfg, int tmax, int f16);
 cudaError_t launch_attention_rows(const float* qkv, const int2* tiles, int ntiles, int rows_max, const DConfig& cfg,
                                   const DCache& cache, const int* row_stream, const int* row_pos, int layer,
                                   int max_tk, float* att, cudaStream_t s, int all_keys = 0);

@@ -408,8 +408,9 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
   const int pitch = f16 ? 68 : 132;           // floats a staged row (16-byte aligned, banks staggered)
   float* q = sm;                              // [RQ][128]
   float* sc = q + RQ * 128;                   // [RQ][tmax]
-  float* kv = sc + (size_t)RQ * tmax;         // [AR_KT][pitch]
-  float* inv = kv + AR_KT * pitch;            // [RQ]
+  float* kvb[2] = {sc + (size_t)RQ * tmax,   // [2][AR_KT][pitch]: tile t in buffer t % 2
+                   sc + (size_t)RQ * tmax + AR_KT * pitch};
+  float* inv = kvb[1] + AR_KT * pitch;        // [RQ]
   const int stream = row_stream[r0];
   const int p0 = row_pos[r0];
   const int T = all_keys > 0 ? all_keys : p0 + R;  // keys the last row sees
@@ -420,21 +421,34 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
     q[i] = __fmul_rn(qkv[(size_t)(r0 + r) * stride + (kvh * qpk + h) * 128 + e], scale);
   }
   // Keys (which 0) or values (1) [j0, j0 + n) into kv, row pitch `pitch` floats.
-  auto stage = [&](int which, int j0, int n) {
+  // Keys (which 0) or values (1) [j0, j0 + n) into dst (cp.async, one
+  // commit group; the caller waits).
+  auto stage = [&](int which, int j0, int n, float* dst) {
     const int cpr = f16 ? 16 : 32;  // 16-byte chunks a row
     for (int ci = t; ci < n * cpr; ci += 256) {
       int jj = ci / cpr, cc = ci % cpr, j = j0 + jj;
       int page = cache.page_table[(size_t)stream * cache.pages_per_stream + j / cache.page_tokens];
       size_t off = kv_offset(cache, cfg, page, layer, which, kvh, j % cache.page_tokens);
       const int4* src = f16 ? (const int4*)((const __half*)cache.pool + off) : (const int4*)((const float*)cache.pool + off);
-      cp_async16(kv + jj * pitch + cc * 4, src + cc);
+      cp_async16(dst + jj * pitch + cc * 4, src + cc);
     }
     cp_commit();
-    cp_wait_all();
+  };
+  // Tile ti of keys or values: the next tile goes out before this one is
+  // waited for (double buffering).
+  const int ntile = (T + AR_KT - 1) / AR_KT;
+  auto tile_ready = [&](int which, int ti) {
+    if (ti + 1 < ntile) {
+      stage(which, (ti + 1) * AR_KT, min(AR_KT, T - (ti + 1) * AR_KT), kvb[(ti + 1) & 1]);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      cp_wait_all();
+    }
     __syncthreads();
   };
   // Eight consecutive dimensions of a staged row as floats (one 16-byte
   // load for f16 rows).
+  const float* kv = kvb[0];  // the staged tile being read (set per tile)
   auto row8 = [&](int jj, int e, float (&o)[8]) {
     if (f16) {
       const uint4 raw = *(const uint4*)((const __half*)(kv + jj * pitch) + e);
@@ -452,10 +466,12 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
     }
   };
   // Scores.
-  for (int j0 = 0; j0 < T; j0 += AR_KT) {
-    const int n = min(AR_KT, T - j0);
-    __syncthreads();
-    stage(0, j0, n);
+  __syncthreads();
+  stage(0, 0, min(AR_KT, T), kvb[0]);
+  for (int ti = 0; ti < ntile; ++ti) {
+    const int j0 = ti * AR_KT, n = min(AR_KT, T - j0);
+    tile_ready(0, ti);
+    kv = kvb[ti & 1];
     const int kg = (n + KB - 1) / KB, items = ((RQ + QB - 1) / QB) * kg;
     for (int it = t; it < items; it += 256) {
       // Keys jb, jb + kg, ...: neighbouring threads read neighbouring
@@ -492,8 +508,10 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
           if (qh < RQ && jj < n && j < visible(qh)) sc[(size_t)qh * tmax + j] = acc[a][b];
         }
     }
+    __syncthreads();  // the buffer is refilled two tiles on
   }
-  __syncthreads();
+  // Value tile 0 goes out before the softmax.
+  stage(1, 0, min(AR_KT, T), kvb[0]);
   // Max and exp: a warp per query head; then the sums in key order, one
   // thread per query head (all heads at once); then the probabilities.
   const int warp = t >> 5, lane = t & 31;
@@ -530,10 +548,10 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
   for (int u = 0; u < MAXI; ++u)
 #pragma unroll
     for (int c = 0; c < DW; ++c) acc[u][c] = 0.0f;
-  for (int j0 = 0; j0 < T; j0 += AR_KT) {
-    const int n = min(AR_KT, T - j0);
-    __syncthreads();
-    stage(1, j0, n);
+  for (int ti = 0; ti < ntile; ++ti) {
+    const int j0 = ti * AR_KT, n = min(AR_KT, T - j0);
+    tile_ready(1, ti);
+    kv = kvb[ti & 1];
 #pragma unroll
     for (int u = 0; u < MAXI; ++u) {
       const int it = t + u * 256;
@@ -564,6 +582,7 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
         }
       }
     }
+    __syncthreads();  // the buffer is refilled two tiles on
   }
 #pragma unroll
   for (int u = 0; u < MAXI; ++u) {
@@ -577,12 +596,14 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
   }
 }
 
-int attention_tile_rows(const DConfig& cfg, int tmax) {
-  // Scores of R rows x qpk heads x tmax keys within ~110 KB, at most 64
-  // query heads a block, and whole groups of 4 query heads.
+int attention_tile_rows(const DConfig& cfg, int tmax, int f16) {
+  // A block's shared memory (220 KB): two staged K/V tiles, and for every
+  // query head of the tile its q row and its scores; at most 16 rows and
+  // 64 query heads a block, and whole groups of 4 query heads.
   const int qpk = cfg.heads / cfg.kv_heads;
-  long cap = 28160L / ((long)qpk * std::max(tmax, 1));
-  int r = (int)std::min<long>(std::min<long>(16, cap), 64 / std::max(qpk, 1));
+  const long budget = 220L * 1024 / 4 - 2L * AR_KT * (f16 ? 68 : 132) - 64;
+  const long rq = budget / (128L + std::max(tmax, 1));
+  int r = (int)std::min<long>(std::min<long>(16, rq / qpk), 64 / std::max(qpk, 1));
   if (r * qpk >= 16) r = r / (4 / std::__gcd(qpk, 4)) * (4 / std::__gcd(qpk, 4));
   return std::max(r, 1);
 }
@@ -594,7 +615,7 @@ cudaError_t launch_attention_rows(const float* qkv, const int2* tiles, int ntile
   const int RQ = rows_max * qpk;
   if (RQ > 64 || all_keys > max_tk) return cudaErrorInvalidValue;
   const int tmax = (max_tk + 3) / 4 * 4;
-  size_t smem = ((size_t)RQ * 128 + (size_t)RQ * tmax + (size_t)AR_KT * (cache.f16 ? 68 : 132) + RQ) * 4;
+  size_t smem = ((size_t)RQ * 128 + (size_t)RQ * tmax + (size_t)2 * AR_KT * (cache.f16 ? 68 : 132) + RQ) * 4;
   if (smem > 220 * 1024) return cudaErrorInvalidValue;
   // Blocks of 4 query heads for tiles of 16 or more query heads.
   const bool quad = tiles && RQ >= 16;
