@@ -10,19 +10,24 @@
 // One CTA owns 128 weight rows (the MMA's M, one TMEM lane each) and 64
 // frames (N). Warp roles:
 //   warp 0     TMA producer: a stage is 128 bytes of K for the CTA's weight
-//              rows and frames, laid out as 8-row x 16-byte core matrices
-//              (the no-swizzle K-major canonical layout of the tcgen05
-//              shared-memory descriptor) by one 4-D tensor copy each;
+//              rows and frames, one 128-byte line per row with the 128-byte
+//              swizzle (16-byte chunk c of row r at chunk c ^ (r % 8)), the
+//              K-major SWIZZLE_128B layout of the tcgen05 shared-memory
+//              descriptor, by one 2-D tensor copy each;
 //   warp 1     allocates TMEM; lane 0 issues one MMA (K = 32) per step into
 //              one of four TMEM accumulators and commits it to an mbarrier:
 //              a 32-value group (Q8_0) is one MMA, a 128-value group
 //              (per-row int8, ternary) four MMAs into the same accumulator;
-//   warps 2-9  epilogue: per group, load the 128 x 64 i32 accumulator from
-//              TMEM (warp w: lanes 32 (w % 4).., columns 32 ((w - 2) / 4)..),
-//              free it, and fold it into 32 f32 chains per thread with
-//              packed f32x2 arithmetic (each lane rounds as the scalar
-//              instruction does). A dot (|dot| < 2^22) becomes a float
-//              exactly through the 1.5 * 2^23 bias.
+//   warps 2-9  epilogue: per group, load the 128 x 64 accumulator from TMEM
+//              (warp w: lanes 32 (w % 4).., columns 32 ((w - 2) / 4)..),
+//              store the bias back (tcgen05.st), free the buffer, and fold
+//              the group into 32 f32 chains per thread with packed f32x2
+//              arithmetic (each lane rounds as the scalar instruction does).
+//              Every accumulator starts at the bits of 1.5 * 2^23, so after
+//              the MMAs it holds the float 1.5 * 2^23 + dot (|dot| < 2^22)
+//              and one exact subtraction gives f32(dot). The epilogue warps
+//              also stage the frames' activation scales while the first
+//              stages load.
 // Every wait is bounded in time; a wait that runs out sets the kernel's
 // status, the CTA waits (bounded) for its copies and MMAs in flight, frees
 // its TMEM and returns.
@@ -95,22 +100,23 @@ __device__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort) {
   }
 }
 
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
-                                            int c3) {
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
       "[%2];" ::"r"(smem_u32(dst)),
-      "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
 
-// Shared-memory matrix descriptor, K-major, no swizzle: 8-row x 16-byte
-// core matrices; `lbo` = bytes between the two 16-byte halves of a K step,
-// `sbo` = bytes between 8-row groups. Bit 46 is the descriptor version of
-// sm_100.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
+// Shared-memory matrix descriptor, K-major with the 128-byte swizzle: rows
+// of 128 bytes, 8-row groups 1024 bytes apart (SBO); the leading offset is
+// unused for this layout (encoded 1). `addr` may step through the 128-byte
+// line in 32-byte K steps: the swizzle applies to the absolute address, and
+// the stage bases are 1024-byte aligned (base offset 0). Bit 46 is the
+// descriptor version of sm_100; bits 61-63 = 2 select SWIZZLE_128B.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+         (2ull << 61);
 }
 
 // Instruction descriptor of kind::i8: D s32 (bits 4-5 = 2), A and B s8
@@ -168,13 +174,25 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
 }
-// Two i32 dots as exact floats: 1.5 * 2^23 + dot has ulp 1 for |dot| < 2^22.
-__device__ __forceinline__ float2 dots_to_float2(uint32_t a, uint32_t b) {
-  return add2(make_float2(__int_as_float(0x4B400000 + (int)a), __int_as_float(0x4B400000 + (int)b)),
-              make_float2(-12582912.0f, -12582912.0f));
+// Every accumulator starts at the bits of 1.5 * 2^23 (kBias); after the
+// MMAs add the i32 dot, the word is the float 1.5 * 2^23 + dot (ulp 1 for
+// |dot| <= 2^22), and subtracting 1.5 * 2^23 gives f32(dot) exactly.
+constexpr uint32_t kBias = 0x4B400000u;
+__device__ __forceinline__ float2 biased_dots(uint32_t a, uint32_t b) {
+  return add2(make_float2(__uint_as_float(a), __uint_as_float(b)), make_float2(-12582912.0f, -12582912.0f));
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// kBias into 32 consecutive TMEM columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_st32_bias(uint32_t taddr) {
+  const uint32_t v = kBias;
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+      "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
+      "r"(v)
+      : "memory");
+}
 
 struct TcSmem {
   uint64_t full[TC_STAGES], empty[TC_STAGES], tfull[TC_BUFS], tempty[TC_BUFS], drain;
@@ -188,7 +206,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, DMat W,
               const float* xs, int m, int mode, float* y, int ldy, float resid_mult, int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* a_st = base;
   uint8_t* b_st = a_st + TC_STAGES * A_STAGE;
   const int G = W.agroup, groups = W.k / G;
@@ -218,11 +236,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // The frames' activation scales, [group][frame] (rows past m read as 0).
-  for (int i = threadIdx.x; i < TC_N * groups; i += TC_THREADS) {
-    int g = i / TC_N, f = i % TC_N;
-    xs_s[i] = (f0 + f < m) ? xs[(size_t)(f0 + f) * groups + g] : 0.0f;
-  }
   fence_before();
   __syncthreads();
   fence_after();
@@ -235,8 +248,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int s = kt % TC_STAGES;
         if (!mbar_wait(&S->empty[s], ((kt / TC_STAGES) & 1) ^ 1, abort)) break;
         mbar_expect_tx(&S->full[s], A_STAGE + B_STAGE);
-        tma_load_4d(a_st + s * A_STAGE, &amap, &S->full[s], 0, 0, kt * (TC_KT / 16), n0 / 8);
-        tma_load_4d(b_st + s * B_STAGE, &bmap, &S->full[s], 0, 0, kt * (TC_KT / 16), f0 / 8);
+        tma_load_2d(a_st + s * A_STAGE, &amap, &S->full[s], kt * TC_KT, n0);
+        tma_load_2d(b_st + s * B_STAGE, &bmap, &S->full[s], kt * TC_KT, f0);
         issued = kt + 1;
       }
       if (*abort) {
@@ -262,15 +275,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const bool first = (step * 32) % G == 0, last = ((step + 1) * 32) % G == 0;
           const int b = g % TC_BUFS;
           if (first) {
-            if (!mbar_wait(&S->tempty[b], ((g / TC_BUFS) & 1) ^ 1, abort)) {
+            if (!mbar_wait(&S->tempty[b], (g / TC_BUFS) & 1, abort)) {
               ok = false;
               break;
             }
             fence_after();
           }
-          const uint64_t ad = smem_desc(a0 + s * A_STAGE + j * 256, 128, 1024);
-          const uint64_t bd = smem_desc(b0 + s * B_STAGE + j * 256, 128, 1024);
-          mma_i8(tmem + b * TC_N, ad, bd, first ? 0u : 1u);
+          const uint64_t ad = smem_desc_sw128(a0 + s * A_STAGE + j * 32);
+          const uint64_t bd = smem_desc_sw128(b0 + s * B_STAGE + j * 32);
+          mma_i8(tmem + b * TC_N, ad, bd, 1u);
           if (last) mma_commit(&S->tfull[b]);
         }
         mma_commit(&S->empty[s]);
@@ -286,62 +299,94 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int lr = quarter * 32 + lane;
     const int row = n0 + lr;
     const bool live = row < W.n;
-    float2 acc[16];  // frames 32 half + 2 i, + 1
-#pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] = make_float2(0.0f, 0.0f);
+    const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16) + half * 32;  // + buffer * TC_N
+    // Bias every accumulator, then hand all of them to the MMA thread.
+    for (int b = 0; b < TC_BUFS; ++b) tmem_st32_bias(tl + b * TC_N);
+    tmem_wait_st();
+    fence_before();
+    for (int b = 0; b < TC_BUFS; ++b) mbar_arrive(&S->tempty[b]);
     // Weight scales 8 groups ahead, so their loads overlap the MMAs.
     float wcur[8], wnxt[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) wcur[i] = (live && i < groups) ? weight_scale(W, row, i) : 0.0f;
-    // The next group's accumulator is loaded from TMEM while this group's
-    // chains run (tcgen05.wait::ld waits for both at the end).
-    bool ok = true;
-    uint32_t rc[32], rn[32];
+    // The frames' activation scales, [group][frame] (frames past m read as
+    // 0): coalesced reads of xs rows, eight in flight per thread, while the
+    // first stages load and multiply.
+    {
+      const int total = TC_N * groups, t0 = threadIdx.x - 64, nt = 32 * TC_EPI_WARPS;
+      for (int i0 = t0; i0 < total; i0 += 8 * nt) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = i0 + u * nt, f = i / groups, g = i - f * groups;
+          v[u] = (i < total && f0 + f < m) ? __ldg(xs + (size_t)(f0 + f) * groups + g) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = i0 + u * nt, f = i / groups, g = i - f * groups;
+          if (i < total) xs_s[g * TC_N + f] = v[u];
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * TC_EPI_WARPS) : "memory");
+    }
+    float2 acc[16];  // frames 32 half + 2 i, + 1
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = make_float2(0.0f, 0.0f);
     auto fetch = [&](int g, uint32_t (&r)[32]) -> bool {
       const int b = g % TC_BUFS;
       if (!mbar_wait(&S->tfull[b], (g / TC_BUFS) & 1, abort)) return false;
       fence_after();
-      tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + b * TC_N + half * 32, r);
+      tmem_ld32(tl + b * TC_N, r);
       return true;
     };
-    ok = fetch(0, rc);
+    // One group: the next group's accumulator loads from TMEM while this
+    // group's chains run; this group's buffer goes back to the MMA thread
+    // once its bias store (issued a group earlier) has landed.
+    auto step = [&](int g, float w, const uint32_t (&rc)[32], uint32_t (&rn)[32]) -> bool {
+      const bool more = g + 1 < groups;
+      if (more && !fetch(g + 1, rn)) return false;
+      const float2 ws2 = make_float2(w, w);
+      const float4* xg = (const float4*)(xs_s + g * TC_N + half * 32);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 xv = xg[q];
+        acc[2 * q] = fma2(biased_dots(rc[4 * q], rc[4 * q + 1]), mul2(ws2, make_float2(xv.x, xv.y)), acc[2 * q]);
+        acc[2 * q + 1] =
+            fma2(biased_dots(rc[4 * q + 2], rc[4 * q + 3]), mul2(ws2, make_float2(xv.z, xv.w)), acc[2 * q + 1]);
+      }
+      tmem_wait_ld();
+      tmem_wait_st();
+      fence_before();
+      mbar_arrive(&S->tempty[g % TC_BUFS]);
+      if (more) tmem_st32_bias(tl + ((g + 1) % TC_BUFS) * TC_N);
+      return true;
+    };
+    uint32_t ra[32], rb[32];
+    bool ok = fetch(0, ra);
     if (ok) {
       tmem_wait_ld();
-      fence_before();
-      mbar_arrive(&S->tempty[0]);
+      tmem_st32_bias(tl);
     }
     for (int gc = 0; gc < groups && ok; gc += 8) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) wnxt[i] = (live && gc + 8 + i < groups) ? weight_scale(W, row, gc + 8 + i) : 0.0f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int g = gc + i;
-        if (g >= groups) break;
-        const bool more = g + 1 < groups;
-        if (more && !fetch(g + 1, rn)) {
+      for (int i = 0; i < 8; i += 2) {
+        if (gc + i >= groups) break;
+        if (!step(gc + i, wcur[i], ra, rb)) {
           ok = false;
           break;
         }
-        const float2 ws2 = make_float2(wcur[i], wcur[i]);
-        const float4* xg = (const float4*)(xs_s + g * TC_N + half * 32);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 xv = xg[q];
-          acc[2 * q] = fma2(dots_to_float2(rc[4 * q], rc[4 * q + 1]), mul2(ws2, make_float2(xv.x, xv.y)), acc[2 * q]);
-          acc[2 * q + 1] =
-              fma2(dots_to_float2(rc[4 * q + 2], rc[4 * q + 3]), mul2(ws2, make_float2(xv.z, xv.w)), acc[2 * q + 1]);
-        }
-        if (more) {
-          tmem_wait_ld();
-          fence_before();
-          mbar_arrive(&S->tempty[(g + 1) % TC_BUFS]);
-#pragma unroll
-          for (int c = 0; c < 32; ++c) rc[c] = rn[c];
+        if (gc + i + 1 >= groups) break;
+        if (!step(gc + i + 1, wcur[i + 1], rb, ra)) {
+          ok = false;
+          break;
         }
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i) wcur[i] = wnxt[i];
     }
+    tmem_wait_st();
     if (ok && live) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -418,21 +463,21 @@ EncodeTiled encoder() {
 
 int tc_frames() { return TC_N; }
 
-// A 4-D view of a row-major int8 matrix [rows][k] whose boxes land in
-// shared memory as 8-row x 16-byte core matrices: dims (16 bytes, 8 rows,
-// k / 16 chunks, rows / 8 row groups); a box is one stage (TC_KT bytes of
-// K) of `box_rows` rows.
+// A 2-D view (k bytes, rows) of a row-major int8 matrix [rows][k]; a box is
+// one stage (TC_KT = 128 bytes of K) of `box_rows` rows, written to shared
+// memory with the 128-byte swizzle. Rows past `rows` read as zero.
 cudaError_t make_tc_map(TcMap* out, const void* base, size_t rows, size_t k, int box_rows) {
   EncodeTiled enc = encoder();
   if (!enc) return cudaErrorNotSupported;
-  if (rows % 8 || k % TC_KT || ((uintptr_t)base & 15) || box_rows % 8) return cudaErrorInvalidValue;
-  cuuint64_t dims[4] = {16, 8, k / 16, rows / 8};
-  cuuint64_t strides[3] = {k, 16, 8 * k};
-  cuuint32_t box[4] = {16, 8, TC_KT / 16, (cuuint32_t)(box_rows / 8)};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
+  if (rows % 8 || k % TC_KT || ((uintptr_t)base & 15) || box_rows % 8 || box_rows > 256) return cudaErrorInvalidValue;
+  static_assert(TC_KT == 128, "a stage's K is one 128-byte swizzle line");
+  cuuint64_t dims[2] = {k, rows};
+  cuuint64_t strides[1] = {k};
+  cuuint32_t box[2] = {TC_KT, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
   static_assert(sizeof(TcMap) == sizeof(CUtensorMap), "TcMap holds a CUtensorMap");
-  CUresult r = enc((CUtensorMap*)out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box,
-                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+  CUresult r = enc((CUtensorMap*)out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
