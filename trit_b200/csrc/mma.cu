@@ -34,6 +34,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "device.cuh"
@@ -43,16 +44,28 @@ namespace trit {
 namespace {
 
 constexpr int TC_M = 128;
-constexpr int TC_N = 64;
-constexpr int TC_KT = 128;  // K bytes a stage (four MMA steps of K = 32)
+constexpr int TC_NMAX = 64;  // frames a CTA at most: the frame buffers' row multiple
+constexpr int TC_FBOX = 16;  // frame rows a TMA box (a CTA of N frames loads N / 16)
+constexpr int TC_KT = 128;   // K bytes a stage (four MMA steps of K = 32)
+constexpr int TC_GPS = TC_KT / 32;  // groups a stage holds at most (Q8_0)
 constexpr int TC_STAGES = 4;
-constexpr int TC_BUFS = 4;
-constexpr int TC_EPI_WARPS = 8;   // two per TMEM lane quarter, 32 columns each
+constexpr int TC_EPI_WARPS = 8;  // two per TMEM lane quarter, N / 2 columns each
 constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
 constexpr int A_STAGE = TC_M * TC_KT;  // 16 KB
-constexpr int B_STAGE = TC_N * TC_KT;  // 8 KB
-constexpr int TC_TMEM_COLS = TC_BUFS * TC_N;  // 256 (a power of two >= 32)
 constexpr long long TC_WAIT_NS = 2000000000ll;  // 2 s
+
+// A CTA's frame tile: N frames (the MMA's N). A TMEM buffer holds one
+// stage's group accumulators side by side (TC_GPS x N columns).
+template <int N>
+struct TcShape {
+  static_assert(N == 16 || N == 32 || N == 64, "frame tiles of 16, 32 or 64");
+  static constexpr int B_STAGE = N * TC_KT;
+  static constexpr int BUF_COLS = TC_GPS * N;
+  static constexpr int BUFS = N == 16 ? 4 : 2;
+  static constexpr int TMEM_COLS = BUFS * BUF_COLS;  // 512, 256, 256: powers of two
+  static constexpr int CW = N / 2;                   // columns an epilogue warp folds
+  static constexpr int CTAS = N == 64 ? 1 : 2;       // CTAs an SM holds (TMEM, shared memory)
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -121,16 +134,18 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
 
 // Instruction descriptor of kind::i8: D s32 (bits 4-5 = 2), A and B s8
 // (bits 7-9, 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_N >> 3) << 17) |
-                            ((uint32_t)(TC_M >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_i8(int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
+}
 
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+// D = A B (+ D when `accumulate`).
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
   uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate), "r"(mask0), "r"(mask1), "r"(mask2), "r"(mask3));
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(mask0), "r"(mask1), "r"(mask2), "r"(mask3));
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -141,14 +156,28 @@ __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::aft
 
 #define TC_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), \
                  "=r"(r[i + 6]), "=r"(r[i + 7])
-// 32 consecutive TMEM columns of this warp's 32 lanes: r[j] = column j of
+// C consecutive TMEM columns of this warp's 32 lanes: r[j] = column j of
 // the thread's lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : TC_R8(0), TC_R8(8), TC_R8(16), TC_R8(24)
-      : "r"(taddr));
+template <int C>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[C]) {
+  static_assert(C == 8 || C == 16 || C == 32, "8, 16 or 32 columns");
+  if constexpr (C == 32) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : TC_R8(0), TC_R8(8), TC_R8(16), TC_R8(24)
+        : "r"(taddr));
+  } else if constexpr (C == 16) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : TC_R8(0), TC_R8(8)
+        : "r"(taddr));
+  } else {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : TC_R8(0)
+                 : "r"(taddr));
+  }
 }
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   float2 d;
@@ -174,46 +203,96 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
 }
-// Every accumulator starts at the bits of 1.5 * 2^23 (kBias); after the
-// MMAs add the i32 dot, the word is the float 1.5 * 2^23 + dot (ulp 1 for
-// |dot| <= 2^22), and subtracting 1.5 * 2^23 gives f32(dot) exactly.
-constexpr uint32_t kBias = 0x4B400000u;
-__device__ __forceinline__ float2 biased_dots(uint32_t a, uint32_t b) {
-  return add2(make_float2(__uint_as_float(a), __uint_as_float(b)), make_float2(-12582912.0f, -12582912.0f));
+// Two i32 dots as exact floats: the bits of 1.5 * 2^23 plus the dot are
+// the float 1.5 * 2^23 + dot (ulp 1 for |dot| <= 2^22), and subtracting
+// 1.5 * 2^23 gives f32(dot) exactly.
+__device__ __forceinline__ float2 dots_to_float2(uint32_t a, uint32_t b) {
+  return add2(make_float2(__int_as_float(0x4B400000 + (int)a), __int_as_float(0x4B400000 + (int)b)),
+              make_float2(-12582912.0f, -12582912.0f));
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-// kBias into 32 consecutive TMEM columns of this warp's 32 lanes.
-__device__ __forceinline__ void tmem_st32_bias(uint32_t taddr) {
-  const uint32_t v = kBias;
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-      "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
-      "r"(v)
-      : "memory");
+// The weight scales of 8 consecutive groups of one row, as loaded: Q8_0 f16
+// (a: 8 halves), f32 per group (a, b: 8 floats) or one f32 per row (a.x).
+struct Ws8 {
+  uint4 a, b;
+  __device__ float get(const DMat& W, int i) const {
+    if (W.kind == kQ8_0) {
+      const uint32_t w = (i < 2) ? a.x : (i < 4) ? a.y : (i < 6) ? a.z : a.w;
+      return f16_bits_to_f32((i & 1) ? (w >> 16) : (w & 0xFFFF));
+    }
+    if (W.kind == kInt8Row) return __uint_as_float(a.x);
+    const uint4 v = (i < 4) ? a : b;
+    const int j = i & 3;
+    return __uint_as_float(j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w);
+  }
+};
+// Whether every row's chunks of 8 scales start 16-byte aligned.
+__device__ __forceinline__ bool ws_vector_ok(const DMat& W, int groups) {
+  if (W.kind == kQ8_0) return groups % 8 == 0 && ((uintptr_t)W.scales & 15) == 0;
+  if (W.kind == kInt8Row) return true;
+  return groups % 4 == 0 && ((uintptr_t)W.scales & 15) == 0;
+}
+__device__ __forceinline__ Ws8 load_ws8(const DMat& W, int row, bool live, int g0, int groups, bool vec) {
+  Ws8 r{make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+  if (!live || g0 >= groups) return r;
+  if (W.kind == kInt8Row) {
+    r.a.x = __float_as_uint(((const float*)W.scales)[row]);
+    return r;
+  }
+  if (vec && g0 + 8 <= groups) {
+    if (W.kind == kQ8_0) {
+      r.a = __ldg((const uint4*)((const uint16_t*)W.scales + (size_t)row * groups + g0));
+    } else {
+      const uint4* p = (const uint4*)((const float*)W.scales + (size_t)row * groups + g0);
+      r.a = __ldg(p);
+      r.b = __ldg(p + 1);
+    }
+    return r;
+  }
+  // Unaligned rows or the last chunk: one scale at a time.
+  uint32_t v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = 0;
+  for (int i = 0; i < 8 && g0 + i < groups; ++i) {
+    if (W.kind == kQ8_0) v[i] = ((const uint16_t*)W.scales)[(size_t)row * groups + g0 + i];
+    else v[i] = __float_as_uint(((const float*)W.scales)[(size_t)row * groups + g0 + i]);
+  }
+  if (W.kind == kQ8_0) {
+    r.a = make_uint4(v[0] | (v[1] << 16), v[2] | (v[3] << 16), v[4] | (v[5] << 16), v[6] | (v[7] << 16));
+  } else {
+    r.a = make_uint4(v[0], v[1], v[2], v[3]);
+    r.b = make_uint4(v[4], v[5], v[6], v[7]);
+  }
+  return r;
 }
 
 struct TcSmem {
-  uint64_t full[TC_STAGES], empty[TC_STAGES], tfull[TC_BUFS], tempty[TC_BUFS], drain;
+  uint64_t full[TC_STAGES], empty[TC_STAGES], tfull[4], tempty[4], drain;
   uint32_t tmem;
   int abort;
 };
 
 // y (m x ldy) <- the product of W (rows [0, n)) and the quantized frames
 // xq / xs (m rows). mode kEpOut: y = acc; kEpResid: y += acc (times mult).
-__global__ void __launch_bounds__(TC_THREADS, 1)
+template <int N>
+__global__ void __launch_bounds__(TC_THREADS, TcShape<N>::CTAS)
     k_gemm_tc(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, DMat W,
               const float* xs, int m, int mode, float* y, int ldy, float resid_mult, int* status) {
+  using T = TcShape<N>;
+  constexpr int CW = T::CW;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* a_st = base;
   uint8_t* b_st = a_st + TC_STAGES * A_STAGE;
   const int G = W.agroup, groups = W.k / G;
-  float* xs_s = (float*)(b_st + TC_STAGES * B_STAGE);  // [groups][TC_N]
-  TcSmem* S = (TcSmem*)(xs_s + TC_N * groups);
+  // A stage holds 4 groups of 32 (Q8_0) or one of 128.
+  const int gshift = (G == 32) ? 2 : 0, gmask = (1 << gshift) - 1;
+  constexpr int XP = N + 4;  // xs_s row pitch: conflict-free staging, 16-byte rows
+  float* xs_s = (float*)(b_st + TC_STAGES * T::B_STAGE);  // [groups][XP]
+  TcSmem* S = (TcSmem*)(xs_s + XP * groups);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * TC_M, f0 = blockIdx.y * TC_N;
+  const int n0 = blockIdx.x * TC_M, f0 = blockIdx.y * N;
   const int ktiles = W.k / TC_KT;
   volatile int* abort = &S->abort;
 
@@ -222,7 +301,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&S->full[s], 1);
       mbar_init(&S->empty[s], 1);
     }
-    for (int b = 0; b < TC_BUFS; ++b) {
+    for (int b = 0; b < T::BUFS; ++b) {
       mbar_init(&S->tfull[b], 1);
       mbar_init(&S->tempty[b], 32 * TC_EPI_WARPS);
     }
@@ -232,7 +311,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S->tmem)),
-                 "r"(TC_TMEM_COLS)
+                 "r"(T::TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -247,9 +326,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int kt = 0; kt < ktiles; ++kt) {
         const int s = kt % TC_STAGES;
         if (!mbar_wait(&S->empty[s], ((kt / TC_STAGES) & 1) ^ 1, abort)) break;
-        mbar_expect_tx(&S->full[s], A_STAGE + B_STAGE);
+        mbar_expect_tx(&S->full[s], A_STAGE + T::B_STAGE);
         tma_load_2d(a_st + s * A_STAGE, &amap, &S->full[s], kt * TC_KT, n0);
-        tma_load_2d(b_st + s * B_STAGE, &bmap, &S->full[s], kt * TC_KT, f0);
+#pragma unroll
+        for (int i = 0; i < N / TC_FBOX; ++i)
+          tma_load_2d(b_st + s * T::B_STAGE + i * TC_FBOX * TC_KT, &bmap, &S->full[s], kt * TC_KT, f0 + i * TC_FBOX);
         issued = kt + 1;
       }
       if (*abort) {
@@ -264,28 +345,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t a0 = smem_u32(a_st), b0 = smem_u32(b_st);
-      bool ok = true;
-      for (int kt = 0; kt < ktiles && ok; ++kt) {
-        const int s = kt % TC_STAGES;
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int s = kt % TC_STAGES, b = kt % T::BUFS;
         if (!mbar_wait(&S->full[s], (kt / TC_STAGES) & 1, abort)) break;
+        // The stage's accumulators, read back by the epilogue.
+        if (!mbar_wait(&S->tempty[b], (kt / T::BUFS) & 1, abort)) break;
         fence_after();
+#pragma unroll
         for (int j = 0; j < TC_KT / 32; ++j) {
-          const int step = kt * (TC_KT / 32) + j;  // K = 32 steps so far
-          const int g = step * 32 / G;
-          const bool first = (step * 32) % G == 0, last = ((step + 1) * 32) % G == 0;
-          const int b = g % TC_BUFS;
-          if (first) {
-            if (!mbar_wait(&S->tempty[b], (g / TC_BUFS) & 1, abort)) {
-              ok = false;
-              break;
-            }
-            fence_after();
-          }
+          const int gi = (j * 32) / G;  // the group within the stage
           const uint64_t ad = smem_desc_sw128(a0 + s * A_STAGE + j * 32);
-          const uint64_t bd = smem_desc_sw128(b0 + s * B_STAGE + j * 32);
-          mma_i8(tmem + b * TC_N, ad, bd, 1u);
-          if (last) mma_commit(&S->tfull[b]);
+          const uint64_t bd = smem_desc_sw128(b0 + s * T::B_STAGE + j * 32);
+          mma_i8(tmem + b * T::BUF_COLS + gi * N, ad, bd, idesc_i8(N), (j * 32) % G ? 1u : 0u);
         }
+        mma_commit(&S->tfull[b]);
         mma_commit(&S->empty[s]);
       }
       // Every MMA issued has finished once `drain` completes.
@@ -299,98 +372,103 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int lr = quarter * 32 + lane;
     const int row = n0 + lr;
     const bool live = row < W.n;
-    const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16) + half * 32;  // + buffer * TC_N
-    // Bias every accumulator, then hand all of them to the MMA thread.
-    for (int b = 0; b < TC_BUFS; ++b) tmem_st32_bias(tl + b * TC_N);
-    tmem_wait_st();
-    fence_before();
-    for (int b = 0; b < TC_BUFS; ++b) mbar_arrive(&S->tempty[b]);
-    // Weight scales 8 groups ahead, so their loads overlap the MMAs.
-    float wcur[8], wnxt[8];
+    const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16) + half * CW;
+    // Every buffer starts free.
+    for (int b = 0; b < T::BUFS; ++b) mbar_arrive(&S->tempty[b]);
+    // Weight scales in chunks of 8 groups, loaded 3 chunks ahead.
+    const bool wvec = ws_vector_ok(W, groups);
+    Ws8 wq[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) wcur[i] = (live && i < groups) ? weight_scale(W, row, i) : 0.0f;
+    for (int c = 0; c < 3; ++c) wq[c] = load_ws8(W, row, live, c * 8, groups, wvec);
     // The frames' activation scales, [group][frame] (frames past m read as
-    // 0): coalesced reads of xs rows, eight in flight per thread, while the
-    // first stages load and multiply.
+    // 0), while the first stages load and multiply. A warp moves blocks of
+    // 8 groups x 4 frames: 32-byte pieces of 4 xs rows, stored at pitch
+    // XP (XP % 32 is 4 or 20) on 32 distinct banks; eight in flight per
+    // thread.
     {
-      const int total = TC_N * groups, t0 = threadIdx.x - 64, nt = 32 * TC_EPI_WARPS;
-      for (int i0 = t0; i0 < total; i0 += 8 * nt) {
+      const int gblocks = (groups + 7) / 8, tasks = gblocks * (N / 4) * 32;
+      const int t0 = threadIdx.x - 64, nt = 32 * TC_EPI_WARPS;
+      for (int i0 = t0; i0 < tasks; i0 += 8 * nt) {
         float v[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          const int i = i0 + u * nt, f = i / groups, g = i - f * groups;
-          v[u] = (i < total && f0 + f < m) ? __ldg(xs + (size_t)(f0 + f) * groups + g) : 0.0f;
+          const int i = i0 + u * nt, b = i >> 5, l = i & 31;
+          const int g = (b % gblocks) * 8 + (l >> 2), f = (b / gblocks) * 4 + (l & 3);
+          v[u] = (i < tasks && g < groups && f0 + f < m) ? __ldg(xs + (size_t)(f0 + f) * groups + g) : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          const int i = i0 + u * nt, f = i / groups, g = i - f * groups;
-          if (i < total) xs_s[g * TC_N + f] = v[u];
+          const int i = i0 + u * nt, b = i >> 5, l = i & 31;
+          const int g = (b % gblocks) * 8 + (l >> 2), f = (b / gblocks) * 4 + (l & 3);
+          if (i < tasks && g < groups) xs_s[g * XP + f] = v[u];
         }
       }
       asm volatile("bar.sync 1, %0;" ::"r"(32 * TC_EPI_WARPS) : "memory");
     }
-    float2 acc[16];  // frames 32 half + 2 i, + 1
+    float2 acc[CW / 2];  // frames CW half + 2 i, + 1
 #pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] = make_float2(0.0f, 0.0f);
-    auto fetch = [&](int g, uint32_t (&r)[32]) -> bool {
-      const int b = g % TC_BUFS;
-      if (!mbar_wait(&S->tfull[b], (g / TC_BUFS) & 1, abort)) return false;
+    for (int i = 0; i < CW / 2; ++i) acc[i] = make_float2(0.0f, 0.0f);
+    // Group g: stage g >> gshift, TMEM buffer stage % BUFS, columns
+    // (g & gmask) * N.. of it.
+    auto col = [&](int g) -> uint32_t {
+      return tl + ((g >> gshift) % T::BUFS) * T::BUF_COLS + (g & gmask) * N;
+    };
+    auto stage_ready = [&](int st) -> bool {
+      if (!mbar_wait(&S->tfull[st % T::BUFS], (st / T::BUFS) & 1, abort)) return false;
       fence_after();
-      tmem_ld32(tl + b * TC_N, r);
       return true;
     };
     // One group: the next group's accumulator loads from TMEM while this
-    // group's chains run; this group's buffer goes back to the MMA thread
-    // once its bias store (issued a group earlier) has landed.
-    auto step = [&](int g, float w, const uint32_t (&rc)[32], uint32_t (&rn)[32]) -> bool {
-      const bool more = g + 1 < groups;
-      if (more && !fetch(g + 1, rn)) return false;
+    // group's chains run; the last group of a stage hands the stage's
+    // buffer back.
+    auto step = [&](int g, float w, const uint32_t (&rc)[CW], uint32_t (&rn)[CW]) -> bool {
+      const bool more = g + 1 < groups, ends = ((g + 1) & gmask) == 0;
+      if (more) {
+        if (ends && !stage_ready((g + 1) >> gshift)) return false;
+        tmem_ld<CW>(col(g + 1), rn);
+      }
       const float2 ws2 = make_float2(w, w);
-      const float4* xg = (const float4*)(xs_s + g * TC_N + half * 32);
+      const float4* xg = (const float4*)(xs_s + g * XP + half * CW);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < CW / 4; ++q) {
         const float4 xv = xg[q];
-        acc[2 * q] = fma2(biased_dots(rc[4 * q], rc[4 * q + 1]), mul2(ws2, make_float2(xv.x, xv.y)), acc[2 * q]);
+        acc[2 * q] = fma2(dots_to_float2(rc[4 * q], rc[4 * q + 1]), mul2(ws2, make_float2(xv.x, xv.y)), acc[2 * q]);
         acc[2 * q + 1] =
-            fma2(biased_dots(rc[4 * q + 2], rc[4 * q + 3]), mul2(ws2, make_float2(xv.z, xv.w)), acc[2 * q + 1]);
+            fma2(dots_to_float2(rc[4 * q + 2], rc[4 * q + 3]), mul2(ws2, make_float2(xv.z, xv.w)), acc[2 * q + 1]);
       }
       tmem_wait_ld();
-      tmem_wait_st();
-      fence_before();
-      mbar_arrive(&S->tempty[g % TC_BUFS]);
-      if (more) tmem_st32_bias(tl + ((g + 1) % TC_BUFS) * TC_N);
+      if (ends) {
+        fence_before();
+        mbar_arrive(&S->tempty[(g >> gshift) % T::BUFS]);
+      }
       return true;
     };
-    uint32_t ra[32], rb[32];
-    bool ok = fetch(0, ra);
+    uint32_t ra[CW], rb[CW];
+    bool ok = stage_ready(0);
     if (ok) {
+      tmem_ld<CW>(col(0), ra);
       tmem_wait_ld();
-      tmem_st32_bias(tl);
     }
-    for (int gc = 0; gc < groups && ok; gc += 8) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) wnxt[i] = (live && gc + 8 + i < groups) ? weight_scale(W, row, gc + 8 + i) : 0.0f;
+    // Eight groups with the scales of chunk buffer `c`; the buffer three
+    // chunks on starts loading first.
+    auto chunk = [&](int gc, int c) -> bool {
+      wq[(c + 3) & 3] = load_ws8(W, row, live, gc + 24, groups, wvec);
 #pragma unroll
       for (int i = 0; i < 8; i += 2) {
-        if (gc + i >= groups) break;
-        if (!step(gc + i, wcur[i], ra, rb)) {
-          ok = false;
-          break;
-        }
-        if (gc + i + 1 >= groups) break;
-        if (!step(gc + i + 1, wcur[i + 1], rb, ra)) {
-          ok = false;
-          break;
-        }
+        if (gc + i >= groups) return true;
+        if (!step(gc + i, wq[c].get(W, i), ra, rb)) return false;
+        if (gc + i + 1 >= groups) return true;
+        if (!step(gc + i + 1, wq[c].get(W, i + 1), rb, ra)) return false;
       }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) wcur[i] = wnxt[i];
+      return true;
+    };
+    for (int gc = 0; gc < groups && ok; gc += 32) {
+      ok = chunk(gc, 0) && chunk(gc + 8, 1) && chunk(gc + 16, 2) && chunk(gc + 24, 3);
     }
-    tmem_wait_st();
     if (ok && live) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int f = f0 + half * 32 + j;
+      for (int j = 0; j < CW; ++j) {
+        const int f = f0 + half * CW + j;
         const float v = (j & 1) ? acc[j >> 1].y : acc[j >> 1].x;
         if (f < m) {
           float* p = y + (size_t)f * ldy + row;
@@ -404,7 +482,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(T::TMEM_COLS) : "memory");
   }
   if (threadIdx.x == 0 && S->abort) atomicExch(status, 1);
 }
@@ -437,9 +515,9 @@ __global__ void k_expand_ternary(const uint32_t* words, size_t n, int k, int8_t*
   }
 }
 
-size_t tc_smem_bytes(const DMat& W) {
+size_t tc_smem_bytes(const DMat& W, int n) {
   size_t groups = W.k / W.agroup;
-  return 1024 + (size_t)TC_STAGES * (A_STAGE + B_STAGE) + (size_t)TC_N * groups * 4 + sizeof(TcSmem);
+  return 1024 + (size_t)TC_STAGES * (A_STAGE + (size_t)n * TC_KT) + (size_t)(n + 4) * groups * 4 + sizeof(TcSmem);
 }
 
 typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -461,7 +539,7 @@ EncodeTiled encoder() {
 
 }  // namespace
 
-int tc_frames() { return TC_N; }
+int tc_frames() { return TC_NMAX; }
 
 // A 2-D view (k bytes, rows) of a row-major int8 matrix [rows][k]; a box is
 // one stage (TC_KT = 128 bytes of K) of `box_rows` rows, written to shared
@@ -486,26 +564,64 @@ cudaError_t make_tc_weight_map(TcMap* out, const DMat& W, const void* codes8) {
   return make_tc_map(out, codes8, (size_t)W.n, (size_t)W.k, TC_M);
 }
 cudaError_t make_tc_frame_map(TcMap* out, const int8_t* xq, size_t rows_cap, size_t k) {
-  return make_tc_map(out, xq, rows_cap, k, TC_N);
+  return make_tc_map(out, xq, rows_cap, k, TC_FBOX);
+}
+
+// The frame tile (16, 32 or 64 frames a CTA) for an n x k product of m
+// frames: the fewest waves of CTAs, each wave weighted by the time a CTA
+// of that tile takes per stage relative to a 64-frame CTA (measured).
+int tc_frame_tile(int n, int m, int sms) {
+  const int rows = (n + TC_M - 1) / TC_M;
+  const int tiles[3] = {64, 32, 16}, per_sm[3] = {1, 2, 2};
+  const double weight[3] = {1.0, 0.965, 0.6};
+  int best = 64;
+  double best_cost = 1e30;
+  for (int i = 0; i < 3; ++i) {
+    const long ctas = (long)rows * ((m + tiles[i] - 1) / tiles[i]);
+    const long waves = (ctas + (long)sms * per_sm[i] - 1) / ((long)sms * per_sm[i]);
+    const double cost = waves * weight[i];
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = tiles[i];
+    }
+  }
+  return best;
+}
+
+template <int N>
+cudaError_t launch_tc_n(const TcMap& amap, const TcMap& bmap, const DMat& W, const float* xs, int m, int mode,
+                        float* y, int ldy, float resid_mult, int* status, cudaStream_t s, int dev) {
+  size_t smem = tc_smem_bytes(W, N);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  static bool configured[64] = {};
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  dim3 grid((W.n + TC_M - 1) / TC_M, (m + N - 1) / N);
+  k_gemm_tc<N><<<grid, TC_THREADS, smem, s>>>(*(const CUtensorMap*)&amap, *(const CUtensorMap*)&bmap, W, xs, m, mode,
+                                               y, ldy, resid_mult, status);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_gemm_tc(const TcMap& amap, const TcMap& bmap, const DMat& W, const float* xs, int m, int mode,
                            float* y, int ldy, float resid_mult, int* status, cudaStream_t s) {
   if (W.k % TC_KT || (W.agroup != 32 && W.agroup != 128) || m <= 0) return cudaErrorInvalidValue;
-  size_t smem = tc_smem_bytes(W);
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
-  dim3 grid((W.n + TC_M - 1) / TC_M, (m + TC_N - 1) / TC_N);
-  k_gemm_tc<<<grid, TC_THREADS, smem, s>>>(*(const CUtensorMap*)&amap, *(const CUtensorMap*)&bmap, W, xs, m, mode, y,
-                                            ldy, resid_mult, status);
-  return cudaGetLastError();
+  static int sms[64] = {};
+  if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  // TRIT_TC_FRAMES=16, 32 or 64 fixes the frame tile (tests, tuning).
+  static const int forced = [] {
+    const char* e = getenv("TRIT_TC_FRAMES");
+    const int v = e ? atoi(e) : 0;
+    return (v == 16 || v == 32 || v == 64) ? v : 0;
+  }();
+  const int tile = forced ? forced : tc_frame_tile(W.n, m, std::max(dev < 64 ? sms[dev] : 148, 1));
+  if (tile == 16) return launch_tc_n<16>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
+  if (tile == 32) return launch_tc_n<32>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
+  return launch_tc_n<64>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
 }
 
 cudaError_t launch_expand_ternary(const DMat& W, int8_t* out, cudaStream_t s) {
