@@ -371,6 +371,18 @@ def q8_0_blocks(values: np.ndarray) -> np.ndarray:
     return out.reshape(-1)
 
 
+def sweep_shapes(args) -> list:
+    if not getattr(args, "shapes", None):
+        return SWEEP_SHAPES
+    return [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",")]
+
+
+def sweep_rows(args) -> list:
+    if not getattr(args, "rows", None):
+        return SWEEP_ROWS
+    return [int(v) for v in args.rows.split(",")]
+
+
 def run_sweep(args, r: dp.Rank) -> None:
     """C4: each Q8_0 product (W8A8, Int8::from_q8_0) at 1, 4, 16, 64 rows,
     `reps` repetitions through trit_dense_forward_device; copies of the
@@ -386,12 +398,12 @@ def run_sweep(args, r: dp.Rank) -> None:
     cases, total_bytes, total_s = [], 0.0, 0.0
     launches = 0
     with Clocks(r.local) as clocks:
-        for (n, k) in SWEEP_SHAPES:
+        for (n, k) in sweep_shapes(args):
             blocks = q8_0_blocks(rng.normal(0, 0.02, (n, k)).astype(np.float32))
             wbytes = n * k * 34 // 32
             copies = max(1, -(-256 * 2 ** 20 // wbytes))
             layers = [Dense.q8_0(blocks, n, k, device=r.local) for _ in range(copies)]
-            for m in SWEEP_ROWS:
+            for m in sweep_rows(args):
                 x = torch.from_numpy(rng.normal(0, 1, (m, k)).astype(np.float32)).cuda()
                 y = torch.empty((m, n), dtype=torch.float32, device="cuda")
                 # A stream of our own: its handle is never 0, which the C ABI
@@ -465,6 +477,8 @@ def main() -> None:
     ap.add_argument("--decode", default=os.environ.get("TRIT_DECODE", "persistent"))
     ap.add_argument("--kv", default="f16")
     ap.add_argument("--reps", type=int, default=1000, help="repetitions per case of the op sweep")
+    ap.add_argument("--shapes", help="op sweep shapes instead of the workload's, e.g. 16384x3072,3072x8192")
+    ap.add_argument("--rows", help="op sweep row counts instead of the workload's, e.g. 64,128,512")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--streams", type=int, help="streams per GPU instead of the workload's (profiling runs)")
     ap.add_argument("--prompt", type=int, help="prompt ids instead of the workload's")

@@ -11,7 +11,8 @@ from trit_b200 import CausalLm
 
 pytestmark = pytest.mark.gpu
 
-FORMATS = ["mini_qwen3_q8_0", "mini_qwen3_int8", "mini_qwen3_ternary", "mini_mistral_q8_0", "mini_granite_q8_0"]
+FORMATS = ["mini_qwen3_q8_0", "mini_qwen3_int8", "mini_qwen3_ternary", "mini_mistral_q8_0", "mini_granite_q8_0",
+           "mini_gqa8_q8_0", "mini_mha_q8_0"]
 
 
 def _prompts(vocab, lens, seed):
@@ -33,6 +34,23 @@ def test_batch_matches_oracle_per_stream(mini_models, name, kv):
         assert lm.generate_batch(prompts, max_new=12) == want
         t = lm.last_timing()
         assert t["decode_steps"] == 11 * len(prompts) and t["launches"] > 0
+
+
+@pytest.mark.parametrize("name", ["mini_qwen3_q8_0", "mini_mistral_q8_0", "mini_gqa8_q8_0", "mini_mha_q8_0"])
+@pytest.mark.parametrize("kv", ["f32", "f16"])
+def test_one_row_attention_logits_match_oracle(mini_models, name, kv):
+    """The one-row attention of decode steps (2, 4, 8 and 1 query heads a kv
+    head) through the layered decode loop: tokens and logits bit for bit,
+    over cache pages of 64 positions."""
+    path = mini_models[name]
+    oracle = O.Oracle(path, kv_f16=(kv == "f16"))
+    prompt = np.random.default_rng(41).integers(0, oracle.vocab, size=70).tolist()
+    ref = oracle.generate(prompt, 10, trace=True)
+    with CausalLm.load(path, kv=kv, decode="layered", max_context=160) as lm:
+        toks, logits = lm.generate_traced(prompt, max_new=10)
+    assert toks == ref["tokens"]
+    for i in range(len(toks)):
+        assert np.array_equal(logits[i], ref["logits"][i]), f"step {i}"
 
 
 def test_many_streams_and_stops(mini_models):

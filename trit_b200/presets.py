@@ -27,6 +27,9 @@ MINI_MISTRAL = dict(MINISTRAL_3B, hidden_size=256, intermediate_size=512, num_hi
 
 MINI_GRANITE = dict(MINI_QWEN3, model_type="granite", embedding_multiplier=2.0, attention_multiplier=0.0078125,
                     residual_multiplier=0.8, logits_scaling=4.0)
+# Eight query heads a kv head, and one (plain multi-head attention).
+MINI_GQA8 = dict(MINI_QWEN3, num_attention_heads=8, num_key_value_heads=1)
+MINI_MHA = dict(MINI_QWEN3, num_attention_heads=4, num_key_value_heads=4)
 
 CONFIGS = {
     # name: (config, format, seed)
@@ -39,6 +42,8 @@ CONFIGS = {
     "mini_qwen3_ternary": (MINI_QWEN3, "ternary", 9),
     "mini_mistral_q8_0": (MINI_MISTRAL, "q8_0", 10),
     "mini_granite_q8_0": (MINI_GRANITE, "q8_0", 11),
+    "mini_gqa8_q8_0": (MINI_GQA8, "q8_0", 12),
+    "mini_mha_q8_0": (MINI_MHA, "q8_0", 13),
 }
 
 
