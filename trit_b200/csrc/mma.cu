@@ -418,15 +418,8 @@ __global__ void __launch_bounds__(TC_THREADS, TcShape<N>::CTAS)
       fence_after();
       return true;
     };
-    // One group: the next group's accumulator loads from TMEM while this
-    // group's chains run; the last group of a stage hands the stage's
-    // buffer back.
-    auto step = [&](int g, float w, const uint32_t (&rc)[CW], uint32_t (&rn)[CW]) -> bool {
-      const bool more = g + 1 < groups, ends = ((g + 1) & gmask) == 0;
-      if (more) {
-        if (ends && !stage_ready((g + 1) >> gshift)) return false;
-        tmem_ld<CW>(col(g + 1), rn);
-      }
+    // The f32 chains of group g from its dots.
+    auto fold = [&](int g, float w, const uint32_t (&rc)[CW]) {
       const float2 ws2 = make_float2(w, w);
       const float4* xg = (const float4*)(xs_s + g * XP + half * CW);
 #pragma unroll
@@ -436,34 +429,79 @@ __global__ void __launch_bounds__(TC_THREADS, TcShape<N>::CTAS)
         acc[2 * q + 1] =
             fma2(dots_to_float2(rc[4 * q + 2], rc[4 * q + 3]), mul2(ws2, make_float2(xv.z, xv.w)), acc[2 * q + 1]);
       }
-      tmem_wait_ld();
-      if (ends) {
-        fence_before();
-        mbar_arrive(&S->tempty[(g >> gshift) % T::BUFS]);
-      }
-      return true;
     };
-    uint32_t ra[CW], rb[CW];
-    bool ok = stage_ready(0);
-    if (ok) {
-      tmem_ld<CW>(col(0), ra);
-      tmem_wait_ld();
-    }
-    // Eight groups with the scales of chunk buffer `c`; the buffer three
-    // chunks on starts loading first.
-    auto chunk = [&](int gc, int c) -> bool {
-      wq[(c + 3) & 3] = load_ws8(W, row, live, gc + 24, groups, wvec);
+    bool ok = true;
+    if (G == 32) {
+      // Q8_0: a stage's four accumulators load GB at a time (one TMEM wait
+      // per batch and one hand-off per stage), then fold in order.
+      constexpr int GB = CW <= 8 ? 4 : 2;
+      auto chunk = [&](int gc, int c) -> bool {
+        wq[(c + 3) & 3] = load_ws8(W, row, live, gc + 24, groups, wvec);
 #pragma unroll
-      for (int i = 0; i < 8; i += 2) {
-        if (gc + i >= groups) return true;
-        if (!step(gc + i, wq[c].get(W, i), ra, rb)) return false;
-        if (gc + i + 1 >= groups) return true;
-        if (!step(gc + i + 1, wq[c].get(W, i + 1), rb, ra)) return false;
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int g0 = gc + 4 * h2, st = g0 >> 2;
+          if (g0 >= groups) return true;
+          if (!stage_ready(st)) return false;
+          const uint32_t base = tl + (st % T::BUFS) * T::BUF_COLS;
+#pragma unroll
+          for (int b0 = 0; b0 < 4; b0 += GB) {
+            uint32_t rs[GB][CW];
+#pragma unroll
+            for (int gi = 0; gi < GB; ++gi) tmem_ld<CW>(base + (b0 + gi) * N, rs[gi]);
+            tmem_wait_ld();
+            if (b0 + GB == 4) {
+              fence_before();
+              mbar_arrive(&S->tempty[st % T::BUFS]);
+            }
+#pragma unroll
+            for (int gi = 0; gi < GB; ++gi) fold(g0 + b0 + gi, wq[c].get(W, 4 * h2 + b0 + gi), rs[gi]);
+          }
+        }
+        return true;
+      };
+      for (int gc = 0; gc < groups && ok; gc += 32) {
+        ok = chunk(gc, 0) && chunk(gc + 8, 1) && chunk(gc + 16, 2) && chunk(gc + 24, 3);
       }
-      return true;
-    };
-    for (int gc = 0; gc < groups && ok; gc += 32) {
-      ok = chunk(gc, 0) && chunk(gc + 8, 1) && chunk(gc + 16, 2) && chunk(gc + 24, 3);
+    } else {
+      // One group: the next group's accumulator loads from TMEM while this
+      // group's chains run; the last group of a stage hands the stage's
+      // buffer back.
+      auto step = [&](int g, float w, const uint32_t (&rc)[CW], uint32_t (&rn)[CW]) -> bool {
+        const bool more = g + 1 < groups, ends = ((g + 1) & gmask) == 0;
+        if (more) {
+          if (ends && !stage_ready((g + 1) >> gshift)) return false;
+          tmem_ld<CW>(col(g + 1), rn);
+        }
+        fold(g, w, rc);
+        tmem_wait_ld();
+        if (ends) {
+          fence_before();
+          mbar_arrive(&S->tempty[(g >> gshift) % T::BUFS]);
+        }
+        return true;
+      };
+      uint32_t ra[CW], rb[CW];
+      ok = stage_ready(0);
+      if (ok) {
+        tmem_ld<CW>(col(0), ra);
+        tmem_wait_ld();
+      }
+      // Eight groups with the scales of chunk buffer `c`; the buffer three
+      // chunks on starts loading first.
+      auto chunk = [&](int gc, int c) -> bool {
+        wq[(c + 3) & 3] = load_ws8(W, row, live, gc + 24, groups, wvec);
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          if (gc + i >= groups) return true;
+          if (!step(gc + i, wq[c].get(W, i), ra, rb)) return false;
+          if (gc + i + 1 >= groups) return true;
+          if (!step(gc + i + 1, wq[c].get(W, i + 1), rb, ra)) return false;
+        }
+        return true;
+      };
+      for (int gc = 0; gc < groups && ok; gc += 32) {
+        ok = chunk(gc, 0) && chunk(gc + 8, 1) && chunk(gc + 16, 2) && chunk(gc + 24, 3);
+      }
     }
     if (ok && live) {
 #pragma unroll
@@ -573,7 +611,7 @@ cudaError_t make_tc_frame_map(TcMap* out, const int8_t* xq, size_t rows_cap, siz
 int tc_frame_tile(int n, int m, int sms) {
   const int rows = (n + TC_M - 1) / TC_M;
   const int tiles[3] = {64, 32, 16}, per_sm[3] = {1, 2, 2};
-  const double weight[3] = {1.0, 0.965, 0.6};
+  const double weight[3] = {1.0, 0.95, 0.6};
   int best = 64;
   double best_cost = 1e30;
   for (int i = 0; i < 3; ++i) {
