@@ -288,6 +288,9 @@ __global__ void __launch_bounds__(TC_THREADS, TcShape<N>::CTAS)
   const int G = W.agroup, groups = W.k / G;
   // A stage holds 4 groups of 32 (Q8_0) or one of 128.
   const int gshift = (G == 32) ? 2 : 0, gmask = (1 << gshift) - 1;
+  // 128-value groups with a multiple of 4 of them: four consecutive stages
+  // (one group each) share a TMEM buffer, as a Q8_0 stage's four groups do.
+  const bool quad128 = G == 128 && groups % 4 == 0;
   constexpr int XP = N + 4;  // xs_s row pitch: conflict-free staging, 16-byte rows
   float* xs_s = (float*)(b_st + TC_STAGES * T::B_STAGE);  // [groups][XP]
   TcSmem* S = (TcSmem*)(xs_s + XP * groups);
@@ -346,19 +349,22 @@ __global__ void __launch_bounds__(TC_THREADS, TcShape<N>::CTAS)
     if (lane == 0) {
       const uint32_t a0 = smem_u32(a_st), b0 = smem_u32(b_st);
       for (int kt = 0; kt < ktiles; ++kt) {
-        const int s = kt % TC_STAGES, b = kt % T::BUFS;
+        // Buffer use u: a stage (Q8_0, other 128-value layers) or four
+        // stages (quad128), each group in its own N columns of the buffer.
+        const int u = quad128 ? kt >> 2 : kt, slot = quad128 ? kt & 3 : 0;
+        const int s = kt % TC_STAGES, b = u % T::BUFS;
         if (!mbar_wait(&S->full[s], (kt / TC_STAGES) & 1, abort)) break;
-        // The stage's accumulators, read back by the epilogue.
-        if (!mbar_wait(&S->tempty[b], (kt / T::BUFS) & 1, abort)) break;
+        // The buffer's accumulators, read back by the epilogue.
+        if (slot == 0 && !mbar_wait(&S->tempty[b], (u / T::BUFS) & 1, abort)) break;
         fence_after();
 #pragma unroll
         for (int j = 0; j < TC_KT / 32; ++j) {
-          const int gi = (j * 32) / G;  // the group within the stage
+          const int gi = slot + (j * 32) / G;  // the group within the buffer
           const uint64_t ad = smem_desc_sw128(a0 + s * A_STAGE + j * 32);
           const uint64_t bd = smem_desc_sw128(b0 + s * T::B_STAGE + j * 32);
           mma_i8(tmem + b * T::BUF_COLS + gi * N, ad, bd, idesc_i8(N), (j * 32) % G ? 1u : 0u);
         }
-        mma_commit(&S->tfull[b]);
+        if (slot == 3 || !quad128) mma_commit(&S->tfull[b]);
         mma_commit(&S->empty[s]);
       }
       // Every MMA issued has finished once `drain` completes.
@@ -431,8 +437,9 @@ __global__ void __launch_bounds__(TC_THREADS, TcShape<N>::CTAS)
       }
     };
     bool ok = true;
-    if (G == 32) {
-      // Q8_0: a stage's four accumulators load GB at a time (one TMEM wait
+    if (G == 32 || quad128) {
+      // Four groups a buffer (a Q8_0 stage, or four 128-value stages):
+      // the four accumulators load GB at a time (one TMEM wait
       // per batch and one hand-off per stage), then fold in order.
       constexpr int GB = CW <= 8 ? 4 : 2;
       auto chunk = [&](int gc, int c) -> bool {
