@@ -20,7 +20,7 @@ def _layer(n, k, seed):
 
 
 @pytest.mark.parametrize("n, k", [(1024, 3072), (3072, 1024), (151936, 1024)])
-@pytest.mark.parametrize("m", [1, 16, 64])
+@pytest.mark.parametrize("m", [1, 5, 16, 64])
 def test_w8a8_product_matches_oracle(n, k, m):
     codes, scales = _layer(n, k, n + k)
     blocks = O.q8_0_blocks(codes.reshape(-1), scales.reshape(-1))

@@ -738,18 +738,34 @@ __global__ void __launch_bounds__(256) k_table(DTable T, const float* xn, int nb
 
 // The token table for batches of streams: each thread keeps lane l of the
 // reference's 16-lane accumulator (k = l mod 16) for 4 vocabulary rows and
-// B streams, so every x value read from shared memory feeds 4 fma and
-// every widened weight B of them. A block owns TABLE_ROWS rows: 16 row
-// groups x 16 lanes. The streams' rows come through shared memory in
-// chunks of TB_KC values (cp.async, double-buffered); codes and scales
-// are read from global memory one k step ahead. The 16 lanes of a row then
-// reduce in the order of _mm512_reduce_add_ps, as k_table does.
+// B streams, so every widened weight feeds B fma and every x pair 4 of
+// them. A block owns TABLE_ROWS rows: 16 row groups x 16 lanes. The
+// streams' rows come through shared memory in chunks of TB_KC values
+// (cp.async, double-buffered), are turned k-major ([k][stream], pitch B + 2
+// so that a half-warp's 8-byte reads of 16 consecutive k hit 32 distinct
+// banks) and are read as stream pairs: one packed f32x2 fma (each lane
+// rounded as the scalar fma) updates one row's chains of two streams.
+// Codes and scales are read from global memory one k step ahead. The 16
+// lanes of a row then reduce in the order of _mm512_reduce_add_ps, as
+// k_table does.
 constexpr int TB_KC = 256;
+
+__device__ __forceinline__ float2 table_fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
 
 template <int B>
 __global__ void __launch_bounds__(256) k_table_rows(DTable T, const float* xn, int nb, float logit_mult,
                                                     float* logits, float* best_val, int* best_idx, int nblocks) {
-  extern __shared__ __align__(16) float xb[];  // [2][B][TB_KC]
+  static_assert(B % 2 == 0, "stream pairs");
+  constexpr int PB = B + 2;                    // k-major pitch
+  extern __shared__ __align__(16) float xb[];  // [2][B][TB_KC] staged, then [TB_KC][PB] k-major
+  float* xt = xb + 2 * B * TB_KC;
   __shared__ float fin[B][TABLE_ROWS];
   const int t = threadIdx.x, l = t & 15, rg = t >> 4;
   const int row0 = blockIdx.x * TABLE_ROWS + rg * 4;
@@ -764,11 +780,11 @@ __global__ void __launch_bounds__(256) k_table_rows(DTable T, const float* xn, i
     }
     cp_commit();
   };
-  float acc[4][B];
+  float2 acc[4][B / 2];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < B; ++b) acc[a][b] = 0.0f;
+    for (int p = 0; p < B / 2; ++p) acc[a][p] = make_float2(0.0f, 0.0f);
   bool live[4];
   const int8_t* crow[4];
 #pragma unroll
@@ -783,7 +799,14 @@ __global__ void __launch_bounds__(256) k_table_rows(DTable T, const float* xn, i
     if (c + 1 < chunks) asm volatile("cp.async.wait_group 1;" ::: "memory");
     else cp_wait_all();
     __syncthreads();
-    const float* xc = xb + (size_t)(c & 1) * B * TB_KC;
+    {
+      const float* xc = xb + (size_t)(c & 1) * B * TB_KC;
+      for (int i = t; i < B * TB_KC; i += 256) {
+        const int b = i / TB_KC, kk = i % TB_KC;
+        xt[kk * PB + b] = xc[b * TB_KC + kk];
+      }
+    }
+    __syncthreads();
     int code[4];
 #pragma unroll
     for (int a = 0; a < 4; ++a) code[a] = crow[a][c * TB_KC + l];
@@ -792,14 +815,18 @@ __global__ void __launch_bounds__(256) k_table_rows(DTable T, const float* xn, i
       int next[4];
 #pragma unroll
       for (int a = 0; a < 4; ++a) next[a] = (st + 1 < TB_KC / 16) ? crow[a][kg + 16] : 0;
-      float w[4];
+      float2 w2[4];
 #pragma unroll
-      for (int a = 0; a < 4; ++a) w[a] = __fmul_rn((float)code[a], table_scale(T, live[a] ? row0 + a : 0, kg / 32));
+      for (int a = 0; a < 4; ++a) {
+        const float w = __fmul_rn((float)code[a], table_scale(T, live[a] ? row0 + a : 0, kg / 32));
+        w2[a] = make_float2(w, w);
+      }
+      const float2* xr = (const float2*)(xt + kk * PB);
 #pragma unroll
-      for (int b = 0; b < B; ++b) {
-        const float xv = xc[b * TB_KC + kk];
+      for (int p = 0; p < B / 2; ++p) {
+        const float2 x2 = xr[p];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) acc[a][b] = __fmaf_rn(xv, w[a], acc[a][b]);
+        for (int a = 0; a < 4; ++a) acc[a][p] = table_fma2(x2, w2[a], acc[a][p]);
       }
 #pragma unroll
       for (int a = 0; a < 4; ++a) code[a] = next[a];
@@ -812,7 +839,7 @@ __global__ void __launch_bounds__(256) k_table_rows(DTable T, const float* xn, i
   for (int a = 0; a < 4; ++a)
 #pragma unroll
     for (int b = 0; b < B; ++b) {
-      float v = acc[a][b];
+      float v = (b & 1) ? acc[a][b >> 1].y : acc[a][b >> 1].x;
       v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 8, 16));
       v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4, 16));
       v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2, 16));
@@ -996,7 +1023,7 @@ static cudaError_t table_pass(const DTable& T, const float* xn, int nb, float mu
 template <int B>
 static cudaError_t table_rows_pass(const DTable& T, const float* xn, int nb, float mult, float* logits,
                                    float* best_val, int* best_idx, cudaStream_t s) {
-  size_t smem = (size_t)2 * B * TB_KC * 4;
+  size_t smem = ((size_t)2 * B * TB_KC + (size_t)TB_KC * (B + 2)) * 4;
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
