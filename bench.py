@@ -373,6 +373,13 @@ def q8_0_blocks(values: np.ndarray) -> np.ndarray:
     return out.reshape(-1)
 
 
+def dense_kernel(n: int, m: int) -> str:
+    """The product kernel trit_dense_forward_device runs for n rows and m
+    frames (the library's rule: the tensor cores from 16 frames, from 4 on
+    matrices of 6144 rows or more, always from 32768 rows)."""
+    return "k_gemm_tc" if (m >= 16 or (m >= 4 and n >= 6144) or n >= 32768) else "k_gemv_slots"
+
+
 def sweep_shapes(args) -> list:
     if not getattr(args, "shapes", None):
         return SWEEP_SHAPES
@@ -459,7 +466,7 @@ def run_sweep(args, r: dp.Rank) -> None:
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "achieved": best["gbs"], "peak": hbm, "unit": "GB/s",
                      "frac": best["gbs"] / hbm, "peak_kind": peak_kind, "traffic": None,
-                     "kernel": f"k_gemv, best case n={best['n']} k={best['k']} m={best['m']}"},
+                     "kernel": f"{dense_kernel(best['n'], best['m'])}, best case n={best['n']} k={best['k']} m={best['m']}"},
         "cases": cases,
         "clocks": clocks.summary(),
     }

@@ -1308,9 +1308,10 @@ void DenseOp::forward_device(const float* x, size_t m, float* y, cudaStream_t s)
     TRIT_CUDA(launch_table(tab, x, (int)m, 1.0f, y, best_val, best_idx, s));
   } else {
     TRIT_CUDA(launch_norm_quant(x, (int)m, mat.k, nullptr, 0.0f, mat.agroup, mat.half, xq, xs, s));
-    // The tensor cores from 16 rows, and from 4 on matrices of 6144 rows or
-    // more (measured with the op sweep: below that the dp4a GEMV wins).
-    const bool use_tc = tc_ok && (m >= 16 || (m >= 4 && mat.n >= 6144));
+    // The tensor cores from 16 rows, from 4 on matrices of 6144 rows or
+    // more, and always from 32768 rows (measured with the op sweep: below
+    // that the dp4a GEMV wins).
+    const bool use_tc = tc_ok && (m >= 16 || (m >= 4 && mat.n >= 6144) || mat.n >= 32768);
     if (use_tc && !tc_tried) {
       // The frame map of the current activation buffer (made again after
       // the buffer grows).
