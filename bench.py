@@ -276,6 +276,8 @@ def run_decode(args, r: dp.Rank) -> None:
         opts.update(max_streams=S, prefill_rows=max(512, S))
     if args.tc_rows is not None:
         opts.update(tc_rows=args.tc_rows)
+    if args.prefill_rows is not None:
+        opts.update(prefill_rows=args.prefill_rows)
     else:
         opts.update(decode=args.decode)
     lm = CausalLm.load(model_dir, **opts)
@@ -485,6 +487,7 @@ def main() -> None:
     ap.add_argument("--config", default="c1", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--decode", default=os.environ.get("TRIT_DECODE", "persistent"))
     ap.add_argument("--tc-rows", type=int, help="rows from which products use the tensor cores (engine option)")
+    ap.add_argument("--prefill-rows", type=int, help="rows a prompt pass (engine option)")
     ap.add_argument("--kv", default="f16")
     ap.add_argument("--reps", type=int, default=1000, help="repetitions per case of the op sweep")
     ap.add_argument("--shapes", help="op sweep shapes instead of the workload's, e.g. 16384x3072,3072x8192")
