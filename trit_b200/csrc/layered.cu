@@ -423,13 +423,24 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
   // Keys (which 0) or values (1) [j0, j0 + n) into kv, row pitch `pitch` floats.
   // Keys (which 0) or values (1) [j0, j0 + n) into dst (cp.async, one
   // commit group; the caller waits).
+  // A thread's chunks walk the rows in order, so the page's base address
+  // is worked out only when a row starts a new page.
   auto stage = [&](int which, int j0, int n, float* dst) {
-    const int cpr = f16 ? 16 : 32;  // 16-byte chunks a row
-    for (int ci = t; ci < n * cpr; ci += 256) {
-      int jj = ci / cpr, cc = ci % cpr, j = j0 + jj;
-      int page = cache.page_table[(size_t)stream * cache.pages_per_stream + j / cache.page_tokens];
-      size_t off = kv_offset(cache, cfg, page, layer, which, kvh, j % cache.page_tokens);
-      const int4* src = f16 ? (const int4*)((const __half*)cache.pool + off) : (const int4*)((const float*)cache.pool + off);
+    const int cshift = f16 ? 4 : 5;  // 16-byte chunks a row: 16 or 32
+    const size_t row_bytes = f16 ? 256 : 512;
+    int pg_start = 0, pg_end = -1;
+    const char* base = nullptr;
+    for (int ci = t; ci < (n << cshift); ci += 256) {
+      const int jj = ci >> cshift, cc = ci & ((1 << cshift) - 1), j = j0 + jj;
+      if (j >= pg_end) {
+        const int pgi = j / cache.page_tokens;
+        pg_start = pgi * cache.page_tokens;
+        pg_end = pg_start + cache.page_tokens;
+        const int page = cache.page_table[(size_t)stream * cache.pages_per_stream + pgi];
+        const size_t off = kv_offset(cache, cfg, page, layer, which, kvh, 0);
+        base = f16 ? (const char*)((const __half*)cache.pool + off) : (const char*)((const float*)cache.pool + off);
+      }
+      const int4* src = (const int4*)(base + (size_t)(j - pg_start) * row_bytes);
       cp_async16(dst + jj * pitch + cc * 4, src + cc);
     }
     cp_commit();
