@@ -73,6 +73,9 @@ void trit_free_text(char *text);
  *   "decode":       "persistent" (default: one kernel runs every greedy
  *                   step of a batch-1 generation) or "layered" (a kernel
  *                   per operation and step)
+ *   "tensor_cores": true (default on sm_100) or false: products of
+ *                   "tc_rows" rows or more on the tensor cores
+ *   "tc_rows":      rows from which a product uses the tensor cores (64)
  *   "config_at":    key path of the decoder settings in config.json ("";
  *                   "thinker_config.text_config." in Qwen3-ASR)
  *   "prefix":       start of every tensor name ("", "thinker.", "llm.")
