@@ -229,7 +229,7 @@ def run_reference(args, r: dp.Rank) -> None:
     if r.rank != 0:
         return
     from oracle import oracle as O
-    from trit_b200 import presets
+    from tests.synth import presets
 
     # Every host thread this process may use: torchrun sets OMP_NUM_THREADS=1
     # for multi-rank runs, which would leave the reference arm one core.
@@ -263,7 +263,8 @@ def run_reference(args, r: dp.Rank) -> None:
 
 # ------------------------------------------------------------ GPU legs ----
 def run_decode(args, r: dp.Rank) -> None:
-    from trit_b200 import CausalLm, lm as lmmod, presets
+    from trit_b200 import CausalLm, lm as lmmod
+    from tests.synth import presets
 
     w = dict(WORKLOADS[args.config])
     for key in ("streams", "prompt", "new"):

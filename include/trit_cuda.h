@@ -6,8 +6,12 @@
  * Hi9841/trit; the entry points follow that interface (each cites the
  * function it stands for) and the rules of include/trit.h:7-18:
  * - Strings are UTF-8 and NUL-terminated.
- * - A call that fails returns NULL or -1; trit_last_error() then gives the
- *   reason, for the calling thread. No C++ exception crosses the ABI.
+ * - A call that fails returns NULL or -1; trit_cuda_last_error() then gives
+ *   the reason, for the calling thread. No C++ exception crosses the ABI.
+ * - Every exported name starts with trit_cuda_, trit_lm_ or trit_dense_, so
+ *   the library can share a process with the reference's own libtrit,
+ *   whose trit_last_error and trit_free_text (ffi/src/lib.rs:186,641) keep
+ *   their meaning; nothing else is exported.
  * - One model handle may be used from several threads; calls on it take
  *   turns (a mutex), as calls on one Trit engine share one worker team.
  *   Do not free a handle while another thread is in a call on it.
@@ -43,8 +47,8 @@ const char *trit_cuda_version(void);
 
 /* The error of the last failed call on this thread, or "" after a success.
  * Valid until the next call on this thread; do not free.
- * (trit_last_error, include/trit.h:44-46; ffi/src/lib.rs:20-45.) */
-const char *trit_last_error(void);
+ * (trit_last_error, include/trit.h:44-46; ffi/src/lib.rs:20-45,186.) */
+const char *trit_cuda_last_error(void);
 
 /* A model folder described without a GPU, as JSON text: its settings as
  * Config::parse reads them (causal_lm.rs:41-77: q/k norms iff model_type
@@ -53,12 +57,13 @@ const char *trit_last_error(void);
  * products and token tables, and the bytes a greedy step reads from device
  * memory for the products and the output table. `options_json` takes the
  * "config_at" and "prefix" keys of trit_lm_load (others are ignored).
- * Free the text with trit_free_text. NULL on failure. */
+ * Free the text with trit_cuda_free_text. NULL on failure. */
 char *trit_lm_inspect(const char *model_dir, const char *options_json);
 
-/* Frees text returned by this library. NULL is a no-op. (trit_free_text,
- * include/trit.h:11.) */
-void trit_free_text(char *text);
+/* Frees text returned by this library (and only by it: the reference's
+ * trit_free_text frees with its own allocator). NULL is a no-op.
+ * (trit_free_text, include/trit.h:11; ffi/src/lib.rs:641.) */
+void trit_cuda_free_text(char *text);
 
 /* Loads a decoder onto a GPU. `options_json` is NULL, "" or an object;
  * every key is optional and an unknown key fails (as trit_load_json,
@@ -202,7 +207,8 @@ void trit_dense_free(TritDense *layer);
  * computes, on device pointers: `codes` (n x k int8, row-major) and
  * `scales` (n x k/32 f16 bits) are the split form of ggml Q8_0 blocks
  * (block b of row r: scales[r * k/32 + b], codes[r * k + 32 b ...]); x is
- * rows x k f32; out is rows x n f32. Its scratch (the int8 activations and
+ * rows x k f32; out is rows x n f32; k is a multiple of 128 from 128 to
+ * 8192 and n a positive multiple of 32. Its scratch (the int8 activations and
  * their scales) is one 1 MiB device array that the library holds on every
  * GPU it is loaded on until the process exits, so rows * k * 9 / 8 must stay
  * within 1 MiB (larger calls fail). All calls share that array and leave
@@ -210,7 +216,7 @@ void trit_dense_free(TritDense *layer);
  * other threads) race; order them on one stream. The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress); make
  * that first call before any stream capture. Returns 0, or -1 with
- * trit_last_error(). Queued on `cuda_stream` (NULL: the default stream);
+ * trit_cuda_last_error(). Queued on `cuda_stream` (NULL: the default stream);
  * does not wait. */
 int trit_dense_q8_0_forward_static(const void *codes, const void *scales, size_t n, size_t k, const float *x,
                                    size_t rows, float *out, void *cuda_stream);

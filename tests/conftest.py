@@ -14,6 +14,6 @@ def pytest_configure(config):
 
 @pytest.fixture(scope="session")
 def mini_models():
-    from trit_b200 import presets
+    from tests.synth import presets
 
     return {name: presets.model_path(name) for name in presets.CONFIGS if name.startswith("mini_")}

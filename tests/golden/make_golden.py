@@ -23,7 +23,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)
 sys.path.insert(0, ROOT)
 
 from oracle import oracle  # noqa: E402
-from trit_b200 import presets  # noqa: E402
+from tests.synth import presets  # noqa: E402
 
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "greedy.json")
 MAX_NEW = 12

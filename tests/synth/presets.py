@@ -63,7 +63,7 @@ def cache_dir() -> str:
 
 def model_path(name: str) -> str:
     """The folder of a synthetic model, written on first use."""
-    from .lm import synthesize
+    from . import synthesize
 
     config, fmt, seed = CONFIGS[name]
     std = weight_std(name)

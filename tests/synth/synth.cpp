@@ -1,4 +1,6 @@
-// Seeded synthetic decoder models for the benchmarks and tests: a model
+// Seeded synthetic decoder models for the benchmarks and tests (test
+// infrastructure, built into tests/synth/libtrit_synth.so, not into the
+// product library): a model
 // folder (config.json + model.gguf) with the tensor names of a Hugging
 // Face Qwen3/Llama checkpoint, which trit_lm_load and the CPU oracle read.
 //
@@ -19,7 +21,8 @@
 #include <cmath>
 #include <thread>
 
-#include "host.h"
+#include "../../trit_b200/csrc/host.h"
+#include "trit_synth.h"
 
 namespace trit {
 namespace {
@@ -318,8 +321,32 @@ void synthesize(const std::string& dir, const std::string& spec_json) {
   w.close();
 }
 
-void synth_normal_row(uint64_t seed, const std::string& name, uint64_t row, size_t k, float sd, float* out) {
-  normal_row(seed, name, row, k, sd, out);
+}  // namespace trit
+
+namespace {
+thread_local std::string g_synth_error;
+}  // namespace
+
+extern "C" {
+
+const char* trit_synth_last_error(void) { return g_synth_error.c_str(); }
+
+int trit_synth_model(const char* dir, const char* spec_json) {
+  g_synth_error.clear();
+  try {
+    if (!dir || !spec_json) throw trit::Error("dir or spec_json is NULL");
+    trit::synthesize(dir, spec_json);
+    return 0;
+  } catch (const std::exception& e) {
+    g_synth_error = e.what();
+  } catch (...) {
+    g_synth_error = "internal error in trit_synth";
+  }
+  return -1;
 }
 
-}  // namespace trit
+void trit_synth_normal_row(uint64_t seed, const char* name, uint64_t row, size_t k, float sd, float* out) {
+  if (name && out) trit::normal_row(seed, name, row, k, sd, out);
+}
+
+}  // extern "C"

@@ -1,5 +1,6 @@
-/* Seeded synthetic decoder models for benchmarks and tests (part of
- * libtrit_cuda.so; host code only, no GPU needed). The reference has no
+/* Seeded synthetic decoder models for benchmarks and tests
+ * (tests/synth/libtrit_synth.so, apart from the product library; host code
+ * only, no GPU needed). The reference has no
  * counterpart: its benchmarks run downloaded checkpoints, which this build
  * replaces with seeded weights of the same shapes.
  */
@@ -22,8 +23,11 @@ extern "C" {
  * "format": "q8_0" | "int8" | "ternary", "seed": N, "std": 0.02,
  * "prefix": start of every tensor name (""), "config_at": key path the
  * settings are nested under in config.json ("", or for example
- * "thinker_config.text_config.")}. Returns 0, or -1 (trit_last_error). */
+ * "thinker_config.text_config.")}. Returns 0, or -1 (trit_synth_last_error). */
 int trit_synth_model(const char *dir, const char *spec_json);
+
+/* The error of the last failed trit_synth_model on this thread. */
+const char *trit_synth_last_error(void);
 
 /* The f32 values of row `row` of tensor `name` (without ".weight") before
  * quantization: k values of N(0, sd) from the model's seed. */

@@ -2,7 +2,7 @@
 that include/*.h declares is exported, the Python signatures cover them,
 and the calls that need no GPU (options, config parsing, argument checks,
 model description) behave as the reference's interface does: a failure
-returns NULL or -1 with the reason in trit_last_error (include/trit.h:7-18,
+returns NULL or -1 with the reason in trit_cuda_last_error (include/trit.h:7-18,
 ffi/src/lib.rs:20-45)."""
 import ctypes
 import glob
@@ -14,7 +14,9 @@ import tempfile
 import numpy as np
 import pytest
 
-from trit_b200 import lm, presets
+from trit_b200 import lm
+from tests import synth
+from tests.synth import presets
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -50,7 +52,7 @@ def test_library_is_built_for_sm_100a_only():
 
 
 def last_error() -> str:
-    return lm.library().trit_last_error().decode()
+    return lm.library().trit_cuda_last_error().decode()
 
 
 def test_version_and_error_text():
@@ -133,7 +135,7 @@ def test_config_at_and_tensor_prefix():
     settings under a key path and tensor names under a prefix."""
     with tempfile.TemporaryDirectory() as tmp:
         cfg = dict(presets.MINI_QWEN3, num_hidden_layers=1, vocab_size=512)
-        lm.synthesize(tmp, cfg, "q8_0", 3, prefix="thinker.", config_at="thinker_config.text_config.")
+        synth.synthesize(tmp, cfg, "q8_0", 3, prefix="thinker.", config_at="thinker_config.text_config.")
         with pytest.raises(lm.TritError):
             lm.inspect(tmp)
         info = lm.inspect(tmp, config_at="thinker_config.text_config.", prefix="thinker.")
@@ -147,7 +149,11 @@ def test_static_entry_checks_its_limits_before_any_device_work():
     assert fn(dummy, dummy, 1024, 1024, dummy, 1024, dummy, None) == -1
     assert "too large for the static scratch" in last_error()
     assert fn(dummy, dummy, 1024, 1000, dummy, 1, dummy, None) == -1
-    assert "multiple of 32" in last_error()
+    assert "multiple of 128" in last_error()
+    # k = 96 is whole Q8_0 blocks but not whole 128-value chunks: rejected
+    # with the reason, before any device work.
+    assert fn(dummy, dummy, 1024, 96, dummy, 1, dummy, None) == -1
+    assert "multiple of 128" in last_error()
     assert fn(None, dummy, 1024, 1024, dummy, 1, dummy, None) == -1
     assert "NULL" in last_error()
 
@@ -156,6 +162,11 @@ def test_dense_argument_checks():
     lib = lm.library()
     assert lib.trit_dense_q8_0(None, 32, 32, 0, 0) is None
     assert "blocks" in last_error()
+    # A W8A8 layer whose k is whole Q8_0 blocks but not whole 128-value
+    # chunks fails at creation (before any device work), not at forward.
+    blocks = np.zeros(32 * 96 // 32 * 34, np.uint8)
+    assert lib.trit_dense_q8_0(blocks.ctypes.data_as(ctypes.c_void_p), 32, 96, 0, 0) is None
+    assert "multiple of 128" in last_error()
     assert lib.trit_dense_forward(None, None, 1, None) == -1
     assert "layer" in last_error()
 
@@ -165,4 +176,34 @@ def test_free_functions_accept_null():
     lib.trit_lm_free(None)
     lib.trit_lm_prefix_free(None)
     lib.trit_dense_free(None)
-    lib.trit_free_text(None)
+    lib.trit_cuda_free_text(None)
+
+
+# The names the reference's own C library (the trit cdylib) exports, from
+# its #[no_mangle] functions (ffi/src/lib.rs); tests/golden/reference_ffi_exports.py
+# wrote the list.
+REFERENCE_EXPORTS = os.path.join(ROOT, "tests", "golden", "reference_ffi_exports.txt")
+
+
+def test_no_export_collides_with_the_reference_library():
+    """A drop-in shares a process with the reference's libtrit (its Rust
+    crate links both): no name may be defined by both libraries, or the
+    dynamic linker binds one library's callers to the other's function."""
+    theirs = set(open(REFERENCE_EXPORTS).read().split())
+    assert "trit_last_error" in theirs and "trit_free_text" in theirs
+    lib = ctypes.CDLL(lm.LIBRARY)
+    clashes = sorted(n for n in theirs if hasattr(lib, n))
+    assert not clashes, clashes
+    ours = set(declared_functions())
+    assert not ours & theirs
+
+
+def test_only_the_header_names_are_exported():
+    import shutil
+    import subprocess
+
+    if not shutil.which("nm"):
+        pytest.skip("nm is not installed")
+    out = subprocess.run(["nm", "-D", "--defined-only", lm.LIBRARY], capture_output=True, text=True, check=True)
+    exported = {line.split()[-1] for line in out.stdout.splitlines() if line.strip()}
+    assert exported == set(declared_functions())

@@ -9,7 +9,7 @@ import numpy as np
 
 import bench
 from oracle import oracle as O
-from trit_b200 import presets
+from tests.synth import presets
 
 
 def test_q8_0_blocks_equal_the_oracle_quantizer():

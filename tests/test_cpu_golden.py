@@ -10,7 +10,7 @@ import pytest
 
 from oracle import oracle
 from tests import golden_cases
-from trit_b200 import presets
+from tests.synth import presets
 
 GOLDEN = golden_cases.load()
 

@@ -16,7 +16,9 @@ import numpy as np
 import pytest
 
 from tests.gguf_read import GGML_F32, GGML_I8, GGML_Q8_0, Gguf
-from trit_b200 import lm, presets
+from trit_b200 import lm
+from tests import synth
+from tests.synth import presets
 
 
 def q8_0_numpy(v: np.ndarray):
@@ -45,9 +47,9 @@ def folders():
 
 
 def test_normal_rows_are_seeded_and_normal():
-    a = lm.normal_row(5, "w", 3, 4096)
-    b = lm.normal_row(5, "w", 3, 4096)
-    c = lm.normal_row(5, "w", 4, 4096)
+    a = synth.normal_row(5, "w", 3, 4096)
+    b = synth.normal_row(5, "w", 3, 4096)
+    c = synth.normal_row(5, "w", 4, 4096)
     assert np.array_equal(a, b) and not np.array_equal(a, c)
     assert abs(a.mean()) < 0.02 * 0.1 and abs(a.std() - 0.02) < 0.02 * 0.05
 
@@ -83,7 +85,7 @@ def test_q8_0_blocks_are_the_reference_quantizer(folders):
                        ("model.embed_tokens", [0, 17, 4095])):
         codes, scales = g.q8_0(name + ".weight")
         for r in rows:
-            v = lm.normal_row(seed, name, r, codes.shape[1], presets.MINI_STD)
+            v = synth.normal_row(seed, name, r, codes.shape[1], presets.MINI_STD)
             c, s = q8_0_numpy(v)
             assert np.array_equal(codes[r], c), (name, r)
             assert np.array_equal(scales[r].view(np.uint16), s.view(np.uint16)), (name, r)
@@ -110,11 +112,11 @@ def test_int8_rows_and_table(folders):
     name = "model.layers.0.mlp.gate_proj"
     codes, scales = g.array(name + ".weight"), g.array(name + ".scales")
     for r in (0, 5, 767):
-        c, s = row_int8_numpy(lm.normal_row(seed, name, r, codes.shape[1], presets.MINI_STD))
+        c, s = row_int8_numpy(synth.normal_row(seed, name, r, codes.shape[1], presets.MINI_STD))
         assert np.array_equal(codes[r], c) and scales[r] == s
     tcodes, tscales = g.array("model.embed_tokens.weight"), g.array("model.embed_tokens.scales")
     for r in (0, 4095):
-        v = lm.normal_row(seed, "model.embed_tokens", r, tcodes.shape[1], presets.MINI_STD)
+        v = synth.normal_row(seed, "model.embed_tokens", r, tcodes.shape[1], presets.MINI_STD)
         for grp in range(tcodes.shape[1] // 32):
             c, s = row_int8_numpy(v[grp * 32:(grp + 1) * 32])
             assert np.array_equal(tcodes[r, grp * 32:(grp + 1) * 32], c) and tscales[r, grp] == s

@@ -6,7 +6,8 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from trit_b200 import CausalLm, presets
+from trit_b200 import CausalLm
+from tests.synth import presets
 
 pytestmark = pytest.mark.gpu
 

@@ -4,7 +4,8 @@ case, greedy tokens equal and logits bit-identical, through the C ABI
 import pytest
 
 from tests import golden_cases
-from trit_b200 import lm, presets
+from trit_b200 import lm
+from tests.synth import presets
 
 GOLDEN = golden_cases.load()
 

@@ -45,7 +45,7 @@ def test_static_scratch_equals_allocating_entry_point():
         dense.forward_device(x_d.data_ptr(), rows, want_d.data_ptr(), None)
         rc = lib.trit_dense_q8_0_forward_static(codes_d.data_ptr(), scales_d.data_ptr(), n, k, x_d.data_ptr(), rows,
                                                 got_d.data_ptr(), None)
-        assert rc == 0, lib.trit_last_error().decode()
+        assert rc == 0, lib.trit_cuda_last_error().decode()
         torch.cuda.synchronize()
         want, got = want_d.cpu().numpy(), got_d.cpu().numpy()
         # The same kernels on the same inputs: equal bit for bit (the tests'
@@ -67,4 +67,72 @@ def test_static_scratch_rejects_sizes_beyond_its_limit():
     rc = lib.trit_dense_q8_0_forward_static(codes_d.data_ptr(), scales_d.data_ptr(), n, k, x_d.data_ptr(), rows,
                                             out_d.data_ptr(), None)
     assert rc == -1
-    assert "static scratch" in lib.trit_last_error().decode()
+    assert "static scratch" in lib.trit_cuda_last_error().decode()
+
+
+def _device_layer(torch, n, k, seed):
+    codes, scales = _q8_0(n, k, seed)
+    dense = Dense.q8_0(O.q8_0_blocks(codes.reshape(-1), scales.reshape(-1)), n, k)
+    dev = torch.device("cuda", 0)
+    return (dense, torch.from_numpy(codes.view(np.int8)).to(dev), torch.from_numpy(scales.view(np.int16)).to(dev))
+
+
+def test_static_scratch_at_its_size_limit():
+    """The largest call the 1 MiB array takes for k = 8192 (113 rows: codes
+    plus scales fill 1,041,408 bytes; the GEMV runs it in passes of 8
+    frames) equals the allocating entry point; one more row is refused."""
+    torch = pytest.importorskip("torch")
+    lib = library()
+    n, k = 256, 8192
+    dense, codes_d, scales_d = _device_layer(torch, n, k, 11)
+    dev = torch.device("cuda", 0)
+    for call in range(2):
+        rows = 113
+        x_d = torch.from_numpy(np.random.default_rng(300 + call).standard_normal((rows, k)).astype(np.float32)).to(dev)
+        want_d = torch.zeros((rows, n), dtype=torch.float32, device=dev)
+        got_d = torch.full((rows, n), float("nan"), dtype=torch.float32, device=dev)
+        torch.cuda.synchronize()
+        dense.forward_device(x_d.data_ptr(), rows, want_d.data_ptr(), None)
+        rc = lib.trit_dense_q8_0_forward_static(codes_d.data_ptr(), scales_d.data_ptr(), n, k, x_d.data_ptr(), rows,
+                                                got_d.data_ptr(), None)
+        assert rc == 0, lib.trit_cuda_last_error().decode()
+        torch.cuda.synchronize()
+        assert torch.equal(got_d, want_d), f"call {call}: max diff {(got_d - want_d).abs().max().item()}"
+    x_d = torch.zeros((114, k), dtype=torch.float32, device=dev)
+    out_d = torch.zeros((114, n), dtype=torch.float32, device=dev)
+    assert lib.trit_dense_q8_0_forward_static(codes_d.data_ptr(), scales_d.data_ptr(), n, k, x_d.data_ptr(), 114,
+                                              out_d.data_ptr(), None) == -1
+    assert "static scratch" in lib.trit_cuda_last_error().decode()
+
+
+def test_static_entry_recorded_in_a_graph_capture():
+    """The case the entry point exists for: after one ordinary call on the
+    device (which looks up the array's address and sets every kernel
+    attribute), a call with another row count is recorded inside someone
+    else's CUDA graph capture and replayed."""
+    torch = pytest.importorskip("torch")
+    lib = library()
+    n, k = 512, 1024
+    dense, codes_d, scales_d = _device_layer(torch, n, k, 13)
+    dev = torch.device("cuda", 0)
+    warm = torch.zeros((2, k), dtype=torch.float32, device=dev)
+    warm_out = torch.zeros((2, n), dtype=torch.float32, device=dev)
+    assert lib.trit_dense_q8_0_forward_static(codes_d.data_ptr(), scales_d.data_ptr(), n, k, warm.data_ptr(), 2,
+                                              warm_out.data_ptr(), None) == 0
+    rows = 12
+    x_d = torch.empty((rows, k), dtype=torch.float32, device=dev)
+    got_d = torch.full((rows, n), float("nan"), dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        stream = torch.cuda.current_stream().cuda_stream
+        rc = lib.trit_dense_q8_0_forward_static(codes_d.data_ptr(), scales_d.data_ptr(), n, k, x_d.data_ptr(), rows,
+                                                got_d.data_ptr(), ctypes.c_void_p(stream))
+    assert rc == 0, lib.trit_cuda_last_error().decode()
+    for call in range(2):
+        x = np.random.default_rng(400 + call).standard_normal((rows, k)).astype(np.float32)
+        x_d.copy_(torch.from_numpy(x))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert np.array_equal(got_d.cpu().numpy(), dense.forward(x)), f"replay {call}"
+    del graph

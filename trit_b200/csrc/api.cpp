@@ -1,4 +1,4 @@
-// The C ABI of include/trit_cuda.h and include/trit_synth.h. Every entry
+// The C ABI of include/trit_cuda.h. Every entry
 // point runs its body under `guard`, which turns a C++ exception into the
 // thread's error text and the failure value, as ffi/src/lib.rs:20-45 does
 // for Rust panics.
@@ -9,7 +9,6 @@
 #include <string>
 
 #include "../../include/trit_cuda.h"
-#include "../../include/trit_synth.h"
 #include "engine.h"
 
 struct TritLm {
@@ -64,7 +63,7 @@ extern "C" {
 
 const char* trit_cuda_version(void) { return "0.1.0"; }
 
-const char* trit_last_error(void) { return g_error.c_str(); }
+const char* trit_cuda_last_error(void) { return g_error.c_str(); }
 
 char* trit_lm_inspect(const char* model_dir, const char* options_json) {
   return guard<char*>(nullptr, [&]() {
@@ -78,7 +77,7 @@ char* trit_lm_inspect(const char* model_dir, const char* options_json) {
   });
 }
 
-void trit_free_text(char* text) { std::free(text); }
+void trit_cuda_free_text(char* text) { std::free(text); }
 
 TritLm* trit_lm_load(const char* model_dir, const char* options_json) {
   return guard<TritLm*>(nullptr, [&]() {
@@ -308,18 +307,5 @@ int trit_dense_forward_device(TritDense* layer, const float* x, size_t rows, flo
 }
 
 void trit_dense_free(TritDense* layer) { delete layer; }
-
-int trit_synth_model(const char* dir, const char* spec_json) {
-  return guard<int>(-1, [&]() {
-    need(dir, "dir");
-    need(spec_json, "spec_json");
-    trit::synthesize(dir, spec_json);
-    return 0;
-  });
-}
-
-void trit_synth_normal_row(uint64_t seed, const char* name, uint64_t row, size_t k, float sd, float* out) {
-  if (name && out) trit::synth_normal_row(seed, name, row, k, sd, out);
-}
 
 }  // extern "C"

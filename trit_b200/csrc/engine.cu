@@ -1248,6 +1248,9 @@ DenseOp::~DenseOp() {
 std::unique_ptr<DenseOp> dense_q8_0(const void* blocks, size_t n, size_t k, int device, bool table) {
   if (k % 32) throw Error("Q8_0 rows are whole blocks of 32");
   if (!table && n % 32) throw Error("a W8A8 layer needs a multiple of 32 output rows");
+  // The W8A8 products (k_gemv_slots, k_gemm_tc) take rows of whole
+  // 128-value chunks; the table product takes any whole blocks.
+  if (!table && k % 128) throw Error("a W8A8 layer needs k a multiple of 128");
   auto op = std::make_unique<DenseOp>();
   op->device = device;
   op->table = table;

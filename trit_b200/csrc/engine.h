@@ -216,10 +216,7 @@ struct DenseOp {
 
 std::unique_ptr<DenseOp> dense_q8_0(const void* blocks, size_t n, size_t k, int device, bool table);
 
-// The text trit_last_error() returns on this thread ("" clears it).
+// The text trit_cuda_last_error() returns on this thread ("" clears it).
 void set_last_error(const std::string& text);
-
-void synthesize(const std::string& dir, const std::string& spec_json);
-void synth_normal_row(uint64_t seed, const std::string& name, uint64_t row, size_t k, float sd, float* out);
 
 }  // namespace trit

@@ -3,9 +3,28 @@
 
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "types.h"
 
 namespace trit {
+
+// One-time set-up per device (kernel attributes, device properties), safe
+// when several host threads make their first call at once: f runs once per
+// device index and its result is kept for later calls.
+constexpr int kMaxDevices = 64;
+struct DeviceOnce {
+  std::once_flag flag[kMaxDevices];
+  cudaError_t result[kMaxDevices] = {};
+  template <class F>
+  cudaError_t run(int dev, F f) {
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::call_once(flag[dev], [&] { result[dev] = f(); });
+    return result[dev];
+  }
+};
+// The SM count of the current device (148 on B200), looked up once.
+int current_sm_count();
 
 enum Epilogue : int { kEpOut = 0, kEpResid = 1, kEpSilu = 2 };
 

@@ -630,14 +630,17 @@ cudaError_t launch_attention_rows(const float* qkv, const int2* tiles, int ntile
   if (smem > 220 * 1024) return cudaErrorInvalidValue;
   // Blocks of 4 query heads for tiles of 16 or more query heads.
   const bool quad = tiles && RQ >= 16;
-  static bool configured[64][2] = {};
+  static DeviceOnce once;
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev][quad]) {
-    cudaFuncSetAttribute(quad ? k_attention_rows<4, 4, 8> : k_attention_rows<1, 2, 2>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-    configured[dev][quad] = true;
-  }
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = once.run(dev, [] {
+    cudaError_t r = cudaFuncSetAttribute(k_attention_rows<4, 4, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         220 * 1024);
+    if (r != cudaSuccess) return r;
+    return cudaFuncSetAttribute(k_attention_rows<1, 2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  });
+  if (e != cudaSuccess) return e;
   if (quad)
     k_attention_rows<4, 4, 8><<<dim3(ntiles, cfg.kv_heads), 256, smem, s>>>(qkv, tiles, cfg, cache, row_stream, row_pos,
                                                                       layer, tmax, all_keys, att);
@@ -956,25 +959,48 @@ cudaError_t launch_norm_quant(const float* x, int m, int d, const float* w, floa
   return cudaSuccess;
 }
 
+int current_sm_count() {
+  static DeviceOnce once;
+  static int sms[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (once.run(dev, [&] { return cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev); }) !=
+      cudaSuccess)
+    return 148;
+  return std::max(sms[dev], 1);
+}
+
+// The shared-memory limits of every frame-count variant of k_gemv_slots,
+// set on the first product on each device (whatever its row count), so a
+// later call with another row count makes no driver calls.
+static cudaError_t configure_gemv_slots() {
+  static DeviceOnce once;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  return once.run(dev, [] {
+    const void* fns[] = {(const void*)k_gemv_slots<1>, (const void*)k_gemv_slots<4>, (const void*)k_gemv_slots<8>,
+                         (const void*)k_gemv_slots<16>};
+    for (const void* f : fns) {
+      cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (r != cudaSuccess) return r;
+    }
+    return cudaSuccess;
+  });
+}
+
 template <int FR>
 static cudaError_t gemv_slots_pass(const DMat& W, const int8_t* xq, const float* xs, int m, int mode, float* y,
                                    int ldy, float resid_mult, cudaStream_t s) {
   const int units = (mode == kEpSilu) ? W.n / 2 : W.n;
   const int per_block = (mode == kEpSilu) ? GS_WARPS / 2 : GS_WARPS;
   const size_t smem = gemv_slots_smem(W, FR);
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    cudaFuncSetAttribute(k_gemv_slots<FR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    configured[dev] = true;
-  }
+  cudaError_t e = configure_gemv_slots();
+  if (e != cudaSuccess) return e;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   // At most 8 blocks an SM; each loops over row tiles.
-  static int sms[64] = {};
-  if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
   const int ntiles = (units + per_block - 1) / per_block;
-  const int grid = std::min(ntiles, 8 * std::max(dev < 64 ? sms[dev] : 148, 1));
+  const int grid = std::min(ntiles, 8 * current_sm_count());
   k_gemv_slots<FR><<<grid, GS_WARPS * 32, smem, s>>>(W, xq, xs, m, mode, y, ldy, resid_mult, units);
   return cudaGetLastError();
 }
@@ -1015,17 +1041,33 @@ __global__ void __launch_bounds__(256) k_final_norm_rows(const float* x, int ldx
   for (int i = threadIdx.x; i < d; i += 256) out[i] = __fmul_rn(rowv[i], __fmul_rn(s_inv, w[i]));
 }
 
+// The shared-memory limits of every variant of the table kernels, set once
+// per device on its first table product.
+static cudaError_t configure_tables() {
+  static DeviceOnce once;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  return once.run(dev, [] {
+    const void* fns[] = {(const void*)k_table<1>, (const void*)k_table<4>, (const void*)k_table<16>};
+    for (const void* f : fns) {
+      cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (r != cudaSuccess) return r;
+    }
+    const int rows16 = (int)(((size_t)2 * 16 * TB_KC + (size_t)TB_KC * 18) * 4);
+    const int rows32 = (int)(((size_t)2 * 32 * TB_KC + (size_t)TB_KC * 34) * 4);
+    cudaError_t r = cudaFuncSetAttribute(k_table_rows<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, rows16);
+    if (r != cudaSuccess) return r;
+    return cudaFuncSetAttribute(k_table_rows<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, rows32);
+  });
+}
+
 template <int B>
 static cudaError_t table_pass(const DTable& T, const float* xn, int nb, float mult, float* logits, float* best_val,
                               int* best_idx, cudaStream_t s) {
   size_t smem = (size_t)T.k * B * 4;
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    cudaFuncSetAttribute(k_table<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    configured[dev] = true;
-  }
+  cudaError_t e = configure_tables();
+  if (e != cudaSuccess) return e;
   int blocks = table_blocks(T.n);
   k_table<B><<<blocks, 256, smem, s>>>(T, xn, nb, mult, logits, best_val, best_idx, blocks);
   return cudaGetLastError();
@@ -1035,13 +1077,8 @@ template <int B>
 static cudaError_t table_rows_pass(const DTable& T, const float* xn, int nb, float mult, float* logits,
                                    float* best_val, int* best_idx, cudaStream_t s) {
   size_t smem = ((size_t)2 * B * TB_KC + (size_t)TB_KC * (B + 2)) * 4;
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    cudaFuncSetAttribute(k_table_rows<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    configured[dev] = true;
-  }
+  cudaError_t e = configure_tables();
+  if (e != cudaSuccess) return e;
   int blocks = table_blocks(T.n);
   k_table_rows<B><<<blocks, 256, smem, s>>>(T, xn, nb, mult, logits, best_val, best_idx, blocks);
   return cudaGetLastError();

@@ -633,17 +633,25 @@ int tc_frame_tile(int n, int m, int sms) {
   return best;
 }
 
+// The shared-memory limit of every frame tile of k_gemm_tc, set once per
+// device on its first tensor-core product.
+static cudaError_t configure_gemm_tc(int dev) {
+  static DeviceOnce once;
+  return once.run(dev, [] {
+    cudaError_t r = cudaFuncSetAttribute(k_gemm_tc<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (r == cudaSuccess) r = cudaFuncSetAttribute(k_gemm_tc<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (r == cudaSuccess) r = cudaFuncSetAttribute(k_gemm_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    return r;
+  });
+}
+
 template <int N>
 cudaError_t launch_tc_n(const TcMap& amap, const TcMap& bmap, const DMat& W, const float* xs, int m, int mode,
                         float* y, int ldy, float resid_mult, int* status, cudaStream_t s, int dev) {
   size_t smem = tc_smem_bytes(W, N);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  static bool configured[64] = {};
-  if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
+  cudaError_t e = configure_gemm_tc(dev);
+  if (e != cudaSuccess) return e;
   dim3 grid((W.n + TC_M - 1) / TC_M, (m + N - 1) / N);
   k_gemm_tc<N><<<grid, TC_THREADS, smem, s>>>(*(const CUtensorMap*)&amap, *(const CUtensorMap*)&bmap, W, xs, m, mode,
                                                y, ldy, resid_mult, status);
@@ -655,15 +663,13 @@ cudaError_t launch_gemm_tc(const TcMap& amap, const TcMap& bmap, const DMat& W, 
   if (W.k % TC_KT || (W.agroup != 32 && W.agroup != 128) || m <= 0) return cudaErrorInvalidValue;
   int dev = 0;
   cudaGetDevice(&dev);
-  static int sms[64] = {};
-  if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
   // TRIT_TC_FRAMES=16, 32 or 64 fixes the frame tile (tests, tuning).
   static const int forced = [] {
     const char* e = getenv("TRIT_TC_FRAMES");
     const int v = e ? atoi(e) : 0;
     return (v == 16 || v == 32 || v == 64) ? v : 0;
   }();
-  const int tile = forced ? forced : tc_frame_tile(W.n, m, std::max(dev < 64 ? sms[dev] : 148, 1));
+  const int tile = forced ? forced : tc_frame_tile(W.n, m, current_sm_count());
   if (tile == 16) return launch_tc_n<16>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
   if (tile == 32) return launch_tc_n<32>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
   return launch_tc_n<64>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);

@@ -49,7 +49,8 @@ extern "C" int trit_dense_q8_0_forward_static(const void* codes, const void* sca
   try {
     trit::set_last_error("");
     if (!codes || !scales || !x || !out) throw trit::Error("a pointer argument is NULL");
-    if (k == 0 || k % 32 || k > 8192) throw trit::Error("k must be a multiple of 32 from 32 to 8192");
+    // The W8A8 GEMV (k_gemv_slots) takes rows of whole 128-value chunks.
+    if (k == 0 || k % 128 || k > 8192) throw trit::Error("k must be a multiple of 128 from 128 to 8192");
     if (n == 0 || n % 32) throw trit::Error("n must be a positive multiple of 32");
     if (rows == 0) return 0;
     const size_t codes_bytes = (rows * k + 255) / 256 * 256;

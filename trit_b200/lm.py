@@ -2,7 +2,7 @@
 decoder (src/models/parts/causal_lm.rs) and `Dense` (src/cpu/gemm.rs) over
 the C ABI of include/trit_cuda.h.
 
-Failures raise `TritError` with the library's `trit_last_error()` text, as
+Failures raise `TritError` with the library's `trit_cuda_last_error()` text, as
 the reference's functions return `Err(String)`. There is no fallback: if
 the shared library is missing or no GPU can be used, loading fails.
 """
@@ -27,7 +27,7 @@ _size = ctypes.c_size_t
 
 
 class TritError(RuntimeError):
-    """A failed call into libtrit_cuda (the text of trit_last_error)."""
+    """A failed call into libtrit_cuda (the text of trit_cuda_last_error)."""
 
 
 _lib = None
@@ -43,9 +43,9 @@ def library() -> ctypes.CDLL:
     lib = ctypes.CDLL(LIBRARY)
     sig = {
         "trit_cuda_version": (ctypes.c_char_p, []),
-        "trit_last_error": (ctypes.c_char_p, []),
+        "trit_cuda_last_error": (ctypes.c_char_p, []),
         "trit_lm_inspect": (ctypes.c_void_p, [ctypes.c_char_p, ctypes.c_char_p]),
-        "trit_free_text": (None, [ctypes.c_void_p]),
+        "trit_cuda_free_text": (None, [ctypes.c_void_p]),
         "trit_lm_load": (ctypes.c_void_p, [ctypes.c_char_p, ctypes.c_char_p]),
         "trit_lm_free": (None, [ctypes.c_void_p]),
         "trit_lm_width": (ctypes.c_int64, [ctypes.c_void_p]),
@@ -79,9 +79,6 @@ def library() -> ctypes.CDLL:
         "trit_dense_free": (None, [ctypes.c_void_p]),
         "trit_dense_q8_0_forward_static": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, _size, _size,
                                                           ctypes.c_void_p, _size, ctypes.c_void_p, ctypes.c_void_p]),
-        "trit_synth_model": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p]),
-        "trit_synth_normal_row": (None, [ctypes.c_uint64, ctypes.c_char_p, ctypes.c_uint64, _size, ctypes.c_float,
-                                         _f32p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -92,7 +89,7 @@ def library() -> ctypes.CDLL:
 
 
 def _error() -> TritError:
-    return TritError(library().trit_last_error().decode("utf-8", "replace"))
+    return TritError(library().trit_cuda_last_error().decode("utf-8", "replace"))
 
 
 def _ids(values: Iterable[int]) -> np.ndarray:
@@ -335,26 +332,4 @@ def inspect(model_dir: str, **options) -> dict:
     try:
         return json.loads(ctypes.string_at(ptr).decode())
     finally:
-        lib.trit_free_text(ptr)
-
-
-def synthesize(model_dir: str, config: dict, fmt: str = "q8_0", seed: int = 0, std: float = 0.02,
-               prefix: str = "", config_at: str = "") -> str:
-    """Writes a seeded synthetic model folder (include/trit_synth.h)."""
-    os.makedirs(model_dir, exist_ok=True)
-    spec = {"config": config, "format": fmt, "seed": seed, "std": std}
-    if prefix:
-        spec["prefix"] = prefix
-    if config_at:
-        spec["config_at"] = config_at
-    spec = json.dumps(spec).encode()
-    if library().trit_synth_model(str(model_dir).encode(), spec) != 0:
-        raise _error()
-    return model_dir
-
-
-def normal_row(seed: int, name: str, row: int, k: int, std: float = 0.02) -> np.ndarray:
-    """The f32 values of a synthetic tensor's row before quantization."""
-    out = np.zeros(k, dtype=np.float32)
-    library().trit_synth_normal_row(seed, name.encode(), row, k, std, _ptr(out, _f32p))
-    return out
+        lib.trit_cuda_free_text(ptr)
