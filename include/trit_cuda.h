@@ -81,6 +81,14 @@ void trit_cuda_free_text(char *text);
  *   "tensor_cores": true (default on sm_100) or false: products of
  *                   "tc_rows" rows or more on the tensor cores
  *   "tc_rows":      rows from which a product uses the tensor cores (64)
+ *   "exact":        false (default) or true. true: every floating-point
+ *                   step in the order of the reference's CPU decoder, so
+ *                   logits equal its logits bit for bit. false: the batch-1
+ *                   decode sums in tree order and splits attention over
+ *                   keys, which is faster; tokens stay the reference's and
+ *                   logits stay within max-abs 2e-2 / cosine 0.9995 of its
+ *                   logits (a token can differ only where the reference's
+ *                   top two logits are closer than that)
  *   "config_at":    key path of the decoder settings in config.json ("";
  *                   "thinker_config.text_config." in Qwen3-ASR)
  *   "prefix":       start of every tensor name ("", "thinker.", "llm.")

@@ -47,6 +47,9 @@ Options Options::parse(const char* text, bool lenient) {
       o.tensor_cores = v.b;
     } else if (k == "tc_rows") {
       o.tc_rows = count(1, 1 << 20);
+    } else if (k == "exact") {
+      if (v.kind != Json::Bool) throw Error("options: exact is true or false");
+      o.exact = v.b;
     } else if (k == "config_at" || k == "prefix") {
       if (v.kind != Json::String) throw Error("options: " + k + " must be a string");
       (k == "config_at" ? o.config_at : o.prefix) = v.str;

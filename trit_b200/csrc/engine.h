@@ -26,6 +26,11 @@ struct Options {
   std::string decode = "persistent";  // "persistent" (one kernel per generation) or "layered"
   bool tensor_cores = true;      // tcgen05 products for prefill and batches of >= tc_rows rows
   int tc_rows = 64;
+  // true: every floating-point step in the reference's order (logits bit
+  // for bit those of the CPU decoder); false: the batch-1 decode reorders
+  // sums (tree reductions, split attention) within the north-star
+  // tolerance, which is faster.
+  bool exact = false;
   std::string config_at;         // key path of the settings in config.json (from_tensors' config_at)
   std::string prefix;            // start of every tensor name (from_tensors' prefix)
   // `lenient`: keys other than config_at and prefix are skipped unchecked.
