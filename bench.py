@@ -262,15 +262,13 @@ def run_reference(args, r: dp.Rank) -> None:
 
 
 # ------------------------------------------------------------ GPU legs ----
-def run_decode(args, r: dp.Rank) -> None:
+def measure(w: dict, args, r: dp.Rank, steps: int, warmup: int, decode: str, exact: bool) -> tuple[dict, str]:
+    """One workload on this rank's GPU: `warmup` untimed generations, then
+    `steps` timed ones between barriers. Returns the JSON fields of its line
+    (whole-job values: the max of the ranks' times) and the model folder."""
     from trit_b200 import CausalLm, lm as lmmod
     from tests.synth import presets
 
-    w = dict(WORKLOADS[args.config])
-    for key in ("streams", "prompt", "new"):
-        if getattr(args, key) is not None:
-            w[key] = getattr(args, key)
-            w["workload"] += f" ({key} set to {getattr(args, key)})"
     if r.rank == 0:
         model_dir = presets.model_path(w["model"])
     dp.barrier(r)
@@ -278,7 +276,7 @@ def run_decode(args, r: dp.Rank) -> None:
     info = lmmod.inspect(model_dir)
     S = w["streams"]
     prompt_len = w["prompt"] + w.get("rows", 0)
-    opts = {"device": r.local, "kv": args.kv, "max_context": prompt_len + w["new"] + 8}
+    opts = {"device": r.local, "kv": args.kv, "max_context": prompt_len + w["new"] + 8, "exact": exact}
     if w["kind"] == "batch":
         # Prompt passes of 4096 rows: 15 % more end to end on C5 than 512
         # (fuller tensor-core and attention grids).
@@ -288,7 +286,7 @@ def run_decode(args, r: dp.Rank) -> None:
     if args.prefill_rows is not None:
         opts.update(prefill_rows=args.prefill_rows)
     else:
-        opts.update(decode=args.decode)
+        opts.update(decode=decode)
     lm = CausalLm.load(model_dir, **opts)
     vocab, width = lm.vocab(), lm.width()
 
@@ -306,15 +304,15 @@ def run_decode(args, r: dp.Rank) -> None:
             return len(lm.answer([], rows, prompts[0], max_new=w["new"]))
         return sum(len(t) for t in lm.generate_batch(prompts, max_new=w["new"]))
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         one(i)
     decode_ms = prefill_ms = 0.0
     decode_steps = made = launches = 0
     with Clocks(r.local) as clocks:
         dp.barrier(r)
         t0 = time.perf_counter()
-        for i in range(args.steps):
-            made += one(args.warmup + i)
+        for i in range(steps):
+            made += one(warmup + i)
             t = lm.last_timing()
             decode_ms += t["decode_ms"]
             prefill_ms += t["prefill_ms"]
@@ -322,6 +320,7 @@ def run_decode(args, r: dp.Rank) -> None:
             launches += t["launches"]
         dp.barrier(r)
         wall = time.perf_counter() - t0
+    lm.close()
     wall_max = dp.reduce(wall, r, "max")
     decode_max = dp.reduce(decode_ms, r, "max")
     steps_all = dp.reduce(float(decode_steps), r, "sum")
@@ -334,38 +333,67 @@ def run_decode(args, r: dp.Rank) -> None:
     greedy_steps = decode_steps / S  # forwards of the whole batch
     per_step_s = decode_ms / 1e3 / max(1.0, greedy_steps)
     achieved = alg["total"] / per_step_s / 1e9
-    kernel = {"generate": "decode step (persistent kernel)" if args.decode == "persistent" else "layered step",
-              "answer": "decode step (persistent kernel)" if args.decode == "persistent" else "layered step",
+    path = "tree-order sums" if not exact else "exact reference order"
+    kernel = {"generate": f"decode step (persistent kernel, {path})" if decode == "persistent" else "layered step",
+              "answer": f"decode step (persistent kernel, {path})" if decode == "persistent" else "layered step",
               "batch": "batched decode step (layered kernels, one CUDA graph)"}[w["kind"]]
     h2d = S * w["prompt"] * 4 + w.get("rows", 0) * width * 4
-    line = {
+    fields = {
         "metric": w["metric"], "value": value, "unit": "tok/s", "n_gpus": r.world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall_max * 1e3 / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> i32, f32",
-        "data": "synthetic (seeded N(0,0.02) weights, uniform random prompt ids"
-                + (", N(0,1) prefix rows)" if w["kind"] == "answer" else ")"),
+        "steps": steps, "warmup": warmup, "ms_per_step": wall_max * 1e3 / steps,
         "config": {"workload": w["workload"], "model": w["model"], "global_batch": S * r.world,
                    "seq_len": prompt_len + w["new"], "parallelism": f"dp{r.world} (independent streams, no collective)",
-                   "decode": args.decode if w["kind"] != "batch" else "batched", "kv_cache": args.kv,
+                   "decode": decode if w["kind"] != "batch" else "batched", "exact": exact, "kv_cache": args.kv,
                    "l2": f"weights {alg['weights'] / 1e6:.0f} MB > 126 MB L2; no flush"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": S * w["new"] * 4},
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": peak_kind, "traffic": TRAFFIC.get(args.config),
+                     "peak_kind": peak_kind, "traffic": TRAFFIC.get(w["key"]) if not exact else TRAFFIC_EXACT.get(w["key"]),
                      "algorithmic_bytes_per_step": alg["total"], "kv_bytes_per_step": alg["kv"], "kernel": kernel},
-        "prefill_ms_per_step": prefill_ms / args.steps,
+        "prefill_ms_per_step": prefill_ms / steps,
         "clocks": clocks.summary(),
     }
+    return fields, model_dir
+
+
+def workload(args) -> dict:
+    w = dict(WORKLOADS[args.config], key=args.config)
+    for key in ("streams", "prompt", "new"):
+        if getattr(args, key) is not None:
+            w[key] = getattr(args, key)
+            w["workload"] += f" ({key} set to {getattr(args, key)})"
+    return w
+
+
+def run_decode(args, r: dp.Rank) -> None:
+    w = workload(args)
+    fields, model_dir = measure(w, args, r, args.steps, args.warmup, args.decode, args.exact)
+    line = {**fields, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 x int8 -> i32, f32",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform random prompt ids"
+                    + (", N(0,1) prefix rows)" if w["kind"] == "answer" else ")")}
+    if args.config == "c1" and not args.no_batch64:
+        # The batch-64 half of the metric in the same run (and so in the
+        # driver's 1/2/4/8-GPU scaling run): C5, 64 streams per GPU.
+        b, _ = measure(dict(WORKLOADS["c5"], key="c5"), args, r, BATCH64_STEPS, BATCH64_WARMUP, "persistent",
+                       args.exact)
+        b["note"] = (f"C5 workload measured in the same run as the headline line: {BATCH64_WARMUP} warm-up and "
+                     f"{BATCH64_STEPS} timed generations (fewer than the headline's, to bound the run)")
+        line["batch64"] = b
     if r.rank == 0 and r.world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample(w, model_dir, 8, 1)
     if r.rank == 0:
         print(json.dumps(line), flush=True)
-    lm.close()
 
 
 # Per-step DRAM bytes (read + write) of the dominant kernel from ncu
 # captures, where one was taken for the workload (see profiles/).
-TRAFFIC: dict = {"c1": (82.304342e9 + 46.220032e6) / 127}  # profiles/k_decode_c1.md
+TRAFFIC: dict = {}
+TRAFFIC_EXACT: dict = {"c1": (82.304342e9 + 46.220032e6) / 127}  # profiles/k_decode_c1.md
+# The batch-64 object of the default line: generations timed (C5 takes
+# ~8 s a generation on one B200).
+BATCH64_STEPS = 2
+BATCH64_WARMUP = 1
 
 
 def q8_0_blocks(values: np.ndarray) -> np.ndarray:
@@ -495,6 +523,9 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c1", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--decode", default=os.environ.get("TRIT_DECODE", "persistent"))
+    ap.add_argument("--exact", action="store_true",
+                    help="the exact (reference-order) kernels instead of the default tree-order decode")
+    ap.add_argument("--no-batch64", action="store_true", help="leave the C5 batch-64 object out of the C1 line")
     ap.add_argument("--tc-rows", type=int, help="rows from which products use the tensor cores (engine option)")
     ap.add_argument("--prefill-rows", type=int, help="rows a prompt pass (engine option)")
     ap.add_argument("--kv", default="f16")

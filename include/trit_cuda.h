@@ -19,13 +19,25 @@
  *   the library owns the device memory of a handle until trit_lm_free.
  * - There is no CPU fallback: without a usable GPU the load fails.
  *
- * A model is a folder with config.json (Hugging Face keys, as Config::parse
- * reads them, causal_lm.rs:41-77) and model.gguf holding the tensors under
- * their Hugging Face names: Q8_0 matrices (ggml blocks of 32 codes and an
- * f16 scale), per-row int8 matrices (`.weight` I8 + `.scales` F32 per row),
- * or ternary matrices (`.qweight`, five base-3 codes a byte, + `.scales`
- * F32 per 128 inputs, as src/models/parts/fastconformer.rs:440-452 reads
- * them); norms F32; token tables Q8_0 or int8 with per-32 F32 scales.
+ * A model is a folder in one of three forms (src/models/gguf/mod.rs,
+ * src/cpu/tensors.rs):
+ * - config.json (Hugging Face keys, as Config::parse reads them,
+ *   causal_lm.rs:41-77) and model.gguf with the tensors under their
+ *   Hugging Face names;
+ * - config.json and safetensors files (model.safetensors, the shards of
+ *   model.safetensors.index.json, or every *.safetensors);
+ * - one GGUF file as transcribe.cpp writes it (no config.json): the decoder
+ *   settings come from its stt.<arch>.decoder.* metadata and its dec.*
+ *   tensor names are mapped as the reference maps them (architectures
+ *   qwen3_asr, moss, funasr_nano, canary_qwen, voxtral, voxtral_realtime,
+ *   granite_speech; src/models/gguf/qwen3_asr.rs:103-136).
+ * Products are Q8_0 (ggml blocks of 32 codes and an f16 scale), float (F32,
+ * F16, BF16: quantized to Q8_0 at load as ggml quantizes, gemm.rs:53-76),
+ * per-row int8 (`.weight` I8 + `.scales` F32 per row), or ternary
+ * (`.qweight`, five base-3 codes a byte, + `.scales` F32 per 128 inputs, as
+ * src/models/parts/fastconformer.rs:440-452 reads them); norms F32/F16/BF16;
+ * token tables Q8_0, float (quantized to Q8_0) or int8 with per-32 F32
+ * scales.
  */
 #ifndef TRIT_CUDA_H
 #define TRIT_CUDA_H
@@ -75,12 +87,22 @@ void trit_cuda_free_text(char *text);
  *   "max_streams":  stream slots for trit_lm_generate_batch (1)
  *   "page_tokens":  positions per KV page (64)
  *   "prefill_rows": prompt rows per prefill pass (512)
+ *   "prefix_pages": KV pages kept for trit_lm_prefix (max_context /
+ *                   page_tokens: one stream's worth)
  *   "decode":       "persistent" (default: one kernel runs every greedy
  *                   step of a batch-1 generation) or "layered" (a kernel
  *                   per operation and step)
  *   "tensor_cores": true (default on sm_100) or false: products of
  *                   "tc_rows" rows or more on the tensor cores
  *   "tc_rows":      rows from which a product uses the tensor cores (64)
+ *   "weight_cache": false (default) or true: keep the weights' device
+ *                   layout in a file (in "cache_dir", default
+ *                   <model_dir>/.trit_cuda) on the first load and read it
+ *                   straight into device memory on later loads, with no
+ *                   parsing or conversion; a file that does not match the
+ *                   model's files byte for byte is rewritten, and one that
+ *                   cannot be written is skipped (as src/cpu/store.rs:1-16)
+ *   "cache_dir":    the folder of the weight cache
  *   "exact":        false (default) or true. true: every floating-point
  *                   step in the order of the reference's CPU decoder, so
  *                   logits equal its logits bit for bit. false: the batch-1
@@ -99,6 +121,13 @@ TritLm *trit_lm_load(const char *model_dir, const char *options_json);
  * include/trit.h:115-116.) */
 void trit_lm_free(TritLm *lm);
 
+/* What a load did, as JSON text: "source" (the files' form: "gguf",
+ * "gguf-transcribe" or "safetensors"), "weights_from" ("files", or "cache"
+ * when the weight cache supplied the device layout), "weight_cache" (its
+ * file, or null), "arena_bytes", the KV and decode settings and the
+ * prefix pages in use. Free with trit_cuda_free_text. NULL on failure. */
+char *trit_lm_status(const TritLm *lm);
+
 /* hidden_size, num_hidden_layers, vocab_size; -1 for NULL.
  * (CausalLm::width / layers, causal_lm.rs:307-313,343-345.) */
 int64_t trit_lm_width(const TritLm *lm);
@@ -106,12 +135,22 @@ int64_t trit_lm_layers(const TritLm *lm);
 int64_t trit_lm_vocab(const TritLm *lm);
 
 /* Runs a prompt start that many calls share (a system prompt) once; a
- * trit_lm_generate whose prompt begins with it and is longer starts from
- * its cache. NULL on failure. (CausalLm::prefix, causal_lm.rs:200-215.) */
+ * trit_lm_generate or trit_lm_generate_batch_prefix stream whose prompt
+ * begins with it and is longer starts from its cache. The prefix's full KV
+ * pages are kept read-only in pages the model holds for prefixes (load
+ * option "prefix_pages") and every call reads them in place (the page
+ * tables of its streams point at them); only the page the prefix ends
+ * inside is copied, once per stream and call. NULL on failure (also when
+ * the kept pages are used up). (CausalLm::prefix, causal_lm.rs:200-215.) */
 TritLmPrefix *trit_lm_prefix(TritLm *lm, const int32_t *ids, size_t n);
 
-/* Frees a prefix. NULL is a no-op. */
+/* Frees a prefix and returns its pages. NULL is a no-op. Not while a call
+ * on its model uses it. */
 void trit_lm_prefix_free(TritLmPrefix *prefix);
+
+/* The KV pages kept for prefixes: in use (by live prefixes) and in all.
+ * Returns 0, or -1. */
+int trit_lm_prefix_pages(const TritLm *lm, int64_t *used, int64_t *total);
 
 /* Greedy tokens after `prompt` (n ids), until a token of `stop` (nstop ids,
  * not kept) or `max_new` tokens; writes at most `cap` of them to `out`.
@@ -133,6 +172,22 @@ int64_t trit_lm_generate_rows(TritLm *lm, const float *rows, size_t nrows, int32
 int64_t trit_lm_answer(TritLm *lm, const int32_t *head, size_t nhead, const float *audio, size_t naudio,
                        const int32_t *tail, size_t ntail, int32_t max_new, const int32_t *stop,
                        size_t nstop, int32_t *out, size_t cap);
+
+/* trit_lm_generate_rows and trit_lm_answer with the rows in device memory
+ * of the model's GPU (an encoder's output that stays on the GPU: no copy
+ * through the host). The rows are read after the work queued so far on
+ * `cuda_stream` (a cudaStream_t; NULL: the legacy default stream), as
+ * device-to-device copies; the call returns when the tokens are on the
+ * host, so the caller may reuse the rows' memory then. Fails when the
+ * pointer is not device memory of that GPU. Returns the count, or -1.
+ * (CausalLm::generate_rows / answer, causal_lm.rs:251-282, fed by
+ * Qwen3Asr's encoder rows, src/models/families/qwen3_asr.rs:321-372.) */
+int64_t trit_lm_generate_rows_device(TritLm *lm, const float *rows_device, size_t nrows, int32_t max_new,
+                                     const int32_t *stop, size_t nstop, int32_t *out, size_t cap,
+                                     void *cuda_stream);
+int64_t trit_lm_answer_device(TritLm *lm, const int32_t *head, size_t nhead, const float *audio_device,
+                              size_t naudio, const int32_t *tail, size_t ntail, int32_t max_new,
+                              const int32_t *stop, size_t nstop, int32_t *out, size_t cap, void *cuda_stream);
 
 /* The embeddings of `n` ids, n x trit_lm_width() floats, into `out`.
  * Returns 0, or -1. (CausalLm::embed, causal_lm.rs:347-355.) */
@@ -160,6 +215,14 @@ int64_t trit_lm_answer_traced(TritLm *lm, const int32_t *head, size_t nhead, con
 int trit_lm_generate_batch(TritLm *lm, size_t streams, const int32_t *const *prompts, const size_t *lens,
                            int32_t max_new, const int32_t *stop, size_t nstop, int32_t *out,
                            int64_t *counts);
+
+/* trit_lm_generate_batch where the streams whose prompt begins with
+ * `prefix` (and is longer) read its pages and run only the rest of their
+ * prompt, as S1-mini's cleanup calls share one system prompt
+ * (src/cleanup.rs:208,297-299). `prefix` may be NULL. Returns 0, or -1. */
+int trit_lm_generate_batch_prefix(TritLm *lm, const TritLmPrefix *prefix, size_t streams,
+                                  const int32_t *const *prompts, const size_t *lens, int32_t max_new,
+                                  const int32_t *stop, size_t nstop, int32_t *out, int64_t *counts);
 
 /* CausalLm::set_ffn_scales (causal_lm.rs:305-307): the normed MLP input of
  * layer l is multiplied by scales[l * width ...] (layers x width floats,

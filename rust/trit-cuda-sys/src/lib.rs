@@ -46,6 +46,7 @@ pub mod ffi {
         pub fn trit_cuda_free_text(text: *mut c_char);
         pub fn trit_lm_load(model_dir: *const c_char, options_json: *const c_char) -> *mut TritLm;
         pub fn trit_lm_free(lm: *mut TritLm);
+        pub fn trit_lm_status(lm: *const TritLm) -> *mut c_char;
         pub fn trit_lm_width(lm: *const TritLm) -> i64;
         pub fn trit_lm_layers(lm: *const TritLm) -> i64;
         pub fn trit_lm_vocab(lm: *const TritLm) -> i64;
@@ -64,6 +65,15 @@ pub mod ffi {
             tail: *const i32, ntail: usize, max_new: i32, stop: *const i32, nstop: usize, out: *mut i32,
             cap: usize,
         ) -> i64;
+        pub fn trit_lm_generate_rows_device(
+            lm: *mut TritLm, rows_device: *const f32, nrows: usize, max_new: i32, stop: *const i32, nstop: usize,
+            out: *mut i32, cap: usize, cuda_stream: *mut c_void,
+        ) -> i64;
+        pub fn trit_lm_answer_device(
+            lm: *mut TritLm, head: *const i32, nhead: usize, audio_device: *const f32, naudio: usize,
+            tail: *const i32, ntail: usize, max_new: i32, stop: *const i32, nstop: usize, out: *mut i32,
+            cap: usize, cuda_stream: *mut c_void,
+        ) -> i64;
         pub fn trit_lm_embed(lm: *mut TritLm, ids: *const i32, n: usize, out: *mut f32) -> c_int;
         pub fn trit_lm_generate_traced(
             lm: *mut TritLm, prefix: *const TritLmPrefix, prompt: *const i32, n: usize, max_new: i32,
@@ -78,6 +88,11 @@ pub mod ffi {
             lm: *mut TritLm, streams: usize, prompts: *const *const i32, lens: *const usize, max_new: i32,
             stop: *const i32, nstop: usize, out: *mut i32, counts: *mut i64,
         ) -> c_int;
+        pub fn trit_lm_generate_batch_prefix(
+            lm: *mut TritLm, prefix: *const TritLmPrefix, streams: usize, prompts: *const *const i32,
+            lens: *const usize, max_new: i32, stop: *const i32, nstop: usize, out: *mut i32, counts: *mut i64,
+        ) -> c_int;
+        pub fn trit_lm_prefix_pages(lm: *const TritLm, used: *mut i64, total: *mut i64) -> c_int;
         pub fn trit_lm_set_ffn_scales(lm: *mut TritLm, scales: *const f32, layers: usize, width: usize) -> c_int;
         pub fn trit_lm_generate_additive(
             lm: *mut TritLm, prompt: *const i32, n: usize, audio: *const f32, rows: usize, stop: *const i32,
@@ -244,6 +259,26 @@ impl GpuCausalLm {
                 max_new as i32, s.as_ptr(), s.len(), out.as_mut_ptr(), out.len(),
             )
         };
+        tokens(out, n)
+    }
+
+    /// `answer` with the audio rows (`nrows` x width f32) in device memory of
+    /// the model's GPU, read after the work queued on `cuda_stream` (an
+    /// encoder's output that stays on the GPU).
+    ///
+    /// # Safety
+    /// `audio_device` must point to `nrows * width` floats of device memory
+    /// on the model's GPU, and `cuda_stream` must be a live stream or null.
+    pub unsafe fn answer_device(
+        &self, head: &[usize], audio_device: *const f32, nrows: usize, tail: &[usize], max_new: usize,
+        stop: &[usize], cuda_stream: *mut c_void,
+    ) -> Vec<usize> {
+        let (h, t, s) = (ids(head), ids(tail), ids(stop));
+        let mut out = vec![0i32; max_new];
+        let n = ffi::trit_lm_answer_device(
+            self.raw, h.as_ptr(), h.len(), audio_device, nrows, t.as_ptr(), t.len(), max_new as i32, s.as_ptr(),
+            s.len(), out.as_mut_ptr(), out.len(), cuda_stream,
+        );
         tokens(out, n)
     }
 

@@ -36,10 +36,12 @@ def library() -> ctypes.CDLL:
 
 
 def synthesize(model_dir: str, config: dict, fmt: str = "q8_0", seed: int = 0, std: float = 0.02,
-               prefix: str = "", config_at: str = "") -> str:
-    """Writes a seeded synthetic model folder (trit_synth.h)."""
+               prefix: str = "", config_at: str = "", **extra) -> str:
+    """Writes a seeded synthetic model folder (trit_synth.h). `extra` keys
+    of the spec: container ("gguf", "safetensors"), names ("hf",
+    "transcribe"), arch (of a transcribe file), dtype (of fmt "float")."""
     os.makedirs(model_dir, exist_ok=True)
-    spec = {"config": config, "format": fmt, "seed": seed, "std": std}
+    spec = {"config": config, "format": fmt, "seed": seed, "std": std, **extra}
     if prefix:
         spec["prefix"] = prefix
     if config_at:

@@ -19,6 +19,7 @@
 //             token table Q8_0, as Dense::table keeps it (never ternary).
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <thread>
 
 #include "../../trit_b200/csrc/host.h"
@@ -105,6 +106,159 @@ int8_t code_of(float v, float scale) {
   return (int8_t)std::min(std::max(c, -127.0f), 127.0f);
 }
 
+// A model file being written: declare every tensor (`add`, with ggml type
+// codes and dims innermost first), then `open` writes the header and `put`
+// writes each tensor's bytes in the order of the declarations.
+class Writer {
+ public:
+  virtual ~Writer() = default;
+  virtual void add(const std::string& name, uint32_t type, std::vector<uint64_t> dims) = 0;
+  virtual void open(const std::string& path) = 0;
+  virtual void put(const void* bytes, size_t size) = 0;
+  virtual void close() = 0;
+};
+
+struct Declared {
+  std::string name;
+  uint32_t type;
+  std::vector<uint64_t> dims;
+  size_t bytes;
+};
+
+// GGUF v3 (src/models/gguf/mod.rs:147-215 reads it): typed metadata, then
+// the tensor list, then the data, each tensor 32-byte aligned.
+class GgufOut : public Writer {
+ public:
+  ~GgufOut() override {
+    if (file_) std::fclose(file_);
+  }
+  void meta_str(const std::string& key, const std::string& v) { meta_.push_back({key, 8, v, 0}); }
+  void meta_u32(const std::string& key, uint32_t v) { meta_.push_back({key, 4, "", (double)v}); }
+  void meta_f32(const std::string& key, float v) { meta_.push_back({key, 6, "", (double)v}); }
+  void meta_bool(const std::string& key, bool v) { meta_.push_back({key, 7, "", v ? 1.0 : 0.0}); }
+  void add(const std::string& name, uint32_t type, std::vector<uint64_t> dims) override {
+    uint64_t count = 1;
+    for (auto d : dims) count *= d;
+    infos_.push_back({name, type, std::move(dims), ggml_size(type, count)});
+  }
+  void open(const std::string& path) override {
+    file_ = std::fopen(path.c_str(), "wb");
+    if (!file_) throw Error("cannot write " + path);
+    auto w32 = [&](uint32_t v) { w(&v, 4); };
+    auto w64 = [&](uint64_t v) { w(&v, 8); };
+    auto ws = [&](const std::string& s) { w64(s.size()); w(s.data(), s.size()); };
+    w("GGUF", 4);
+    w32(3);
+    w64(infos_.size());
+    w64(meta_.size() + 1);
+    ws("general.alignment");
+    w32(4);
+    w32(32);
+    for (auto& m : meta_) {
+      ws(m.key);
+      w32(m.type);
+      if (m.type == 8) ws(m.str);
+      else if (m.type == 4) w32((uint32_t)m.num);
+      else if (m.type == 6) { float f = (float)m.num; w(&f, 4); }
+      else { uint8_t b = m.num != 0; w(&b, 1); }
+    }
+    uint64_t offset = 0;
+    for (auto& t : infos_) {
+      ws(t.name);
+      w32((uint32_t)t.dims.size());
+      for (auto d : t.dims) w64(d);
+      w32(t.type);
+      w64(offset);
+      offset = (offset + t.bytes + 31) / 32 * 32;
+    }
+    static const uint8_t zeros[32] = {0};
+    w(zeros, (32 - written_ % 32) % 32);
+    written_ = 0;
+  }
+  void put(const void* bytes, size_t size) override {
+    if (next_ >= infos_.size() || size != infos_[next_].bytes) throw Error("GGUF writer: tensor size mismatch");
+    static const uint8_t zeros[32] = {0};
+    w(bytes, size);
+    w(zeros, (32 - written_ % 32) % 32);
+    ++next_;
+  }
+  void close() override {
+    if (next_ != infos_.size()) throw Error("GGUF writer: not every tensor was written");
+    if (file_ && std::fclose(file_) != 0) {
+      file_ = nullptr;
+      throw Error("GGUF writer: close failed");
+    }
+    file_ = nullptr;
+  }
+
+ private:
+  struct Meta {
+    std::string key;
+    uint32_t type;
+    std::string str;
+    double num;
+  };
+  void w(const void* p, size_t n) {
+    if (n && std::fwrite(p, 1, n, file_) != n) throw Error("GGUF writer: write failed");
+    written_ += n;
+  }
+  std::vector<Meta> meta_;
+  std::vector<Declared> infos_;
+  size_t next_ = 0;
+  uint64_t written_ = 0;
+  std::FILE* file_ = nullptr;
+};
+
+// One safetensors file: an 8-byte header length, a JSON header with each
+// tensor's dtype, shape (outermost first) and byte range, then the data.
+class SafetensorsOut : public Writer {
+ public:
+  ~SafetensorsOut() override {
+    if (file_) std::fclose(file_);
+  }
+  void add(const std::string& name, uint32_t type, std::vector<uint64_t> dims) override {
+    uint64_t count = 1;
+    for (auto d : dims) count *= d;
+    infos_.push_back({name, type, std::move(dims), ggml_size(type, count)});
+  }
+  void open(const std::string& path) override {
+    std::string h = "{\"__metadata__\": {\"format\": \"pt\"}";
+    uint64_t at = 0;
+    for (auto& t : infos_) {
+      const char* dtype = t.type == F32 ? "F32" : t.type == F16 ? "F16" : t.type == BF16 ? "BF16" : t.type == I8 ? "I8" : "I32";
+      h += ", \"" + t.name + "\": {\"dtype\": \"" + dtype + "\", \"shape\": [";
+      for (size_t i = t.dims.size(); i-- > 0;) h += std::to_string(t.dims[i]) + (i ? ", " : "");
+      h += "], \"data_offsets\": [" + std::to_string(at) + ", " + std::to_string(at + t.bytes) + "]}";
+      at += t.bytes;
+    }
+    h += "}";
+    while (h.size() % 8) h += ' ';
+    file_ = std::fopen(path.c_str(), "wb");
+    if (!file_) throw Error("cannot write " + path);
+    uint64_t n = h.size();
+    if (std::fwrite(&n, 8, 1, file_) != 1 || std::fwrite(h.data(), 1, h.size(), file_) != h.size())
+      throw Error("safetensors writer: write failed");
+  }
+  void put(const void* bytes, size_t size) override {
+    if (next_ >= infos_.size() || size != infos_[next_].bytes) throw Error("safetensors writer: tensor size mismatch");
+    if (size && std::fwrite(bytes, 1, size, file_) != size) throw Error("safetensors writer: write failed");
+    ++next_;
+  }
+  void close() override {
+    if (next_ != infos_.size()) throw Error("safetensors writer: not every tensor was written");
+    if (file_ && std::fclose(file_) != 0) {
+      file_ = nullptr;
+      throw Error("safetensors writer: close failed");
+    }
+    file_ = nullptr;
+  }
+
+ private:
+  std::vector<Declared> infos_;
+  size_t next_ = 0;
+  std::FILE* file_ = nullptr;
+};
+
 struct Spec {
   Json config;
   std::string format;
@@ -114,30 +268,83 @@ struct Spec {
   bool tied = true;
   std::string prefix;     // start of every tensor name ("thinker." ...)
   std::string config_at;  // key path the settings are nested under ("a.b.")
+  std::string dtype = "f32";  // the float format's element type: f32, f16 or bf16
+  std::string names = "hf";   // "hf", or "transcribe": dec.* names under the file's arch
+  // The transcribe.cpp name of a Hugging Face tensor name (its inverse is
+  // hf_decoder_name in the product's host.cpp).
+  std::string out_name(const std::string& hf) const {
+    if (names != "transcribe") return hf;
+    std::string n = hf.substr(prefix.size());
+    auto starts = [&](const char* p) { return n.compare(0, std::strlen(p), p) == 0; };
+    if (starts("model.embed_tokens.")) return "dec.token_embd." + n.substr(19);
+    if (starts("model.norm.")) return "dec.output_norm." + n.substr(11);
+    if (starts("lm_head.")) return "dec.output." + n.substr(8);
+    n = n.substr(std::strlen("model.layers."));
+    const size_t dot = n.find('.');
+    const std::string layer = n.substr(0, dot), part = n.substr(dot + 1);
+    static const char* table[][2] = {
+        {"input_layernorm.", "norm_attn."},   {"post_attention_layernorm.", "norm_ffn."},
+        {"self_attn.q_norm.", "attn.q_norm."}, {"self_attn.k_norm.", "attn.k_norm."},
+        {"self_attn.q_proj.", "attn.q."},      {"self_attn.k_proj.", "attn.k."},
+        {"self_attn.v_proj.", "attn.v."},      {"self_attn.o_proj.", "attn.o."},
+        {"mlp.gate_proj.", "ffn.gate."},       {"mlp.up_proj.", "ffn.up."},
+        {"mlp.down_proj.", "ffn.down."},
+    };
+    for (auto& row : table)
+      if (part.compare(0, std::strlen(row[0]), row[0]) == 0)
+        return "dec.blocks." + layer + "." + row[1] + part.substr(std::strlen(row[0]));
+    throw Error("no transcribe.cpp name for " + hf);
+  }
 };
 
-void write_matrix(GgufWriter* w, const Spec& s, const std::string& name, size_t n, size_t k, bool declare) {
+// Float rows in the spec's element type.
+void put_float_rows(Writer* w, const Spec& s, const std::vector<float>& v) {
+  if (s.dtype == "f32") return w->put(v.data(), v.size() * 4);
+  std::vector<uint16_t> h(v.size());
+  for (size_t i = 0; i < v.size(); ++i) {
+    if (s.dtype == "f16") {
+      h[i] = f32_to_f16(v[i]);
+    } else {
+      uint32_t u;
+      std::memcpy(&u, &v[i], 4);
+      u += 0x7fff + ((u >> 16) & 1);  // bf16, nearest even (these values are finite)
+      h[i] = (uint16_t)(u >> 16);
+    }
+  }
+  w->put(h.data(), h.size() * 2);
+}
+uint32_t float_type(const Spec& s) { return s.dtype == "f32" ? F32 : s.dtype == "f16" ? F16 : BF16; }
+
+void write_matrix(Writer* w, const Spec& s, const std::string& hf, size_t n, size_t k, bool declare) {
+  const std::string name = s.out_name(hf + ".weight");
+  const std::string base = name.substr(0, name.size() - 7);  // without ".weight"
+  if (s.format == "float") {
+    if (declare) return w->add(name, float_type(s), {k, n});
+    std::vector<float> all(n * k);
+    parallel_rows(n, [&](size_t r) { normal_row(s.seed, hf, r, k, s.sd, all.data() + r * k); });
+    return put_float_rows(w, s, all);
+  }
   if (s.format == "q8_0") {
     if (k % 32) throw Error("q8_0 needs k to be a multiple of 32");
-    if (declare) return w->add(name + ".weight", Q8_0, {k, n});
+    if (declare) return w->add(base + ".weight", Q8_0, {k, n});
     std::vector<uint8_t> bytes(n * (k / 32) * 34);
     parallel_rows(n, [&](size_t r) {
       std::vector<float> row(k);
-      normal_row(s.seed, name, r, k, s.sd, row.data());
+      normal_row(s.seed, hf, r, k, s.sd, row.data());
       for (size_t b = 0; b < k / 32; ++b) q8_0_block(row.data() + b * 32, bytes.data() + (r * (k / 32) + b) * 34);
     });
     w->put(bytes.data(), bytes.size());
   } else if (s.format == "int8") {
     if (declare) {
-      w->add(name + ".weight", I8, {k, n});
-      w->add(name + ".scales", F32, {n});
+      w->add(base + ".weight", I8, {k, n});
+      w->add(base + ".scales", F32, {n});
       return;
     }
     std::vector<int8_t> codes(n * k);
     std::vector<float> scales(n);
     parallel_rows(n, [&](size_t r) {
       std::vector<float> row(k);
-      normal_row(s.seed, name, r, k, s.sd, row.data());
+      normal_row(s.seed, hf, r, k, s.sd, row.data());
       float max = 0.0f;
       for (float v : row) max = std::max(max, std::fabs(v));
       scales[r] = row_scale(max);
@@ -149,20 +356,20 @@ void write_matrix(GgufWriter* w, const Spec& s, const std::string& name, size_t 
     if (k % 128) throw Error("ternary needs k to be a multiple of 128");
     size_t row_bytes = (k + 4) / 5;
     if (declare) {
-      w->add(name + ".qweight", I8, {row_bytes, n});
-      w->add(name + ".scales", F32, {k / 128, n});
+      w->add(base + ".qweight", I8, {row_bytes, n});
+      w->add(base + ".scales", F32, {k / 128, n});
       return;
     }
     std::vector<uint8_t> packed(n * row_bytes);
     std::vector<float> scales(n * (k / 128));
     parallel_rows(n, [&](size_t r) {
       std::vector<float> row(k);
-      normal_row(s.seed, name, r, k, s.sd, row.data());
+      normal_row(s.seed, hf, r, k, s.sd, row.data());
       double sum = 0;
       for (float v : row) sum += std::fabs(v);
       float absmean = (float)(sum / (double)k);
       for (size_t g = 0; g < k / 128; ++g) scales[r * (k / 128) + g] = absmean;
-      Xorshift codes = stream(s.seed, name + ".codes", r);
+      Xorshift codes = stream(s.seed, hf + ".codes", r);
       uint8_t* dst = packed.data() + r * row_bytes;
       for (size_t b = 0; b < row_bytes; ++b) {
         unsigned byte = 0, place = 1;
@@ -181,23 +388,26 @@ void write_matrix(GgufWriter* w, const Spec& s, const std::string& name, size_t 
     w->put(packed.data(), packed.size());
     w->put(scales.data(), scales.size() * 4);
   } else {
-    throw Error("synthetic format must be q8_0, int8 or ternary, not " + s.format);
+    throw Error("synthetic format must be q8_0, float, int8 or ternary, not " + s.format);
   }
 }
 
-void write_table(GgufWriter* w, const Spec& s, const std::string& name, size_t n, size_t k, bool declare) {
+void write_table(Writer* w, const Spec& s, const std::string& hf, size_t n, size_t k, bool declare) {
+  const std::string name = s.out_name(hf + ".weight");
+  const std::string base = name.substr(0, name.size() - 7);
+  if (s.format == "float") return write_matrix(w, s, hf, n, k, declare);
   if (s.format == "int8") {
     if (k % 32) throw Error("an int8 table needs k to be a multiple of 32");
     if (declare) {
-      w->add(name + ".weight", I8, {k, n});
-      w->add(name + ".scales", F32, {k / 32, n});
+      w->add(base + ".weight", I8, {k, n});
+      w->add(base + ".scales", F32, {k / 32, n});
       return;
     }
     std::vector<int8_t> codes(n * k);
     std::vector<float> scales(n * (k / 32));
     parallel_rows(n, [&](size_t r) {
       std::vector<float> row(k);
-      normal_row(s.seed, name, r, k, s.sd, row.data());
+      normal_row(s.seed, hf, r, k, s.sd, row.data());
       for (size_t g = 0; g < k / 32; ++g) {
         float max = 0.0f;
         for (int i = 0; i < 32; ++i) max = std::max(max, std::fabs(row[g * 32 + i]));
@@ -212,34 +422,34 @@ void write_table(GgufWriter* w, const Spec& s, const std::string& name, size_t n
   }
   Spec q = s;
   q.format = "q8_0";
-  write_matrix(w, q, name, n, k, declare);
+  write_matrix(w, q, hf, n, k, declare);
 }
 
-void write_norm(GgufWriter* w, const std::string& name, size_t n, bool declare) {
-  if (declare) return w->add(name, F32, {n});
+void write_norm(Writer* w, const Spec& s, const std::string& hf, size_t n, bool declare) {
+  if (declare) return w->add(s.out_name(hf), F32, {n});
   std::vector<float> ones(n, 1.0f);
   w->put(ones.data(), n * 4);
 }
 
-void walk(GgufWriter* w, const Spec& s, bool declare) {
+void walk(Writer* w, const Spec& s, bool declare) {
   bool qk_norm = s.config.string_or("model_type", "qwen3") == "qwen3";
   for (size_t l = 0; l < s.layers; ++l) {
     std::string p = s.prefix + "model.layers." + std::to_string(l);
-    write_norm(w, p + ".input_layernorm.weight", s.d, declare);
+    write_norm(w, s, p + ".input_layernorm.weight", s.d, declare);
     write_matrix(w, s, p + ".self_attn.q_proj", s.heads * s.hd, s.d, declare);
     write_matrix(w, s, p + ".self_attn.k_proj", s.kv_heads * s.hd, s.d, declare);
     write_matrix(w, s, p + ".self_attn.v_proj", s.kv_heads * s.hd, s.d, declare);
     if (qk_norm) {
-      write_norm(w, p + ".self_attn.q_norm.weight", s.hd, declare);
-      write_norm(w, p + ".self_attn.k_norm.weight", s.hd, declare);
+      write_norm(w, s, p + ".self_attn.q_norm.weight", s.hd, declare);
+      write_norm(w, s, p + ".self_attn.k_norm.weight", s.hd, declare);
     }
     write_matrix(w, s, p + ".self_attn.o_proj", s.d, s.heads * s.hd, declare);
-    write_norm(w, p + ".post_attention_layernorm.weight", s.d, declare);
+    write_norm(w, s, p + ".post_attention_layernorm.weight", s.d, declare);
     write_matrix(w, s, p + ".mlp.gate_proj", s.ffn, s.d, declare);
     write_matrix(w, s, p + ".mlp.up_proj", s.ffn, s.d, declare);
     write_matrix(w, s, p + ".mlp.down_proj", s.d, s.ffn, declare);
   }
-  write_norm(w, s.prefix + "model.norm.weight", s.d, declare);
+  write_norm(w, s, s.prefix + "model.norm.weight", s.d, declare);
   write_table(w, s, s.prefix + "model.embed_tokens", s.vocab, s.d, declare);
   if (!s.tied) write_table(w, s, s.prefix + "lm_head", s.vocab, s.d, declare);
 }
@@ -307,14 +517,59 @@ void synthesize(const std::string& dir, const std::string& spec_json) {
   std::string type = s.config.string_or("model_type", "qwen3");
   if (type != "qwen3" && type != "llama" && type != "mistral" && type != "granite")
     throw Error("synthetic spec: model_type " + type);
+  s.dtype = spec.string_or("dtype", "f32");
+  s.names = spec.string_or("names", "hf");
+  const std::string container = spec.string_or("container", "gguf");
+  if (s.format == "float" && s.dtype != "f32" && s.dtype != "f16" && s.dtype != "bf16")
+    throw Error("synthetic spec: dtype must be f32, f16 or bf16");
+  if (s.names == "transcribe") {
+    // One GGUF file as transcribe.cpp writes it: no config.json, the
+    // decoder's settings in metadata under stt.<arch>.decoder, dec.* names.
+    const std::string arch = spec.string_or("arch", "qwen3_asr");
+    const std::string meta = "stt." + (arch == "granite_speech" ? std::string("granite") : arch) + ".decoder";
+    s.prefix = arch == "qwen3_asr" ? "thinker." : (arch == "funasr_nano" || arch == "canary_qwen") ? "llm."
+                                                                                                     : "language_model.";
+    if (container != "gguf") throw Error("synthetic spec: transcribe names come in a GGUF file");
+    GgufOut w;
+    w.meta_str("general.architecture", arch);
+    w.meta_str("trit.synthetic", spec_json);
+    w.meta_str(meta + ".hidden_act", "silu");
+    w.meta_u32(meta + ".hidden_size", (uint32_t)s.d);
+    w.meta_u32(meta + ".intermediate_size", (uint32_t)s.ffn);
+    w.meta_u32(meta + ".n_layers", (uint32_t)s.layers);
+    w.meta_u32(meta + ".n_heads", (uint32_t)s.heads);
+    w.meta_u32(meta + ".n_kv_heads", (uint32_t)s.kv_heads);
+    w.meta_u32(meta + ".head_dim", (uint32_t)s.hd);
+    w.meta_u32(meta + ".vocab_size", (uint32_t)s.vocab);
+    w.meta_f32(meta + ".rms_norm_eps", (float)s.config.number("rms_norm_eps", 1e-6));
+    w.meta_f32(meta + ".rope_theta", (float)s.config.number("rope_theta", 1e6));
+    w.meta_bool(meta + ".tie_word_embeddings", s.tied);
+    walk(&w, s, true);
+    w.add("enc.blocks.0.attn.q.weight", F32, {8, 8});  // an encoder tensor the decoder does not read
+    w.open(dir + "/" + arch + ".gguf");
+    walk(&w, s, false);
+    std::vector<float> enc(64, 0.5f);
+    w.put(enc.data(), enc.size() * 4);
+    w.close();
+    return;
+  }
   std::string cfg = config_text(s);
   FILE* f = fopen((dir + "/config.json").c_str(), "wb");
   if (!f) throw Error("cannot write " + dir + "/config.json (does the folder exist?)");
   fwrite(cfg.data(), 1, cfg.size(), f);
   fclose(f);
-  GgufWriter w;
-  w.meta("general.architecture", type);
-  w.meta("trit.synthetic", spec_json);
+  if (container == "safetensors") {
+    SafetensorsOut w;
+    walk(&w, s, true);
+    w.open(dir + "/model.safetensors");
+    walk(&w, s, false);
+    w.close();
+    return;
+  }
+  if (container != "gguf") throw Error("synthetic spec: container must be gguf or safetensors");
+  GgufOut w;
+  w.meta_str("general.architecture", type);
+  w.meta_str("trit.synthetic", spec_json);
   walk(&w, s, true);
   w.open(dir + "/model.gguf");
   walk(&w, s, false);

@@ -20,7 +20,12 @@ extern "C" {
  * num_key_value_heads, head_dim, vocab_size, rms_norm_eps, rope_theta,
  * tie_word_embeddings, and Granite's embedding_multiplier,
  * attention_multiplier, residual_multiplier, logits_scaling},
- * "format": "q8_0" | "int8" | "ternary", "seed": N, "std": 0.02,
+ * "format": "q8_0" | "float" | "int8" | "ternary", "seed": N, "std": 0.02,
+ * "dtype": "f32" | "f16" | "bf16" (the float format's elements),
+ * "container": "gguf" (model.gguf) | "safetensors" (model.safetensors),
+ * "names": "hf" | "transcribe" (one <arch>.gguf as transcribe.cpp writes
+ * it: no config.json, the settings in stt.<arch>.decoder.* metadata, dec.*
+ * tensor names), "arch": "qwen3_asr" (of a transcribe file),
  * "prefix": start of every tensor name (""), "config_at": key path the
  * settings are nested under in config.json ("", or for example
  * "thinker_config.text_config.")}. Returns 0, or -1 (trit_synth_last_error). */

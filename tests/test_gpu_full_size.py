@@ -19,7 +19,7 @@ def c1_path():
 
 def test_c1_persistent_equals_layered_and_oracle(c1_path):
     prompt = np.random.default_rng(1).integers(0, 151936, size=64).tolist()
-    with CausalLm.load(c1_path, kv="f32", decode="persistent", max_context=256) as lm:
+    with CausalLm.load(c1_path, kv="f32", decode="persistent", exact=True, max_context=256) as lm:
         p_toks, p_logits = lm.generate_traced(prompt, max_new=12)
     with CausalLm.load(c1_path, kv="f32", decode="layered", max_context=256) as lm:
         l_toks, l_logits = lm.generate_traced(prompt, max_new=12)

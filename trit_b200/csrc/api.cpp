@@ -79,6 +79,21 @@ char* trit_lm_inspect(const char* model_dir, const char* options_json) {
 
 void trit_cuda_free_text(char* text) { std::free(text); }
 
+char* trit_lm_status(const TritLm* lm) {
+  return guard<char*>(nullptr, [&]() {
+    need(lm, "lm");
+    std::string text;
+    {
+      std::lock_guard<std::mutex> lock(const_cast<TritLm*>(lm)->lm->mutex());
+      text = lm->lm->status();
+    }
+    char* out = (char*)std::malloc(text.size() + 1);
+    if (!out) throw trit::Error("out of host memory");
+    std::memcpy(out, text.c_str(), text.size() + 1);
+    return out;
+  });
+}
+
 TritLm* trit_lm_load(const char* model_dir, const char* options_json) {
   return guard<TritLm*>(nullptr, [&]() {
     need(model_dir, "model_dir");
@@ -141,7 +156,8 @@ int64_t trit_lm_generate_traced(TritLm* lm, const TritLmPrefix* prefix, const in
 
 static int64_t answer_impl(TritLm* lm, const int32_t* head, size_t nhead, const float* audio, size_t naudio,
                            const int32_t* tail, size_t ntail, int32_t max_new, const int32_t* stop, size_t nstop,
-                           int32_t* out, size_t cap, float* logits) {
+                           int32_t* out, size_t cap, float* logits, bool on_device = false,
+                           void* cuda_stream = nullptr) {
   return guard<int64_t>(-1, [&]() {
     need(lm, "lm");
     if (nhead) need(head, "head");
@@ -150,7 +166,8 @@ static int64_t answer_impl(TritLm* lm, const int32_t* head, size_t nhead, const 
     if (nstop) need(stop, "stop");
     if (max_new < 0) throw trit::Error("max_new is negative");
     std::lock_guard<std::mutex> lock(lm->lm->mutex());
-    auto toks = lm->lm->answer(head, nhead, audio, naudio, tail, ntail, max_new, stop, nstop, logits);
+    auto toks = lm->lm->answer(head, nhead, audio, naudio, tail, ntail, max_new, stop, nstop, logits,
+                               (cudaStream_t)cuda_stream, on_device);
     return copy_out(toks, out, cap);
   });
 }
@@ -164,6 +181,19 @@ int64_t trit_lm_answer(TritLm* lm, const int32_t* head, size_t nhead, const floa
                        const int32_t* tail, size_t ntail, int32_t max_new, const int32_t* stop, size_t nstop,
                        int32_t* out, size_t cap) {
   return answer_impl(lm, head, nhead, audio, naudio, tail, ntail, max_new, stop, nstop, out, cap, nullptr);
+}
+
+int64_t trit_lm_generate_rows_device(TritLm* lm, const float* rows, size_t nrows, int32_t max_new,
+                                     const int32_t* stop, size_t nstop, int32_t* out, size_t cap, void* cuda_stream) {
+  return answer_impl(lm, nullptr, 0, rows, nrows, nullptr, 0, max_new, stop, nstop, out, cap, nullptr, true,
+                     cuda_stream);
+}
+
+int64_t trit_lm_answer_device(TritLm* lm, const int32_t* head, size_t nhead, const float* audio, size_t naudio,
+                              const int32_t* tail, size_t ntail, int32_t max_new, const int32_t* stop, size_t nstop,
+                              int32_t* out, size_t cap, void* cuda_stream) {
+  return answer_impl(lm, head, nhead, audio, naudio, tail, ntail, max_new, stop, nstop, out, cap, nullptr, true,
+                     cuda_stream);
 }
 
 int64_t trit_lm_answer_traced(TritLm* lm, const int32_t* head, size_t nhead, const float* audio, size_t naudio,
@@ -227,8 +257,9 @@ int64_t trit_lm_bidirectional_tokens(TritLm* lm, const float* rows, size_t m, si
   });
 }
 
-int trit_lm_generate_batch(TritLm* lm, size_t streams, const int32_t* const* prompts, const size_t* lens,
-                           int32_t max_new, const int32_t* stop, size_t nstop, int32_t* out, int64_t* counts) {
+static int batch_impl(TritLm* lm, const TritLmPrefix* prefix, size_t streams, const int32_t* const* prompts,
+                      const size_t* lens, int32_t max_new, const int32_t* stop, size_t nstop, int32_t* out,
+                      int64_t* counts) {
   return guard<int>(-1, [&]() {
     need(lm, "lm");
     need(prompts, "prompts");
@@ -237,8 +268,33 @@ int trit_lm_generate_batch(TritLm* lm, size_t streams, const int32_t* const* pro
     need(counts, "counts");
     if (nstop) need(stop, "stop");
     if (max_new < 0) throw trit::Error("max_new is negative");
+    if (prefix && prefix->owner != lm) throw trit::Error("the prefix belongs to another model");
     std::lock_guard<std::mutex> lock(lm->lm->mutex());
-    lm->lm->generate_batch(streams, prompts, lens, max_new, stop, nstop, out, counts);
+    lm->lm->generate_batch(streams, prompts, lens, max_new, stop, nstop, out, counts,
+                           prefix ? prefix->state.get() : nullptr);
+    return 0;
+  });
+}
+
+int trit_lm_generate_batch(TritLm* lm, size_t streams, const int32_t* const* prompts, const size_t* lens,
+                           int32_t max_new, const int32_t* stop, size_t nstop, int32_t* out, int64_t* counts) {
+  return batch_impl(lm, nullptr, streams, prompts, lens, max_new, stop, nstop, out, counts);
+}
+
+int trit_lm_generate_batch_prefix(TritLm* lm, const TritLmPrefix* prefix, size_t streams,
+                                  const int32_t* const* prompts, const size_t* lens, int32_t max_new,
+                                  const int32_t* stop, size_t nstop, int32_t* out, int64_t* counts) {
+  return batch_impl(lm, prefix, streams, prompts, lens, max_new, stop, nstop, out, counts);
+}
+
+int trit_lm_prefix_pages(const TritLm* lm, int64_t* used, int64_t* total) {
+  return guard<int>(-1, [&]() {
+    need(lm, "lm");
+    need(used, "used");
+    need(total, "total");
+    std::lock_guard<std::mutex> lock(const_cast<TritLm*>(lm)->lm->mutex());
+    *used = lm->lm->prefix_pages_used();
+    *total = lm->lm->prefix_pages_total();
     return 0;
   });
 }

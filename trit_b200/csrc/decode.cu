@@ -31,6 +31,7 @@
 #include "attention.cuh"
 #include "device.cuh"
 #include "kernels.h"
+#include "ll.cuh"
 
 namespace trit {
 namespace {
@@ -41,38 +42,8 @@ constexpr int TAB_SLAB = 128;    // bytes of a table row per pipeline stage
 constexpr int TAB_STAGES = 6;
 constexpr int TAB_PITCH = TAB_SLAB + 16;
 constexpr int TAB_ROWS_W = 8;    // table rows per warp group (4 threads a row)
-constexpr long long SPIN_LIMIT = 1ll << 22;
+constexpr long long SPIN_LIMIT = kSpinLimit;
 constexpr int LLW = 4;           // LL words a thread polls at once
-
-__device__ __forceinline__ int ld_volatile(const int* p) { return *(const volatile int*)p; }
-
-__device__ __forceinline__ long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return (long long)t;
-}
-
-__device__ __forceinline__ int split_at(int n, int part, int parts) { return (int)((long long)n * part / parts); }
-
-__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
-  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(s), "l"(gmem) : "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// ------------------------------------------------------------ LL words --
-__device__ __forceinline__ void ll_put(unsigned long long* p, uint32_t data, uint32_t tag) {
-  unsigned long long v = ((unsigned long long)tag << 32) | data;
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ll_get(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // The block waits until words [0, n) of `src` carry `tag` and hands each
 // word's data to sink(i, data). Thread t polls words t, t + DT, ...: every
@@ -177,11 +148,6 @@ __device__ void norm_quant(int d, const float* w, float eps, int G, bool half, S
 
 // ------------------------------------------------------------- products --
 constexpr int WSTAGE = 40 * 1024;  // bytes of one weight staging buffer (two of them)
-
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
-  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem) : "memory");
-}
 
 __host__ __device__ inline int code_row_bytes(const DMat& W) { return W.kind == kTernary ? W.k / 4 : W.k; }
 __host__ __device__ inline int scale_row_bytes(const DMat& W) {

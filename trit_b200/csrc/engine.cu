@@ -2,6 +2,9 @@
 // flows (src/models/parts/causal_lm.rs:141-302) on one GPU.
 #include "engine.h"
 
+#include <sys/stat.h>
+#include <unistd.h>
+
 #include <algorithm>
 #include <climits>
 #include <cmath>
@@ -38,6 +41,7 @@ Options Options::parse(const char* text, bool lenient) {
     else if (k == "max_streams") o.max_streams = count(1, 4096);
     else if (k == "page_tokens") o.page_tokens = count(1, 4096);
     else if (k == "prefill_rows") o.prefill_rows = count(1, 65536);
+    else if (k == "prefix_pages") o.prefix_pages = count(0, 1 << 20);
     else if (k == "decode") {
       if (v.kind != Json::String || (v.str != "persistent" && v.str != "layered"))
         throw Error("options: decode is \"persistent\" or \"layered\"");
@@ -47,6 +51,12 @@ Options Options::parse(const char* text, bool lenient) {
       o.tensor_cores = v.b;
     } else if (k == "tc_rows") {
       o.tc_rows = count(1, 1 << 20);
+    } else if (k == "weight_cache") {
+      if (v.kind != Json::Bool) throw Error("options: weight_cache is true or false");
+      o.weight_cache = v.b;
+    } else if (k == "cache_dir") {
+      if (v.kind != Json::String) throw Error("options: cache_dir must be a string");
+      o.cache_dir = v.str;
     } else if (k == "exact") {
       if (v.kind != Json::Bool) throw Error("options: exact is true or false");
       o.exact = v.b;
@@ -61,7 +71,35 @@ Options Options::parse(const char* text, bool lenient) {
 }
 
 PrefixState::~PrefixState() {
-  if (pages) cudaFree(pages);
+  if (owner) {
+    std::lock_guard<std::mutex> lock(owner->mutex());
+    owner->release_prefix(this);
+  }
+  if (partial) cudaFree(partial);
+}
+
+void Lm::release_prefix(PrefixState* p) {
+  prefix_free_.insert(prefix_free_.end(), p->pages.begin(), p->pages.end());
+  p->pages.clear();
+  p->owner = nullptr;
+  prefixes_.erase(p);
+}
+
+void Lm::map_slot(int slot, const PrefixState* prefix) {
+  const int pps = cache_.pages_per_stream;
+  int* row = table_host_.data() + (size_t)slot * pps;
+  bool changed = false;
+  for (int i = 0; i < pps; ++i) {
+    const int want = (prefix && i < (int)prefix->pages.size()) ? prefix->pages[i] : slot * pps + i;
+    changed |= row[i] != want;
+    row[i] = want;
+  }
+  if (changed)
+    TRIT_CUDA(cudaMemcpyAsync(page_table_ + (size_t)slot * pps, row, (size_t)pps * 4, cudaMemcpyHostToDevice, stream_));
+  if (prefix && prefix->partial) {
+    char* own = (char*)pool_ + ((size_t)slot * pps + prefix->pages.size()) * page_bytes_;
+    TRIT_CUDA(cudaMemcpyAsync(own, prefix->partial, page_bytes_, cudaMemcpyDeviceToDevice, stream_));
+  }
 }
 
 namespace {
@@ -83,25 +121,41 @@ struct Arena {
   const void* ptr(size_t at) const { return base ? base + at : nullptr; }
 };
 
-std::vector<float> f32_of(const GgufFile& g, const std::string& name, size_t len) {
+std::vector<float> f32_of(const TensorFiles& g, const std::string& name, size_t len) {
   const GgufTensor& t = g.at(name);
   if (t.count() != len) throw Error("tensor " + name + " has " + std::to_string(t.count()) + " values, expected " + std::to_string(len));
   std::vector<float> out(len);
   if (t.type == F32) {
     std::memcpy(out.data(), t.data, len * 4);
-  } else if (t.type == F16) {
+  } else if (t.type == F16 || t.type == BF16) {
     for (size_t i = 0; i < len; ++i) {
       uint16_t h;
       std::memcpy(&h, t.data + 2 * i, 2);
-      out[i] = f16_to_f32(h);
+      out[i] = t.type == F16 ? f16_to_f32(h) : bf16_to_f32(h);
     }
   } else {
-    throw Error("tensor " + name + " is not F32 or F16");
+    throw Error("tensor " + name + " is not F32, F16 or BF16");
   }
   return out;
 }
 
-const float* load_vector(const GgufFile& g, Arena& A, const std::string& name, size_t len) {
+bool is_float(uint32_t type) { return type == F32 || type == F16 || type == BF16; }
+
+// Q8_0 blocks of a float tensor of rows x k, quantized as ggml quantizes
+// (Tensors::q8_0 -> Blocks::quantize, src/cpu/tensors.rs:282-305,
+// src/cpu/gemm.rs:53-76), into split codes and f16 scale planes.
+void quantize_rows_q8_0(const TensorFiles& g, const std::string& name, size_t rows, size_t k, uint8_t* codes,
+                        uint8_t* scales) {
+  std::vector<float> v = f32_of(g, name, rows * k);
+  uint8_t blk[34];
+  for (size_t b = 0; b < rows * k / 32; ++b) {
+    q8_0_quantize_block(v.data() + b * 32, blk);
+    std::memcpy(scales + b * 2, blk, 2);
+    std::memcpy(codes + b * 32, blk + 2, 32);
+  }
+}
+
+const float* load_vector(const TensorFiles& g, Arena& A, const std::string& name, size_t len) {
   size_t at = A.take(len * 4);
   if (A.fill) {
     std::vector<float> v = f32_of(g, name, len);
@@ -115,14 +169,14 @@ const float* load_vector(const GgufFile& g, Arena& A, const std::string& name, s
 // scale plane (34-byte blocks are not 16-byte aligned); per-row int8 codes
 // and row scales; ternary base-3 bytes (src/cpu/kernels.rs:91-130) repacked
 // 16 codes a word in the pack_span order (kernels.rs:618-628).
-DMat load_mat(const GgufFile& g, Arena& A, const std::vector<std::pair<std::string, int>>& parts, int k) {
+DMat load_mat(const TensorFiles& g, Arena& A, const std::vector<std::pair<std::string, int>>& parts, int k) {
   DMat m;
   m.k = k;
   for (auto& p : parts) m.n += p.second;
   const std::string& first = parts[0].first;
   const GgufTensor* w = g.find(first + ".weight");
-  if (w && w->type == Q8_0) {
-    m.kind = kQ8_0;
+  if (w && (w->type == Q8_0 || is_float(w->type))) {
+    m.kind = kQ8_0;  // float weights are quantized to Q8_0 here
     m.agroup = 32;
     m.half = 1;
   } else if (w && w->type == I8 && g.find(first + ".scales")) {
@@ -132,7 +186,7 @@ DMat load_mat(const GgufFile& g, Arena& A, const std::vector<std::pair<std::stri
     m.kind = kTernary;
     m.agroup = 128;
   } else {
-    throw Error("model.gguf: no Q8_0, int8 or ternary weights for " + first);
+    throw Error(g.what() + ": no Q8_0, float, int8 or ternary weights for " + first);
   }
   if (k % m.agroup != 0) throw Error(first + ": the input width is not whole groups of " + std::to_string(m.agroup));
   if (m.n % 32 != 0) throw Error(first + ": the output rows are not a multiple of 32");
@@ -147,7 +201,9 @@ DMat load_mat(const GgufFile& g, Arena& A, const std::vector<std::pair<std::stri
   size_t row0 = 0;
   for (auto& p : parts) {
     size_t rows = (size_t)p.second;
-    if (m.kind == kQ8_0) {
+    if (m.kind == kQ8_0 && is_float(g.at(p.first + ".weight").type)) {
+      quantize_rows_q8_0(g, p.first + ".weight", rows, k, codes.data() + row0 * k, scales.data() + row0 * (k / 32) * 2);
+    } else if (m.kind == kQ8_0) {
       const GgufTensor& t = g.at(p.first + ".weight");
       if (t.type != Q8_0 || t.count() != rows * k) throw Error("tensor " + p.first + ".weight: expected Q8_0 " + std::to_string(rows) + "x" + std::to_string(k));
       size_t blocks = rows * k / 32;
@@ -197,20 +253,25 @@ DMat load_mat(const GgufFile& g, Arena& A, const std::vector<std::pair<std::stri
 
 // Dense::table (src/cpu/gemm.rs:383-409): Q8_0 blocks (f16 scales) or int8
 // codes with one f32 scale per 32 values, f32 math.
-DTable load_table(const GgufFile& g, Arena& A, const std::string& name, int rows, int cols) {
+DTable load_table(const TensorFiles& g, Arena& A, const std::string& name, int rows, int cols) {
   DTable t;
   t.n = rows;
   t.k = cols;
   if (cols % 32) throw Error(name + ": the width is not whole blocks of 32");
   const GgufTensor& w = g.at(name + ".weight");
   if (w.count() != (uint64_t)rows * cols) throw Error(name + ".weight has the wrong size");
-  t.scale_f16 = w.type == Q8_0;
-  if (w.type != Q8_0 && w.type != I8) throw Error(name + ".weight is neither Q8_0 nor I8");
+  t.scale_f16 = w.type == Q8_0 || is_float(w.type);  // float tables are quantized to Q8_0
+  if (!t.scale_f16 && w.type != I8) throw Error(name + ".weight is neither Q8_0, float nor I8");
   size_t co = A.take((size_t)rows * cols), so = A.take((size_t)rows * (cols / 32) * (t.scale_f16 ? 2 : 4));
   t.codes = (const int8_t*)A.ptr(co);
   t.scales = A.ptr(so);
   if (!A.fill) return t;
-  if (w.type == Q8_0) {
+  if (is_float(w.type)) {
+    std::vector<uint8_t> codes((size_t)rows * cols), scales((size_t)rows * (cols / 32) * 2);
+    quantize_rows_q8_0(g, name + ".weight", rows, cols, codes.data(), scales.data());
+    A.put(co, codes.data(), codes.size());
+    A.put(so, scales.data(), scales.size());
+  } else if (w.type == Q8_0) {
     std::vector<uint8_t> codes((size_t)rows * cols), scales((size_t)rows * (cols / 32) * 2);
     for (size_t b = 0; b < (size_t)rows * cols / 32; ++b) {
       std::memcpy(scales.data() + b * 2, w.data + b * 34, 2);
@@ -292,6 +353,8 @@ void KernelClock::report(const char* what) {
 
 // Frees every device and pinned buffer; safe to call twice.
 void Lm::release() {
+  for (PrefixState* p : prefixes_) p->owner = nullptr;  // their pages go with the pool
+  prefixes_.clear();
   cudaSetDevice(opt_.device);
   if (stream_) cudaStreamSynchronize(stream_);
   void* bufs[] = {arena_, d_layers_, pool_, page_table_, x_, qkv_, att_, h_, xn_, xq_, xs_, row_stream_, row_pos_, ids_,
@@ -320,6 +383,8 @@ void Lm::release() {
   tc_ready_ = false;
   batch_graph_ = nullptr;
   batch_ready_ = false;
+  if (ev_rows_) cudaEventDestroy(ev_rows_);
+  ev_rows_ = nullptr;
   for (auto& e : ev_)
     if (e) cudaEventDestroy(e);
   if (stream_) cudaStreamDestroy(stream_);
@@ -336,9 +401,178 @@ void Lm::release() {
   dcount_ = nullptr; trace_ = nullptr; rope_ = nullptr;
 }
 
+// ------------------------------------------------------------ weight cache --
+// The arena's bytes (every weight in its device layout) in one file, so a
+// later load reads them straight into device memory with no parsing or
+// conversion (the weight store of src/cpu/store.rs:1-16,369-428, for the
+// device layout). The file is named by a hash of what made it: the cache
+// version, the source files' paths, sizes and modification times, the
+// tensor prefix and the arena size. A file that does not match byte for
+// byte (its header, its length, or the hash of its contents) is ignored
+// and rewritten: the cache never changes a result, it only saves time.
+namespace {
+
+constexpr char kCacheMagic[8] = {'T', 'R', 'I', 'T', 'C', 'U', 'D', 'A'};
+constexpr uint32_t kCacheVersion = 1;  // the arena layout; bump when it changes
+constexpr size_t kCacheChunk = 64u << 20;
+
+uint64_t mix64(uint64_t h, uint64_t w) {
+  h ^= w + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
+  return h * 0xff51afd7ed558ccdull;
+}
+uint64_t hash_bytes(uint64_t h, const uint8_t* p, size_t n) {
+  size_t i = 0;
+  for (; i + 8 <= n; i += 8) {
+    uint64_t w;
+    std::memcpy(&w, p + i, 8);
+    h = mix64(h, w);
+  }
+  for (; i < n; ++i) h = mix64(h, p[i]);
+  return h;
+}
+
+struct CacheHeader {
+  char magic[8];
+  uint32_t version;
+  uint32_t identity_bytes;
+  uint64_t arena_bytes;
+  uint64_t content_hash;
+};
+
+struct Pinned {
+  void* p = nullptr;
+  explicit Pinned(size_t n) { TRIT_CUDA(cudaMallocHost(&p, n)); }
+  ~Pinned() {
+    if (p) cudaFreeHost(p);
+  }
+};
+
+}  // namespace
+
+std::string Lm::weight_cache_identity(const ModelSource& src) const {
+  std::string id = "trit-cuda weights v" + std::to_string(kCacheVersion) + "\n" + src.format + "\n" + src.prefix +
+                   "\n" + std::to_string(arena_bytes_) + "\n";
+  for (const std::string& p : src.files->paths()) {
+    struct stat st;
+    if (::stat(p.c_str(), &st) != 0) throw Error("cannot stat " + p);
+    id += p + " " + std::to_string((long long)st.st_size) + " " + std::to_string((long long)st.st_mtim.tv_sec) + "." +
+          std::to_string((long long)st.st_mtim.tv_nsec) + "\n";
+  }
+  return id;
+}
+
+std::string Lm::weight_cache_path(const std::string& dir, const ModelSource& src) const {
+  const std::string id = weight_cache_identity(src);
+  char name[64];
+  std::snprintf(name, sizeof name, "%016llx.bin", (unsigned long long)hash_bytes(1469598103934665603ull,
+                                                                                    (const uint8_t*)id.data(), id.size()));
+  const std::string folder = opt_.cache_dir.empty() ? dir + "/.trit_cuda" : opt_.cache_dir;
+  return folder + "/" + name;
+}
+
+bool Lm::read_weight_cache(const std::string& path, void* arena, size_t bytes, cudaStream_t s) {
+  FILE* f = std::fopen(path.c_str(), "rb");
+  if (!f) return false;
+  bool ok = false;
+  try {
+    CacheHeader h{};
+    std::string want_id;
+    if (std::fread(&h, sizeof h, 1, f) == 1 && std::memcmp(h.magic, kCacheMagic, 8) == 0 &&
+        h.version == kCacheVersion && h.arena_bytes == bytes && h.identity_bytes < (1u << 20)) {
+      std::string id(h.identity_bytes, '\0');
+      if (std::fread(&id[0], 1, id.size(), f) == id.size()) {
+        // Two pinned buffers: one fills from the file while the other copies.
+        Pinned buf(2 * kCacheChunk);
+        uint64_t hash = 1469598103934665603ull;
+        size_t done = 0;
+        int which = 0;
+        bool short_read = false;
+        while (done < bytes) {
+          const size_t n = std::min(kCacheChunk, bytes - done);
+          uint8_t* b = (uint8_t*)buf.p + which * kCacheChunk;
+          TRIT_CUDA(cudaStreamSynchronize(s));  // the copy that used this half two chunks ago
+          if (std::fread(b, 1, n, f) != n) {
+            short_read = true;
+            break;
+          }
+          hash = hash_bytes(hash, b, n);
+          TRIT_CUDA(cudaMemcpyAsync((char*)arena + done, b, n, cudaMemcpyHostToDevice, s));
+          done += n;
+          which ^= 1;
+        }
+        TRIT_CUDA(cudaStreamSynchronize(s));
+        ok = !short_read && hash == h.content_hash && std::fgetc(f) == EOF;
+      }
+    }
+  } catch (...) {
+    ok = false;
+  }
+  std::fclose(f);
+  return ok;
+}
+
+void Lm::write_weight_cache(const std::string& path, const void* arena, size_t bytes, cudaStream_t s) {
+  // Best effort: a folder that cannot be written leaves the load as it is.
+  const std::string folder = path.substr(0, path.find_last_of('/'));
+  ::mkdir(folder.c_str(), 0755);
+  const std::string tmp = path + "." + std::to_string((long long)::getpid()) + ".tmp";
+  FILE* f = std::fopen(tmp.c_str(), "wb");
+  if (!f) return;
+  bool ok = true;
+  try {
+    const std::string id = cache_identity_;
+    CacheHeader h{};
+    std::memcpy(h.magic, kCacheMagic, 8);
+    h.version = kCacheVersion;
+    h.identity_bytes = (uint32_t)id.size();
+    h.arena_bytes = bytes;
+    ok = std::fwrite(&h, sizeof h, 1, f) == 1 && std::fwrite(id.data(), 1, id.size(), f) == id.size();
+    Pinned buf(kCacheChunk);
+    uint64_t hash = 1469598103934665603ull;
+    for (size_t done = 0; ok && done < bytes;) {
+      const size_t n = std::min(kCacheChunk, bytes - done);
+      TRIT_CUDA(cudaMemcpyAsync(buf.p, (const char*)arena + done, n, cudaMemcpyDeviceToHost, s));
+      TRIT_CUDA(cudaStreamSynchronize(s));
+      hash = hash_bytes(hash, (const uint8_t*)buf.p, n);
+      ok = std::fwrite(buf.p, 1, n, f) == n;
+      done += n;
+    }
+    h.content_hash = hash;
+    ok = ok && std::fseek(f, 0, SEEK_SET) == 0 && std::fwrite(&h, sizeof h, 1, f) == 1;
+  } catch (...) {
+    ok = false;
+  }
+  ok = (std::fclose(f) == 0) && ok;
+  if (ok) ok = std::rename(tmp.c_str(), path.c_str()) == 0;
+  if (!ok) std::remove(tmp.c_str());
+}
+
+std::string Lm::status() const {
+  auto quote = [](const std::string& v) {
+    std::string o = "\"";
+    for (char c : v) {
+      if (c == '"' || c == '\\') o += '\\';
+      o += c;
+    }
+    return o + "\"";
+  };
+  char buf[512];
+  std::snprintf(buf, sizeof buf,
+                "\"arena_bytes\": %zu, \"device\": %d, \"kv\": \"%s\", \"decode\": \"%s\", \"exact\": %s, "
+                "\"prefix_pages\": [%d, %d], \"max_streams\": %d, \"max_context\": %d",
+                arena_bytes_, opt_.device, opt_.kv_f16 ? "f16" : "f32", opt_.decode.c_str(),
+                opt_.exact ? "true" : "false", prefix_pages_used(), prefix_pages_total(), opt_.max_streams,
+                opt_.max_context);
+  return "{\"source\": " + quote(source_) + ", \"weights_from\": " + quote(weights_from_) +
+         ", \"weight_cache\": " + (cache_file_.empty() ? std::string("null") : quote(cache_file_)) + ", " + buf + "}";
+}
+
 // Config::parse (causal_lm.rs:41-77) and CausalLm::from_tensors (:141-198).
 void Lm::load(const std::string& dir) {
-  ModelConfig mc = read_model_config(dir, opt_.config_at);
+  ModelSource src = open_model(dir, opt_.config_at, opt_.prefix);
+  const ModelConfig& mc = src.mc;
+  const std::string& prefix = src.prefix;
+  source_ = src.format;
   cfg_ = mc.cfg;
   const bool qk_norm = mc.qk_norm;
   const float rope_base = mc.rope_base;
@@ -346,16 +580,21 @@ void Lm::load(const std::string& dir) {
   if (cfg_.hd != 128) throw Error("head_dim " + std::to_string(cfg_.hd) + ": the CUDA kernels take head_dim 128");
   if (cfg_.d % 128 || cfg_.ffn % 128) throw Error("hidden and intermediate sizes must be multiples of 128");
 
-  GgufFile g(dir + "/model.gguf");
+  const TensorFiles& g = *src.files;
   const int hd = cfg_.hd, qd = cfg_.heads * hd, kvd = cfg_.kv_heads * hd;
-  bool has_head = !tied_ && g.find(opt_.prefix + "lm_head.weight");
+  bool has_head = !tied_ && g.find(prefix + "lm_head.weight");
+  // Pass 0 sizes the arena; pass 1 lays the weights out in it, converting
+  // them from the files, or only naming their places when the weight cache
+  // already put the arena's bytes there.
+  bool from_cache = false;
+  std::string cache_file;
   for (int pass = 0; pass < 2; ++pass) {
     Arena A;
-    A.fill = pass == 1;
+    A.fill = pass == 1 && !from_cache;
     A.base = (char*)arena_;
     layers_.assign(cfg_.layers, DLayer{});
     for (int l = 0; l < cfg_.layers; ++l) {
-      std::string p = opt_.prefix + "model.layers." + std::to_string(l);
+      std::string p = prefix + "model.layers." + std::to_string(l);
       DLayer& L = layers_[l];
       L.norm_attn = load_vector(g, A, p + ".input_layernorm.weight", cfg_.d);
       L.qkv = load_mat(g, A, {{p + ".self_attn.q_proj", qd}, {p + ".self_attn.k_proj", kvd}, {p + ".self_attn.v_proj", kvd}}, cfg_.d);
@@ -368,14 +607,22 @@ void Lm::load(const std::string& dir) {
       L.gate_up = load_mat(g, A, {{p + ".mlp.gate_proj", cfg_.ffn}, {p + ".mlp.up_proj", cfg_.ffn}}, cfg_.d);
       L.down = load_mat(g, A, {{p + ".mlp.down_proj", cfg_.d}}, cfg_.ffn);
     }
-    final_norm_ = load_vector(g, A, opt_.prefix + "model.norm.weight", cfg_.d);
-    embed_ = load_table(g, A, opt_.prefix + "model.embed_tokens", cfg_.vocab, cfg_.d);
-    head_ = has_head ? load_table(g, A, opt_.prefix + "lm_head", cfg_.vocab, cfg_.d) : embed_;
+    final_norm_ = load_vector(g, A, prefix + "model.norm.weight", cfg_.d);
+    embed_ = load_table(g, A, prefix + "model.embed_tokens", cfg_.vocab, cfg_.d);
+    head_ = has_head ? load_table(g, A, prefix + "lm_head", cfg_.vocab, cfg_.d) : embed_;
     if (pass == 0) {
       arena_bytes_ = A.used;
       TRIT_CUDA(cudaMalloc(&arena_, arena_bytes_));
+      if (opt_.weight_cache) {
+        cache_identity_ = weight_cache_identity(src);
+        cache_file = weight_cache_path(dir, src);
+        from_cache = read_weight_cache(cache_file, arena_, arena_bytes_, stream_);
+      }
     }
   }
+  weights_from_ = from_cache ? "cache" : "files";
+  cache_file_ = opt_.weight_cache ? cache_file : "";
+  if (opt_.weight_cache && !from_cache) write_weight_cache(cache_file, arena_, arena_bytes_, stream_);
   TRIT_CUDA(cudaMalloc(&d_layers_, sizeof(DLayer) * cfg_.layers));
   TRIT_CUDA(cudaMemcpy(d_layers_, layers_.data(), sizeof(DLayer) * cfg_.layers, cudaMemcpyHostToDevice));
 
@@ -401,13 +648,17 @@ void Lm::alloc_buffers() {
   cache_.page_tokens = opt_.page_tokens;
   cache_.pages_per_stream = (opt_.max_context + opt_.page_tokens - 1) / opt_.page_tokens;
   page_bytes_ = (size_t)cfg_.layers * 2 * cfg_.kv_heads * opt_.page_tokens * hd * (opt_.kv_f16 ? 2 : 4);
+  // Then the pages kept for prefixes, which any slot's table row may name.
   size_t pages = (size_t)opt_.max_streams * cache_.pages_per_stream;
-  TRIT_CUDA(cudaMalloc(&pool_, pages * page_bytes_));
+  prefix_pages_total_ = opt_.prefix_pages >= 0 ? opt_.prefix_pages : cache_.pages_per_stream;
+  TRIT_CUDA(cudaMalloc(&pool_, (pages + prefix_pages_total_) * page_bytes_));
   cache_.pool = pool_;
-  std::vector<int> table(pages);
-  for (size_t i = 0; i < pages; ++i) table[i] = (int)i;
+  table_host_.resize(pages);
+  for (size_t i = 0; i < pages; ++i) table_host_[i] = (int)i;
+  prefix_free_.clear();
+  for (int i = prefix_pages_total_ - 1; i >= 0; --i) prefix_free_.push_back((int)pages + i);
   TRIT_CUDA(cudaMalloc(&page_table_, pages * sizeof(int)));
-  TRIT_CUDA(cudaMemcpy(page_table_, table.data(), pages * sizeof(int), cudaMemcpyHostToDevice));
+  TRIT_CUDA(cudaMemcpy(page_table_, table_host_.data(), pages * sizeof(int), cudaMemcpyHostToDevice));
   cache_.page_table = page_table_;
 
   rows_cap_ = std::max(opt_.prefill_rows, opt_.max_streams);
@@ -541,6 +792,7 @@ std::vector<int> Lm::generate_additive(const int* ids, size_t n, const float* au
   }
   int* staged = stage_ids(ids, n, nullptr, 0);
   TRIT_CUDA(cudaEventRecord(ev_[0], stream_));
+  map_slot(0, nullptr);
   TRIT_CUDA(cudaMemcpyAsync(audio_, audio, rows * d * 4, cudaMemcpyHostToDevice, stream_));
   run_prompt(n, 0, 0, [&](size_t c0, size_t c1) {
     embed_rows(staged, c0, c1, x_);
@@ -621,6 +873,7 @@ std::vector<int> Lm::bidirectional_tokens(const float* rows, size_t m, size_t fr
     host[rows_cap_ + r] = (int)r;
   }
   TRIT_CUDA(cudaEventRecord(ev_[0], stream_));
+  map_slot(0, nullptr);
   TRIT_CUDA(cudaMemcpyAsync(row_stream_, host, m * 4, cudaMemcpyHostToDevice, stream_));
   TRIT_CUDA(cudaMemcpyAsync(row_pos_, host + rows_cap_, m * 4, cudaMemcpyHostToDevice, stream_));
   TRIT_CUDA(cudaMemcpyAsync(x_, rows, m * d * 4, cudaMemcpyHostToDevice, stream_));
@@ -767,7 +1020,7 @@ std::vector<int> Lm::generate(const PrefixState* prefix, const int* ids, size_t 
   TRIT_CUDA(cudaSetDevice(opt_.device));
   int* staged = stage_ids(ids + done, n - done, nullptr, 0);
   TRIT_CUDA(cudaEventRecord(ev_[0], stream_));
-  if (use) TRIT_CUDA(cudaMemcpyAsync(pool_, prefix->pages, prefix->bytes, cudaMemcpyDeviceToDevice, stream_));
+  map_slot(0, use ? prefix : nullptr);  // the prefix's pages, read in place
   run_prompt(n - done, 0, (int)done, [&](size_t c0, size_t c1) { embed_rows(staged, c0, c1, x_); });
   return finish(0, (int)n, max_new, stop, nstop, logits);
 }
@@ -780,7 +1033,8 @@ std::vector<int> Lm::generate_rows(const float* rows, size_t nrows, int max_new,
 // CausalLm::answer (causal_lm.rs:264-282): [embed(head); audio; embed(tail)]
 // as the prompt rows, then generate_rows (:251-262).
 std::vector<int> Lm::answer(const int* head, size_t nhead, const float* audio, size_t naudio, const int* tail,
-                            size_t ntail, int max_new, const int* stop, size_t nstop, float* logits) {
+                            size_t ntail, int max_new, const int* stop, size_t nstop, float* logits,
+                            cudaStream_t audio_stream, bool audio_on_device) {
   size_t m = nhead + naudio + ntail;
   if (m == 0) throw Error("no prompt rows");
   check_ids(head, nhead);
@@ -790,7 +1044,20 @@ std::vector<int> Lm::answer(const int* head, size_t nhead, const float* audio, s
   timing_ = Timing{};
   TRIT_CUDA(cudaSetDevice(opt_.device));
   int* staged = stage_ids(head, nhead, tail, ntail);  // head ids then tail ids
+  if (audio_on_device && naudio) {
+    // Rows in device memory (an encoder's output on this GPU): check that
+    // they are, then order their reads after the caller's stream.
+    cudaPointerAttributes attr{};
+    TRIT_CUDA(cudaPointerGetAttributes(&attr, audio));
+    if ((attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) || attr.device != opt_.device)
+      throw Error("the rows are not device memory of CUDA device " + std::to_string(opt_.device));
+    if (!ev_rows_) TRIT_CUDA(cudaEventCreateWithFlags(&ev_rows_, cudaEventDisableTiming));
+    TRIT_CUDA(cudaEventRecord(ev_rows_, audio_stream));
+    TRIT_CUDA(cudaStreamWaitEvent(stream_, ev_rows_, 0));
+  }
+  const cudaMemcpyKind rows_kind = audio_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
   TRIT_CUDA(cudaEventRecord(ev_[0], stream_));
+  map_slot(0, nullptr);
   const int d = cfg_.d;
   run_prompt(m, 0, 0, [&](size_t c0, size_t c1) {
     for (size_t r = c0; r < c1;) {
@@ -801,7 +1068,7 @@ std::vector<int> Lm::answer(const int* head, size_t nhead, const float* audio, s
         r = e;
       } else if (r < nhead + naudio) {
         size_t e = std::min(c1, nhead + naudio);
-        TRIT_CUDA(cudaMemcpyAsync(dst, audio + (r - nhead) * d, (e - r) * d * 4, cudaMemcpyHostToDevice, stream_));
+        TRIT_CUDA(cudaMemcpyAsync(dst, audio + (r - nhead) * d, (e - r) * d * 4, rows_kind, stream_));
         r = e;
       } else {
         // Tail ids sit after the head ids in the staging area.
@@ -900,16 +1167,19 @@ void Lm::decode_layered(int slot, int position, int steps, float* trace) {
 // Batch-1 decode in one cooperative kernel (decode.cu): step i feeds
 // tokens_[i] at position + i; the kernel stops at a stop token.
 void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
-  if (!decode_supported(cfg_))
-    throw Error("the persistent decode takes widths up to 8192 in multiples of 128; use {\"decode\": \"layered\"}");
   if (!decode_grid_) {
     decode_grid_ = decode_grid(opt_.device);
     if (decode_grid_ < cfg_.kv_heads) throw Error("too few SMs for the persistent decode");
-    ll_words_ = decode_ll_words(cfg_, decode_grid_);
+    ll_words_ = std::max(decode_ll_words(cfg_, decode_grid_), decode_fast_ll_words(cfg_, decode_grid_));
     TRIT_CUDA(cudaMalloc(&dll_, ll_words_ * 8));
     TRIT_CUDA(cudaMalloc(&dstatus_, 4));
     TRIT_CUDA(cudaMalloc(&dcount_, 4));
   }
+  // The default path sums in tree order (decode_fast.cu); "exact" keeps the
+  // reference's order (decode.cu).
+  const bool fast = !opt_.exact && decode_fast_supported(cfg_, head_, decode_grid_, cache_.f16);
+  if (!fast && !decode_supported(cfg_))
+    throw Error("the persistent decode takes widths up to 8192 in multiples of 128; use {\"decode\": \"layered\"}");
   float* dtrace = nullptr;
   if (trace) {
     size_t need = (size_t)(steps + 1) * cfg_.vocab;
@@ -943,7 +1213,8 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
   // TRIT_PHASE_TRACE=1: stamp every phase of block 0 and print the mean time
   // of each phase kind to stderr (a measurement aid).
   static const bool trace_phases = getenv("TRIT_PHASE_TRACE") && *getenv("TRIT_PHASE_TRACE") == '1';
-  const int marks = 5 * cfg_.layers + 2;
+  const int per_layer = fast ? 4 : 5;
+  const int marks = per_layer * cfg_.layers + 2;
   long long* dphase = nullptr;
   if (trace_phases) {
     TRIT_CUDA(cudaMallocAsync(&dphase, (size_t)steps * marks * 8, stream_));
@@ -954,7 +1225,7 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
   static const bool trace_events = getenv("TRIT_PHASE_TRACE") && *getenv("TRIT_PHASE_TRACE") == '3';
   long long* devents = nullptr;
   const size_t nev = (size_t)cfg_.layers * kEventSlots * decode_grid_;
-  if (trace_events && steps > 3) {
+  if (trace_events && steps > 3 && !fast) {
     TRIT_CUDA(cudaMallocAsync(&devents, nev * 8, stream_));
     TRIT_CUDA(cudaMemsetAsync(devents, 0, nev * 8, stream_));
   }
@@ -962,7 +1233,7 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
   a.event_step = 2;
   TRIT_CUDA(cudaMemsetAsync(dll_, 0, ll_words_ * 8, stream_));
   TRIT_CUDA(cudaMemsetAsync(dstatus_, 0, 4, stream_));
-  TRIT_CUDA(launch_decode(a, decode_grid_, stream_));
+  TRIT_CUDA(fast ? launch_decode_fast(a, decode_grid_, stream_) : launch_decode(a, decode_grid_, stream_));
   timing_.gpu_launches += 1;
   int status = 0;
   TRIT_CUDA(cudaMemcpyAsync(&status, dstatus_, 4, cudaMemcpyDeviceToHost, stream_));
@@ -974,17 +1245,17 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
     std::vector<long long> t((size_t)steps * marks);
     TRIT_CUDA(cudaMemcpy(t.data(), dphase, t.size() * 8, cudaMemcpyDeviceToHost));
     TRIT_CUDA(cudaFree(dphase));
-    // Stamps per step: start, then per layer the ends of P1 (qkv), P2
-    // (attention), P3 (o), P4 (gate_up), P5 (down, before its hand-off),
-    // then the argmax.
+    // Stamps per step: start, then per layer the end of each phase (exact:
+    // qkv, attention, o, gate_up, down; default: qkv, attention + o,
+    // gate_up, down), then the argmax.
     double sum[7] = {0};
     int n[7] = {0};
     for (int st = 1; st < steps; ++st) {
       const long long* r = t.data() + (size_t)st * marks;
       if (!r[marks - 1]) continue;
       for (int l = 0; l < cfg_.layers; ++l)
-        for (int p = 0; p < 5; ++p) {
-          sum[p] += (double)(r[l * 5 + p + 1] - r[l * 5 + p]);
+        for (int p = 0; p < per_layer; ++p) {
+          sum[p] += (double)(r[l * per_layer + p + 1] - r[l * per_layer + p]);
           n[p]++;
         }
       sum[5] += (double)(r[marks - 1] - r[marks - 2]);
@@ -992,7 +1263,9 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
       sum[6] += (double)(r[marks - 1] - r[0]);
       n[6]++;
     }
-    const char* names[7] = {"qkv", "attention", "o", "gate_up", "down", "table", "step"};
+    const char* exact_names[7] = {"qkv", "attention", "o", "gate_up", "down", "table", "step"};
+    const char* fast_names[7] = {"qkv", "attend+o", "gate_up", "down", "", "table", "step"};
+    const char* const* names = fast ? fast_names : exact_names;
     for (int p = 0; p < 7; ++p)
       if (n[p]) fprintf(stderr, "phase %-9s %8.2f us\n", names[p], sum[p] / n[p] / 1e3);
   }
@@ -1055,14 +1328,34 @@ std::unique_ptr<PrefixState> Lm::prefix(const int* ids, size_t n) {
   p->tokens.assign(ids, ids + n);
   if (n == 0) return p;
   TRIT_CUDA(cudaSetDevice(opt_.device));
-  int* staged = stage_ids(ids, n, nullptr, 0);
-  run_prompt(n, 0, 0, [&](size_t c0, size_t c1) { embed_rows(staged, c0, c1, x_); });
-  size_t pages = (n + opt_.page_tokens - 1) / opt_.page_tokens;
-  p->bytes = pages * page_bytes_;
-  TRIT_CUDA(cudaMalloc(&p->pages, p->bytes));
-  TRIT_CUDA(cudaMemcpyAsync(p->pages, pool_, p->bytes, cudaMemcpyDeviceToDevice, stream_));
-  TRIT_CUDA(cudaStreamSynchronize(stream_));
-  check_tc_status();
+  // Its full pages take kept pages, and the prompt is run straight into
+  // them through slot 0's table row; the partial page after them is run
+  // into slot 0's own page and copied out.
+  const size_t full = n / opt_.page_tokens;
+  if (full > prefix_free_.size())
+    throw Error("the prefix needs " + std::to_string(full) + " KV pages and " + std::to_string(prefix_free_.size()) +
+                " of the kept pages are free (load option prefix_pages)");
+  for (size_t i = 0; i < full; ++i) {
+    p->pages.push_back(prefix_free_.back());
+    prefix_free_.pop_back();
+  }
+  p->owner = this;
+  prefixes_.insert(p.get());
+  try {
+    int* staged = stage_ids(ids, n, nullptr, 0);
+    map_slot(0, p.get());
+    run_prompt(n, 0, 0, [&](size_t c0, size_t c1) { embed_rows(staged, c0, c1, x_); });
+    if (n % opt_.page_tokens) {
+      TRIT_CUDA(cudaMalloc(&p->partial, page_bytes_));
+      const char* own = (const char*)pool_ + full * page_bytes_;  // slot 0, logical page `full`
+      TRIT_CUDA(cudaMemcpyAsync(p->partial, own, page_bytes_, cudaMemcpyDeviceToDevice, stream_));
+    }
+    TRIT_CUDA(cudaStreamSynchronize(stream_));
+    check_tc_status();
+  } catch (...) {
+    release_prefix(p.get());  // under the caller's lock already
+    throw;
+  }
   return p;
 }
 
@@ -1075,7 +1368,7 @@ std::unique_ptr<PrefixState> Lm::prefix(const int* ids, size_t n) {
 // positions from device buffers that a small kernel advances. Every stream
 // runs max_new steps; the host cuts each at its first stop token.
 void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens, int max_new, const int* stop,
-                        size_t nstop, int* out, int64_t* counts) {
+                        size_t nstop, int* out, int64_t* counts, const PrefixState* prefix) {
   if (S == 0) return;
   if (S > (size_t)opt_.max_streams)
     throw Error(std::to_string(S) + " streams exceed max_streams " + std::to_string(opt_.max_streams));
@@ -1111,11 +1404,20 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
     batch_graph_ = nullptr;
   }
   TRIT_CUDA(cudaEventRecord(ev_[0], stream_));
+  // A stream whose prompt starts with the prefix (and is longer) points its
+  // first pages at the prefix's and starts its prompt after it.
+  std::vector<size_t> start(S, 0);
+  const size_t plen = prefix ? prefix->tokens.size() : 0;
+  for (size_t q = 0; q < S; ++q) {
+    const bool use = prefix && lens[q] > plen && std::equal(prefix->tokens.begin(), prefix->tokens.end(), prompts[q]);
+    map_slot((int)q, use ? prefix : nullptr);
+    start[q] = use ? plen : 0;
+  }
   // Prefill: rows of every stream in order, rows_cap_ at a time.
   int* hs = batch_host_;
   int* hp = batch_host_ + rows_cap_;
   int* hi = batch_host_ + 2 * rows_cap_;
-  size_t s = 0, p = 0;
+  size_t s = 0, p = start[0];
   while (s < S) {
     TRIT_CUDA(cudaStreamSynchronize(stream_));  // the pinned staging is reused per chunk
     int mc = 0, top = 0;
@@ -1128,7 +1430,7 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
       if (++p == lens[s]) {
         ends.emplace_back(mc, (int)s);
         ++s;
-        p = 0;
+        p = s < S ? start[s] : 0;
       }
       ++mc;
     }

@@ -8,6 +8,7 @@
 #include <functional>
 #include <memory>
 #include <mutex>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -23,6 +24,7 @@ struct Options {
   int max_streams = 1;           // stream slots for generate_batch
   int page_tokens = 64;          // positions per KV page
   int prefill_rows = 512;        // rows per prefill pass
+  int prefix_pages = -1;         // KV pages kept for prefixes (-1: one stream's worth)
   std::string decode = "persistent";  // "persistent" (one kernel per generation) or "layered"
   bool tensor_cores = true;      // tcgen05 products for prefill and batches of >= tc_rows rows
   int tc_rows = 64;
@@ -31,6 +33,10 @@ struct Options {
   // sums (tree reductions, split attention) within the north-star
   // tolerance, which is faster.
   bool exact = false;
+  // Keep the weights' device layout in a cache file and read it on later
+  // loads (cache_dir, default <model folder>/.trit_cuda).
+  bool weight_cache = false;
+  std::string cache_dir;
   std::string config_at;         // key path of the settings in config.json (from_tensors' config_at)
   std::string prefix;            // start of every tensor name (from_tensors' prefix)
   // `lenient`: keys other than config_at and prefix are skipped unchecked.
@@ -42,12 +48,18 @@ struct CudaCheck {
 };
 #define TRIT_CUDA(x) ::trit::CudaCheck::ok((x), #x)
 
-// The KV snapshot of a prompt start that many calls share (Prefix,
-// causal_lm.rs:118-122,202-215): its tokens and a device copy of its pages.
+class Lm;
+
+// A prompt start that many calls share (Prefix, causal_lm.rs:118-122,
+// 202-215): its tokens, the physical KV pages that hold its full pages
+// (read-only once made; a stream's page table points at them), and a device
+// copy of the page after them when the prefix ends inside a page (copied
+// into the stream's own page on use, since the stream appends there).
 struct PrefixState {
   std::vector<int> tokens;
-  void* pages = nullptr;
-  size_t bytes = 0;
+  std::vector<int> pages;
+  void* partial = nullptr;
+  Lm* owner = nullptr;  // gets the pages back; null once the model is gone
   ~PrefixState();
 };
 
@@ -80,6 +92,8 @@ class Lm {
   const Options& options() const { return opt_; }
   std::mutex& mutex() { return mu_; }
   const Timing& timing() const { return timing_; }
+  // What the load did, as JSON text (trit_lm_status).
+  std::string status() const;
 
   // CausalLm::generate with an optional prefix; `logits` (host, may be
   // null) receives the logits of every kept or stopping token, [max_new][vocab].
@@ -88,9 +102,12 @@ class Lm {
   // CausalLm::generate_rows: the prompt as embeddings [nrows][d].
   std::vector<int> generate_rows(const float* rows, size_t nrows, int max_new, const int* stop, size_t nstop,
                                  float* logits);
-  // CausalLm::answer: head ids, audio rows, tail ids.
+  // CausalLm::answer: head ids, audio rows, tail ids. `audio_stream`
+  // non-null: the rows are device memory of this model's GPU, written by
+  // work queued on that stream (the rows never pass through the host).
   std::vector<int> answer(const int* head, size_t nhead, const float* audio, size_t naudio, const int* tail,
-                          size_t ntail, int max_new, const int* stop, size_t nstop, float* logits);
+                          size_t ntail, int max_new, const int* stop, size_t nstop, float* logits,
+                          cudaStream_t audio_stream = nullptr, bool audio_on_device = false);
   void embed(const int* ids, size_t n, float* out);
   std::unique_ptr<PrefixState> prefix(const int* ids, size_t n);
   // CausalLm::set_ffn_scales: [layers][d] host floats, or null to clear.
@@ -101,13 +118,28 @@ class Lm {
   // CausalLm::bidirectional_tokens: rows [m][d] without the causal mask.
   std::vector<int> bidirectional_tokens(const float* rows, size_t m, size_t from);
   // Independent streams, each with its own prompt: out [streams][max_new].
+  // A stream whose prompt starts with `prefix` (and is longer) reads the
+  // prefix's pages instead of recomputing them.
   void generate_batch(size_t streams, const int* const* prompts, const size_t* lens, int max_new, const int* stop,
-                      size_t nstop, int* out, int64_t* counts);
+                      size_t nstop, int* out, int64_t* counts, const PrefixState* prefix = nullptr);
+  // Prefix pages in use and in all.
+  int prefix_pages_used() const { return prefix_pages_total_ - (int)prefix_free_.size(); }
+  int prefix_pages_total() const { return prefix_pages_total_; }
+  // A prefix goes: its pages return to the free list (under mutex()).
+  void release_prefix(PrefixState* p);
 
  private:
   void load(const std::string& dir);
+  std::string weight_cache_identity(const ModelSource& src) const;
+  std::string weight_cache_path(const std::string& dir, const ModelSource& src) const;
+  bool read_weight_cache(const std::string& path, void* arena, size_t bytes, cudaStream_t s);
+  void write_weight_cache(const std::string& path, const void* arena, size_t bytes, cudaStream_t s);
   void release();
   void alloc_buffers();
+  // Points the page table row of `slot` at its own pages, or, with a
+  // prefix, its first pages at the prefix's pages (and copies the prefix's
+  // partial page into the slot's own page).
+  void map_slot(int slot, const PrefixState* prefix);
   void check_ids(const int* ids, size_t n) const;
   // Runs rows x (device, [m][d]) through every layer at positions
   // first.. of stream `slot`; chunks of prefill_rows.
@@ -130,8 +162,13 @@ class Lm {
   Timing timing_;
   cudaStream_t stream_ = nullptr;
   cudaEvent_t ev_[4] = {};
+  cudaEvent_t ev_rows_ = nullptr;  // the caller's device rows are written (answer on device rows)
 
   // weights
+  std::string source_;          // the files' form (open_model)
+  std::string weights_from_;    // "files" or "cache"
+  std::string cache_file_;      // the weight cache file, or ""
+  std::string cache_identity_;
   void* arena_ = nullptr;
   size_t arena_bytes_ = 0;
   std::vector<DLayer> layers_;
@@ -146,6 +183,10 @@ class Lm {
   void* pool_ = nullptr;
   size_t page_bytes_ = 0;
   int* page_table_ = nullptr;
+  std::vector<int> table_host_;       // the page table as the device holds it
+  std::vector<int> prefix_free_;      // free physical pages kept for prefixes
+  int prefix_pages_total_ = 0;
+  std::set<PrefixState*> prefixes_;   // live prefixes, detached when the model goes
 
   // scratch
   int rows_cap_ = 0;

@@ -5,6 +5,10 @@
 #include <sys/mman.h>
 #include <sys/stat.h>
 #include <unistd.h>
+#include <dirent.h>
+
+#include <algorithm>
+#include <set>
 
 namespace trit {
 
@@ -213,11 +217,12 @@ size_t ggml_size(uint32_t type, uint64_t count) {
       return count / 32 * 34;
     case I8: return count;
     case I32: return count * 4;
-    default: throw Error("GGUF: ggml type " + std::to_string(type) + " is not read (F32, F16, Q8_0, I8, I32 are)");
+    case BF16: return count * 2;
+    default: throw Error("GGUF: ggml type " + std::to_string(type) + " is not read (F32, F16, BF16, Q8_0, I8, I32 are)");
   }
 }
 
-GgufFile::GgufFile(const std::string& path) {
+void TensorFiles::map_file(const std::string& path, const uint8_t** base, size_t* size) {
   int fd = ::open(path.c_str(), O_RDONLY);
   if (fd < 0) throw Error("cannot open " + path);
   struct stat st;
@@ -225,14 +230,25 @@ GgufFile::GgufFile(const std::string& path) {
     ::close(fd);
     throw Error("cannot stat " + path);
   }
-  size_ = (size_t)st.st_size;
-  map_ = size_ ? mmap(nullptr, size_, PROT_READ, MAP_PRIVATE, fd, 0) : MAP_FAILED;
+  const size_t n = (size_t)st.st_size;
+  void* m = n ? mmap(nullptr, n, PROT_READ, MAP_PRIVATE, fd, 0) : MAP_FAILED;
   ::close(fd);
-  if (map_ == MAP_FAILED) {
-    map_ = nullptr;
-    throw Error("cannot map " + path);
-  }
-  const uint8_t* base = (const uint8_t*)map_;
+  if (m == MAP_FAILED) throw Error("cannot map " + path);
+  maps_.emplace_back(m, n);
+  paths_.push_back(path);
+  *base = (const uint8_t*)m;
+  *size = n;
+}
+
+std::unique_ptr<TensorFiles> TensorFiles::gguf(const std::string& path) {
+  std::unique_ptr<TensorFiles> f(new TensorFiles());
+  f->what_ = path.substr(path.find_last_of('/') + 1);
+  const uint8_t* base = nullptr;
+  size_t size_ = 0;
+  f->map_file(path, &base, &size_);
+  auto& strings_ = f->strings_;
+  auto& numbers_ = f->numbers_;
+  auto& tensors_ = f->tensors_;
   size_t at = 0;
   auto need = [&](uint64_t n) {
     if (n > size_ || at > size_ - n) throw Error(path + ": the header runs past the end of the file");
@@ -271,12 +287,25 @@ GgufFile::GgufFile(const std::string& path) {
         throw Error(path + ": an array of arrays in the metadata");
       }
     } else if (type < 13 && scalar[type]) {
-      if (key == "general.alignment" && type == 4) {
-        alignment = u32();
-      } else {
-        need(scalar[type]);
-        at += scalar[type];
+      need(scalar[type]);
+      const uint8_t* v = base + at;
+      double num = 0;
+      switch (type) {
+        case 0: num = v[0]; break;
+        case 1: num = (int8_t)v[0]; break;
+        case 2: { uint16_t x; std::memcpy(&x, v, 2); num = x; break; }
+        case 3: { int16_t x; std::memcpy(&x, v, 2); num = x; break; }
+        case 4: { uint32_t x; std::memcpy(&x, v, 4); num = x; break; }
+        case 5: { int32_t x; std::memcpy(&x, v, 4); num = x; break; }
+        case 6: { float x; std::memcpy(&x, v, 4); num = x; break; }
+        case 7: num = v[0] ? 1 : 0; break;
+        case 10: { uint64_t x; std::memcpy(&x, v, 8); num = (double)x; break; }
+        case 11: { int64_t x; std::memcpy(&x, v, 8); num = (double)x; break; }
+        case 12: { double x; std::memcpy(&x, v, 8); num = x; break; }
       }
+      at += scalar[type];
+      numbers_[key] = num;
+      if (key == "general.alignment" && (type == 4 || type == 10)) alignment = (uint64_t)num;
     } else {
       throw Error(path + ": metadata value type " + std::to_string(type));
     }
@@ -306,92 +335,92 @@ GgufFile::GgufFile(const std::string& path) {
     t.data = base + data + t.offset;
     tensors_[t.name] = t;
   }
+  return f;
 }
 
-GgufFile::~GgufFile() {
-  if (map_) munmap(map_, size_);
+std::unique_ptr<TensorFiles> TensorFiles::safetensors(const std::vector<std::string>& paths) {
+  std::unique_ptr<TensorFiles> f(new TensorFiles());
+  f->what_ = paths.size() == 1 ? paths[0].substr(paths[0].find_last_of('/') + 1) : "the safetensors files";
+  for (const std::string& path : paths) {
+    const uint8_t* base = nullptr;
+    size_t size = 0;
+    f->map_file(path, &base, &size);
+    uint64_t header = 0;
+    if (size < 8) throw Error(path + ": not a safetensors file");
+    std::memcpy(&header, base, 8);
+    if (header > size - 8) throw Error(path + ": the safetensors header runs past the end of the file");
+    const size_t data = 8 + (size_t)header;
+    Json j = Json::parse(std::string((const char*)base + 8, (size_t)header));
+    if (j.kind != Json::Object) throw Error(path + ": the safetensors header is not an object");
+    for (auto& kv : j.fields) {
+      if (kv.first == "__metadata__") continue;
+      const Json& e = kv.second;
+      const std::string dtype = e.string_or("dtype", "");
+      GgufTensor t;
+      t.name = kv.first;
+      if (dtype == "F32") t.type = F32;
+      else if (dtype == "F16") t.type = F16;
+      else if (dtype == "BF16") t.type = BF16;
+      else if (dtype == "I8" || dtype == "U8") t.type = I8;
+      else if (dtype == "I32") t.type = I32;
+      else throw Error(path + ": tensor " + t.name + " has dtype " + dtype + " (F32, F16, BF16, I8, U8, I32 are read)");
+      const Json* shape = e.get("shape");
+      const Json* offs = e.get("data_offsets");
+      if (!shape || shape->kind != Json::Array || !offs || offs->kind != Json::Array || offs->items.size() != 2)
+        throw Error(path + ": tensor " + t.name + " has no shape or data_offsets");
+      // Innermost dimension first, as GGUF lists them.
+      for (size_t i = shape->items.size(); i-- > 0;) t.dims.push_back((uint64_t)shape->items[i].num);
+      const uint64_t b = (uint64_t)offs->items[0].num, en = (uint64_t)offs->items[1].num;
+      t.bytes = ggml_size(t.type, t.count());
+      if (en < b || en - b != t.bytes || en > size - data)
+        throw Error(path + ": tensor " + t.name + " has a byte range that does not fit its shape or the file");
+      t.offset = b;
+      t.data = base + data + b;
+      f->tensors_[t.name] = t;
+    }
+  }
+  return f;
 }
 
-const GgufTensor* GgufFile::find(const std::string& name) const {
+TensorFiles::~TensorFiles() {
+  for (auto& m : maps_) munmap(m.first, m.second);
+}
+
+bool TensorFiles::number(const std::string& key, double* out) const {
+  auto it = numbers_.find(key);
+  if (it == numbers_.end()) return false;
+  *out = it->second;
+  return true;
+}
+
+const GgufTensor* TensorFiles::find(const std::string& name) const {
   auto it = tensors_.find(name);
   return it == tensors_.end() ? nullptr : &it->second;
 }
 
-const GgufTensor& GgufFile::at(const std::string& name) const {
+const GgufTensor& TensorFiles::at(const std::string& name) const {
   const GgufTensor* t = find(name);
-  if (!t) throw Error("model.gguf has no tensor " + name);
+  if (!t) throw Error(what_ + " has no tensor " + name);
   return *t;
 }
 
-GgufWriter::~GgufWriter() {
-  if (file_) std::fclose(file_);
+float bf16_to_f32(uint16_t bits) {
+  uint32_t u = (uint32_t)bits << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
 }
 
-void GgufWriter::add(const std::string& name, uint32_t type, std::vector<uint64_t> dims) {
-  GgufTensor t;
-  t.name = name;
-  t.type = type;
-  t.dims = std::move(dims);
-  t.bytes = ggml_size(type, t.count());
-  infos_.push_back(t);
+void q8_0_quantize_block(const float* v, uint8_t* out) {
+  float max = 0.0f;
+  for (int i = 0; i < 32; ++i) max = std::max(max, std::fabs(v[i]));
+  const float d = max / 127.0f;
+  const float inverse = d != 0.0f ? 1.0f / d : 0.0f;
+  const uint16_t h = f32_to_f16(d);
+  std::memcpy(out, &h, 2);
+  for (int i = 0; i < 32; ++i) out[2 + i] = (uint8_t)(int8_t)std::round(v[i] * inverse);
 }
 
-void GgufWriter::open(const std::string& path) {
-  file_ = std::fopen(path.c_str(), "wb");
-  if (!file_) throw Error("cannot write " + path);
-  auto w = [&](const void* p, size_t n) {
-    if (std::fwrite(p, 1, n, file_) != n) throw Error("write failed: " + path);
-    written_ += n;
-  };
-  auto w32 = [&](uint32_t v) { w(&v, 4); };
-  auto w64 = [&](uint64_t v) { w(&v, 8); };
-  auto ws = [&](const std::string& s) { w64(s.size()); w(s.data(), s.size()); };
-  w("GGUF", 4);
-  w32(3);
-  w64(infos_.size());
-  w64(meta_.size() + 1);
-  ws("general.alignment");
-  w32(4);
-  w32(32);
-  for (auto& m : meta_) {
-    ws(m.first);
-    w32(8);
-    ws(m.second);
-  }
-  uint64_t offset = 0;
-  for (auto& t : infos_) {
-    t.offset = offset;
-    ws(t.name);
-    w32((uint32_t)t.dims.size());
-    for (auto d : t.dims) w64(d);
-    w32(t.type);
-    w64(offset);
-    offset = (offset + t.bytes + 31) / 32 * 32;
-  }
-  static const uint8_t zeros[32] = {0};
-  w(zeros, (32 - written_ % 32) % 32);
-  written_ = 0;
-}
-
-void GgufWriter::put(const void* bytes, size_t size) {
-  if (next_ >= infos_.size() || size != infos_[next_].bytes) throw Error("GGUF writer: tensor size mismatch");
-  static const uint8_t zeros[32] = {0};
-  if (std::fwrite(bytes, 1, size, file_) != size) throw Error("GGUF writer: write failed");
-  written_ += size;
-  size_t pad = (32 - written_ % 32) % 32;
-  if (pad && std::fwrite(zeros, 1, pad, file_) != pad) throw Error("GGUF writer: write failed");
-  written_ += pad;
-  ++next_;
-}
-
-void GgufWriter::close() {
-  if (next_ != infos_.size()) throw Error("GGUF writer: not every tensor was written");
-  if (file_ && std::fclose(file_) != 0) {
-    file_ = nullptr;
-    throw Error("GGUF writer: close failed");
-  }
-  file_ = nullptr;
-}
 
 }  // namespace trit
 
@@ -442,11 +471,188 @@ ModelConfig read_model_config(const std::string& dir, const std::string& at) {
 
 namespace {
 
+bool is_file(const std::string& path) {
+  struct stat st;
+  return ::stat(path.c_str(), &st) == 0 && S_ISREG(st.st_mode);
+}
+
+// The files of `dir` that end in `suffix`, sorted.
+std::vector<std::string> files_ending(const std::string& dir, const std::string& suffix) {
+  std::vector<std::string> out;
+  DIR* d = ::opendir(dir.c_str());
+  if (!d) throw Error("cannot list " + dir);
+  while (dirent* e = ::readdir(d)) {
+    std::string n = e->d_name;
+    if (n.size() > suffix.size() && n.compare(n.size() - suffix.size(), suffix.size(), suffix) == 0 &&
+        is_file(dir + "/" + n))
+      out.push_back(dir + "/" + n);
+  }
+  ::closedir(d);
+  std::sort(out.begin(), out.end());
+  return out;
+}
+
+std::string read_text(const std::string& path) {
+  std::string text;
+  FILE* f = std::fopen(path.c_str(), "rb");
+  if (!f) throw Error("cannot read " + path);
+  char buf[65536];
+  size_t n;
+  while ((n = std::fread(buf, 1, sizeof buf, f)) > 0) text.append(buf, n);
+  std::fclose(f);
+  return text;
+}
+
+// The GGUF architectures whose language model is a CausalLm decoder
+// (src/models/gguf/mod.rs:61-103): the metadata prefix of its settings,
+// its model_type, the tie of its head when the file does not say, and the
+// prefix of its tensors' Hugging Face names (qwen3_asr.rs:58,69;
+// moss.rs:50,64; fun_asr.rs:49,60; canary_qwen.rs:39,50; voxtral.rs:41,54;
+// voxtral_realtime.rs:25,85; granite_speech.rs:32-36,94).
+struct DecoderArch {
+  const char* arch;
+  const char* meta;
+  const char* model_type;
+  bool tie;
+  const char* prefix;
+};
+const DecoderArch kDecoderArchs[] = {
+    {"qwen3_asr", "stt.qwen3_asr.decoder", "qwen3", true, "thinker."},
+    {"moss", "stt.moss.decoder", "qwen3", true, "language_model."},
+    {"funasr_nano", "stt.funasr_nano.decoder", "qwen3", true, "llm."},
+    {"canary_qwen", "stt.canary_qwen.decoder", "qwen3", true, "llm."},
+    {"voxtral", "stt.voxtral.decoder", "mistral", false, "language_model."},
+    {"voxtral_realtime", "stt.voxtral_realtime.decoder", "mistral", true, "language_model."},
+    {"granite_speech", "stt.granite.decoder", "granite", false, "language_model."},
+};
+
+// A transcribe.cpp decoder tensor name (`dec.*`) as the Hugging Face
+// checkpoint names it under `prefix` (language_model_name,
+// src/models/gguf/qwen3_asr.rs:103-136; the untied head, voxtral.rs:50-52),
+// or "" for a tensor of another part (the audio encoder).
+std::string hf_decoder_name(const std::string& name, const std::string& prefix) {
+  auto starts = [&](const std::string& s, const char* p) { return s.compare(0, std::strlen(p), p) == 0; };
+  if (starts(name, "dec.token_embd.")) return prefix + "model.embed_tokens." + name.substr(15);
+  if (starts(name, "dec.output_norm.")) return prefix + "model.norm." + name.substr(16);
+  if (starts(name, "dec.output.")) return prefix + "lm_head." + name.substr(11);
+  std::string rest;
+  if (starts(name, "dec.blocks.")) rest = name.substr(11);
+  else if (starts(name, "dec.layers.")) rest = name.substr(11);  // Fun-ASR files
+  else return "";
+  const size_t dot = rest.find('.');
+  if (dot == std::string::npos) return "";
+  const std::string layer = rest.substr(0, dot), part = rest.substr(dot + 1);
+  // A longer source comes before a shorter one it starts with.
+  static const char* table[][2] = {
+      {"norm_attn.", "input_layernorm."},   {"norm_ffn.", "post_attention_layernorm."},
+      {"attn.q_norm.", "self_attn.q_norm."}, {"attn.k_norm.", "self_attn.k_norm."},
+      {"attn.q.", "self_attn.q_proj."},      {"attn.k.", "self_attn.k_proj."},
+      {"attn.v.", "self_attn.v_proj."},      {"attn.o.", "self_attn.o_proj."},
+      {"ffn.gate.", "mlp.gate_proj."},       {"ffn.up.", "mlp.up_proj."},
+      {"ffn.down.", "mlp.down_proj."},
+  };
+  for (auto& row : table)
+    if (starts(part, row[0])) return prefix + "model.layers." + layer + "." + row[1] + part.substr(std::strlen(row[0]));
+  return "";
+}
+
+// The config.json block of a transcribe.cpp decoder (src/models/gguf/
+// blocks.rs:25-45 `llm`, with Granite's multipliers, granite_speech.rs:33-36).
+std::string decoder_config(const TensorFiles& g, const DecoderArch& a) {
+  auto num = [&](const char* key) {
+    double v;
+    if (!g.number(std::string(a.meta) + "." + key, &v))
+      throw Error(g.what() + ": no " + std::string(a.meta) + "." + key);
+    return v;
+  };
+  auto opt = [&](const char* key, double* v) { return g.number(std::string(a.meta) + "." + key, v); };
+  char buf[1024];
+  double eps = 1e-6, theta = 1e6, tie = a.tie ? 1 : 0;
+  opt("rms_norm_eps", &eps);
+  opt("rope_theta", &theta);
+  opt("tie_word_embeddings", &tie);
+  std::snprintf(buf, sizeof buf,
+                "{\"model_type\": \"%s\", \"hidden_size\": %.0f, \"intermediate_size\": %.0f, "
+                "\"num_hidden_layers\": %.0f, \"num_attention_heads\": %.0f, \"num_key_value_heads\": %.0f, "
+                "\"head_dim\": %.0f, \"vocab_size\": %.0f, \"rms_norm_eps\": %.9g, \"rope_theta\": %.9g, "
+                "\"tie_word_embeddings\": %s",
+                a.model_type, num("hidden_size"), num("intermediate_size"), num("n_layers"), num("n_heads"),
+                num("n_kv_heads"), num("head_dim"), num("vocab_size"), eps, theta, tie != 0 ? "true" : "false");
+  std::string out = buf;
+  for (const char* key : {"embedding_multiplier", "attention_multiplier", "residual_multiplier", "logits_scaling"}) {
+    double v;
+    if (opt(key, &v)) {
+      std::snprintf(buf, sizeof buf, ", \"%s\": %.9g", key, v);
+      out += buf;
+    }
+  }
+  return out + "}";
+}
+
+}  // namespace
+
+ModelSource open_model(const std::string& dir, const std::string& at, const std::string& prefix) {
+  ModelSource src;
+  struct stat st;
+  if (::stat(dir.c_str(), &st) != 0 || !S_ISDIR(st.st_mode))
+    throw Error(dir + " is not a model folder (config.json with model.gguf or .safetensors files, or one .gguf file)");
+  if (is_file(dir + "/config.json")) {
+    src.mc = read_model_config(dir, at);
+    src.prefix = prefix;
+    if (is_file(dir + "/model.gguf")) {
+      src.files = TensorFiles::gguf(dir + "/model.gguf");
+      src.format = "gguf";
+      return src;
+    }
+    std::vector<std::string> shards;
+    if (is_file(dir + "/model.safetensors.index.json")) {
+      Json idx = Json::parse(read_text(dir + "/model.safetensors.index.json"));
+      const Json* map = idx.get("weight_map");
+      if (!map || map->kind != Json::Object) throw Error(dir + "/model.safetensors.index.json has no weight_map");
+      std::set<std::string> files;
+      for (auto& kv : map->fields) files.insert(dir + "/" + kv.second.str);
+      shards.assign(files.begin(), files.end());
+    } else if (is_file(dir + "/model.safetensors")) {
+      shards.push_back(dir + "/model.safetensors");
+    } else {
+      shards = files_ending(dir, ".safetensors");
+    }
+    if (shards.empty()) throw Error(dir + " has config.json but no model.gguf or .safetensors files");
+    src.files = TensorFiles::safetensors(shards);
+    src.format = "safetensors";
+    return src;
+  }
+  std::vector<std::string> ggufs = files_ending(dir, ".gguf");
+  if (ggufs.size() != 1)
+    throw Error(dir + ": no config.json, and " + std::to_string(ggufs.size()) + " .gguf files (one is read alone)");
+  src.files = TensorFiles::gguf(ggufs[0]);
+  auto arch_it = src.files->strings().find("general.architecture");
+  const std::string arch = arch_it == src.files->strings().end() ? "" : arch_it->second;
+  const DecoderArch* a = nullptr;
+  for (auto& row : kDecoderArchs)
+    if (arch == row.arch) a = &row;
+  if (!a) {
+    std::string names;
+    for (auto& row : kDecoderArchs) names += (names.empty() ? "" : ", ") + std::string(row.arch);
+    throw Error(src.files->what() + ": GGUF architecture " + (arch.empty() ? "(none)" : arch) +
+                " has no decoder this library runs (" + names + " do)");
+  }
+  src.mc = parse_model_config(decoder_config(*src.files, *a), "");
+  src.prefix = a->prefix;
+  const std::string pre = a->prefix;
+  src.files->rename([&](const std::string& n) { return hf_decoder_name(n, pre); });
+  src.format = "gguf-transcribe";
+  return src;
+}
+
+namespace {
+
 // The storage of the product `name` (without .weight): its kind and the
-// bytes of its codes and scales as the device holds them.
-std::string product_kind(const GgufFile& g, const std::string& name, uint64_t* bytes) {
+// bytes of its codes and scales as the device holds them. Float weights
+// (safetensors, or F32 / F16 / BF16 in GGUF) are quantized to Q8_0 at load.
+std::string product_kind(const TensorFiles& g, const std::string& name, uint64_t* bytes) {
   const GgufTensor* w = g.find(name + ".weight");
-  if (w && w->type == Q8_0) {
+  if (w && (w->type == Q8_0 || w->type == F32 || w->type == F16 || w->type == BF16)) {
     *bytes = w->count() + w->count() / 32 * 2;
     return "q8_0";
   }
@@ -461,15 +667,17 @@ std::string product_kind(const GgufFile& g, const std::string& name, uint64_t* b
     *bytes = s.count() * 128 / 4 + s.count() * 4;
     return "ternary";
   }
-  throw Error("model.gguf: no Q8_0, int8 or ternary weights for " + name);
+  throw Error(g.what() + ": no Q8_0, float, int8 or ternary weights for " + name);
 }
 
 }  // namespace
 
-std::string describe_model(const std::string& dir, const std::string& at, const std::string& prefix) {
-  ModelConfig m = read_model_config(dir, at);
+std::string describe_model(const std::string& dir, const std::string& at, const std::string& prefix_in) {
+  ModelSource src = open_model(dir, at, prefix_in);
+  const ModelConfig& m = src.mc;
   const DConfig& c = m.cfg;
-  GgufFile g(dir + "/model.gguf");
+  const TensorFiles& g = *src.files;
+  const std::string& prefix = src.prefix;
   std::map<std::string, int> kinds;
   uint64_t layer_bytes = 0, b = 0;
   const char* parts[] = {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
@@ -481,7 +689,7 @@ std::string describe_model(const std::string& dir, const std::string& at, const 
     }
   auto table_kind = [&](const std::string& name, uint64_t* bytes) -> std::string {
     const GgufTensor& t = g.at(name);
-    if (t.type == Q8_0) {
+    if (t.type == Q8_0 || t.type == F32 || t.type == F16 || t.type == BF16) {
       *bytes = t.count() + t.count() / 32 * 2;
       return "q8_0";
     }
@@ -489,7 +697,7 @@ std::string describe_model(const std::string& dir, const std::string& at, const 
       *bytes = t.count() + t.count() / 32 * 4;
       return "int8";
     }
-    throw Error("model.gguf: " + name + " is neither Q8_0 nor int8 with per-32 scales");
+    throw Error(g.what() + ": " + name + " is neither Q8_0, float nor int8 with per-32 scales");
   };
   uint64_t embed_bytes = 0, head_bytes = 0;
   std::string embed = table_kind(prefix + "model.embed_tokens.weight", &embed_bytes);
@@ -507,14 +715,15 @@ std::string describe_model(const std::string& dir, const std::string& at, const 
                 "\"rms_norm_eps\": %.9g, \"rope_theta\": %.9g, \"qk_norm\": %s, \"tie_word_embeddings\": %s, "
                 "\"embedding_multiplier\": %.9g, \"attention_multiplier\": %s, \"residual_multiplier\": %.9g, "
                 "\"logits_scaling\": %.9g, \"products\": \"%s\", \"token_table\": \"%s\", \"output_table\": \"%s\", "
-                "\"separate_head\": %s, \"product_bytes\": %llu, \"output_table_bytes\": %llu}",
+                "\"separate_head\": %s, \"product_bytes\": %llu, \"output_table_bytes\": %llu, "
+                "\"source\": \"%s\", \"tensor_prefix\": \"%s\"}",
                 m.type.c_str(), c.d, c.ffn, c.layers, c.heads, c.kv_heads, c.hd, c.vocab, (double)c.eps,
                 (double)m.rope_base, m.qk_norm ? "true" : "false", m.tied ? "true" : "false",
                 (double)c.embedding_multiplier,
                 q_mult,
                 (double)c.residual_multiplier, (double)c.logits_scaling, weights.c_str(), embed.c_str(),
                 head.c_str(), has_head ? "true" : "false", (unsigned long long)layer_bytes,
-                (unsigned long long)head_bytes);
+                (unsigned long long)head_bytes, src.format.c_str(), prefix.c_str());
   return buf;
 }
 

@@ -46,8 +46,9 @@ struct Json {
 };
 
 // ---------------------------------------------------------------- GGUF ----
-enum GgmlType : uint32_t { F32 = 0, F16 = 1, Q8_0 = 8, I8 = 24, I32 = 26 };
+enum GgmlType : uint32_t { F32 = 0, F16 = 1, Q8_0 = 8, I8 = 24, I32 = 26, BF16 = 30 };
 size_t ggml_size(uint32_t type, uint64_t count);
+float bf16_to_f32(uint16_t bits);
 
 struct GgufTensor {
   std::string name;
@@ -63,41 +64,48 @@ struct GgufTensor {
   }
 };
 
-class GgufFile {
+// The tensors of a model's files, mapped read-only: one GGUF file (ggml's
+// container, src/models/gguf/mod.rs:147-215) or safetensors files (an
+// 8-byte header length, a JSON header of dtype / shape / byte range per
+// tensor, the data; src/cpu/tensors.rs:155-180,263-305). Safetensors dtypes
+// F32, F16, BF16, I8, U8 and I32 are held under the ggml type codes.
+class TensorFiles {
  public:
-  explicit GgufFile(const std::string& path);
-  ~GgufFile();
-  GgufFile(const GgufFile&) = delete;
-  GgufFile& operator=(const GgufFile&) = delete;
+  static std::unique_ptr<TensorFiles> gguf(const std::string& path);
+  static std::unique_ptr<TensorFiles> safetensors(const std::vector<std::string>& paths);
+  ~TensorFiles();
+  TensorFiles(const TensorFiles&) = delete;
+  TensorFiles& operator=(const TensorFiles&) = delete;
   const GgufTensor* find(const std::string& name) const;
   const GgufTensor& at(const std::string& name) const;
+  // GGUF metadata: strings, and every scalar (integers, floats, bools) as a double.
   const std::map<std::string, std::string>& strings() const { return strings_; }
+  bool number(const std::string& key, double* out) const;
+  // Renames every tensor: map(name) is the new name, or "" to drop it.
+  template <class F>
+  void rename(F map) {
+    std::map<std::string, GgufTensor> out;
+    for (auto& kv : tensors_) {
+      std::string to = map(kv.first);
+      if (to.empty()) continue;
+      GgufTensor t = kv.second;
+      t.name = to;
+      out[to] = t;
+    }
+    tensors_.swap(out);
+  }
+  const std::vector<std::string>& paths() const { return paths_; }
+  const std::string& what() const { return what_; }  // "model.gguf", ... for messages
 
  private:
-  void* map_ = nullptr;
-  size_t size_ = 0;
+  TensorFiles() = default;
+  void map_file(const std::string& path, const uint8_t** base, size_t* size);
+  std::vector<std::pair<void*, size_t>> maps_;
+  std::vector<std::string> paths_;
+  std::string what_;
   std::map<std::string, GgufTensor> tensors_;
   std::map<std::string, std::string> strings_;
-};
-
-// Streams a GGUF file: declare every tensor (`add`), then `open` writes the
-// header and the tensor list, then `put` writes each tensor's bytes in the
-// order of the declarations.
-class GgufWriter {
- public:
-  ~GgufWriter();
-  void meta(const std::string& key, const std::string& value) { meta_.emplace_back(key, value); }
-  void add(const std::string& name, uint32_t type, std::vector<uint64_t> dims);
-  void open(const std::string& path);
-  void put(const void* bytes, size_t size);
-  void close();
-
- private:
-  std::vector<std::pair<std::string, std::string>> meta_;
-  std::vector<GgufTensor> infos_;
-  size_t next_ = 0;
-  uint64_t written_ = 0;
-  std::FILE* file_ = nullptr;
+  std::map<std::string, double> numbers_;
 };
 
 // The decoder settings of a model folder's config.json, as Config::parse
@@ -117,6 +125,31 @@ struct ModelConfig {
 // "thinker_config.text_config.").
 ModelConfig parse_model_config(const std::string& json_text, const std::string& at = "");
 ModelConfig read_model_config(const std::string& dir, const std::string& at = "");
+
+// A decoder's settings and tensors from a model folder, in one of three
+// forms:
+//   - config.json (settings under `at`) + model.gguf with Hugging Face
+//     tensor names under `prefix`;
+//   - config.json + safetensors files (model.safetensors, the shards of
+//     model.safetensors.index.json, or every *.safetensors);
+//   - one GGUF file as transcribe.cpp writes it, no config.json: the
+//     settings come from its metadata (stt.<arch>.decoder.*, as
+//     src/models/gguf/blocks.rs:25-45 reads them) and its `dec.*` tensor
+//     names are mapped to Hugging Face names under the family's prefix
+//     (src/models/gguf/qwen3_asr.rs:103-136); `at` and `prefix` are not
+//     used, the file says where its decoder is.
+struct ModelSource {
+  ModelConfig mc;
+  std::unique_ptr<TensorFiles> files;
+  std::string prefix;  // the start of the decoder's tensor names
+  std::string format;  // "gguf", "gguf-transcribe" or "safetensors"
+};
+ModelSource open_model(const std::string& dir, const std::string& at = "", const std::string& prefix = "");
+
+// ggml's quantize_row_q8_0_ref for one block of 32 (Blocks::quantize,
+// src/cpu/gemm.rs:53-76): d = max|x| / 127, codes round(x * (1 / d)) half
+// away from zero, d stored as f16; out = 2 bytes of d, 32 codes.
+void q8_0_quantize_block(const float* v, uint8_t* out);
 
 // A JSON description of a model folder without touching a GPU: its
 // settings, the storage of its products and token tables, and the bytes a

@@ -102,9 +102,12 @@ struct DecodeArgs {
   float* logits;         // optional [steps + 1][vocab] trace (row i + 1 from step i), or null
   unsigned long long* ll;   // [decode_ll_words] {data, tag} words, zeroed before the launch
   int* status;           // 0 ok; nonzero: a wait ran out (see decode.cu)
-  long long* phase_ns;   // optional [steps][5 * layers + 2] globaltimer stamps of block 0, or null
+  long long* phase_ns;   // optional [steps][phases * layers + 2] globaltimer stamps of block 0, or null
+                         // (5 phases a layer in decode.cu, 4 in decode_fast.cu)
   long long* events;     // optional [layers][kEventSlots][grid] per-block stamps of step event_step, or null
   int event_step;
+  int key_tile;          // keys a staged attention tile (decode_fast.cu; set by its launcher)
+  int table_stages;      // token-table rows in flight per warp (decode_fast.cu; set by its launcher)
 };
 
 // Whether the persistent decode takes this model (its product widths).
@@ -113,5 +116,13 @@ cudaError_t launch_decode(const DecodeArgs& a, int grid, cudaStream_t s);
 int decode_grid(int device);
 // LL words of the decode's hand-off buffers.
 size_t decode_ll_words(const DConfig& cfg, int grid);
+
+// The persistent batch-1 decode of the default path (decode_fast.cu): the
+// reference's quantizers and integer products, floating-point sums in tree
+// order, four hand-offs a layer. Whether it takes this model on `grid`
+// blocks, its launch, and the LL words of its hand-off buffers.
+bool decode_fast_supported(const DConfig& cfg, const DTable& table, int grid, int f16);
+cudaError_t launch_decode_fast(const DecodeArgs& a, int grid, cudaStream_t s);
+size_t decode_fast_ll_words(const DConfig& cfg, int grid);
 
 }  // namespace trit

@@ -63,11 +63,21 @@ def library() -> ctypes.CDLL:
                                             ctypes.c_int32, _i32p, _size, _i32p, _size]),
         "trit_lm_answer_traced": (ctypes.c_int64, [ctypes.c_void_p, _i32p, _size, _f32p, _size, _i32p, _size,
                                                    ctypes.c_int32, _i32p, _size, _i32p, _size, _f32p]),
+        "trit_lm_generate_rows_device": (ctypes.c_int64, [ctypes.c_void_p, ctypes.c_void_p, _size, ctypes.c_int32,
+                                                          _i32p, _size, _i32p, _size, ctypes.c_void_p]),
+        "trit_lm_answer_device": (ctypes.c_int64, [ctypes.c_void_p, _i32p, _size, ctypes.c_void_p, _size, _i32p,
+                                                   _size, ctypes.c_int32, _i32p, _size, _i32p, _size,
+                                                   ctypes.c_void_p]),
         "trit_lm_embed": (ctypes.c_int, [ctypes.c_void_p, _i32p, _size, _f32p]),
         "trit_lm_generate_batch": (ctypes.c_int, [ctypes.c_void_p, _size, ctypes.POINTER(_i32p),
                                                   ctypes.POINTER(_size), ctypes.c_int32, _i32p, _size, _i32p,
                                                   _i64p]),
         "trit_lm_last_timing": (ctypes.c_int, [ctypes.c_void_p, _f64p, _f64p, _i64p, _i64p]),
+        "trit_lm_status": (ctypes.c_void_p, [ctypes.c_void_p]),
+        "trit_lm_generate_batch_prefix": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, _size,
+                                                         ctypes.POINTER(_i32p), ctypes.POINTER(_size), ctypes.c_int32,
+                                                         _i32p, _size, _i32p, _i64p]),
+        "trit_lm_prefix_pages": (ctypes.c_int, [ctypes.c_void_p, _i64p, _i64p]),
         "trit_lm_set_ffn_scales": (ctypes.c_int, [ctypes.c_void_p, _f32p, _size, _size]),
         "trit_lm_generate_additive": (ctypes.c_int64, [ctypes.c_void_p, _i32p, _size, _f32p, _size, _i32p, _size,
                                                        _i32p, _size]),
@@ -221,6 +231,31 @@ class CausalLm:
             raise _error()
         return (out[:n].tolist(), logits) if trace else out[:n].tolist()
 
+    def answer_device(self, head: Sequence[int], rows_ptr: int, nrows: int, tail: Sequence[int],
+                      max_new: int = 128, stop: Sequence[int] = (), stream: int | None = None) -> list[int]:
+        """answer with the rows (nrows x width f32) at a device pointer of
+        this model's GPU, read after the work queued on `stream` (a
+        cudaStream_t handle, None: the default stream)."""
+        h, t, st = _ids(head), _ids(tail), _ids(stop)
+        out = np.zeros(max(max_new, 1), dtype=np.int32)
+        n = library().trit_lm_answer_device(self._handle, _ptr(h, _i32p), h.size, rows_ptr, nrows, _ptr(t, _i32p),
+                                            t.size, max_new, _ptr(st, _i32p), st.size, _ptr(out, _i32p), out.size,
+                                            stream)
+        if n < 0:
+            raise _error()
+        return out[:n].tolist()
+
+    def generate_rows_device(self, rows_ptr: int, nrows: int, max_new: int = 128, stop: Sequence[int] = (),
+                             stream: int | None = None) -> list[int]:
+        """generate_rows with the rows at a device pointer (see answer_device)."""
+        st = _ids(stop)
+        out = np.zeros(max(max_new, 1), dtype=np.int32)
+        n = library().trit_lm_generate_rows_device(self._handle, rows_ptr, nrows, max_new, _ptr(st, _i32p), st.size,
+                                                   _ptr(out, _i32p), out.size, stream)
+        if n < 0:
+            raise _error()
+        return out[:n].tolist()
+
     def embed(self, tokens: Sequence[int]) -> np.ndarray:
         """CausalLm::embed (causal_lm.rs:347-355)."""
         ids = _ids(tokens)
@@ -230,16 +265,22 @@ class CausalLm:
         return out
 
     def generate_batch(self, prompts: Sequence[Sequence[int]], max_new: int = 128,
-                       stop: Sequence[int] = ()) -> list[list[int]]:
-        """Independent greedy generations decoded side by side."""
+                       stop: Sequence[int] = (), prefix: Prefix | None = None) -> list[list[int]]:
+        """Independent greedy generations decoded side by side; streams whose
+        prompt starts with `prefix` read its KV pages in place."""
         arrays = [_ids(p) for p in prompts]
         ptrs = (_i32p * len(arrays))(*[a.ctypes.data_as(_i32p) for a in arrays])
         lens = (_size * len(arrays))(*[a.size for a in arrays])
         st = _ids(stop)
         out = np.zeros((len(arrays), max(max_new, 1)), dtype=np.int32)
         counts = np.zeros(len(arrays), dtype=np.int64)
-        rc = library().trit_lm_generate_batch(self._handle, len(arrays), ptrs, lens, max_new, _ptr(st, _i32p),
-                                              st.size, _ptr(out, _i32p), _ptr(counts, _i64p))
+        if prefix is not None:
+            rc = library().trit_lm_generate_batch_prefix(self._handle, prefix._handle, len(arrays), ptrs, lens,
+                                                         max_new, _ptr(st, _i32p), st.size, _ptr(out, _i32p),
+                                                         _ptr(counts, _i64p))
+        else:
+            rc = library().trit_lm_generate_batch(self._handle, len(arrays), ptrs, lens, max_new, _ptr(st, _i32p),
+                                                  st.size, _ptr(out, _i32p), _ptr(counts, _i64p))
         if rc != 0:
             raise _error()
         return [out[s, :counts[s]].tolist() for s in range(len(arrays))]
@@ -273,6 +314,25 @@ class CausalLm:
         if n < 0:
             raise _error()
         return out[:n].tolist()
+
+    def status(self) -> dict:
+        """What the load did (trit_lm_status): the files' form, whether the
+        weight cache supplied the weights, the arena size, the settings."""
+        lib = library()
+        ptr = lib.trit_lm_status(self._handle)
+        if not ptr:
+            raise _error()
+        try:
+            return json.loads(ctypes.string_at(ptr).decode())
+        finally:
+            lib.trit_cuda_free_text(ptr)
+
+    def prefix_pages(self) -> tuple[int, int]:
+        """KV pages kept for prefixes: (in use, in all)."""
+        used, total = ctypes.c_int64(), ctypes.c_int64()
+        if library().trit_lm_prefix_pages(self._handle, ctypes.byref(used), ctypes.byref(total)) != 0:
+            raise _error()
+        return used.value, total.value
 
     def last_timing(self) -> dict:
         """Device time of the last generation (CUDA events)."""
