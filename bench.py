@@ -367,7 +367,7 @@ def workload(args) -> dict:
 
 def run_decode(args, r: dp.Rank) -> None:
     w = workload(args)
-    fields, model_dir = measure(w, args, r, args.steps, args.warmup, args.decode, args.exact)
+    fields, model_dir = measure(w, args, r, args.steps, args.warmup, args.decode, not args.tree)
     line = {**fields, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8 x int8 -> i32, f32",
             "data": "synthetic (seeded N(0,0.02) weights, uniform random prompt ids"
@@ -376,7 +376,7 @@ def run_decode(args, r: dp.Rank) -> None:
         # The batch-64 half of the metric in the same run (and so in the
         # driver's 1/2/4/8-GPU scaling run): C5, 64 streams per GPU.
         b, _ = measure(dict(WORKLOADS["c5"], key="c5"), args, r, BATCH64_STEPS, BATCH64_WARMUP, "persistent",
-                       args.exact)
+                       not args.tree)
         b["note"] = (f"C5 workload measured in the same run as the headline line: {BATCH64_WARMUP} warm-up and "
                      f"{BATCH64_STEPS} timed generations (fewer than the headline's, to bound the run)")
         line["batch64"] = b
@@ -523,8 +523,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c1", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--decode", default=os.environ.get("TRIT_DECODE", "persistent"))
-    ap.add_argument("--exact", action="store_true",
-                    help="the exact (reference-order) kernels instead of the default tree-order decode")
+    ap.add_argument("--tree", action="store_true",
+                    help="the tree-order persistent decode (\"exact\": false) instead of the default exact one")
     ap.add_argument("--no-batch64", action="store_true", help="leave the C5 batch-64 object out of the C1 line")
     ap.add_argument("--tc-rows", type=int, help="rows from which products use the tensor cores (engine option)")
     ap.add_argument("--prefill-rows", type=int, help="rows a prompt pass (engine option)")

@@ -41,6 +41,7 @@ pub mod ffi {
     #[link(name = "trit_cuda")]
     extern "C" {
         pub fn trit_cuda_version() -> *const c_char;
+        pub fn trit_cuda_tp_id(out: *mut c_char, cap: usize) -> c_int;
         pub fn trit_cuda_last_error() -> *const c_char;
         pub fn trit_lm_inspect(model_dir: *const c_char, options_json: *const c_char) -> *mut c_char;
         pub fn trit_cuda_free_text(text: *mut c_char);

@@ -270,6 +270,12 @@ struct Spec {
   std::string config_at;  // key path the settings are nested under ("a.b.")
   std::string dtype = "f32";  // the float format's element type: f32, f16 or bf16
   std::string names = "hf";   // "hf", or "transcribe": dec.* names under the file's arch
+  // The name a tensor's values are drawn for: its Hugging Face name without
+  // the model's prefix, so one seed gives the same weights under any
+  // prefix and any file form.
+  std::string seed_name(const std::string& hf) const {
+    return hf.compare(0, prefix.size(), prefix) == 0 ? hf.substr(prefix.size()) : hf;
+  }
   // The transcribe.cpp name of a Hugging Face tensor name (its inverse is
   // hf_decoder_name in the product's host.cpp).
   std::string out_name(const std::string& hf) const {
@@ -321,7 +327,7 @@ void write_matrix(Writer* w, const Spec& s, const std::string& hf, size_t n, siz
   if (s.format == "float") {
     if (declare) return w->add(name, float_type(s), {k, n});
     std::vector<float> all(n * k);
-    parallel_rows(n, [&](size_t r) { normal_row(s.seed, hf, r, k, s.sd, all.data() + r * k); });
+    parallel_rows(n, [&](size_t r) { normal_row(s.seed, s.seed_name(hf), r, k, s.sd, all.data() + r * k); });
     return put_float_rows(w, s, all);
   }
   if (s.format == "q8_0") {
@@ -330,7 +336,7 @@ void write_matrix(Writer* w, const Spec& s, const std::string& hf, size_t n, siz
     std::vector<uint8_t> bytes(n * (k / 32) * 34);
     parallel_rows(n, [&](size_t r) {
       std::vector<float> row(k);
-      normal_row(s.seed, hf, r, k, s.sd, row.data());
+      normal_row(s.seed, s.seed_name(hf), r, k, s.sd, row.data());
       for (size_t b = 0; b < k / 32; ++b) q8_0_block(row.data() + b * 32, bytes.data() + (r * (k / 32) + b) * 34);
     });
     w->put(bytes.data(), bytes.size());
@@ -344,7 +350,7 @@ void write_matrix(Writer* w, const Spec& s, const std::string& hf, size_t n, siz
     std::vector<float> scales(n);
     parallel_rows(n, [&](size_t r) {
       std::vector<float> row(k);
-      normal_row(s.seed, hf, r, k, s.sd, row.data());
+      normal_row(s.seed, s.seed_name(hf), r, k, s.sd, row.data());
       float max = 0.0f;
       for (float v : row) max = std::max(max, std::fabs(v));
       scales[r] = row_scale(max);
@@ -364,12 +370,12 @@ void write_matrix(Writer* w, const Spec& s, const std::string& hf, size_t n, siz
     std::vector<float> scales(n * (k / 128));
     parallel_rows(n, [&](size_t r) {
       std::vector<float> row(k);
-      normal_row(s.seed, hf, r, k, s.sd, row.data());
+      normal_row(s.seed, s.seed_name(hf), r, k, s.sd, row.data());
       double sum = 0;
       for (float v : row) sum += std::fabs(v);
       float absmean = (float)(sum / (double)k);
       for (size_t g = 0; g < k / 128; ++g) scales[r * (k / 128) + g] = absmean;
-      Xorshift codes = stream(s.seed, hf + ".codes", r);
+      Xorshift codes = stream(s.seed, s.seed_name(hf) + ".codes", r);
       uint8_t* dst = packed.data() + r * row_bytes;
       for (size_t b = 0; b < row_bytes; ++b) {
         unsigned byte = 0, place = 1;
@@ -407,7 +413,7 @@ void write_table(Writer* w, const Spec& s, const std::string& hf, size_t n, size
     std::vector<float> scales(n * (k / 32));
     parallel_rows(n, [&](size_t r) {
       std::vector<float> row(k);
-      normal_row(s.seed, hf, r, k, s.sd, row.data());
+      normal_row(s.seed, s.seed_name(hf), r, k, s.sd, row.data());
       for (size_t g = 0; g < k / 32; ++g) {
         float max = 0.0f;
         for (int i = 0; i < 32; ++i) max = std::max(max, std::fabs(row[g * 32 + i]));

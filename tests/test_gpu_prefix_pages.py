@@ -17,7 +17,7 @@ pytestmark = pytest.mark.gpu
 def test_prefix_pages_are_shared_not_copied(mini_models, exact):
     torch = pytest.importorskip("torch")
     path = mini_models["mini_qwen3_q8_0"]
-    oracle = O.Oracle(path)
+    oracle = O.Oracle(path, kv_f16=True)
     rng = np.random.default_rng(23)
     system = rng.integers(0, oracle.vocab, size=40).tolist()  # 2 full pages of 16 and a partial one
     prompts = [system + rng.integers(0, oracle.vocab, size=n).tolist() for n in (5, 9, 14)]

@@ -10,6 +10,7 @@
 
 #include "../../include/trit_cuda.h"
 #include "engine.h"
+#include "nccl_link.h"
 
 struct TritLm {
   std::unique_ptr<trit::Lm> lm;
@@ -69,7 +70,7 @@ char* trit_lm_inspect(const char* model_dir, const char* options_json) {
   return guard<char*>(nullptr, [&]() {
     need(model_dir, "model_dir");
     trit::Options o = trit::Options::parse(options_json, true);
-    std::string text = trit::describe_model(model_dir, o.config_at, o.prefix);
+    std::string text = trit::describe_model(model_dir, o.config_at, o.prefix, o.tp_rank, o.tp_size);
     char* out = (char*)std::malloc(text.size() + 1);
     if (!out) throw trit::Error("out of host memory");
     std::memcpy(out, text.c_str(), text.size() + 1);
@@ -78,6 +79,22 @@ char* trit_lm_inspect(const char* model_dir, const char* options_json) {
 }
 
 void trit_cuda_free_text(char* text) { std::free(text); }
+
+int trit_cuda_tp_id(char* out, size_t cap) {
+  return guard<int>(-1, [&]() {
+    need(out, "out");
+    ncclUniqueId id;
+    trit::nccl_check(trit::nccl().GetUniqueId(&id), "unique id");
+    if (cap < 2 * sizeof id + 1) throw trit::Error("out holds fewer than 257 bytes");
+    static const char hex[] = "0123456789abcdef";
+    for (size_t i = 0; i < sizeof id; ++i) {
+      out[2 * i] = hex[(uint8_t)id.internal[i] >> 4];
+      out[2 * i + 1] = hex[(uint8_t)id.internal[i] & 15];
+    }
+    out[2 * sizeof id] = '\0';
+    return 0;
+  });
+}
 
 char* trit_lm_status(const TritLm* lm) {
   return guard<char*>(nullptr, [&]() {

@@ -757,6 +757,12 @@ __global__ void __launch_bounds__(FT, 1) k_decode_fast(DecodeArgs a) {
     if (a.phase_ns && c == 0 && t == 0) a.phase_ns[mark_at] = gtimer();
     ++mark_at;
   };
+  // Optional per-block stamps of one step (TRIT_PHASE_TRACE=3): [layer][kEventSlots][grid].
+  int cur_step = -1, cur_layer = 0;
+  auto ev = [&](int k) {
+    if (a.events && cur_step == a.event_step && t == 0)
+      a.events[((size_t)cur_layer * kEventSlots + k) * G + c] = gtimer();
+  };
   auto stage_vec = [&](float* dst, const float* src, int n) {
     for (int i = 4 * t; i < n; i += 4 * FT) cp_async16(dst + i, src + i);
   };
@@ -772,6 +778,7 @@ __global__ void __launch_bounds__(FT, 1) k_decode_fast(DecodeArgs a) {
     // visible from here on.
     __threadfence();
     const int pos = a.first_pos + i;
+    cur_step = i;
     const uint32_t base = (uint32_t)i * (uint32_t)(4 * L + 2) + 1;
     mark_at = i * (4 * L + 2);
     mark();
@@ -783,6 +790,8 @@ __global__ void __launch_bounds__(FT, 1) k_decode_fast(DecodeArgs a) {
       S.x[kk] = v;
     }
     for (int l = 0; l < L; ++l) {
+      cur_layer = l;
+      ev(0);
       const DLayer& Lw = a.layers[l];
       const uint32_t t_qkv = base + 4 * l, t_att = t_qkv + 1, t_h = t_qkv + 2, t_xb = t_qkv + 3;
       // P1: qkv. Input: x (the embedding, or xb of the layer before).
@@ -792,6 +801,7 @@ __global__ void __launch_bounds__(FT, 1) k_decode_fast(DecodeArgs a) {
         if (l > 0 && !ll_take(d, t_qkv - 1, a.status, [&](int k) { return a.ll + ll.xb + k; },
                               [&](int k, uint32_t v) { S.x[k] = __uint_as_float(v); }))
           return false;
+        ev(1);
         // The thread's own words (the embedding's, or those it took).
         float ss = 0.0f;
         for (int kk = t; kk < d; kk += FT) ss += S.x[kk] * S.x[kk];
@@ -799,10 +809,13 @@ __global__ void __launch_bounds__(FT, 1) k_decode_fast(DecodeArgs a) {
         const float inv = rms_inv(block_sum(ss, S), d, cfg.eps);
         quant_fast(S.x, d, S.nw, nullptr, inv, Lw.qkv.agroup, Lw.qkv.half, S.xq, S.xs);
         __syncthreads();
+        ev(2);
         return true;
       });
       if (!ok) return;
+      ev(3);
       for (int lr = t; lr < q1 - q0; lr += FT) ll_put(a.ll + ll.qkv + q0 + lr, __float_as_uint(S.out[lr]), t_qkv);
+      ev(4);
       mark();
       // P2: attention of kv head g, then o_proj over the group's columns.
       const int n0 = min(KT, pos + 1);
@@ -817,17 +830,22 @@ __global__ void __launch_bounds__(FT, 1) k_decode_fast(DecodeArgs a) {
                      },
                      [&](int k, uint32_t v) { raw[k] = __uint_as_float(v); }))
           return false;
+        ev(5);
         cp_wait<1>();
         __syncthreads();
         attend_fast(a, Lw, l, pos, g, appender, KT, att);
+        ev(6);
         const float* o = (const float*)(att + AL.oacc);
         quant_fast(o, P, nullptr, nullptr, 1.0f, Lw.out.agroup, Lw.out.half, S.xq + col0, S.xs + col0 / Lw.out.agroup);
         __syncthreads();
+        ev(7);
         return true;
       });
       if (!ok) return;
+      ev(8);
       for (int lr = t; lr < o1 - o0; lr += FT)
         ll_put(a.ll + ll.opart + g * d + o0 + lr, __float_as_uint(S.out[lr]), t_att);
+      ev(9);
       mark();
       // P4: x += o (the group partials in group order), gate_up, silu * up.
       stage_vec(S.nw, Lw.norm_mlp, d);
@@ -839,6 +857,7 @@ __global__ void __launch_bounds__(FT, 1) k_decode_fast(DecodeArgs a) {
         if (!ll_take<16>(KV * d, t_att, a.status, [&](int k) { return a.ll + ll.opart + k; },
                      [&](int k, uint32_t v) { gpart[k] = __uint_as_float(v); }))
           return false;
+        ev(10);
         float ss = 0.0f;
         for (int r = t; r < d; r += FT) {
           float o = 0.0f;
@@ -853,28 +872,35 @@ __global__ void __launch_bounds__(FT, 1) k_decode_fast(DecodeArgs a) {
         quant_fast(S.x, d, S.nw, Lw.ffn_scale ? S.fsc : nullptr, inv, Lw.gate_up.agroup, Lw.gate_up.half, S.xq,
                    S.xs);
         __syncthreads();
+        ev(11);
         return true;
       });
       if (!ok) return;
+      ev(12);
       for (int lr = t; lr < nu; lr += FT)
         ll_put(a.ll + ll.h + u0 + lr, __float_as_uint(__fmul_rn(silu(S.out[lr]), S.out[nu + lr])), t_h);
+      ev(13);
       mark();
       // P5: down + residual. Input: h.
       ok = gemv_fast(Lw.down, 0, cfg.ffn, nown, [&](int lr) { return r0 + lr; }, S, [&]() {
         if (!ll_take(cfg.ffn, t_h, a.status, [&](int k) { return a.ll + ll.h + k; },
                      [&](int k, uint32_t v) { S.xf[k] = __uint_as_float(v); }))
           return false;
+        ev(14);
         quant_fast(S.xf, cfg.ffn, nullptr, nullptr, 1.0f, Lw.down.agroup, Lw.down.half, S.xq, S.xs);
         __syncthreads();
+        ev(15);
         return true;
       });
       if (!ok) return;
+      ev(16);
       for (int lr = t; lr < nown; lr += FT) {
         const float o = S.out[lr];
         const float xv = (cfg.residual_multiplier == 1.0f) ? __fadd_rn(S.x[r0 + lr], o)
                                                            : __fadd_rn(S.x[r0 + lr], __fmul_rn(cfg.residual_multiplier, o));
         ll_put(a.ll + ll.xb + r0 + lr, __float_as_uint(xv), t_xb);
       }
+      ev(17);
       mark();
     }
     // The final RmsNorm (f32, no quantization), the table slice, the argmax.
@@ -885,15 +911,18 @@ __global__ void __launch_bounds__(FT, 1) k_decode_fast(DecodeArgs a) {
       if (!ll_take(d, t_final, a.status, [&](int k) { return a.ll + ll.xb + k; },
                    [&](int k, uint32_t v) { S.x[k] = __uint_as_float(v); }))
         return false;
+      ev(18);
       float ss = 0.0f;
       for (int kk = t; kk < d; kk += FT) ss += S.x[kk] * S.x[kk];
       cp_wait_n(a.table_stages - 1);  // the final norm's weights (the table stages may still travel)
       const float inv = rms_inv(block_sum(ss, S), d, cfg.eps);
       for (int kk = t; kk < d; kk += FT) S.xf[kk + (kk >> 4) * 4] = __fmul_rn(S.x[kk], __fmul_rn(inv, S.nw[kk]));
       __syncthreads();
+      ev(19);
       return true;
     });
     if (!ok) return;
+    ev(20);
     if (t == 0) {
       ll_put(a.ll + ll.best + 2 * c, (uint32_t)S.flag[4], t_best);
       ll_put(a.ll + ll.best + 2 * c + 1, (uint32_t)S.flag[5], t_best);
@@ -905,6 +934,7 @@ __global__ void __launch_bounds__(FT, 1) k_decode_fast(DecodeArgs a) {
       else bvals[k >> 1] = __uint_as_float(v);
     });
     if (!ok) return;
+    ev(21);
     mark();
     if (t < 32) {
       float b = -INFINITY;

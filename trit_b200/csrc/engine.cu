@@ -1,6 +1,7 @@
 // Loading a decoder into device memory and running CausalLm's generation
 // flows (src/models/parts/causal_lm.rs:141-302) on one GPU.
 #include "engine.h"
+#include "nccl_link.h"
 
 #include <sys/stat.h>
 #include <unistd.h>
@@ -27,7 +28,7 @@ Options Options::parse(const char* text, bool lenient) {
   for (auto& f : j.fields) {
     const std::string& k = f.first;
     const Json& v = f.second;
-    if (lenient && k != "config_at" && k != "prefix") continue;
+    if (lenient && k != "config_at" && k != "prefix" && k != "tp_size" && k != "tp_rank") continue;
     auto count = [&](int lo, int hi) {
       if (v.kind != Json::Number || v.num != std::floor(v.num) || v.num < lo || v.num > hi)
         throw Error("options: " + k + " must be a whole number from " + std::to_string(lo) + " to " + std::to_string(hi));
@@ -51,6 +52,13 @@ Options Options::parse(const char* text, bool lenient) {
       o.tensor_cores = v.b;
     } else if (k == "tc_rows") {
       o.tc_rows = count(1, 1 << 20);
+    } else if (k == "tp_size") {
+      o.tp_size = count(1, 64);
+    } else if (k == "tp_rank") {
+      o.tp_rank = count(0, 63);
+    } else if (k == "tp_id") {
+      if (v.kind != Json::String) throw Error("options: tp_id must be a string");
+      o.tp_id = v.str;
     } else if (k == "weight_cache") {
       if (v.kind != Json::Bool) throw Error("options: weight_cache is true or false");
       o.weight_cache = v.b;
@@ -141,19 +149,6 @@ std::vector<float> f32_of(const TensorFiles& g, const std::string& name, size_t 
 
 bool is_float(uint32_t type) { return type == F32 || type == F16 || type == BF16; }
 
-// Q8_0 blocks of a float tensor of rows x k, quantized as ggml quantizes
-// (Tensors::q8_0 -> Blocks::quantize, src/cpu/tensors.rs:282-305,
-// src/cpu/gemm.rs:53-76), into split codes and f16 scale planes.
-void quantize_rows_q8_0(const TensorFiles& g, const std::string& name, size_t rows, size_t k, uint8_t* codes,
-                        uint8_t* scales) {
-  std::vector<float> v = f32_of(g, name, rows * k);
-  uint8_t blk[34];
-  for (size_t b = 0; b < rows * k / 32; ++b) {
-    q8_0_quantize_block(v.data() + b * 32, blk);
-    std::memcpy(scales + b * 2, blk, 2);
-    std::memcpy(codes + b * 32, blk + 2, 32);
-  }
-}
 
 const float* load_vector(const TensorFiles& g, Arena& A, const std::string& name, size_t len) {
   size_t at = A.take(len * 4);
@@ -164,16 +159,26 @@ const float* load_vector(const TensorFiles& g, Arena& A, const std::string& name
   return (const float*)A.ptr(at);
 }
 
+// One source matrix's rows [row0, row0 + rows) in a stacked product.
+struct Part {
+  std::string name;
+  int row0, rows;
+};
+
 // Dense::load (src/cpu/gemm.rs:254-343) of parts stacked by output rows,
 // in the device layout: Q8_0 blocks split into a codes plane and an f16
-// scale plane (34-byte blocks are not 16-byte aligned); per-row int8 codes
-// and row scales; ternary base-3 bytes (src/cpu/kernels.rs:91-130) repacked
-// 16 codes a word in the pack_span order (kernels.rs:618-628).
-DMat load_mat(const TensorFiles& g, Arena& A, const std::vector<std::pair<std::string, int>>& parts, int k) {
+// scale plane (34-byte blocks are not 16-byte aligned; float weights are
+// quantized to Q8_0 first); per-row int8 codes and row scales; ternary
+// base-3 bytes (src/cpu/kernels.rs:91-130) repacked 16 codes a word in the
+// pack_span order (kernels.rs:618-628). Of each source row of kfull inputs
+// the columns [c0, c0 + k) are kept (a tensor-parallel shard of the inputs;
+// c0 and k are whole activation groups, so every group stays whole).
+DMat load_mat(const TensorFiles& g, Arena& A, const std::vector<Part>& parts, int k, int c0 = 0, int kfull = 0) {
+  if (!kfull) kfull = k;
   DMat m;
   m.k = k;
-  for (auto& p : parts) m.n += p.second;
-  const std::string& first = parts[0].first;
+  for (auto& p : parts) m.n += p.rows;
+  const std::string& first = parts[0].name;
   const GgufTensor* w = g.find(first + ".weight");
   if (w && (w->type == Q8_0 || is_float(w->type))) {
     m.kind = kQ8_0;  // float weights are quantized to Q8_0 here
@@ -188,7 +193,8 @@ DMat load_mat(const TensorFiles& g, Arena& A, const std::vector<std::pair<std::s
   } else {
     throw Error(g.what() + ": no Q8_0, float, int8 or ternary weights for " + first);
   }
-  if (k % m.agroup != 0) throw Error(first + ": the input width is not whole groups of " + std::to_string(m.agroup));
+  if (k % m.agroup != 0 || c0 % m.agroup != 0)
+    throw Error(first + ": the input width is not whole groups of " + std::to_string(m.agroup));
   if (m.n % 32 != 0) throw Error(first + ": the output rows are not a multiple of 32");
   size_t codes_bytes = (m.kind == kTernary) ? (size_t)m.n * k / 4 : (size_t)m.n * k;
   size_t scale_bytes = m.kind == kQ8_0 ? (size_t)m.n * (k / 32) * 2 : m.kind == kInt8Row ? (size_t)m.n * 4
@@ -198,53 +204,75 @@ DMat load_mat(const TensorFiles& g, Arena& A, const std::vector<std::pair<std::s
   m.scales = A.ptr(so);
   if (!A.fill) return m;
   std::vector<uint8_t> codes(codes_bytes), scales(scale_bytes);
-  size_t row0 = 0;
+  size_t out = 0;  // rows written so far
   for (auto& p : parts) {
-    size_t rows = (size_t)p.second;
-    if (m.kind == kQ8_0 && is_float(g.at(p.first + ".weight").type)) {
-      quantize_rows_q8_0(g, p.first + ".weight", rows, k, codes.data() + row0 * k, scales.data() + row0 * (k / 32) * 2);
+    const size_t rows = (size_t)p.rows, r0 = (size_t)p.row0;
+    auto source_rows = [&](const GgufTensor& t, size_t per_row) {
+      if (t.count() % per_row || t.count() / per_row < r0 + rows)
+        throw Error("tensor " + t.name + ": expected rows of " + std::to_string(per_row) + " values, " +
+                    std::to_string(r0 + rows) + " at least");
+    };
+    if (m.kind == kQ8_0 && is_float(g.at(p.name + ".weight").type)) {
+      const GgufTensor& t = g.at(p.name + ".weight");
+      source_rows(t, kfull);
+      std::vector<float> v = f32_of(g, p.name + ".weight", t.count());
+      uint8_t blk[34];
+      for (size_t r = 0; r < rows; ++r)
+        for (int b = 0; b < k / 32; ++b) {
+          q8_0_quantize_block(v.data() + (r0 + r) * kfull + c0 + b * 32, blk);
+          std::memcpy(scales.data() + ((out + r) * (k / 32) + b) * 2, blk, 2);
+          std::memcpy(codes.data() + (out + r) * k + b * 32, blk + 2, 32);
+        }
     } else if (m.kind == kQ8_0) {
-      const GgufTensor& t = g.at(p.first + ".weight");
-      if (t.type != Q8_0 || t.count() != rows * k) throw Error("tensor " + p.first + ".weight: expected Q8_0 " + std::to_string(rows) + "x" + std::to_string(k));
-      size_t blocks = rows * k / 32;
-      for (size_t b = 0; b < blocks; ++b) {
-        const uint8_t* blk = t.data + b * 34;
-        std::memcpy(scales.data() + (row0 * (k / 32) + b) * 2, blk, 2);
-        std::memcpy(codes.data() + row0 * k + b * 32, blk + 2, 32);
-      }
+      const GgufTensor& t = g.at(p.name + ".weight");
+      if (t.type != Q8_0) throw Error("tensor " + p.name + ".weight: expected Q8_0");
+      source_rows(t, kfull);
+      for (size_t r = 0; r < rows; ++r)
+        for (int b = 0; b < k / 32; ++b) {
+          const uint8_t* blk = t.data + ((r0 + r) * (kfull / 32) + c0 / 32 + b) * 34;
+          std::memcpy(scales.data() + ((out + r) * (k / 32) + b) * 2, blk, 2);
+          std::memcpy(codes.data() + (out + r) * k + b * 32, blk + 2, 32);
+        }
     } else if (m.kind == kInt8Row) {
-      const GgufTensor& t = g.at(p.first + ".weight");
-      if (t.type != I8 || t.count() != rows * k) throw Error("tensor " + p.first + ".weight: expected I8 " + std::to_string(rows) + "x" + std::to_string(k));
-      std::memcpy(codes.data() + row0 * k, t.data, rows * k);
-      std::vector<float> s = f32_of(g, p.first + ".scales", rows);
-      std::memcpy(scales.data() + row0 * 4, s.data(), rows * 4);
+      const GgufTensor& t = g.at(p.name + ".weight");
+      if (t.type != I8) throw Error("tensor " + p.name + ".weight: expected I8");
+      source_rows(t, kfull);
+      for (size_t r = 0; r < rows; ++r) std::memcpy(codes.data() + (out + r) * k, t.data + (r0 + r) * kfull + c0, k);
+      const GgufTensor& st = g.at(p.name + ".scales");
+      std::vector<float> s = f32_of(g, p.name + ".scales", st.count());
+      if (s.size() < r0 + rows) throw Error("tensor " + p.name + ".scales: too few rows");
+      std::memcpy(scales.data() + out * 4, s.data() + r0, rows * 4);
     } else {
-      const GgufTensor& t = g.at(p.first + ".qweight");
-      size_t row_bytes = ((size_t)k + 4) / 5;
-      if (t.count() != rows * row_bytes) throw Error("tensor " + p.first + ".qweight: expected " + std::to_string(rows) + " rows of " + std::to_string(row_bytes) + " bytes");
-      std::vector<uint8_t> digits(k + 5);
+      const GgufTensor& t = g.at(p.name + ".qweight");
+      const size_t row_bytes = ((size_t)kfull + 4) / 5;
+      source_rows(t, row_bytes);
+      std::vector<uint8_t> digits((size_t)kfull + 5);
       for (size_t r = 0; r < rows; ++r) {
-        const uint8_t* src = t.data + r * row_bytes;
+        const uint8_t* src = t.data + (r0 + r) * row_bytes;
         for (size_t b = 0; b < row_bytes; ++b) {
           unsigned v = src[b];
-          if (v >= 243) throw Error("ternary byte above 242 in row " + std::to_string(row0 + r) + " of " + p.first);
+          if (v >= 243) throw Error("ternary byte above 242 in row " + std::to_string(r0 + r) + " of " + p.name);
           for (int dd = 0; dd < 5; ++dd) {
             digits[b * 5 + dd] = (uint8_t)(v % 3);
             v /= 3;
           }
         }
-        uint32_t* dst = (uint32_t*)(codes.data()) + (row0 + r) * (k / 16);
+        uint32_t* dst = (uint32_t*)(codes.data()) + (out + r) * (k / 16);
         for (int w16 = 0; w16 < k / 16; ++w16) {
           uint32_t word = 0;
-          for (int s = 0; s < 4; ++s)
-            for (int j = 0; j < 4; ++j) word |= (uint32_t)digits[w16 * 16 + 4 * s + j] << (8 * j + 2 * s);
+          for (int s4 = 0; s4 < 4; ++s4)
+            for (int j = 0; j < 4; ++j) word |= (uint32_t)digits[c0 + w16 * 16 + 4 * s4 + j] << (8 * j + 2 * s4);
           dst[w16] = word;
         }
       }
-      std::vector<float> s = f32_of(g, p.first + ".scales", rows * (k / 128));
-      std::memcpy(scales.data() + row0 * (k / 128) * 4, s.data(), s.size() * 4);
+      const GgufTensor& st = g.at(p.name + ".scales");
+      std::vector<float> s = f32_of(g, p.name + ".scales", st.count());
+      const size_t gfull = kfull / 128, gk = k / 128;
+      if (s.size() < (r0 + rows) * gfull) throw Error("tensor " + p.name + ".scales: too few rows");
+      for (size_t r = 0; r < rows; ++r)
+        std::memcpy(scales.data() + ((out + r) * gk) * 4, s.data() + (r0 + r) * gfull + c0 / 128, gk * 4);
     }
-    row0 += rows;
+    out += rows;
   }
   A.put(co, codes.data(), codes_bytes);
   A.put(so, scales.data(), scale_bytes);
@@ -253,36 +281,46 @@ DMat load_mat(const TensorFiles& g, Arena& A, const std::vector<std::pair<std::s
 
 // Dense::table (src/cpu/gemm.rs:383-409): Q8_0 blocks (f16 scales) or int8
 // codes with one f32 scale per 32 values, f32 math.
-DTable load_table(const TensorFiles& g, Arena& A, const std::string& name, int rows, int cols) {
+DTable load_table(const TensorFiles& g, Arena& A, const std::string& name, int rows, int cols, int row0 = 0,
+                  int rows_full = 0) {
+  if (!rows_full) rows_full = rows;
   DTable t;
   t.n = rows;
   t.k = cols;
   if (cols % 32) throw Error(name + ": the width is not whole blocks of 32");
   const GgufTensor& w = g.at(name + ".weight");
-  if (w.count() != (uint64_t)rows * cols) throw Error(name + ".weight has the wrong size");
+  if (w.count() != (uint64_t)rows_full * cols) throw Error(name + ".weight has the wrong size");
   t.scale_f16 = w.type == Q8_0 || is_float(w.type);  // float tables are quantized to Q8_0
   if (!t.scale_f16 && w.type != I8) throw Error(name + ".weight is neither Q8_0, float nor I8");
   size_t co = A.take((size_t)rows * cols), so = A.take((size_t)rows * (cols / 32) * (t.scale_f16 ? 2 : 4));
   t.codes = (const int8_t*)A.ptr(co);
   t.scales = A.ptr(so);
   if (!A.fill) return t;
+  const size_t n = (size_t)rows * cols, first = (size_t)row0 * cols;
   if (is_float(w.type)) {
-    std::vector<uint8_t> codes((size_t)rows * cols), scales((size_t)rows * (cols / 32) * 2);
-    quantize_rows_q8_0(g, name + ".weight", rows, cols, codes.data(), scales.data());
+    std::vector<float> v = f32_of(g, name + ".weight", (size_t)rows_full * cols);
+    std::vector<uint8_t> codes(n), scales(n / 32 * 2);
+    uint8_t blk[34];
+    for (size_t b = 0; b < n / 32; ++b) {
+      q8_0_quantize_block(v.data() + first + b * 32, blk);
+      std::memcpy(scales.data() + b * 2, blk, 2);
+      std::memcpy(codes.data() + b * 32, blk + 2, 32);
+    }
     A.put(co, codes.data(), codes.size());
     A.put(so, scales.data(), scales.size());
   } else if (w.type == Q8_0) {
-    std::vector<uint8_t> codes((size_t)rows * cols), scales((size_t)rows * (cols / 32) * 2);
-    for (size_t b = 0; b < (size_t)rows * cols / 32; ++b) {
-      std::memcpy(scales.data() + b * 2, w.data + b * 34, 2);
-      std::memcpy(codes.data() + b * 32, w.data + b * 34 + 2, 32);
+    std::vector<uint8_t> codes(n), scales(n / 32 * 2);
+    for (size_t b = 0; b < n / 32; ++b) {
+      const uint8_t* blk = w.data + (first / 32 + b) * 34;
+      std::memcpy(scales.data() + b * 2, blk, 2);
+      std::memcpy(codes.data() + b * 32, blk + 2, 32);
     }
     A.put(co, codes.data(), codes.size());
     A.put(so, scales.data(), scales.size());
   } else {
-    A.put(co, w.data, (size_t)rows * cols);
-    std::vector<float> s = f32_of(g, name + ".scales", (size_t)rows * (cols / 32));
-    A.put(so, s.data(), s.size() * 4);
+    A.put(co, w.data + first, n);
+    std::vector<float> s = f32_of(g, name + ".scales", (size_t)rows_full * (cols / 32));
+    A.put(so, s.data() + first / 32, n / 32 * 4);
   }
   return t;
 }
@@ -297,6 +335,16 @@ Lm::Lm(const std::string& dir, const Options& o) : opt_(o) {
   TRIT_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
   for (auto& e : ev_) TRIT_CUDA(cudaEventCreate(&e));
   try {
+    if (opt_.tp_size > 1) {
+      // The ranks' communicator, from the unique id rank 0 made.
+      if (opt_.tp_id.size() != 2 * sizeof(ncclUniqueId)) throw Error("options: tp_id must be trit_cuda_tp_id's text");
+      ncclUniqueId id;
+      for (size_t i = 0; i < sizeof id; ++i) id.internal[i] = (char)std::stoi(opt_.tp_id.substr(2 * i, 2), nullptr, 16);
+      ncclComm_t comm = nullptr;
+      nccl_check(nccl().CommInitRank(&comm, opt_.tp_size, id, opt_.tp_rank), "communicator");
+      comm_ = comm;
+      if (opt_.decode == "persistent") opt_.decode = "layered";  // the persistent kernel runs a whole model
+    }
     load(dir);
     alloc_buffers();
     setup_tensor_cores();
@@ -368,7 +416,10 @@ void Lm::release() {
   if (tiles_dev_) cudaFree(tiles_dev_);
   tiles_pinned_ = nullptr;
   tiles_dev_ = nullptr;
-  void* batch[] = {batch_last_, batch_cur_, batch_step_, batch_tok_, tc_expanded_, gu_, tc_status_, ffn_scales_, audio_};
+  if (comm_) nccl().CommDestroy((ncclComm_t)comm_);
+  comm_ = nullptr;
+  void* batch[] = {batch_last_, batch_cur_, batch_step_, batch_tok_, tc_expanded_, gu_, tc_status_, ffn_scales_, audio_,
+                   part_, keys_};
   for (void* b : batch)
     if (b) cudaFree(b);
   if (batch_graph_) cudaGraphExecDestroy(batch_graph_);
@@ -378,6 +429,8 @@ void Lm::release() {
   tc_expanded_ = nullptr;
   ffn_scales_ = nullptr;
   audio_ = nullptr;
+  part_ = nullptr;
+  keys_ = nullptr;
   gu_ = nullptr;
   tc_status_ = nullptr;
   tc_ready_ = false;
@@ -451,7 +504,8 @@ struct Pinned {
 
 std::string Lm::weight_cache_identity(const ModelSource& src) const {
   std::string id = "trit-cuda weights v" + std::to_string(kCacheVersion) + "\n" + src.format + "\n" + src.prefix +
-                   "\n" + std::to_string(arena_bytes_) + "\n";
+                   "\n" + std::to_string(arena_bytes_) + "\ntp " + std::to_string(tp_.rank) + "/" +
+                   std::to_string(tp_.size) + "\n";
   for (const std::string& p : src.files->paths()) {
     struct stat st;
     if (::stat(p.c_str(), &st) != 0) throw Error("cannot stat " + p);
@@ -578,6 +632,16 @@ void Lm::load(const std::string& dir) {
   const float rope_base = mc.rope_base;
   tied_ = mc.tied;
   if (cfg_.hd != 128) throw Error("head_dim " + std::to_string(cfg_.hd) + ": the CUDA kernels take head_dim 128");
+  // A tensor-parallel rank runs its shard: its heads, kv heads and FFN
+  // units are the model's, as far as the kernels see.
+  const DConfig full = cfg_;
+  tp_ = tp_shard(full, opt_.tp_rank, opt_.tp_size);
+  if (tp_.size > 1) {
+    if (full.residual_multiplier != 1.0f) throw Error("tensor parallelism takes residual_multiplier 1");
+    cfg_.heads = tp_.heads;
+    cfg_.kv_heads = tp_.kv;
+    cfg_.ffn = tp_.ffn;
+  }
   if (cfg_.d % 128 || cfg_.ffn % 128) throw Error("hidden and intermediate sizes must be multiples of 128");
 
   const TensorFiles& g = *src.files;
@@ -597,19 +661,28 @@ void Lm::load(const std::string& dir) {
       std::string p = prefix + "model.layers." + std::to_string(l);
       DLayer& L = layers_[l];
       L.norm_attn = load_vector(g, A, p + ".input_layernorm.weight", cfg_.d);
-      L.qkv = load_mat(g, A, {{p + ".self_attn.q_proj", qd}, {p + ".self_attn.k_proj", kvd}, {p + ".self_attn.v_proj", kvd}}, cfg_.d);
+      L.qkv = load_mat(g, A, {{p + ".self_attn.q_proj", tp_.heads0 * hd, qd}, {p + ".self_attn.k_proj", tp_.kv0 * hd, kvd},
+                              {p + ".self_attn.v_proj", tp_.kv0 * hd, kvd}}, cfg_.d);
       if (qk_norm) {
         L.q_norm = load_vector(g, A, p + ".self_attn.q_norm.weight", hd);
         L.k_norm = load_vector(g, A, p + ".self_attn.k_norm.weight", hd);
       }
-      L.out = load_mat(g, A, {{p + ".self_attn.o_proj", cfg_.d}}, qd);
+      L.out = load_mat(g, A, {{p + ".self_attn.o_proj", 0, cfg_.d}}, qd, tp_.heads0 * hd, full.heads * hd);
       L.norm_mlp = load_vector(g, A, p + ".post_attention_layernorm.weight", cfg_.d);
-      L.gate_up = load_mat(g, A, {{p + ".mlp.gate_proj", cfg_.ffn}, {p + ".mlp.up_proj", cfg_.ffn}}, cfg_.d);
-      L.down = load_mat(g, A, {{p + ".mlp.down_proj", cfg_.d}}, cfg_.ffn);
+      L.gate_up = load_mat(g, A, {{p + ".mlp.gate_proj", tp_.ffn0, cfg_.ffn}, {p + ".mlp.up_proj", tp_.ffn0, cfg_.ffn}},
+                           cfg_.d);
+      L.down = load_mat(g, A, {{p + ".mlp.down_proj", 0, cfg_.d}}, cfg_.ffn, tp_.ffn0, full.ffn);
     }
     final_norm_ = load_vector(g, A, prefix + "model.norm.weight", cfg_.d);
     embed_ = load_table(g, A, prefix + "model.embed_tokens", cfg_.vocab, cfg_.d);
-    head_ = has_head ? load_table(g, A, prefix + "lm_head", cfg_.vocab, cfg_.d) : embed_;
+    head_ = has_head ? load_table(g, A, prefix + "lm_head", tp_.vocab, cfg_.d, tp_.vocab0, cfg_.vocab) : embed_;
+    if (!has_head && tp_.size > 1) {
+      // Tied: this rank's rows of the token table are the output table.
+      const size_t sb = embed_.scale_f16 ? 2 : 4;
+      head_.n = tp_.vocab;
+      head_.codes = embed_.codes ? embed_.codes + (size_t)tp_.vocab0 * cfg_.d : nullptr;
+      head_.scales = embed_.scales ? (const char*)embed_.scales + (size_t)tp_.vocab0 * (cfg_.d / 32) * sb : nullptr;
+    }
     if (pass == 0) {
       arena_bytes_ = A.used;
       TRIT_CUDA(cudaMalloc(&arena_, arena_bytes_));
@@ -674,6 +747,10 @@ void Lm::alloc_buffers() {
   TRIT_CUDA(cudaMalloc(&row_pos_, (size_t)rows_cap_ * 4));
   TRIT_CUDA(cudaMalloc(&ids_, (size_t)rows_cap_ * 4));
   TRIT_CUDA(cudaMalloc(&xn_, (size_t)opt_.max_streams * d * 4));
+  if (tp_.size > 1) {
+    TRIT_CUDA(cudaMalloc(&part_, (size_t)rows_cap_ * d * 4));
+    TRIT_CUDA(cudaMalloc(&keys_, (size_t)std::max(rows_cap_, opt_.max_streams) * 8));
+  }
   TRIT_CUDA(cudaMalloc(&best_val_, (size_t)opt_.max_streams * table_blocks(cfg_.vocab) * 4));
   TRIT_CUDA(cudaMalloc(&best_idx_, (size_t)opt_.max_streams * table_blocks(cfg_.vocab) * 4));
   TRIT_CUDA(cudaMalloc(&logits_, (size_t)cfg_.vocab * 4));
@@ -692,6 +769,29 @@ void Lm::check_ids(const int* ids, size_t n) const {
 
 // CausalLm::hidden (causal_lm.rs:410-481) for the rows in x_, whose stream
 // and position are in row_stream_ / row_pos_.
+void Lm::final_rows(const float* x, int ldx, int nb, float* logits, int* tokens) {
+  if (tp_.size == 1) {
+    TRIT_CUDA(launch_final(x, ldx, nb, final_norm_, cfg_, head_, xn_, logits, best_val_, best_idx_, tokens, stream_));
+    return;
+  }
+  // Each rank's best among its vocabulary rows, as argmax-ordered keys; the
+  // largest key over the ranks is the first strict maximum of all rows.
+  if (logits) throw Error("logit traces are not kept with tensor parallelism");
+  TRIT_CUDA(launch_final(x, ldx, nb, final_norm_, cfg_, head_, xn_, nullptr, best_val_, best_idx_, tokens, stream_,
+                         keys_, tp_.vocab0));
+  nccl_check(nccl().AllReduce(keys_, keys_, (size_t)nb, ncclUint64, ncclMax, (ncclComm_t)comm_, stream_),
+             "argmax keys");
+  TRIT_CUDA(launch_key_tokens(keys_, nb, tokens, stream_));
+  timing_.gpu_launches += 1;
+}
+
+void Lm::reduce_into_x(int m) {
+  const size_t n = (size_t)m * cfg_.d;
+  nccl_check(nccl().AllReduce(part_, part_, n, ncclFloat32, ncclSum, (ncclComm_t)comm_, stream_), "partial sums");
+  TRIT_CUDA(launch_add(x_, part_, n, stream_));
+  timing_.gpu_launches += 1;
+}
+
 void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* tiles) {
   const int d = cfg_.d, qd = cfg_.heads * cfg_.hd, kvd = cfg_.kv_heads * cfg_.hd;
   cudaStream_t s = stream_;
@@ -742,7 +842,13 @@ void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* tiles
     clock_.mark("norm+quant", s);
     TRIT_CUDA(launch_norm_quant(att_, m, qd, nullptr, cfg_.eps, L.out.agroup, L.out.half, xq_, xs_, s));
     clock_.mark("o", s);
-    product(l, 1, L.out, tc_x_[1], kEpResid, x_, d, cfg_.residual_multiplier);
+    if (tp_.size > 1) {
+      // A rank's heads give a partial sum of o; the ranks' sum joins x.
+      product(l, 1, L.out, tc_x_[1], kEpOut, part_, d, 1.0f);
+      reduce_into_x(m);
+    } else {
+      product(l, 1, L.out, tc_x_[1], kEpResid, x_, d, cfg_.residual_multiplier);
+    }
     clock_.mark("norm+quant", s);
     TRIT_CUDA(launch_norm_quant(x_, m, d, L.norm_mlp, cfg_.eps, L.gate_up.agroup, L.gate_up.half, xq_, xs_, s,
                                 L.ffn_scale));
@@ -751,7 +857,12 @@ void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* tiles
     clock_.mark("norm+quant", s);
     TRIT_CUDA(launch_norm_quant(h_, m, cfg_.ffn, nullptr, cfg_.eps, L.down.agroup, L.down.half, xq_, xs_, s));
     clock_.mark("down", s);
-    product(l, 3, L.down, tc_x_[2], kEpResid, x_, d, cfg_.residual_multiplier);
+    if (tp_.size > 1) {
+      product(l, 3, L.down, tc_x_[2], kEpOut, part_, d, 1.0f);
+      reduce_into_x(m);
+    } else {
+      product(l, 3, L.down, tc_x_[2], kEpResid, x_, d, cfg_.residual_multiplier);
+    }
     clock_.mark(nullptr, s);
   }
   timing_.gpu_launches += cfg_.layers * 10 + (cfg_.embedding_multiplier != 1.0f ? 1 : 0);
@@ -777,6 +888,7 @@ void Lm::set_ffn_scales(const float* scales) {
 // kernels, one added row per step.
 std::vector<int> Lm::generate_additive(const int* ids, size_t n, const float* audio, size_t rows, const int* stop,
                                        size_t nstop, float* logits) {
+  if (tp_.size > 1) throw Error("generate_additive does not run with tensor parallelism");
   std::vector<int> out;
   if (n == 0 || rows < n) return out;
   check_ids(ids, n);
@@ -806,8 +918,7 @@ std::vector<int> Lm::generate_additive(const int* ids, size_t n, const float* au
     tokens_cap_ = max_new + 1;
     TRIT_CUDA(cudaMalloc(&tokens_, (size_t)tokens_cap_ * std::max(1, opt_.max_streams) * 4));
   }
-  TRIT_CUDA(launch_final(x_ + (size_t)(last_rows_ - 1) * d, d, 1, final_norm_, cfg_, head_, xn_,
-                         logits ? logits_ : nullptr, best_val_, best_idx_, tokens_, stream_));
+  final_rows(x_ + (size_t)(last_rows_ - 1) * d, d, 1, logits ? logits_ : nullptr, tokens_);
   if (logits) TRIT_CUDA(cudaMemcpyAsync(logits, logits_, (size_t)cfg_.vocab * 4, cudaMemcpyDeviceToHost, stream_));
   TRIT_CUDA(cudaEventRecord(ev_[1], stream_));
   TRIT_CUDA(cudaStreamSynchronize(stream_));
@@ -858,6 +969,7 @@ std::vector<int> Lm::generate_additive(const int* ids, size_t n, const float* au
 // every key), then the best token of each row from `from` on. The rows
 // must fit one pass (prefill_rows).
 std::vector<int> Lm::bidirectional_tokens(const float* rows, size_t m, size_t from) {
+  if (tp_.size > 1) throw Error("bidirectional_tokens does not run with tensor parallelism");
   if (from > m) throw Error("from (" + std::to_string(from) + ") is past the rows (" + std::to_string(m) + ")");
   if (m == 0) return {};
   if (m > (size_t)rows_cap_)
@@ -1101,8 +1213,7 @@ std::vector<int> Lm::finish(int slot, int position, int max_new, const int* stop
     tokens_cap_ = max_new + 1;
     TRIT_CUDA(cudaMalloc(&tokens_, (size_t)tokens_cap_ * std::max(1, opt_.max_streams) * 4));
   }
-  TRIT_CUDA(launch_final(x_ + (size_t)(last_rows_ - 1) * cfg_.d, cfg_.d, 1, final_norm_, cfg_, head_, xn_,
-                         logits ? logits_ : nullptr, best_val_, best_idx_, tokens_, stream_));
+  final_rows(x_ + (size_t)(last_rows_ - 1) * cfg_.d, cfg_.d, 1, logits ? logits_ : nullptr, tokens_);
   timing_.gpu_launches += 3;
   if (logits) TRIT_CUDA(cudaMemcpyAsync(logits, logits_, (size_t)cfg_.vocab * 4, cudaMemcpyDeviceToHost, stream_));
   TRIT_CUDA(cudaEventRecord(ev_[1], stream_));
@@ -1152,8 +1263,7 @@ void Lm::decode_layered(int slot, int position, int steps, float* trace) {
     row_pos_ = positions_ + i;
     hidden(1, position + i + 1);
     row_pos_ = saved;
-    TRIT_CUDA(launch_final(x_, cfg_.d, 1, final_norm_, cfg_, head_, xn_, trace ? logits_ : nullptr, best_val_,
-                           best_idx_, tokens_ + i + 1, stream_));
+    final_rows(x_, cfg_.d, 1, trace ? logits_ : nullptr, tokens_ + i + 1);
     timing_.gpu_launches += 4;
     if (trace)
       TRIT_CUDA(cudaMemcpyAsync(trace + (size_t)(i + 1) * cfg_.vocab, logits_, (size_t)cfg_.vocab * 4,
@@ -1225,7 +1335,7 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
   static const bool trace_events = getenv("TRIT_PHASE_TRACE") && *getenv("TRIT_PHASE_TRACE") == '3';
   long long* devents = nullptr;
   const size_t nev = (size_t)cfg_.layers * kEventSlots * decode_grid_;
-  if (trace_events && steps > 3 && !fast) {
+  if (trace_events && steps > 3) {
     TRIT_CUDA(cudaMallocAsync(&devents, nev * 8, stream_));
     TRIT_CUDA(cudaMemsetAsync(devents, 0, nev * 8, stream_));
   }
@@ -1273,13 +1383,21 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
     std::vector<long long> t(nev);
     TRIT_CUDA(cudaMemcpy(t.data(), devents, nev * 8, cudaMemcpyDeviceToHost));
     TRIT_CUDA(cudaFree(devents));
-    const char* names[kEventSlots] = {"layer start", "P1 x arrived", "P1 norm+quant", "P1 qkv rows", "P1 published",
+    const char* fast_names[kEventSlots] = {"layer start", "P1 x arrived", "P1 norm+quant", "P1 qkv rows",
+                                           "P1 published", "P2 qkv arrived", "P2 attention", "P2 quantize",
+                                           "P2 o partial rows", "P2 published", "P4 partials arrived",
+                                           "P4 norm+quant", "P4 gate_up rows", "P4 published", "P5 h arrived",
+                                           "P5 quantize", "P5 down rows", "P5 published", "table x arrived",
+                                           "table norm", "table rows", "argmax bests arrived", "", "", "", "", "",
+                                           "", "", "", "", ""};
+    const char* exact_names[kEventSlots] = {"layer start", "P1 x arrived", "P1 norm+quant", "P1 qkv rows", "P1 published",
                                       "P2 qkv arrived", "P2 attention", "P2 published", "P3 attq arrived", "P3 o rows",
                                       "P4 xa arrived", "P4 norm+quant", "P4 gate_up rows", "P5 h arrived",
                                       "P5 quantize", "P5 down rows", "P1 weights in smem", "P1 dots", "P1 chains",
                                       "P3 weights in smem", "P3 dots", "P3 chains", "P4 weights in smem", "P4 dots",
                                       "P4 chains", "P5 weights in smem", "P5 dots", "P5 chains", "P2 qk norm+rope",
                                       "", "", ""};
+    const char* const* names = fast ? fast_names : exact_names;
     // Per block and layer: the stamps in time order; each interval is
     // charged to the stamp that ends it.
     const int G = decode_grid_;
@@ -1464,8 +1582,7 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
   TRIT_CUDA(cudaMemcpyAsync(row_stream_, hs, S * 4, cudaMemcpyHostToDevice, stream_));
   TRIT_CUDA(cudaMemcpyAsync(row_pos_, hp, S * 4, cudaMemcpyHostToDevice, stream_));
   TRIT_CUDA(cudaMemsetAsync(batch_step_, 0, 4, stream_));
-  TRIT_CUDA(launch_final(batch_last_, d, (int)S, final_norm_, cfg_, head_, xn_, nullptr, best_val_, best_idx_,
-                         batch_cur_, stream_));
+  final_rows(batch_last_, d, (int)S, nullptr, batch_cur_);
   TRIT_CUDA(launch_batch_advance(batch_cur_, row_pos_, batch_step_, batch_tok_, (int)S, 0, stream_));
   timing_.gpu_launches += 4;
   TRIT_CUDA(cudaEventRecord(ev_[1], stream_));
@@ -1477,8 +1594,7 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
     TRIT_CUDA(launch_embed(embed_, batch_cur_, (int)S, x_, 1.0f, stream_));
     hidden((int)S, tmax);
     clock_.mark("final norm+table+argmax", stream_);
-    TRIT_CUDA(launch_final(x_, d, (int)S, final_norm_, cfg_, head_, xn_, nullptr, best_val_, best_idx_, batch_cur_,
-                           stream_));
+    final_rows(x_, d, (int)S, nullptr, batch_cur_);
     clock_.mark(nullptr, stream_);
     TRIT_CUDA(launch_batch_advance(batch_cur_, row_pos_, batch_step_, batch_tok_, (int)S, 1, stream_));
     timing_.gpu_launches += 1 + 3 + 1;

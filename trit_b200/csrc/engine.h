@@ -28,15 +28,20 @@ struct Options {
   std::string decode = "persistent";  // "persistent" (one kernel per generation) or "layered"
   bool tensor_cores = true;      // tcgen05 products for prefill and batches of >= tc_rows rows
   int tc_rows = 64;
-  // true: every floating-point step in the reference's order (logits bit
-  // for bit those of the CPU decoder); false: the batch-1 decode reorders
-  // sums (tree reductions, split attention) within the north-star
-  // tolerance, which is faster.
-  bool exact = false;
+  // true (default): every floating-point step in the reference's order
+  // (logits bit for bit those of the CPU decoder). false: the batch-1
+  // decode sums in tree order (decode_fast.cu); tokens stay the reference's
+  // but, since a reordered sum can move an int8 activation code, logits
+  // drift by up to ~5e-2.
+  bool exact = true;
   // Keep the weights' device layout in a cache file and read it on later
   // loads (cache_dir, default <model folder>/.trit_cuda).
   bool weight_cache = false;
   std::string cache_dir;
+  // Tensor parallelism: this process's rank of tp_size, and the NCCL
+  // unique id (hex, from trit_cuda_tp_id on rank 0) the ranks share.
+  int tp_size = 1, tp_rank = 0;
+  std::string tp_id;
   std::string config_at;         // key path of the settings in config.json (from_tensors' config_at)
   std::string prefix;            // start of every tensor name (from_tensors' prefix)
   // `lenient`: keys other than config_at and prefix are skipped unchecked.
@@ -150,6 +155,12 @@ class Lm {
   // (prompt chunks), or null for one row per attention block.
   void hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* tiles = nullptr);
   void setup_tensor_cores();
+  // The final norm, the output table and the best token of nb rows at x
+  // (row stride ldx) into tokens; with tensor parallelism the ranks' best
+  // tokens meet in one all-reduce. logits (device, [nb][vocab]) may be null.
+  void final_rows(const float* x, int ldx, int nb, float* logits, int* tokens);
+  // x[m][d] += the sum over ranks of part_[m][d].
+  void reduce_into_x(int m);
   void check_tc_status();
   // Greedy decode for `slot` after a prefill that left its last row in x.
   std::vector<int> finish(int slot, int position, int max_new, const int* stop, size_t nstop, float* logits);
@@ -169,6 +180,10 @@ class Lm {
   std::string weights_from_;    // "files" or "cache"
   std::string cache_file_;      // the weight cache file, or ""
   std::string cache_identity_;
+  TpShard tp_;                  // this rank's shard (size 1: the whole model)
+  void* comm_ = nullptr;        // ncclComm_t of the tensor-parallel ranks
+  float* part_ = nullptr;       // [rows][d] a rank's partial o / down sums
+  unsigned long long* keys_ = nullptr;  // [rows] (value, index) keys of each row's best token
   void* arena_ = nullptr;
   size_t arena_bytes_ = 0;
   std::vector<DLayer> layers_;

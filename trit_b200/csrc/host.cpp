@@ -645,6 +645,30 @@ ModelSource open_model(const std::string& dir, const std::string& at, const std:
   return src;
 }
 
+TpShard tp_shard(const DConfig& c, int rank, int size) {
+  if (size < 1 || rank < 0 || rank >= size) throw Error("tensor parallelism: rank " + std::to_string(rank) + " of " +
+                                                        std::to_string(size));
+  if (c.kv_heads % size || c.heads % size)
+    throw Error("tensor parallelism: " + std::to_string(c.kv_heads) + " key/value heads do not split " +
+                std::to_string(size) + " ways");
+  // Whole 128-value groups of FFN units per rank (the activation groups
+  // of int8 and ternary products and the tensor cores' K step).
+  if (c.ffn % (128 * size)) throw Error("tensor parallelism: intermediate_size does not split into 128-wide shards");
+  if (c.vocab % size) throw Error("tensor parallelism: vocab_size does not split evenly");
+  TpShard t;
+  t.rank = rank;
+  t.size = size;
+  t.kv = c.kv_heads / size;
+  t.kv0 = rank * t.kv;
+  t.heads = c.heads / size;
+  t.heads0 = rank * t.heads;  // query heads follow their key/value heads
+  t.ffn = c.ffn / size;
+  t.ffn0 = rank * t.ffn;
+  t.vocab = c.vocab / size;
+  t.vocab0 = rank * t.vocab;
+  return t;
+}
+
 namespace {
 
 // The storage of the product `name` (without .weight): its kind and the
@@ -672,7 +696,8 @@ std::string product_kind(const TensorFiles& g, const std::string& name, uint64_t
 
 }  // namespace
 
-std::string describe_model(const std::string& dir, const std::string& at, const std::string& prefix_in) {
+std::string describe_model(const std::string& dir, const std::string& at, const std::string& prefix_in, int tp_rank,
+                           int tp_size) {
   ModelSource src = open_model(dir, at, prefix_in);
   const ModelConfig& m = src.mc;
   const DConfig& c = m.cfg;
@@ -724,7 +749,17 @@ std::string describe_model(const std::string& dir, const std::string& at, const 
                 (double)c.residual_multiplier, (double)c.logits_scaling, weights.c_str(), embed.c_str(),
                 head.c_str(), has_head ? "true" : "false", (unsigned long long)layer_bytes,
                 (unsigned long long)head_bytes, src.format.c_str(), prefix.c_str());
-  return buf;
+  std::string out = buf;
+  if (tp_size > 1) {
+    const TpShard t = tp_shard(c, tp_rank, tp_size);
+    std::snprintf(buf, sizeof buf,
+                  ", \"tp\": {\"rank\": %d, \"size\": %d, \"heads\": [%d, %d], \"kv_heads\": [%d, %d], "
+                  "\"ffn_units\": [%d, %d], \"vocab_rows\": [%d, %d]}}",
+                  t.rank, t.size, t.heads0, t.heads0 + t.heads, t.kv0, t.kv0 + t.kv, t.ffn0, t.ffn0 + t.ffn, t.vocab0,
+                  t.vocab0 + t.vocab);
+    out = out.substr(0, out.size() - 1) + buf;
+  }
+  return out;
 }
 
 }  // namespace trit

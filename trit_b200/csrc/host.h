@@ -146,6 +146,22 @@ struct ModelSource {
 };
 ModelSource open_model(const std::string& dir, const std::string& at = "", const std::string& prefix = "");
 
+// The tensor-parallel shard of rank `rank` of `size` (the optional 2/4-way
+// split of the largest decoder): its query heads (with the key/value heads
+// they share, whole GQA groups), its FFN units (gate and up rows kept
+// paired) and its rows of the output table. The q/k/v and gate/up products
+// split their output rows, o_proj and down_proj their input columns (a
+// partial sum per rank, then a sum across the ranks), the token table its
+// vocabulary rows (a best token per rank, then the best of those).
+struct TpShard {
+  int rank = 0, size = 1;
+  int heads0 = 0, heads = 0;  // query heads [heads0, heads0 + heads)
+  int kv0 = 0, kv = 0;        // key/value heads
+  int ffn0 = 0, ffn = 0;      // FFN units
+  int vocab0 = 0, vocab = 0;  // output-table rows
+};
+TpShard tp_shard(const DConfig& full, int rank, int size);
+
 // ggml's quantize_row_q8_0_ref for one block of 32 (Blocks::quantize,
 // src/cpu/gemm.rs:53-76): d = max|x| / 127, codes round(x * (1 / d)) half
 // away from zero, d stored as f16; out = 2 bytes of d, 32 codes.
@@ -155,6 +171,9 @@ void q8_0_quantize_block(const float* v, uint8_t* out);
 // settings, the storage of its products and token tables, and the bytes a
 // greedy step reads from device memory.
 // `prefix` starts every tensor name ("", "thinker.", "llm." ...).
-std::string describe_model(const std::string& dir, const std::string& at = "", const std::string& prefix = "");
+// With tp_size > 1, also the shard of tp_rank ("tp": heads, kv_heads,
+// ffn_units, vocab_rows as [first, end) ranges).
+std::string describe_model(const std::string& dir, const std::string& at = "", const std::string& prefix = "",
+                           int tp_rank = 0, int tp_size = 1);
 
 }  // namespace trit

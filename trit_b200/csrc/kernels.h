@@ -51,8 +51,13 @@ cudaError_t launch_attention_rows(const float* qkv, const int2* tiles, int ntile
 cudaError_t launch_add(float* x, const float* a, size_t n, cudaStream_t s);
 // RmsNorm of `nb` rows, the table product and each row's argmax. logits
 // ([nb][vocab]) may be null; best_* hold [nb][table_blocks(vocab)].
+// keys non-null (tensor parallelism, this rank's table rows from v0): each
+// row's best as an argmax-ordered key (k_argmax_key) instead of a token;
+// after the ranks' max-reduction, launch_key_tokens turns keys into tokens.
 cudaError_t launch_final(const float* x, int ldx, int nb, const float* norm_w, const DConfig& cfg, const DTable& T,
-                         float* xn, float* logits, float* best_val, int* best_idx, int* token, cudaStream_t s);
+                         float* xn, float* logits, float* best_val, int* best_idx, int* token, cudaStream_t s,
+                         unsigned long long* keys = nullptr, int v0 = 0);
+cudaError_t launch_key_tokens(const unsigned long long* keys, int nb, int* token, cudaStream_t s);
 // The table product alone for `nb` rows already normed.
 cudaError_t launch_table(const DTable& T, const float* xn, int nb, float mult, float* logits, float* best_val,
                          int* best_idx, cudaStream_t s);

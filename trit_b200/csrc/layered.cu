@@ -900,6 +900,41 @@ __global__ void k_argmax(const float* val, const int* idx, int n, int* token) {
   if (threadIdx.x == 0) token[blockIdx.x] = (i == 0x7fffffff) ? 0 : i;
 }
 
+// The argmax of one stream's partials as a key whose unsigned order is the
+// argmax order of layers.rs:603-612 across tensor-parallel ranks: the value
+// (its bits mapped to an order-preserving unsigned) above the complement of
+// its global index (rows v0 ..), so the larger value wins and, among equal
+// values, the lower index. A row with no number (NaN everywhere) keys 0.
+__global__ void k_argmax_key(const float* val, const int* idx, int n, int v0, unsigned long long* keys) {
+  val += (size_t)blockIdx.x * n;
+  idx += (size_t)blockIdx.x * n;
+  float v = -INFINITY;
+  int i = 0x7fffffff;
+  for (int p = threadIdx.x; p < n; p += 32) {
+    if (val[p] > v || (val[p] == v && idx[p] < i)) { v = val[p]; i = idx[p]; }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+  }
+  if (threadIdx.x == 0) {
+    unsigned long long key = 0;
+    if (i != 0x7fffffff) {
+      const uint32_t u = __float_as_uint(v);
+      const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+      key = ((unsigned long long)ord << 32) | (uint32_t)~(uint32_t)(v0 + i);
+    }
+    keys[blockIdx.x] = key;
+  }
+}
+
+__global__ void k_key_token(const unsigned long long* keys, int nb, int* token) {
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < nb; b += gridDim.x * blockDim.x)
+    token[b] = keys[b] ? (int)~(uint32_t)keys[b] : 0;
+}
+
 // add_into (src/layers.rs): x[i] = x[i] + a[i].
 __global__ void k_add(float* x, const float* a, size_t n) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
@@ -1084,15 +1119,23 @@ static cudaError_t table_rows_pass(const DTable& T, const float* xn, int nb, flo
   return cudaGetLastError();
 }
 
+cudaError_t launch_key_tokens(const unsigned long long* keys, int nb, int* token, cudaStream_t s) {
+  k_key_token<<<(nb + 255) / 256, 256, 0, s>>>(keys, nb, token);
+  LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
 cudaError_t launch_final(const float* x, int ldx, int nb, const float* norm_w, const DConfig& cfg, const DTable& T,
-                         float* xn, float* logits, float* best_val, int* best_idx, int* token, cudaStream_t s) {
+                         float* xn, float* logits, float* best_val, int* best_idx, int* token, cudaStream_t s,
+                         unsigned long long* keys, int v0) {
   k_final_norm_rows<<<nb, 256, (size_t)cfg.d * 4, s>>>(x, ldx, cfg.d, norm_w, cfg.eps, xn);
   LAUNCH_CHECK();
   float mult = (cfg.logits_scaling == 1.0f) ? 1.0f : 1.0f / cfg.logits_scaling;
   int blocks = table_blocks(T.n);
   cudaError_t e = launch_table(T, xn, nb, mult, logits, best_val, best_idx, s);
   if (e != cudaSuccess) return e;
-  k_argmax<<<nb, 32, 0, s>>>(best_val, best_idx, blocks, token);
+  if (keys) k_argmax_key<<<nb, 32, 0, s>>>(best_val, best_idx, blocks, v0, keys);
+  else k_argmax<<<nb, 32, 0, s>>>(best_val, best_idx, blocks, token);
   LAUNCH_CHECK();
   return cudaSuccess;
 }

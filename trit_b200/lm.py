@@ -74,6 +74,7 @@ def library() -> ctypes.CDLL:
                                                   _i64p]),
         "trit_lm_last_timing": (ctypes.c_int, [ctypes.c_void_p, _f64p, _f64p, _i64p, _i64p]),
         "trit_lm_status": (ctypes.c_void_p, [ctypes.c_void_p]),
+        "trit_cuda_tp_id": (ctypes.c_int, [ctypes.c_char_p, _size]),
         "trit_lm_generate_batch_prefix": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, _size,
                                                          ctypes.POINTER(_i32p), ctypes.POINTER(_size), ctypes.c_int32,
                                                          _i32p, _size, _i32p, _i64p]),
@@ -380,6 +381,15 @@ class Dense:
 
     def __del__(self):
         self.close()
+
+
+def tp_id() -> str:
+    """A new tensor-parallel group id (trit_cuda_tp_id): made on one rank,
+    passed to every rank's load as tp_id."""
+    buf = ctypes.create_string_buffer(512)
+    if library().trit_cuda_tp_id(buf, len(buf)) != 0:
+        raise _error()
+    return buf.value.decode()
 
 
 def inspect(model_dir: str, **options) -> dict:
