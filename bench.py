@@ -262,6 +262,43 @@ def run_reference(args, r: dp.Rank) -> None:
 
 
 # ------------------------------------------------------------ GPU legs ----
+def tp_group_id(r: dp.Rank, tp: int) -> str:
+    """The NCCL group id of this rank's tensor-parallel group: made by the
+    group's first rank (trit_cuda_tp_id) and handed to the others."""
+    import torch.distributed as dist
+
+    from trit_b200 import lm as lmmod
+
+    ids = [None] * r.world
+    dist.all_gather_object(ids, lmmod.tp_id() if r.rank % tp == 0 else "")
+    return ids[(r.rank // tp) * tp]
+
+
+def allreduce_us(r: dp.Rank, tp: int, nbytes: int, reps: int = 200) -> float:
+    """Device time of one f32 sum all-reduce of `nbytes` within a
+    tensor-parallel group (torch's NCCL, the size the library reduces after
+    o_proj and down_proj), max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    groups = [dist.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(r.world // tp)]
+    mine = groups[r.rank // tp]
+    x = torch.zeros(max(1, nbytes // 4), dtype=torch.float32, device="cuda")
+    for _ in range(10):
+        dist.all_reduce(x, group=mine)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        dist.all_reduce(x, group=mine)
+    end.record()
+    torch.cuda.synchronize()
+    us = start.elapsed_time(end) * 1e3 / reps
+    for g in groups:
+        dist.destroy_process_group(g)
+    return dp.reduce(us, r, "max")
+
+
 def measure(w: dict, args, r: dp.Rank, steps: int, warmup: int, decode: str, exact: bool) -> tuple[dict, str]:
     """One workload on this rank's GPU: `warmup` untimed generations, then
     `steps` timed ones between barriers. Returns the JSON fields of its line
@@ -277,6 +314,10 @@ def measure(w: dict, args, r: dp.Rank, steps: int, warmup: int, decode: str, exa
     S = w["streams"]
     prompt_len = w["prompt"] + w.get("rows", 0)
     opts = {"device": r.local, "kv": args.kv, "max_context": prompt_len + w["new"] + 8, "exact": exact}
+    tp = max(1, getattr(args, "tp", 1) or 1)
+    group = r.rank // tp  # ranks of one tensor-parallel group serve the same streams
+    if tp > 1:
+        opts.update(tp_size=tp, tp_rank=r.rank % tp, tp_id=tp_group_id(r, tp))
     if w["kind"] == "batch":
         # Prompt passes of 4096 rows: 15 % more end to end on C5 than 512
         # (fuller tensor-core and attention grids).
@@ -291,7 +332,7 @@ def measure(w: dict, args, r: dp.Rank, steps: int, warmup: int, decode: str, exa
     vocab, width = lm.vocab(), lm.width()
 
     def inputs(step: int):
-        base = (r.rank * 1_000_003 + step) * S
+        base = (group * 1_000_003 + step) * S
         prompts = [dp.stream_prompt(SEED, base + s, w["prompt"], vocab) for s in range(S)]
         rows = audio_rows(width, w["rows"], base) if w["kind"] == "answer" else None
         return prompts, rows
@@ -323,8 +364,9 @@ def measure(w: dict, args, r: dp.Rank, steps: int, warmup: int, decode: str, exa
     lm.close()
     wall_max = dp.reduce(wall, r, "max")
     decode_max = dp.reduce(decode_ms, r, "max")
-    steps_all = dp.reduce(float(decode_steps), r, "sum")
-    made_all = dp.reduce(float(made), r, "sum")
+    # Every rank of a tensor-parallel group reports its group's tokens.
+    steps_all = dp.reduce(float(decode_steps), r, "sum") / tp
+    made_all = dp.reduce(float(made), r, "sum") / tp
     value = steps_all / (decode_max / 1e3)
     e2e = made_all / wall_max
     positions = [prompt_len + i for i in range(w["new"] - 1)]
@@ -332,7 +374,7 @@ def measure(w: dict, args, r: dp.Rank, steps: int, warmup: int, decode: str, exa
     hbm, peak_kind = peaks()
     greedy_steps = decode_steps / S  # forwards of the whole batch
     per_step_s = decode_ms / 1e3 / max(1.0, greedy_steps)
-    achieved = alg["total"] / per_step_s / 1e9
+    achieved = alg["total"] / per_step_s / 1e9 / tp  # per GPU: a group's ranks share the step's bytes
     path = "tree-order sums" if not exact else "exact reference order"
     kernel = {"generate": f"decode step (persistent kernel, {path})" if decode == "persistent" else "layered step",
               "answer": f"decode step (persistent kernel, {path})" if decode == "persistent" else "layered step",
@@ -342,7 +384,8 @@ def measure(w: dict, args, r: dp.Rank, steps: int, warmup: int, decode: str, exa
         "metric": w["metric"], "value": value, "unit": "tok/s", "n_gpus": r.world,
         "steps": steps, "warmup": warmup, "ms_per_step": wall_max * 1e3 / steps,
         "config": {"workload": w["workload"], "model": w["model"], "global_batch": S * r.world,
-                   "seq_len": prompt_len + w["new"], "parallelism": f"dp{r.world} (independent streams, no collective)",
+                   "seq_len": prompt_len + w["new"], "parallelism": (f"dp{r.world} (independent streams, no collective)" if tp == 1 else
+                                   f"tp{tp} x dp{r.world // tp} (NCCL all-reduce of o/down partials, argmax keys)"),
                    "decode": decode if w["kind"] != "batch" else "batched", "exact": exact, "kv_cache": args.kv,
                    "l2": f"weights {alg['weights'] / 1e6:.0f} MB > 126 MB L2; no flush"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": S * w["new"] * 4},
@@ -353,6 +396,16 @@ def measure(w: dict, args, r: dp.Rank, steps: int, warmup: int, decode: str, exa
         "prefill_ms_per_step": prefill_ms / steps,
         "clocks": clocks.summary(),
     }
+    if tp > 1:
+        # The collective's share of a decode step: two f32 all-reduces a layer
+        # of [streams x width] (o_proj and down_proj partials) plus one of
+        # the argmax keys, timed alone at the same size.
+        nbytes = S * info["hidden_size"] * 4
+        us = allreduce_us(r, tp, nbytes)
+        per_step = 2 * info["num_hidden_layers"]
+        fields["tp"] = {"size": tp, "allreduce_bytes": nbytes, "allreduce_us": us, "allreduces_per_step": per_step + 1,
+                        "decode_step_us": per_step_s * 1e6,
+                        "collective_share": per_step * us / (per_step_s * 1e6)}
     return fields, model_dir
 
 
@@ -372,7 +425,7 @@ def run_decode(args, r: dp.Rank) -> None:
             "dtype": "int8 x int8 -> i32, f32",
             "data": "synthetic (seeded N(0,0.02) weights, uniform random prompt ids"
                     + (", N(0,1) prefix rows)" if w["kind"] == "answer" else ")")}
-    if args.config == "c1" and not args.no_batch64:
+    if args.config == "c1" and not args.no_batch64 and args.tp == 1:
         # The batch-64 half of the metric in the same run (and so in the
         # driver's 1/2/4/8-GPU scaling run): C5, 64 streams per GPU.
         b, _ = measure(dict(WORKLOADS["c5"], key="c5"), args, r, BATCH64_STEPS, BATCH64_WARMUP, "persistent",
@@ -529,6 +582,8 @@ def main() -> None:
     ap.add_argument("--tc-rows", type=int, help="rows from which products use the tensor cores (engine option)")
     ap.add_argument("--prefill-rows", type=int, help="rows a prompt pass (engine option)")
     ap.add_argument("--kv", default="f16")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor-parallel group size (ranks of a group split each layer; --gpus a multiple of it)")
     ap.add_argument("--reps", type=int, default=1000, help="repetitions per case of the op sweep")
     ap.add_argument("--shapes", help="op sweep shapes instead of the workload's, e.g. 16384x3072,3072x8192")
     ap.add_argument("--rows", help="op sweep row counts instead of the workload's, e.g. 64,128,512")
@@ -541,6 +596,8 @@ def main() -> None:
     if args.impl == "reference":
         backend = "gloo"
     r = dp.init(backend, timeout_s=900)
+    if args.impl != "reference" and (args.tp < 1 or r.world % args.tp):
+        raise SystemExit(f"--tp {args.tp} does not divide the {r.world} ranks")
     try:
         if args.impl == "reference":
             run_reference(args, r)

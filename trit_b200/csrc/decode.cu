@@ -298,12 +298,25 @@ struct LlLayout {
   }
 };
 
-__host__ __device__ inline int attend_kt(int f16) { return f16 ? 128 : 64; }
+// The LL word of row `row` of the stacked q | k | v product: the words of
+// each kv head's query heads, key and value lie together, [kv head][q heads
+// of the group | k | v][128], so its attention block waits on one run.
+__device__ __forceinline__ int qkv_slot(const DConfig& cfg, int row) {
+  const int qpk = cfg.heads / cfg.kv_heads, qd = cfg.heads * 128, kvd = cfg.kv_heads * 128;
+  const int run = (qpk + 2) * 128;
+  if (row < qd) return (row / 128 / qpk) * run + row % (qpk * 128);
+  if (row < qd + kvd) return ((row - qd) / 128) * run + qpk * 128 + row % 128;
+  return ((row - qd - kvd) / 128) * run + (qpk + 1) * 128 + row % 128;
+}
+
+// Keys a staged attention tile: 256 (f16) or 128 (f32) when the shared
+// memory has room (launch_decode picks it), so a short context is one tile.
+__host__ __device__ inline int attend_kt(int f16, bool wide) { return (f16 ? 128 : 64) * (wide ? 2 : 1); }
 
 // Shared memory of the attention phase, in floats.
-__host__ __device__ inline size_t attend_smem_floats(int qpk, int tmax, int f16) {
+__host__ __device__ inline size_t attend_smem_floats(int qpk, int tmax, int f16, int kt) {
   return (size_t)(qpk + 2) * 128 + (size_t)qpk * 128 + 2 * 128 + (size_t)qpk * 128 + (size_t)qpk * 4 +
-         (size_t)qpk * 32 + attention_smem_floats(qpk, tmax, attend_kt(f16), f16);
+         (size_t)qpk * 32 + 3 * 128 + attention_smem_floats(qpk, tmax, kt, f16);
 }
 
 // Block kvh of the P2 phase: the query heads of kv head kvh over keys
@@ -315,7 +328,7 @@ template <class Ev>
 __device__ bool attend(const DecodeArgs& a, const DLayer& L, int layer, int pos, int kvh, int tmax, uint32_t tag_in,
                        uint32_t tag_out, Shared& S, Ev ev) {
   const DConfig& cfg = a.cfg;
-  const int hd = 128, qpk = cfg.heads / cfg.kv_heads, qd = cfg.heads * hd, kvd = cfg.kv_heads * hd;
+  const int hd = 128, qpk = cfg.heads / cfg.kv_heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
   const int T = pos + 1;
   const DCache& cache = a.cache;
@@ -328,24 +341,30 @@ __device__ bool attend(const DecodeArgs& a, const DLayer& L, int layer, int pos,
   float* out = vf + hd;             // [qpk][128]
   float* scales = out + nq;         // [qpk * 4]: one a group of 32 at most
   int8_t* codes = (int8_t*)(scales + qpk * 4);  // [qpk * 128] bytes
-  float* region = scales + qpk * 4 + qpk * 32;
-  const int kt = attend_kt(cache.f16), row = cache.f16 ? 64 : 128;
+  float* nrm = scales + qpk * 4 + qpk * 32;  // [3][128]: q norm, k norm weights, the RoPE row (sin | cos)
+  float* region = nrm + 3 * 128;
+  const int kt = a.key_tile, row = cache.f16 ? 64 : 128;
   float* sc = region;
   float* ktl = sc + qpk * tmax;
   float* vtl = ktl + kt * (row + 4);
   float* stat = vtl + kt * row;
   Attention<DT> A{cache, cfg, a.stream, layer, kvh, qpk, kt, sc, ktl, vtl, stat, tmax};
+  // The norm weights and the position's RoPE row go out with tile 0 of the
+  // cached keys and values, before the wait for q, k and v.
+  for (int i = 4 * t; i < 3 * hd; i += 4 * DT) {
+    const float* src = i < hd ? L.q_norm : i < 2 * hd ? L.k_norm : a.rope + (size_t)min(pos, a.rope_rows - 1) * hd;
+    if (src) cp_async16(nrm + i, src + i % hd);
+  }
   A.preload(T, true);
   // q heads, k and v of this kv head, as P1 made them.
-  bool ok = ll_wait(a.ll + ll.qkv + kvh * nq, nq, tag_in, a.status, [&](int i, uint32_t v) { raw[i] = __uint_as_float(v); });
-  if (!ok) return false;
-  ok = ll_wait(a.ll + ll.qkv + qd + kvh * hd, hd, tag_in, a.status, [&](int i, uint32_t v) { raw[nq + i] = __uint_as_float(v); });
-  if (!ok) return false;
-  ok = ll_wait(a.ll + ll.qkv + qd + kvd + kvh * hd, hd, tag_in, a.status,
-               [&](int i, uint32_t v) { raw[nq + hd + i] = __uint_as_float(v); });
+  // q heads, k and v of this kv head: one run of LL words (qkv_slot).
+  bool ok = ll_wait(a.ll + ll.qkv + kvh * (nq + 2 * hd), nq + 2 * hd, tag_in, a.status,
+                    [&](int i, uint32_t v) { raw[i] = __uint_as_float(v); });
   if (!ok) return false;
   ev(5);
-  const float* sn = a.rope + (size_t)min(pos, a.rope_rows - 1) * hd;
+  cp_wait_all();  // the staged norm weights and RoPE row (tile 0 as well)
+  __syncthreads();
+  const float* sn = nrm + 2 * hd;
   const float* cs = sn + hd / 2;
   // Warp 0: k, warp 1: v, warps 2..: q heads (causal_lm.rs:428-446).
   for (int h = warp; h < 2 + qpk; h += DW) {
@@ -354,7 +373,7 @@ __device__ bool attend(const DecodeArgs& a, const DLayer& L, int layer, int pos,
 #pragma unroll
     for (int i = 0; i < 4; ++i) v[i] = src[lane * 4 + i];
     if (h != 1) {
-      const float* nw = (h == 0) ? L.k_norm : L.q_norm;
+      const float* nw = (h == 0) ? (L.k_norm ? nrm + hd : nullptr) : (L.q_norm ? nrm : nullptr);
       if (nw) {
         float inv = 0.0f;
         if (lane == 0) inv = rms_inv(seq_sum_squares(src, hd), hd, cfg.eps);
@@ -404,19 +423,7 @@ __device__ bool attend(const DecodeArgs& a, const DLayer& L, int layer, int pos,
   // then publish codes (4 a word) and scales as LL words.
   const DMat& O = L.out;
   const int G = O.agroup;
-  for (int g = warp; g < nq / G; g += DW) {
-    float sc2;
-    if (G == 32) {
-      float v[1] = {out[g * 32 + lane]};
-      sc2 = warp_quantize_group<32>(v, codes + g * 32, O.half);
-    } else {
-      float v[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) v[i] = out[g * 128 + lane * 4 + i];
-      sc2 = warp_quantize_group<128>(v, codes + g * 128, O.half);
-    }
-    if (lane == 0) scales[g] = sc2;
-  }
+  quantize_groups<DT, 4>(out, nq, nullptr, nullptr, 1.0f, G, O.half, codes, scales);
   __syncthreads();
   const int qh0 = kvh * qpk;
   for (int wd = t; wd < nq / 4; wd += DT) ll_put(a.ll + ll.attq + qh0 * hd / 4 + wd, ((const uint32_t*)codes)[wd], tag_out);
@@ -472,7 +479,10 @@ __device__ bool table_slice(const DecodeArgs& a, int v0, int v1, int step, Share
     cp_wait<0>();
     return false;
   }
-  float lanes[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  // The thread's 4 lanes as two packed pairs: byte -> float, times the
+  // scale, fma into the chain, each rounded as the scalar steps are.
+  float2 l01 = make_float2(0.0f, 0.0f), l23 = make_float2(0.0f, 0.0f);
+  const float2 bias = make_float2(8388736.0f, 8388736.0f);
   for (int item = 0; item < items; ++item) {
     issue(item + TAB_STAGES - 1);
     cp_wait<TAB_STAGES - 1>();
@@ -487,11 +497,15 @@ __device__ bool table_slice(const DecodeArgs& a, int v0, int v1, int step, Share
       float s = T.scale_f16 ? f16_bits_to_f32(((const uint16_t*)(srow + TAB_SLAB))[st >> 1])
                             : ((const float*)(srow + TAB_SLAB))[st >> 1];
       float4 xv = *(const float4*)(S.xf + kk);
-      lanes[0] = __fmaf_rn(xv.x, __fmul_rn(byte_to_float(word, 0), s), lanes[0]);
-      lanes[1] = __fmaf_rn(xv.y, __fmul_rn(byte_to_float(word, 1), s), lanes[1]);
-      lanes[2] = __fmaf_rn(xv.z, __fmul_rn(byte_to_float(word, 2), s), lanes[2]);
-      lanes[3] = __fmaf_rn(xv.w, __fmul_rn(byte_to_float(word, 3), s), lanes[3]);
+      const float2 c01 = sub2(make_float2(__uint_as_float(__byte_perm(word, 0x4B000000u, 0x7650)),
+                                          __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7651))), bias);
+      const float2 c23 = sub2(make_float2(__uint_as_float(__byte_perm(word, 0x4B000000u, 0x7652)),
+                                          __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7653))), bias);
+      const float2 s2 = make_float2(s, s);
+      l01 = fma2(make_float2(xv.x, xv.y), mul2(c01, s2), l01);
+      l23 = fma2(make_float2(xv.z, xv.w), mul2(c23, s2), l23);
     }
+    const float lanes[4] = {l01.x, l01.y, l23.x, l23.y};
     if (slab == slabs - 1) {
       // The row is done: _mm512_reduce_add_ps across the 4 threads.
       float s8[4], s4[4];
@@ -505,8 +519,8 @@ __device__ bool table_slice(const DecodeArgs& a, int v0, int v1, int step, Share
         if (a.logits) a.logits[(size_t)step * T.n + row] = v;
         if (v > bv || (v == bv && row < bi)) { bv = v; bi = row; }
       }
-#pragma unroll
-      for (int l = 0; l < 4; ++l) lanes[l] = 0.0f;
+      l01 = make_float2(0.0f, 0.0f);
+      l23 = make_float2(0.0f, 0.0f);
     }
     __syncwarp();  // the stage is refilled by the next issue
   }
@@ -615,7 +629,8 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
       }, ev, 16);
       if (!ok) return;
       ev(3);
-      for (int lr = threadIdx.x; lr < q1 - q0; lr += DT) ll_put(a.ll + ll.qkv + q0 + lr, __float_as_uint(S.out[lr]), t_qkv);
+      for (int lr = threadIdx.x; lr < q1 - q0; lr += DT)
+        ll_put(a.ll + ll.qkv + qkv_slot(cfg, q0 + lr), __float_as_uint(S.out[lr]), t_qkv);
       ev(4);
       mark();
       // P2: attention.
@@ -626,9 +641,11 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
       // P3: o_proj + residual. Input: the quantized attention output.
       const int ncode = qd / 4, nsc = qd / Lw.out.agroup;
       ok = gemv(Lw.out, nown, [&](int lr) { return r0 + lr; }, S, [&]() {
-        if (!ll_wait(a.ll + ll.attq, ncode, t_att, a.status, [&](int k, uint32_t v) { ((uint32_t*)S.xq)[k] = v; }))
-          return false;
-        if (!ll_wait(a.ll + ll.attq_scales, nsc, t_att, a.status, [&](int k, uint32_t v) { S.xs[k] = __uint_as_float(v); }))
+        // The codes (4 a word) and then the scales: one run of LL words.
+        if (!ll_wait(a.ll + ll.attq, ncode + nsc, t_att, a.status, [&](int k, uint32_t v) {
+              if (k < ncode) ((uint32_t*)S.xq)[k] = v;
+              else ((uint32_t*)S.xs)[k - ncode] = v;
+            }))
           return false;
         ev(8);
         return true;
@@ -662,7 +679,11 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
         if (!ll_wait(a.ll + ll.h, cfg.ffn, t_h, a.status, [&](int k, uint32_t v) { S.xf[k] = __uint_as_float(v); }))
           return false;
         ev(13);
-        norm_quant(cfg.ffn, nullptr, cfg.eps, Lw.down.agroup, Lw.down.half, S);
+        // h, every group at once (no norm): the FFN width is long enough
+        // that a warp per group takes several rounds.
+        __syncthreads();
+        quantize_groups<DT, 4>(S.xf, cfg.ffn, nullptr, nullptr, 1.0f, Lw.down.agroup, Lw.down.half, S.xq, S.xs);
+        __syncthreads();
         ev(14);
         return true;
       }, ev, 25);
@@ -734,7 +755,7 @@ size_t head_smem(const DConfig& cfg) {
 
 // The union region: the largest of the GEMV group dots and scales, the
 // attention scratch, the table stages and the argmax partials.
-size_t union_smem(const DConfig& cfg, int grid, int f16, int tmax) {
+size_t union_smem(const DConfig& cfg, int grid, int f16, int tmax, int kt) {
   const int qd = cfg.heads * 128;
   size_t u = 0;
   const int kmax = std::max(std::max(cfg.d, qd), cfg.ffn);
@@ -744,7 +765,7 @@ size_t union_smem(const DConfig& cfg, int grid, int f16, int tmax) {
   u = std::max(u, (size_t)2 * WSTAGE + (size_t)(WSTAGE / 32) * 8);
   u = std::max(u, (size_t)DW * TAB_STAGES * TAB_ROWS_W * TAB_PITCH);
   u = std::max(u, (size_t)grid * 8);
-  u = std::max(u, attend_smem_floats(cfg.heads / cfg.kv_heads, tmax, f16) * 4);
+  u = std::max(u, attend_smem_floats(cfg.heads / cfg.kv_heads, tmax, f16, kt) * 4);
   return u;
 }
 
@@ -777,7 +798,12 @@ cudaError_t launch_decode(const DecodeArgs& a, int grid, cudaStream_t s) {
   // Per block: at most 512 own rows and 256 ffn units (S.own, S.out).
   if ((a.cfg.d + grid - 1) / grid > 512 || 2 * ((a.cfg.ffn + grid - 1) / grid) > 512) return cudaErrorInvalidValue;
   if (((a.cfg.heads * 128 + 2 * a.cfg.kv_heads * 128) + grid - 1) / grid > 512) return cudaErrorInvalidValue;
-  size_t smem = head_smem(a.cfg) + union_smem(a.cfg, grid, a.cache.f16, tmax);
+  int kt = attend_kt(a.cache.f16, true);
+  size_t smem = head_smem(a.cfg) + union_smem(a.cfg, grid, a.cache.f16, tmax, kt);
+  if (smem > 227 * 1024) {
+    kt = attend_kt(a.cache.f16, false);
+    smem = head_smem(a.cfg) + union_smem(a.cfg, grid, a.cache.f16, tmax, kt);
+  }
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -786,6 +812,7 @@ cudaError_t launch_decode(const DecodeArgs& a, int grid, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
   DecodeArgs args = a;
+  args.key_tile = kt;
   void* params[] = {&args};
   return cudaLaunchCooperativeKernel((const void*)k_decode, dim3(grid), dim3(DT), params, smem, s);
 }

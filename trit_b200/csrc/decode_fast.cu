@@ -201,47 +201,9 @@ __device__ __forceinline__ bool ll_take(int n, uint32_t tag, int* status, Addr a
 }
 
 // ------------------------------------------------------------ quantizer --
-// Quantized::grouped (src/cpu/kernels.rs:769-807) of k values src[i]
-// (times inv * w[i] when w is given: the RmsNorm of layers.rs:135-144;
-// times sc[i] when sc is given) in groups of G: thread t takes values
-// 8t .. 8t + 7 (then 8(t + FT) ...), and the G / 8 threads of a group
-// share its max by shuffles. Codes to q, scales to s (f16-rounded for
-// Q8_0). The codes equal the reference's for the same inputs.
-__device__ void quant_fast(const float* src, int k, const float* w, const float* sc, float inv, int G, bool half,
-                           int8_t* q, float* s) {
-  const int lanes = G / 8;
-  for (int base = 0; base < k; base += 8 * FT) {
-    const int i0 = base + 8 * threadIdx.x;
-    const bool live = i0 < k;
-    float v[8];
-    float m = 0.0f;
-    if (live) {
-      const float4 a = *(const float4*)(src + i0), b = *(const float4*)(src + i0 + 4);
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      if (w) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(v[i], __fmul_rn(inv, w[i0 + i]));
-      }
-      if (sc) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(v[i], sc[i0 + i]);
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
-    }
-    for (int o = 1; o < lanes; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (live) {
-      const float scale = group_scale(m);
-      const float r = __fdiv_rn(1.0f, scale);
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) lo |= (uint32_t)(uint8_t)quantize_value(v[i], r) << (8 * i);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) hi |= (uint32_t)(uint8_t)quantize_value(v[4 + i], r) << (8 * i);
-      *(uint2*)(q + i0) = make_uint2(lo, hi);
-      if ((threadIdx.x & (lanes - 1)) == 0) s[i0 / G] = half ? round_f16(scale) : scale;
-    }
-  }
+__device__ __forceinline__ void quant_fast(const float* src, int k, const float* w, const float* sc, float inv, int G,
+                                           bool half, int8_t* q, float* s) {
+  quantize_groups<FT>(src, k, w, sc, inv, G, half, q, s);
 }
 
 // -------------------------------------------------------------- products --

@@ -82,6 +82,41 @@ __device__ __forceinline__ float rms_inv(float sum, int d, float eps) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)d), eps)));
 }
 
+// Packed f32x2 arithmetic (sm_100): two lanes a instruction, each rounded
+// as the scalar operation (IEEE round to nearest even).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 // ------------------------------------------------------------- warps ----
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -124,6 +159,57 @@ __device__ __forceinline__ float warp_quantize_group(const float (&v)[G / 32], i
 #pragma unroll
   for (int i = 0; i < G / 32; ++i) codes[lane * (G / 32) + i] = (int8_t)quantize_value(v[i], inv);
   return half ? round_f16(scale) : scale;
+}
+
+// Quantized::grouped of k values (kernels.rs:769-807) by a block of NT
+// threads, every group at once: thread t takes VPT (4 or 8) consecutive
+// values from VPT * t (then VPT * (t + NT) ...), and the G / VPT threads of
+// a group (G = 32 or 128) share its max by shuffles. Each value is src[i],
+// times inv * w[i] when w is given (RmsNorm, layers.rs:135-144), times sc[i]
+// when sc is given. Codes to q, scales to s (f16-rounded when `half`). The
+// max of a group does not depend on the order it is taken in, so the codes
+// and scales are those of warp_quantize_group. src, q: 16- and VPT-byte
+// aligned; k a multiple of G.
+template <int NT, int VPT = 8>
+__device__ __forceinline__ void quantize_groups(const float* src, int k, const float* w, const float* sc, float inv,
+                                                int G, bool half, int8_t* q, float* s) {
+  const int lanes = G / VPT;
+  for (int base = 0; base < k; base += VPT * NT) {
+    const int i0 = base + VPT * threadIdx.x;
+    const bool live = i0 < k;
+    float v[VPT];
+    float m = 0.0f;
+    if (live) {
+#pragma unroll
+      for (int j = 0; j < VPT; j += 4) {
+        const float4 a = *(const float4*)(src + i0 + j);
+        v[j] = a.x; v[j + 1] = a.y; v[j + 2] = a.z; v[j + 3] = a.w;
+      }
+      if (w) {
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) v[i] = __fmul_rn(v[i], __fmul_rn(inv, w[i0 + i]));
+      }
+      if (sc) {
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) v[i] = __fmul_rn(v[i], sc[i0 + i]);
+      }
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) m = fmaxf(m, fabsf(v[i]));
+    }
+    for (int o = 1; o < lanes; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (live) {
+      const float scale = group_scale(m);
+      const float r = __fdiv_rn(1.0f, scale);
+#pragma unroll
+      for (int j = 0; j < VPT; j += 4) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) word |= (uint32_t)(uint8_t)quantize_value(v[j + i], r) << (8 * i);
+        *(uint32_t*)(q + i0 + j) = word;
+      }
+      if ((threadIdx.x & (lanes - 1)) == 0) s[i0 / G] = half ? round_f16(scale) : scale;
+    }
+  }
 }
 
 // ------------------------------------------------------------ loads ----

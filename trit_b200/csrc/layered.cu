@@ -764,14 +764,6 @@ __global__ void __launch_bounds__(256) k_table(DTable T, const float* xn, int nb
 // k_table does.
 constexpr int TB_KC = 256;
 
-__device__ __forceinline__ float2 table_fma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
 
 template <int B>
 __global__ void __launch_bounds__(256) k_table_rows(DTable T, const float* xn, int nb, float logit_mult,
@@ -840,7 +832,7 @@ __global__ void __launch_bounds__(256) k_table_rows(DTable T, const float* xn, i
       for (int p = 0; p < B / 2; ++p) {
         const float2 x2 = xr[p];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) acc[a][p] = table_fma2(x2, w2[a], acc[a][p]);
+        for (int a = 0; a < 4; ++a) acc[a][p] = fma2(x2, w2[a], acc[a][p]);
       }
 #pragma unroll
       for (int a = 0; a < 4; ++a) code[a] = next[a];
