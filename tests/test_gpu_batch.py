@@ -38,15 +38,18 @@ def test_batch_matches_oracle_per_stream(mini_models, name, kv):
 
 @pytest.mark.parametrize("name", ["mini_qwen3_q8_0", "mini_mistral_q8_0", "mini_gqa8_q8_0", "mini_mha_q8_0"])
 @pytest.mark.parametrize("kv", ["f32", "f16"])
-def test_one_row_attention_logits_match_oracle(mini_models, name, kv):
+@pytest.mark.parametrize("length", [70, 300])
+def test_one_row_attention_logits_match_oracle(mini_models, name, kv, length):
     """The one-row attention of decode steps (2, 4, 8 and 1 query heads a kv
     head) through the layered decode loop: tokens and logits bit for bit,
-    over cache pages of 64 positions."""
+    over cache pages of 64 positions; 300 prompt ids span several staged
+    key tiles (256 keys a tile for f16, 128 for f32) with odd and even key
+    counts."""
     path = mini_models[name]
     oracle = O.Oracle(path, kv_f16=(kv == "f16"))
-    prompt = np.random.default_rng(41).integers(0, oracle.vocab, size=70).tolist()
+    prompt = np.random.default_rng(41).integers(0, oracle.vocab, size=length).tolist()
     ref = oracle.generate(prompt, 10, trace=True)
-    with CausalLm.load(path, kv=kv, decode="layered", max_context=160) as lm:
+    with CausalLm.load(path, kv=kv, decode="layered", max_context=length + 90) as lm:
         toks, logits = lm.generate_traced(prompt, max_new=10)
     assert toks == ref["tokens"]
     for i in range(len(toks)):

@@ -147,7 +147,7 @@ __device__ void norm_quant(int d, const float* w, float eps, int G, bool half, S
 }
 
 // ------------------------------------------------------------- products --
-constexpr int WSTAGE = 40 * 1024;  // bytes of one weight staging buffer (two of them)
+constexpr int WSTAGE = 48 * 1024;  // bytes of one weight staging buffer (two of them): a block's C1 gate/up rows fit one
 
 __host__ __device__ inline int code_row_bytes(const DMat& W) { return W.kind == kTernary ? W.k / 4 : W.k; }
 __host__ __device__ inline int scale_row_bytes(const DMat& W) {
@@ -161,18 +161,17 @@ __host__ __device__ inline int staged_row_bytes(const DMat& W) {
 // local row lr). The rows' codes and scales stream into shared memory by
 // cp.async in batches of up to WSTAGE bytes, double-buffered; the first
 // batch is issued before `ready()` (the block's wait for its input and its
-// quantization), so the weights travel while the block waits. Warp w takes
-// local rows w, w + DW, ...: its lanes form the i32 group dots from 16-byte
-// chunks, then lane 0 runs the row's group chain of int8.rs:560-570 in
-// order into S.out[lr].
+// quantization), so the weights travel while the block waits. A thread
+// forms whole i32 group dots (a (row, group) pair at a time), then one
+// thread a row runs the row's group chain of int8.rs:560-570 in order into
+// S.out[lr].
 // ev(evbase + 0..2): the first batch's weights in shared memory, its group
 // dots, its chains (event trace only).
 template <class RowOf, class Ready, class Ev>
 __device__ bool gemv(const DMat& Wg, int nrows, RowOf row_of, Shared& S, Ready ready, Ev ev, int evbase) {
   const DMat W = Wg;  // in registers: the loops below store to shared memory, which would force reloads
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int k = W.k, groups = k / W.agroup, lpg = W.agroup / 16, chunks = k / 16;
-  const int lpg_shift = lpg == 2 ? 1 : 3;  // lanes a group: 2 (groups of 32) or 8 (groups of 128)
+  const int k = W.k, groups = k / W.agroup, lpg = W.agroup / 16;  // 16-byte chunks a group: 2 or 8
   const int crow = code_row_bytes(W), srow = scale_row_bytes(W);
   const int cpad = (crow + 15) / 16 * 16, rbytes = staged_row_bytes(W);
   const int per = min(nrows, WSTAGE / rbytes);  // rows a batch (the host checks rbytes <= WSTAGE)
@@ -213,54 +212,43 @@ __device__ bool gemv(const DMat& Wg, int nrows, RowOf row_of, Shared& S, Ready r
     if (b == 0) ev(evbase);
     const uint8_t* src = (b & 1) ? buf1 : buf0;
     const int lr0 = b * per, n = min(per, nrows - lr0);
-    // The batch's (row, chunk) dots. With at least a row per warp, a warp
-    // takes whole rows; with fewer rows, the dots spread over all threads:
-    // thread t takes flat indices t, t + DT, ... Either way the lpg lanes of
-    // a group are adjacent (chunks and DT are multiples of lpg), so a
-    // shuffle sums the group.
-    auto group_dot = [&](int r, int c, int dot) {
-      if ((lane & (lpg - 1)) == 0) {
+    // The batch's group dots: thread t takes the (row, group) pairs t,
+    // t + DT, ... of the batch, each a whole group (lpg 16-byte chunks), so
+    // no lanes wait on each other and a thread's loads go out together.
+    // Integer dots: the order of their terms changes nothing.
+    {
+      const int dr = DT / groups, dg = DT - dr * groups;
+      int r = t / groups, g = t - r * groups;
+      const int total = n * groups;
+#pragma unroll 2
+      for (int idx = t; idx < total; idx += DT) {
         const uint8_t* rowp = src + r * rbytes;
-        const int g = c >> lpg_shift;
-        float ws = W.kind == kQ8_0 ? f16_bits_to_f32(((const uint16_t*)(rowp + cpad))[g])
-                   : W.kind == kInt8Row ? ((const float*)(rowp + cpad))[0]
-                                        : ((const float*)(rowp + cpad))[g];
+        int dot = 0;
+        if (lpg == 2) {
+          const int c = 2 * g;
+          const int4 a0 = ((const int4*)S.xq)[c], a1 = ((const int4*)S.xq)[c + 1];
+          if (W.kind == kTernary) {
+            dot = dot16_ternary(((const uint32_t*)rowp)[c], a0) + dot16_ternary(((const uint32_t*)rowp)[c + 1], a1);
+          } else {
+            dot = dot16(((const int4*)rowp)[c], a0) + dot16(((const int4*)rowp)[c + 1], a1);
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int c = 8 * g + u;
+            const int4 a = ((const int4*)S.xq)[c];
+            dot += W.kind == kTernary ? dot16_ternary(((const uint32_t*)rowp)[c], a) : dot16(((const int4*)rowp)[c], a);
+          }
+        }
+        const float ws = W.kind == kQ8_0 ? f16_bits_to_f32(((const uint16_t*)(rowp + cpad))[g])
+                         : W.kind == kInt8Row ? ((const float*)(rowp + cpad))[0]
+                                              : ((const float*)(rowp + cpad))[g];
         pdot[g * per + r] = __int2float_rn(dot);
         pscl[g * per + r] = __fmul_rn(ws, S.xs[g]);
-      }
-    };
-    if (n >= DW) {
-      for (int r = warp; r < n; r += DW) {
-        const uint8_t* rowp = src + r * rbytes;
-        for (int c0 = 0; c0 < chunks; c0 += 32) {
-          const int c = c0 + lane;
-          int dot = 0;
-          if (c < chunks) {
-            int4 act = ((const int4*)S.xq)[c];
-            if (W.kind == kTernary) dot = dot16_ternary(((const uint32_t*)rowp)[c], act);
-            else dot = dot16(((const int4*)rowp)[c], act);
-          }
-          for (int o = 1; o < lpg; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-          if (c < chunks) group_dot(r, c, dot);
-        }
-      }
-    } else {
-      int r = t / chunks, c = t - r * chunks;
-      const int steps = (n * chunks + DT - 1) / DT;
-      for (int it = 0; it < steps; ++it) {
-        const bool live = r < n;
-        int dot = 0;
-        if (live) {
-          const uint8_t* rowp = src + r * rbytes;
-          int4 act = ((const int4*)S.xq)[c];
-          if (W.kind == kTernary) dot = dot16_ternary(((const uint32_t*)rowp)[c], act);
-          else dot = dot16(((const int4*)rowp)[c], act);
-        }
-        for (int o = 1; o < lpg; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-        if (live) group_dot(r, c, dot);
-        c += DT;
-        while (c >= chunks) {
-          c -= chunks;
+        g += dg;
+        r += dr;
+        if (g >= groups) {
+          g -= groups;
           ++r;
         }
       }

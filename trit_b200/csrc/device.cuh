@@ -60,6 +60,65 @@ __device__ __forceinline__ float seq_sum_squares(const float* v, int n) {
   return s;
 }
 
+// seq_sum_squares with the loads run ahead: the next 16 values are loaded
+// while the current 16 are squared and added, so the adds wait only on
+// each other. The same sum, in the same order. v is 16-byte aligned.
+__device__ __forceinline__ float seq_sum_squares_ahead(const float* v, int n) {
+  const float4* p = (const float4*)v;
+  const int nb = n / 16;
+  float s = 0.0f;
+  float4 a[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) a[u] = nb > 0 ? p[u] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int b = 0; b < nb; ++b) {
+    float4 c[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) c[u] = a[u];
+    if (b + 1 < nb) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = p[4 * (b + 1) + u];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      s = __fadd_rn(s, __fmul_rn(c[u].x, c[u].x));
+      s = __fadd_rn(s, __fmul_rn(c[u].y, c[u].y));
+      s = __fadd_rn(s, __fmul_rn(c[u].z, c[u].z));
+      s = __fadd_rn(s, __fmul_rn(c[u].w, c[u].w));
+    }
+  }
+  for (int i = nb * 16; i < n; ++i) s = __fadd_rn(s, __fmul_rn(v[i], v[i]));
+  return s;
+}
+
+// seq_sum with the loads run ahead as above: the same sum, in the same
+// order. v is 16-byte aligned.
+__device__ __forceinline__ float seq_sum_ahead(const float* v, int n) {
+  const float4* p = (const float4*)v;
+  const int nb = n / 16;
+  float s = 0.0f;
+  float4 a[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) a[u] = nb > 0 ? p[u] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int b = 0; b < nb; ++b) {
+    float4 c[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) c[u] = a[u];
+    if (b + 1 < nb) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = p[4 * (b + 1) + u];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      s = __fadd_rn(s, c[u].x);
+      s = __fadd_rn(s, c[u].y);
+      s = __fadd_rn(s, c[u].z);
+      s = __fadd_rn(s, c[u].w);
+    }
+  }
+  for (int i = nb * 16; i < n; ++i) s = __fadd_rn(s, v[i]);
+  return s;
+}
+
 // A sum left to right (the reference's f32 `sum()`), reading 4 values at a
 // time so that only the adds wait on each other. v is 16-byte aligned.
 __device__ __forceinline__ float seq_sum(const float* v, int n) {

@@ -7,12 +7,14 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <chrono>
 #include <climits>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <functional>
+#include <thread>
 
 namespace trit {
 
@@ -56,6 +58,9 @@ Options Options::parse(const char* text, bool lenient) {
       o.tp_size = count(1, 64);
     } else if (k == "tp_rank") {
       o.tp_rank = count(0, 63);
+    } else if (k == "tp_timeout_s") {
+      if (v.kind != Json::Number || v.num <= 0) throw Error("options: tp_timeout_s must be a positive number");
+      o.tp_timeout_s = v.num;
     } else if (k == "tp_id") {
       if (v.kind != Json::String) throw Error("options: tp_id must be a string");
       o.tp_id = v.str;
@@ -340,9 +345,7 @@ Lm::Lm(const std::string& dir, const Options& o) : opt_(o) {
       if (opt_.tp_id.size() != 2 * sizeof(ncclUniqueId)) throw Error("options: tp_id must be trit_cuda_tp_id's text");
       ncclUniqueId id;
       for (size_t i = 0; i < sizeof id; ++i) id.internal[i] = (char)std::stoi(opt_.tp_id.substr(2 * i, 2), nullptr, 16);
-      ncclComm_t comm = nullptr;
-      nccl_check(nccl().CommInitRank(&comm, opt_.tp_size, id, opt_.tp_rank), "communicator");
-      comm_ = comm;
+      comm_ = nccl_join(id, opt_.tp_size, opt_.tp_rank, opt_.device, opt_.tp_timeout_s);
       if (opt_.decode == "persistent") opt_.decode = "layered";  // the persistent kernel runs a whole model
     }
     load(dir);
@@ -404,7 +407,12 @@ void Lm::release() {
   for (PrefixState* p : prefixes_) p->owner = nullptr;  // their pages go with the pool
   prefixes_.clear();
   cudaSetDevice(opt_.device);
-  if (stream_) cudaStreamSynchronize(stream_);
+  if (stream_) {
+    try {
+      wait();
+    } catch (const std::exception&) {  // the communicator is aborted; the stream has drained
+    }
+  }
   void* bufs[] = {arena_, d_layers_, pool_, page_table_, x_, qkv_, att_, h_, xn_, xq_, xs_, row_stream_, row_pos_, ids_,
                   best_val_, best_idx_, tokens_, logits_, stop_, positions_, dll_, dstatus_, dcount_,
                   trace_, rope_};
@@ -416,8 +424,6 @@ void Lm::release() {
   if (tiles_dev_) cudaFree(tiles_dev_);
   tiles_pinned_ = nullptr;
   tiles_dev_ = nullptr;
-  if (comm_) nccl().CommDestroy((ncclComm_t)comm_);
-  comm_ = nullptr;
   void* batch[] = {batch_last_, batch_cur_, batch_step_, batch_tok_, tc_expanded_, gu_, tc_status_, ffn_scales_, audio_,
                    part_, keys_};
   for (void* b : batch)
@@ -435,6 +441,9 @@ void Lm::release() {
   tc_status_ = nullptr;
   tc_ready_ = false;
   batch_graph_ = nullptr;
+  // After the graph that holds its collectives.
+  if (comm_) nccl().CommDestroy((ncclComm_t)comm_);
+  comm_ = nullptr;
   batch_ready_ = false;
   if (ev_rows_) cudaEventDestroy(ev_rows_);
   ev_rows_ = nullptr;
@@ -777,6 +786,7 @@ void Lm::final_rows(const float* x, int ldx, int nb, float* logits, int* tokens)
   // Each rank's best among its vocabulary rows, as argmax-ordered keys; the
   // largest key over the ranks is the first strict maximum of all rows.
   if (logits) throw Error("logit traces are not kept with tensor parallelism");
+  if (!comm_) throw Error("tensor parallelism: this rank's communicator was aborted; load the model again");
   TRIT_CUDA(launch_final(x, ldx, nb, final_norm_, cfg_, head_, xn_, nullptr, best_val_, best_idx_, tokens, stream_,
                          keys_, tp_.vocab0));
   nccl_check(nccl().AllReduce(keys_, keys_, (size_t)nb, ncclUint64, ncclMax, (ncclComm_t)comm_, stream_),
@@ -785,7 +795,38 @@ void Lm::final_rows(const float* x, int ldx, int nb, float* logits, int* tokens)
   timing_.gpu_launches += 1;
 }
 
+void Lm::wait() {
+  if (!comm_) {
+    if (tp_lost_) throw Error("tensor parallelism: this rank's communicator was aborted; load the model again");
+    TRIT_CUDA(cudaStreamSynchronize(stream_));
+    return;
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t e = cudaStreamQuery(stream_);
+    if (e == cudaSuccess) return;
+    if (e != cudaErrorNotReady) TRIT_CUDA(e);
+    ncclResult_t async = ncclSuccess;
+    nccl().CommGetAsyncError((ncclComm_t)comm_, &async);
+    const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if ((async != ncclSuccess && async != ncclInProgress) || waited > opt_.tp_timeout_s) {
+      // Aborting ends the collectives in flight; the stream then drains.
+      nccl().CommAbort((ncclComm_t)comm_);
+      comm_ = nullptr;
+      tp_lost_ = true;
+      cudaStreamSynchronize(stream_);
+      cudaGetLastError();
+      if (async != ncclSuccess && async != ncclInProgress)
+        throw Error(std::string("tensor parallelism: NCCL reported ") + nccl().GetErrorString(async));
+      throw Error("tensor parallelism: the other ranks did not answer within " +
+                  std::to_string((int)opt_.tp_timeout_s) + " s (a rank failed or left); the communicator is aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
 void Lm::reduce_into_x(int m) {
+  if (!comm_) throw Error("tensor parallelism: this rank's communicator was aborted; load the model again");
   const size_t n = (size_t)m * cfg_.d;
   nccl_check(nccl().AllReduce(part_, part_, n, ncclFloat32, ncclSum, (ncclComm_t)comm_, stream_), "partial sums");
   TRIT_CUDA(launch_add(x_, part_, n, stream_));
@@ -872,7 +913,7 @@ void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* tiles
 // layer l times scales[l] (hidden, :458-463); null clears them.
 void Lm::set_ffn_scales(const float* scales) {
   TRIT_CUDA(cudaSetDevice(opt_.device));
-  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  wait();
   if (scales) {
     if (!ffn_scales_) TRIT_CUDA(cudaMalloc(&ffn_scales_, (size_t)cfg_.layers * cfg_.d * 4));
     TRIT_CUDA(cudaMemcpy(ffn_scales_, scales, (size_t)cfg_.layers * cfg_.d * 4, cudaMemcpyHostToDevice));
@@ -921,7 +962,7 @@ std::vector<int> Lm::generate_additive(const int* ids, size_t n, const float* au
   final_rows(x_ + (size_t)(last_rows_ - 1) * d, d, 1, logits ? logits_ : nullptr, tokens_);
   if (logits) TRIT_CUDA(cudaMemcpyAsync(logits, logits_, (size_t)cfg_.vocab * 4, cudaMemcpyDeviceToHost, stream_));
   TRIT_CUDA(cudaEventRecord(ev_[1], stream_));
-  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  wait();
   int* host = host_rows_;
   host[0] = 0;
   TRIT_CUDA(cudaMemcpyAsync(row_stream_, host, 4, cudaMemcpyHostToDevice, stream_));
@@ -947,7 +988,7 @@ std::vector<int> Lm::generate_additive(const int* ids, size_t n, const float* au
   TRIT_CUDA(cudaEventRecord(ev_[2], stream_));
   std::vector<int> toks(max_new);
   TRIT_CUDA(cudaMemcpyAsync(toks.data(), tokens_, (size_t)max_new * 4, cudaMemcpyDeviceToHost, stream_));
-  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  wait();
   check_tc_status();
   float ms = 0;
   TRIT_CUDA(cudaEventElapsedTime(&ms, ev_[0], ev_[1]));
@@ -978,7 +1019,7 @@ std::vector<int> Lm::bidirectional_tokens(const float* rows, size_t m, size_t fr
   timing_ = Timing{};
   TRIT_CUDA(cudaSetDevice(opt_.device));
   const int d = cfg_.d;
-  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  wait();
   int* host = host_rows_;
   for (size_t r = 0; r < m; ++r) {
     host[r] = 0;
@@ -1014,7 +1055,7 @@ std::vector<int> Lm::bidirectional_tokens(const float* rows, size_t m, size_t fr
   std::vector<int> out(nb);
   TRIT_CUDA(cudaMemcpyAsync(out.data(), tokens_, nb * 4, cudaMemcpyDeviceToHost, stream_));
   TRIT_CUDA(cudaEventRecord(ev_[1], stream_));
-  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  wait();
   check_tc_status();
   float ms = 0;
   TRIT_CUDA(cudaEventElapsedTime(&ms, ev_[0], ev_[1]));
@@ -1060,7 +1101,7 @@ void Lm::setup_tensor_cores() {
   TRIT_CUDA(cudaMalloc(&gu_, (size_t)rows_cap_ * 2 * cfg_.ffn * 4));
   TRIT_CUDA(cudaMalloc(&tc_status_, 4));
   TRIT_CUDA(cudaMemset(tc_status_, 0, 4));
-  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  wait();
   tc_ready_ = true;
 }
 
@@ -1083,7 +1124,7 @@ void Lm::run_prompt(size_t m, int slot, int first, const std::function<void(size
   int* host = host_rows_;
   for (size_t c0 = 0; c0 < m; c0 += rows_cap_) {
     int mc = (int)std::min<size_t>(rows_cap_, m - c0);
-    TRIT_CUDA(cudaStreamSynchronize(stream_));  // the pinned row metadata is reused per chunk
+    wait();  // the pinned row metadata is reused per chunk
     for (int r = 0; r < mc; ++r) {
       host[r] = slot;
       host[rows_cap_ + r] = first + (int)c0 + r;
@@ -1112,7 +1153,7 @@ void Lm::embed_rows(const int* ids, size_t c0, size_t c1, float* x) {
 
 int* Lm::stage_ids(const int* a, size_t na, const int* b, size_t nb) {
   if (na + nb > (size_t)opt_.max_context) throw Error("more prompt ids than max_context");
-  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  wait();
   int* staged = host_rows_ + 2 * rows_cap_;
   if (na) std::memcpy(staged, a, na * 4);
   if (nb) std::memcpy(staged + na, b, nb * 4);
@@ -1203,7 +1244,7 @@ std::vector<int> Lm::finish(int slot, int position, int max_new, const int* stop
   std::vector<int> out;
   clock_.report("prefill");
   if (max_new <= 0) {
-    TRIT_CUDA(cudaStreamSynchronize(stream_));
+    wait();
     check_tc_status();
     return out;
   }
@@ -1229,7 +1270,7 @@ std::vector<int> Lm::finish(int slot, int position, int max_new, const int* stop
   clock_.report("generate");
   std::vector<int> toks(max_new);
   TRIT_CUDA(cudaMemcpyAsync(toks.data(), tokens_, (size_t)max_new * 4, cudaMemcpyDeviceToHost, stream_));
-  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  wait();
   check_tc_status();
   float ms = 0;
   TRIT_CUDA(cudaEventElapsedTime(&ms, ev_[0], ev_[1]));
@@ -1250,7 +1291,7 @@ std::vector<int> Lm::finish(int slot, int position, int max_new, const int* stop
 // position + i and writes tokens_[i + 1]; every step's position is in
 // positions_ from the start, so no step waits for the host.
 void Lm::decode_layered(int slot, int position, int steps, float* trace) {
-  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  wait();
   int* host = host_rows_;
   host[0] = slot;
   int* hp = host_rows_ + 2 * rows_cap_;  // free again: the prompt is in
@@ -1350,7 +1391,7 @@ void Lm::decode_persistent(int slot, int position, int steps, float* trace) {
   if (trace)
     TRIT_CUDA(cudaMemcpyAsync(trace + cfg_.vocab, dtrace + cfg_.vocab, (size_t)steps * cfg_.vocab * 4,
                               cudaMemcpyDeviceToHost, stream_));
-  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  wait();
   if (dphase) {
     std::vector<long long> t((size_t)steps * marks);
     TRIT_CUDA(cudaMemcpy(t.data(), dphase, t.size() * 8, cudaMemcpyDeviceToHost));
@@ -1433,7 +1474,7 @@ void Lm::embed(const int* ids, size_t n, float* out) {
     TRIT_CUDA(cudaMemcpyAsync(ids_, ids + c0, mc * 4, cudaMemcpyHostToDevice, stream_));
     TRIT_CUDA(launch_embed(embed_, ids_, (int)mc, x_, 1.0f, stream_));
     TRIT_CUDA(cudaMemcpyAsync(out + c0 * cfg_.d, x_, mc * cfg_.d * 4, cudaMemcpyDeviceToHost, stream_));
-    TRIT_CUDA(cudaStreamSynchronize(stream_));
+    wait();
   }
 }
 
@@ -1468,7 +1509,7 @@ std::unique_ptr<PrefixState> Lm::prefix(const int* ids, size_t n) {
       const char* own = (const char*)pool_ + full * page_bytes_;  // slot 0, logical page `full`
       TRIT_CUDA(cudaMemcpyAsync(p->partial, own, page_bytes_, cudaMemcpyDeviceToDevice, stream_));
     }
-    TRIT_CUDA(cudaStreamSynchronize(stream_));
+    wait();
     check_tc_status();
   } catch (...) {
     release_prefix(p.get());  // under the caller's lock already
@@ -1537,7 +1578,7 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
   int* hi = batch_host_ + 2 * rows_cap_;
   size_t s = 0, p = start[0];
   while (s < S) {
-    TRIT_CUDA(cudaStreamSynchronize(stream_));  // the pinned staging is reused per chunk
+    wait();  // the pinned staging is reused per chunk
     int mc = 0, top = 0;
     std::vector<std::pair<int, int>> ends;  // (chunk row, stream) of each stream's last prompt row
     while (s < S && mc < rows_cap_) {
@@ -1574,7 +1615,7 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
   // The first token of every stream, then the decode state: stream s sits
   // in slot s at position lens[s] with its last token in batch_cur_.
   clock_.report("batch prefill");
-  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  wait();
   for (size_t i = 0; i < S; ++i) {
     hs[i] = (int)i;
     hp[i] = (int)lens[i];
@@ -1634,7 +1675,7 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
   clock_.report("generate_batch");
   std::vector<int> toks((size_t)max_new * S);
   TRIT_CUDA(cudaMemcpyAsync(toks.data(), batch_tok_, toks.size() * 4, cudaMemcpyDeviceToHost, stream_));
-  TRIT_CUDA(cudaStreamSynchronize(stream_));
+  wait();
   check_tc_status();
   float ms = 0;
   TRIT_CUDA(cudaEventElapsedTime(&ms, ev_[0], ev_[1]));

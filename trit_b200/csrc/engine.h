@@ -42,6 +42,11 @@ struct Options {
   // unique id (hex, from trit_cuda_tp_id on rank 0) the ranks share.
   int tp_size = 1, tp_rank = 0;
   std::string tp_id;
+  // Seconds a rank waits for the others (joining the group, or a step whose
+  // collectives they must answer) before the communicator is aborted and
+  // the call fails: a rank that failed or left ends the others' calls with
+  // an error instead of a hang.
+  double tp_timeout_s = 120.0;
   std::string config_at;         // key path of the settings in config.json (from_tensors' config_at)
   std::string prefix;            // start of every tensor name (from_tensors' prefix)
   // `lenient`: keys other than config_at and prefix are skipped unchecked.
@@ -182,6 +187,10 @@ class Lm {
   std::string cache_identity_;
   TpShard tp_;                  // this rank's shard (size 1: the whole model)
   void* comm_ = nullptr;        // ncclComm_t of the tensor-parallel ranks
+  bool tp_lost_ = false;        // the communicator was aborted: the handle is unusable
+  // Waits for stream_; with tensor parallelism a bounded wait that aborts
+  // the communicator when the other ranks do not answer.
+  void wait();
   float* part_ = nullptr;       // [rows][d] a rank's partial o / down sums
   unsigned long long* keys_ = nullptr;  // [rows] (value, index) keys of each row's best token
   void* arena_ = nullptr;

@@ -40,13 +40,13 @@ __global__ void k_scale(float* x, size_t n, float mult) {
 template <int G>
 __global__ void __launch_bounds__(256) k_norm_quant(const float* x, int d, const float* w, float eps, int half,
                                                     int8_t* xq, float* xs, const float* sc) {
-  extern __shared__ float rowv[];  // [d]
+  extern __shared__ __align__(16) float rowv[];  // [d]
   int r = blockIdx.x;
   const float* row = x + (size_t)r * d;
   __shared__ float s_inv;
   for (int i = threadIdx.x; i < d; i += 256) rowv[i] = row[i];
   __syncthreads();
-  if (threadIdx.x == 0) s_inv = w ? rms_inv(seq_sum_squares(rowv, d), d, eps) : 1.0f;
+  if (threadIdx.x == 0) s_inv = w ? rms_inv(seq_sum_squares_ahead(rowv, d), d, eps) : 1.0f;
   __syncthreads();
   float inv = s_inv;
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(256) k_qk_rope_append(float* qkv, int m, DConf
                                                         const float* k_norm, const float* rope, int rope_rows,
                                                         DCache cache, const int* row_stream, const int* row_pos,
                                                         int layer) {
-  __shared__ float headv[8][128];
+  __shared__ __align__(16) float headv[8][128];
   int r = blockIdx.x;
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qd = cfg.heads * cfg.hd, kvd = cfg.kv_heads * cfg.hd, stride = qd + 2 * kvd;
@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(256) k_qk_rope_append(float* qkv, int m, DConf
         for (int i = 0; i < 4; ++i) headv[warp][lane * 4 + i] = v[i];
         __syncwarp();
         float inv = 0.0f;
-        if (lane == 0) inv = rms_inv(seq_sum_squares(headv[warp], cfg.hd), cfg.hd, cfg.eps);
+        if (lane == 0) inv = rms_inv(seq_sum_squares_ahead(headv[warp], cfg.hd), cfg.hd, cfg.eps);
         inv = __shfl_sync(0xffffffffu, inv, 0);
         __syncwarp();
 #pragma unroll
@@ -607,6 +607,220 @@ __global__ void __launch_bounds__(256) k_attention_rows(const float* qkv, const 
   }
 }
 
+// ------------------------------------------- attention of decode rows ----
+// One row (a stream's next position) per block and kv head: the row's QPK
+// query heads over keys [0, T), with the same operations in the same order
+// as k_attention_rows (each chain starts at 0 and takes its terms in
+// order), laid out for one row so that a staged key or value is converted
+// once for several chains and two chains share one packed f32x2 fma (each
+// lane rounded as the scalar fma).
+//   scores: a task keeps keys j and j + pairs (rows read by neighbouring
+//           threads are neighbours: no bank conflicts) for HG query heads:
+//           per dimension one converted key pair feeds HG packed fmas with
+//           the head's q duplicated as (q, q) in shared memory;
+//   softmax: max and exp a warp per head; the sum in key order by one
+//           thread per head, its loads running ahead of the adds;
+//   values: a task keeps one query head and dimensions (2d, 2d + 1), one
+//           packed fma a key with the probability duplicated.
+// Keys and values are staged KT at a time by cp.async into one buffer
+// (two blocks an SM: while one waits for its tile the other computes;
+// measured faster than two buffers of half the keys, which halve the
+// score tasks a tile).
+template <int QPK, bool F16>
+struct StepShape {
+  static constexpr int HG = QPK >= 2 ? 2 : 1;     // query heads a score task
+  static constexpr int KT = F16 ? 256 : 128;      // keys a staged tile
+  static constexpr int PITCH = F16 ? 68 : 132;    // floats a staged row (16-byte aligned, banks staggered)
+  static size_t smem(int tmax) { return ((size_t)QPK * 256 + (size_t)QPK * tmax + (size_t)KT * PITCH + 8) * 4; }
+};
+
+template <int QPK, bool F16>
+__global__ void __launch_bounds__(256, 2) k_attention_step(const float* qkv, DConfig cfg, DCache cache,
+                                                           const int* row_stream, const int* row_pos, int layer,
+                                                           int tmax, int all_keys, float* att) {
+  using S = StepShape<QPK, F16>;
+  constexpr int HG = S::HG, KT = S::KT, PITCH = S::PITCH;
+  extern __shared__ __align__(16) float sm[];
+  const int r = blockIdx.x, kvh = blockIdx.y, t = threadIdx.x;
+  const int qd = cfg.heads * 128, stride = qd + 2 * cfg.kv_heads * 128;
+  float2* qdup = (float2*)sm;
+  float* sc = sm + QPK * 256;
+  float* kv = sc + (size_t)QPK * tmax;
+  float* inv = kv + KT * PITCH;
+  const int stream = row_stream[r], pos = row_pos[r];
+  const int T = all_keys > 0 ? all_keys : pos + 1;
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
+  for (int i = t; i < QPK * 128; i += 256) {
+    const int h = i / 128, e = i % 128;
+    const float v = __fmul_rn(qkv[(size_t)r * stride + (kvh * QPK + h) * 128 + e], scale);
+    qdup[((h / HG) * 128 + e) * HG + h % HG] = make_float2(v, v);
+  }
+  auto stage = [&](int which, int j0, int n) {
+    constexpr int cshift = F16 ? 4 : 5;
+    constexpr size_t row_bytes = F16 ? 256 : 512;
+    int pg_start = 0, pg_end = -1;
+    const char* base = nullptr;
+    for (int ci = t; ci < (n << cshift); ci += 256) {
+      const int jj = ci >> cshift, cc = ci & ((1 << cshift) - 1), j = j0 + jj;
+      if (j >= pg_end) {
+        const int pgi = j / cache.page_tokens;
+        pg_start = pgi * cache.page_tokens;
+        pg_end = pg_start + cache.page_tokens;
+        const int page = cache.page_table[(size_t)stream * cache.pages_per_stream + pgi];
+        const size_t off = kv_offset(cache, cfg, page, layer, which, kvh, 0);
+        base = F16 ? (const char*)((const __half*)cache.pool + off) : (const char*)((const float*)cache.pool + off);
+      }
+      cp_async16(kv + jj * PITCH + cc * 4, (const int4*)(base + (size_t)(j - pg_start) * row_bytes) + cc);
+    }
+    cp_commit();
+  };
+  auto row8 = [&](int jj, int e, float (&o)[8]) {
+    if (F16) {
+      const uint4 raw = *(const uint4*)((const __half*)(kv + jj * PITCH) + e);
+      const __half2* h = (const __half2*)&raw;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        o[2 * i] = f.x;
+        o[2 * i + 1] = f.y;
+      }
+    } else {
+      const float4 a = *(const float4*)(kv + jj * PITCH + e), b = *(const float4*)(kv + jj * PITCH + e + 4);
+      o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+      o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+    }
+  };
+  const int ntile = (T + KT - 1) / KT;
+  __syncthreads();
+  for (int ti = 0; ti < ntile; ++ti) {
+    const int j0 = ti * KT, n = min(KT, T - j0);
+    stage(0, j0, n);
+    cp_wait_all();
+    __syncthreads();
+    const int pairs = (n + 1) / 2, tasks = pairs * (QPK / HG);
+    for (int it = t; it < tasks; it += 256) {
+      const int g = it / pairs, ja = it % pairs, jb = min(ja + pairs, n - 1);
+      float2 acc[HG];
+#pragma unroll
+      for (int h = 0; h < HG; ++h) acc[h] = make_float2(0.0f, 0.0f);
+      const float2* qg = qdup + g * 128 * HG;
+#pragma unroll 2
+      for (int e = 0; e < 128; e += 8) {
+        float ka[8], kb[8];
+        row8(ja, e, ka);
+        row8(jb, e, kb);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float2 kk = make_float2(ka[c], kb[c]);
+          if (HG == 2) {
+            const float4 qq = *(const float4*)(qg + (e + c) * 2);
+            acc[0] = fma2(make_float2(qq.x, qq.y), kk, acc[0]);
+            acc[HG - 1] = fma2(make_float2(qq.z, qq.w), kk, acc[HG - 1]);
+          } else {
+            acc[0] = fma2(qg[e + c], kk, acc[0]);
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < HG; ++h) {
+        float* srow = sc + (size_t)(g * HG + h) * tmax + j0;
+        srow[ja] = acc[h].x;
+        if (ja + pairs < n) srow[ja + pairs] = acc[h].y;
+      }
+    }
+    __syncthreads();
+  }
+  stage(1, 0, min(KT, T));
+  const int warp = t >> 5, lane = t & 31;
+  for (int h = warp; h < QPK; h += 8) {
+    float* srow = sc + (size_t)h * tmax;
+    float mx = -INFINITY;
+    for (int j = lane; j < T; j += 32) mx = fmaxf(mx, srow[j]);
+    mx = warp_max(mx);
+    for (int j = lane; j < T; j += 32) srow[j] = cephes_exp(__fsub_rn(srow[j], mx));
+  }
+  __syncthreads();
+  if (t < QPK) {
+    inv[t] = __fdiv_rn(1.0f, seq_sum_ahead(sc + (size_t)t * tmax, T));
+  }
+  __syncthreads();
+  for (int h = warp; h < QPK; h += 8) {
+    float* srow = sc + (size_t)h * tmax;
+    const float iv = inv[h];
+    for (int j = lane; j < T; j += 32) srow[j] = __fmul_rn(srow[j], iv);
+  }
+  constexpr int TASKS = QPK * 64;
+  constexpr int PER = (TASKS + 255) / 256;
+  float2 acc[PER];
+#pragma unroll
+  for (int u = 0; u < PER; ++u) acc[u] = make_float2(0.0f, 0.0f);
+  for (int ti = 0; ti < ntile; ++ti) {
+    const int j0 = ti * KT, n = min(KT, T - j0);
+    if (ti > 0) stage(1, j0, n);
+    cp_wait_all();
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int it = t + u * 256;
+      if (it < TASKS) {
+        const int h = it / 64, d = it % 64;
+        const float* pr = sc + (size_t)h * tmax + j0;
+        float2 a = acc[u];
+#pragma unroll 8
+        for (int jj = 0; jj < n; ++jj) {
+          const float p = pr[jj];
+          const float2 v = F16 ? __half22float2(*((const __half2*)(kv + jj * PITCH) + d))
+                               : *(const float2*)(kv + jj * PITCH + 2 * d);
+          a = fma2(make_float2(p, p), v, a);
+        }
+        acc[u] = a;
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int it = t + u * 256;
+    if (it < TASKS) {
+      const int h = it / 64, d = it % 64;
+      *(float2*)(att + (size_t)r * qd + (kvh * QPK + h) * 128 + 2 * d) = acc[u];
+    }
+  }
+}
+
+template <int QPK, bool F16>
+static cudaError_t step_attention(const float* qkv, int m, const DConfig& cfg, const DCache& cache,
+                                  const int* row_stream, const int* row_pos, int layer, int tmax, int all_keys,
+                                  float* att, cudaStream_t s) {
+  static DeviceOnce once;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = once.run(dev, [] {
+    return cudaFuncSetAttribute(k_attention_step<QPK, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  if (e != cudaSuccess) return e;
+  k_attention_step<QPK, F16><<<dim3(m, cfg.kv_heads), 256, StepShape<QPK, F16>::smem(tmax), s>>>(
+      qkv, cfg, cache, row_stream, row_pos, layer, tmax, all_keys, att);
+  return cudaGetLastError();
+}
+
+// The decode-row kernel for this shape, or null when it does not apply
+// (query heads a kv head other than 1, 2, 4, 8; shared memory too small).
+using StepFn = cudaError_t (*)(const float*, int, const DConfig&, const DCache&, const int*, const int*, int, int, int,
+                               float*, cudaStream_t);
+template <bool F16>
+static StepFn step_kernel(int qpk, int tmax) {
+  const size_t limit = 227 * 1024;
+  switch (qpk) {
+    case 1: return StepShape<1, F16>::smem(tmax) <= limit ? step_attention<1, F16> : nullptr;
+    case 2: return StepShape<2, F16>::smem(tmax) <= limit ? step_attention<2, F16> : nullptr;
+    case 4: return StepShape<4, F16>::smem(tmax) <= limit ? step_attention<4, F16> : nullptr;
+    case 8: return StepShape<8, F16>::smem(tmax) <= limit ? step_attention<8, F16> : nullptr;
+    default: return nullptr;
+  }
+}
+
 int attention_tile_rows(const DConfig& cfg, int tmax, int f16) {
   // A block's shared memory (220 KB): two staged K/V tiles, and for every
   // query head of the tile its q row and its scores; at most 16 rows and
@@ -627,6 +841,12 @@ cudaError_t launch_attention_rows(const float* qkv, const int2* tiles, int ntile
   if (RQ > 64 || all_keys > max_tk) return cudaErrorInvalidValue;
   const int tmax = (max_tk + 3) / 4 * 4;
   size_t smem = ((size_t)RQ * 128 + (size_t)RQ * tmax + (size_t)2 * AR_KT * (cache.f16 ? 68 : 132) + RQ) * 4;
+  // One row a block (decode steps): the decode-row kernel where it applies.
+  static const bool legacy_step = getenv("TRIT_ATTENTION_ROWS") != nullptr;  // the row-tile kernel instead
+  if (!tiles && rows_max == 1 && !legacy_step) {
+    StepFn fn = cache.f16 ? step_kernel<true>(qpk, tmax) : step_kernel<false>(qpk, tmax);
+    if (fn) return fn(qkv, ntiles, cfg, cache, row_stream, row_pos, layer, tmax, all_keys, att, s);
+  }
   if (smem > 220 * 1024) return cudaErrorInvalidValue;
   // Blocks of 4 query heads for tiles of 16 or more query heads.
   const bool quad = tiles && RQ >= 16;
@@ -1057,13 +1277,13 @@ cudaError_t launch_qk_rope_append(float* qkv, int m, const DConfig& cfg, const f
 // argmax of every row: token[b].
 __global__ void __launch_bounds__(256) k_final_norm_rows(const float* x, int ldx, int d, const float* w, float eps,
                                                          float* xn) {
-  extern __shared__ float rowv[];  // [d]
+  extern __shared__ __align__(16) float rowv[];  // [d]
   const float* row = x + (size_t)blockIdx.x * ldx;
   float* out = xn + (size_t)blockIdx.x * d;
   __shared__ float s_inv;
   for (int i = threadIdx.x; i < d; i += 256) rowv[i] = row[i];
   __syncthreads();
-  if (threadIdx.x == 0) s_inv = rms_inv(seq_sum_squares(rowv, d), d, eps);
+  if (threadIdx.x == 0) s_inv = rms_inv(seq_sum_squares_ahead(rowv, d), d, eps);
   __syncthreads();
   for (int i = threadIdx.x; i < d; i += 256) out[i] = __fmul_rn(rowv[i], __fmul_rn(s_inv, w[i]));
 }
