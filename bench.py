@@ -442,7 +442,9 @@ def run_decode(args, r: dp.Rank) -> None:
 # Per-step DRAM bytes (read + write) of the dominant kernel from ncu
 # captures, where one was taken for the workload (see profiles/).
 TRAFFIC: dict = {}
-TRAFFIC_EXACT: dict = {"c1": (82.304342e9 + 46.220032e6) / 127}  # profiles/k_decode_c1.md
+# C1: a 15-step capture (read + write per step) plus the KV bytes of the
+# bench's 56 more positions on average (profiles/k_decode_c1.md).
+TRAFFIC_EXACT: dict = {"c1": (9.629315e9 + 11.049728e6) / 15 + 56 * 114688}
 # The batch-64 object of the default line: generations timed (C5 takes
 # ~8 s a generation on one B200).
 BATCH64_STEPS = 2

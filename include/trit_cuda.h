@@ -124,7 +124,9 @@ void trit_cuda_free_text(char *text);
  *                   step in the order of the reference's CPU decoder, so
  *                   logits equal its logits bit for bit. false: the batch-1
  *                   decode sums in tree order and splits attention and
- *                   o_proj by kv head; the int8 activation codes can then
+ *                   o_proj by kv head, and prompt attention runs on the
+ *                   tensor cores (f16 flash attention; f16 cache, pages of
+ *                   a multiple of 64 positions); the int8 activation codes can then
  *                   move where a value sits on a rounding boundary, so
  *                   logits drift (measured up to 5e-2 max-abs, cosine
  *                   >= 0.9999; the reference restatement with only its

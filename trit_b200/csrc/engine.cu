@@ -733,7 +733,11 @@ void Lm::alloc_buffers() {
   // Then the pages kept for prefixes, which any slot's table row may name.
   size_t pages = (size_t)opt_.max_streams * cache_.pages_per_stream;
   prefix_pages_total_ = opt_.prefix_pages >= 0 ? opt_.prefix_pages : cache_.pages_per_stream;
-  TRIT_CUDA(cudaMalloc(&pool_, (pages + prefix_pages_total_) * page_bytes_));
+  pool_pages_ = (size_t)pages + prefix_pages_total_;
+  TRIT_CUDA(cudaMalloc(&pool_, pool_pages_ * page_bytes_));
+  // Zeroed: positions past a stream's end are read (and masked) by the
+  // tensor-core prompt attention, which must see finite values there.
+  TRIT_CUDA(cudaMemset(pool_, 0, pool_pages_ * page_bytes_));
   cache_.pool = pool_;
   table_host_.resize(pages);
   for (size_t i = 0; i < pages; ++i) table_host_[i] = (int)i;
@@ -833,18 +837,23 @@ void Lm::reduce_into_x(int m) {
   timing_.gpu_launches += 1;
 }
 
-void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* tiles) {
+void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* runs) {
   const int d = cfg_.d, qd = cfg_.heads * cfg_.hd, kvd = cfg_.kv_heads * cfg_.hd;
   cudaStream_t s = stream_;
-  // Prompt tiles: attention shares each stream's keys among a tile's rows.
+  // Prompt tiles: a run of one stream's rows is cut into tiles whose rows
+  // share the keys they read (the exact kernel's size, or 128 query rows of
+  // the tensor-core kernel when "exact" is off).
   int ntiles = 0, rows_max = 0;
-  if (tiles && causal_ && !tiles->empty()) {
-    ntiles = (int)tiles->size();
-    for (int i = 0; i < ntiles; ++i) {
-      tiles_pinned_[2 * i] = (*tiles)[i].first;
-      tiles_pinned_[2 * i + 1] = (*tiles)[i].second;
-      rows_max = std::max(rows_max, (*tiles)[i].second);
-    }
+  const bool tc_attention = attention_tc_ && runs && causal_;
+  if (runs && causal_ && !runs->empty()) {
+    const int R = tc_attention ? attention_tc_rows(cfg_) : attention_tile_rows(cfg_, (max_tk + 3) / 4 * 4, cache_.f16);
+    for (const auto& run : *runs)
+      for (int r = 0; r < run.second; r += R) {
+        tiles_pinned_[2 * ntiles] = run.first + r;
+        tiles_pinned_[2 * ntiles + 1] = std::min(R, run.second - r);
+        rows_max = std::max(rows_max, tiles_pinned_[2 * ntiles + 1]);
+        ++ntiles;
+      }
     TRIT_CUDA(cudaMemcpyAsync(tiles_dev_, tiles_pinned_, (size_t)ntiles * 8, cudaMemcpyHostToDevice, s));
   }
   const bool tc = tc_ready_ && m >= opt_.tc_rows;
@@ -874,7 +883,10 @@ void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* tiles
     TRIT_CUDA(launch_qk_rope_append(qkv_, m, cfg_, L.q_norm, L.k_norm, rope_, opt_.max_context, cache_, row_stream_,
                                     row_pos_, l, s));
     clock_.mark("attention", s);
-    if (ntiles)
+    if (ntiles && tc_attention)
+      TRIT_CUDA(launch_attention_tc(kv_map_, qkv_, (const int2*)tiles_dev_, ntiles, cfg_, cache_, row_stream_, row_pos_,
+                                    l, att_, tc_status_, s));
+    else if (ntiles)
       TRIT_CUDA(launch_attention_rows(qkv_, (const int2*)tiles_dev_, ntiles, rows_max, cfg_, cache_, row_stream_,
                                       row_pos_, l, max_tk, att_, s));
     else
@@ -1101,6 +1113,13 @@ void Lm::setup_tensor_cores() {
   TRIT_CUDA(cudaMalloc(&gu_, (size_t)rows_cap_ * 2 * cfg_.ffn * 4));
   TRIT_CUDA(cudaMalloc(&tc_status_, 4));
   TRIT_CUDA(cudaMemset(tc_status_, 0, 4));
+  // "exact": false: prompt attention on the tensor cores (f16 cache, pages
+  // of a multiple of 64 positions), over a TMA view of the whole pool.
+  if (!opt_.exact && attention_tc_supported(cfg_, cache_)) {
+    const size_t rows = pool_pages_ * (size_t)cfg_.layers * 2 * cfg_.kv_heads * cache_.page_tokens;
+    TRIT_CUDA(make_kv_map(&kv_map_, pool_, rows));
+    attention_tc_ = true;
+  }
   wait();
   tc_ready_ = true;
 }
@@ -1133,10 +1152,8 @@ void Lm::run_prompt(size_t m, int slot, int first, const std::function<void(size
     TRIT_CUDA(cudaMemcpyAsync(row_pos_, host + rows_cap_, mc * 4, cudaMemcpyHostToDevice, stream_));
     fill(c0, c0 + mc);
     const int top = first + (int)c0 + mc;
-    const int R = attention_tile_rows(cfg_, (top + 3) / 4 * 4, cache_.f16);
-    std::vector<std::pair<int, int>> tiles;
-    for (int r = 0; r < mc; r += R) tiles.emplace_back(r, std::min(R, mc - r));
-    hidden(mc, top, &tiles);
+    const std::vector<std::pair<int, int>> runs = {{0, mc}};  // one stream
+    hidden(mc, top, &runs);
     last_rows_ = mc;
   }
 }
@@ -1597,16 +1614,15 @@ void Lm::generate_batch(size_t S, const int* const* prompts, const size_t* lens,
     TRIT_CUDA(cudaMemcpyAsync(row_pos_, hp, (size_t)mc * 4, cudaMemcpyHostToDevice, stream_));
     TRIT_CUDA(cudaMemcpyAsync(ids_, hi, (size_t)mc * 4, cudaMemcpyHostToDevice, stream_));
     TRIT_CUDA(launch_embed(embed_, ids_, mc, x_, 1.0f, stream_));
-    // Tiles: runs of rows of one stream, at most R rows each.
-    const int R = attention_tile_rows(cfg_, (top + 3) / 4 * 4, cache_.f16);
-    std::vector<std::pair<int, int>> tiles;
+    // Runs of consecutive rows of one stream.
+    std::vector<std::pair<int, int>> runs;
     for (int r = 0; r < mc;) {
       int e = r + 1;
-      while (e < mc && e - r < R && hs[e] == hs[r]) ++e;
-      tiles.emplace_back(r, e - r);
+      while (e < mc && hs[e] == hs[r]) ++e;
+      runs.emplace_back(r, e - r);
       r = e;
     }
-    hidden(mc, top, &tiles);
+    hidden(mc, top, &runs);
     timing_.gpu_launches += 1;
     for (auto& e : ends)
       TRIT_CUDA(cudaMemcpyAsync(batch_last_ + (size_t)e.second * d, x_ + (size_t)e.first * d, (size_t)d * 4,

@@ -158,7 +158,9 @@ class Lm {
   int* stage_ids(const int* a, size_t na, const int* b, size_t nb);
   // `tiles`: {first row, rows} runs of one stream at consecutive positions
   // (prompt chunks), or null for one row per attention block.
-  void hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* tiles = nullptr);
+  // `runs`: prompt rows as runs of consecutive positions of one stream
+  // (first row, rows), cut into attention tiles here; null for decode rows.
+  void hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* runs = nullptr);
   void setup_tensor_cores();
   // The final norm, the output table and the best token of nb rows at x
   // (row stride ldx) into tokens; with tensor parallelism the ranks' best
@@ -250,6 +252,9 @@ class Lm {
   bool tc_ready_ = false;
   std::vector<TcMap> tc_w_;     // [layer][qkv, out, gate_up, down]
   TcMap tc_x_[3] = {};          // quantized frames of width d, heads * hd, ffn
+  TcMap kv_map_{};              // the KV pool for the tensor-core prompt attention
+  bool attention_tc_ = false;   // "exact": false prompt attention on the tensor cores
+  size_t pool_pages_ = 0;
   int8_t* tc_expanded_ = nullptr;  // int8 codes of ternary layers
   float* gu_ = nullptr;         // [rows][2 ffn] gate|up products before silu * up
   int* tc_status_ = nullptr;

@@ -79,6 +79,15 @@ cudaError_t make_tc_frame_map(TcMap* out, const int8_t* xq, size_t rows_cap, siz
 // y (m x ldy) from W times the quantized frames (xq via bmap, scales xs):
 // kEpOut stores, kEpResid adds (times resid_mult). *status is set when a
 // wait inside the kernel ran out.
+// Prompt attention on the tensor cores ("exact": false; mma.cu): tiles of
+// at most attention_tc_rows() rows of one stream, f16 cache, pages of a
+// multiple of 64 positions.
+bool attention_tc_supported(const DConfig& cfg, const DCache& cache);
+int attention_tc_rows(const DConfig& cfg);
+cudaError_t make_kv_map(TcMap* out, const void* pool, size_t rows);
+cudaError_t launch_attention_tc(const TcMap& kvmap, const float* qkv, const int2* tiles, int ntiles,
+                                const DConfig& cfg, const DCache& cache, const int* row_stream, const int* row_pos,
+                                int layer, float* att, int* status, cudaStream_t s);
 cudaError_t launch_gemm_tc(const TcMap& amap, const TcMap& bmap, const DMat& W, const float* xs, int m, int mode,
                            float* y, int ldy, float resid_mult, int* status, cudaStream_t s);
 // h[m][units] = silu(g[.][u]) * g[.][units + u] for g = [m][2 units].

@@ -979,10 +979,18 @@ __global__ void __launch_bounds__(256) k_table(DTable T, const float* xn, int nb
 // so that a half-warp's 8-byte reads of 16 consecutive k hit 32 distinct
 // banks) and are read as stream pairs: one packed f32x2 fma (each lane
 // rounded as the scalar fma) updates one row's chains of two streams.
-// Codes and scales are read from global memory one k step ahead. The 16
-// lanes of a row then reduce in the order of _mm512_reduce_add_ps, as
-// k_table does.
+// The block's codes and scales of each chunk come through shared memory
+// with the chunk's x values (cp.async, double-buffered), so no thread
+// waits on a global load in the fma loop. The 16 lanes of a row then
+// reduce in the order of _mm512_reduce_add_ps, as k_table does.
 constexpr int TB_KC = 256;
+constexpr int TB_CPITCH = TB_KC + 16;  // bytes a staged code row (rows 4 apart land 16 banks apart)
+constexpr int TB_SPITCH = 32;          // bytes a staged scale row (8 scales of a chunk, f16 or f32)
+
+// Shared memory of k_table_rows<B>, in bytes.
+constexpr size_t table_rows_smem(int B) {
+  return ((size_t)2 * B * TB_KC + (size_t)TB_KC * (B + 2)) * 4 + (size_t)2 * TABLE_ROWS * (TB_CPITCH + TB_SPITCH);
+}
 
 
 template <int B>
@@ -992,10 +1000,14 @@ __global__ void __launch_bounds__(256) k_table_rows(DTable T, const float* xn, i
   constexpr int PB = B + 2;                    // k-major pitch
   extern __shared__ __align__(16) float xb[];  // [2][B][TB_KC] staged, then [TB_KC][PB] k-major
   float* xt = xb + 2 * B * TB_KC;
+  uint8_t* cs = (uint8_t*)(xt + TB_KC * PB);           // [2][TABLE_ROWS][TB_CPITCH] codes
+  uint8_t* ss = cs + 2 * TABLE_ROWS * TB_CPITCH;       // [2][TABLE_ROWS][TB_SPITCH] scales
   __shared__ float fin[B][TABLE_ROWS];
   const int t = threadIdx.x, l = t & 15, rg = t >> 4;
-  const int row0 = blockIdx.x * TABLE_ROWS + rg * 4;
+  const int blk0 = blockIdx.x * TABLE_ROWS;
+  const int row0 = blk0 + rg * 4;
   const int k = T.k;
+  const int sb = T.scale_f16 ? 2 : 4;  // bytes a scale
   auto stage = [&](int buf, int k0) {
     float* dst = xb + (size_t)buf * B * TB_KC;
     const int per = TB_KC / 4;  // 16-byte chunks a stream
@@ -1003,6 +1015,20 @@ __global__ void __launch_bounds__(256) k_table_rows(DTable T, const float* xn, i
       int b = i / per, c = i % per;
       if (b < nb) cp_async16(dst + b * TB_KC + c * 4, xn + (size_t)b * k + k0 + c * 4);
       else *(float4*)(dst + b * TB_KC + c * 4) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    // The block's rows: TB_KC code bytes and TB_KC / 32 scales each (rows
+    // past the table read row 0; their results are never kept).
+    uint8_t* cdst = cs + (size_t)buf * TABLE_ROWS * TB_CPITCH;
+    for (int i = t; i < TABLE_ROWS * (TB_KC / 16); i += 256) {
+      const int r = i / (TB_KC / 16), c = i % (TB_KC / 16), row = blk0 + r < T.n ? blk0 + r : 0;
+      cp_async16(cdst + r * TB_CPITCH + c * 16, T.codes + (size_t)row * k + k0 + c * 16);
+    }
+    uint8_t* sdst = ss + (size_t)buf * TABLE_ROWS * TB_SPITCH;
+    const int sper = TB_KC / 32 * sb / 16;  // 16-byte chunks of a row's scales: 1 (f16) or 2 (f32)
+    for (int i = t; i < TABLE_ROWS * sper; i += 256) {
+      const int r = i / sper, c = i % sper, row = blk0 + r < T.n ? blk0 + r : 0;
+      cp_async16(sdst + r * TB_SPITCH + c * 16,
+                 (const uint8_t*)T.scales + ((size_t)row * (k / 32) + k0 / 32) * sb + c * 16);
     }
     cp_commit();
   };
@@ -1012,12 +1038,8 @@ __global__ void __launch_bounds__(256) k_table_rows(DTable T, const float* xn, i
 #pragma unroll
     for (int p = 0; p < B / 2; ++p) acc[a][p] = make_float2(0.0f, 0.0f);
   bool live[4];
-  const int8_t* crow[4];
 #pragma unroll
-  for (int a = 0; a < 4; ++a) {
-    live[a] = row0 + a < T.n;
-    crow[a] = T.codes + (size_t)(live[a] ? row0 + a : 0) * k;
-  }
+  for (int a = 0; a < 4; ++a) live[a] = row0 + a < T.n;
   const int chunks = k / TB_KC;
   stage(0, 0);
   for (int c = 0; c < chunks; ++c) {
@@ -1033,18 +1055,16 @@ __global__ void __launch_bounds__(256) k_table_rows(DTable T, const float* xn, i
       }
     }
     __syncthreads();
-    int code[4];
-#pragma unroll
-    for (int a = 0; a < 4; ++a) code[a] = crow[a][c * TB_KC + l];
+    const int8_t* crow = (const int8_t*)cs + (size_t)(c & 1) * TABLE_ROWS * TB_CPITCH + rg * 4 * TB_CPITCH;
+    const uint8_t* srow = ss + (size_t)(c & 1) * TABLE_ROWS * TB_SPITCH + rg * 4 * TB_SPITCH;
     for (int st = 0; st < TB_KC / 16; ++st) {
-      const int kk = st * 16 + l, kg = c * TB_KC + kk;
-      int next[4];
-#pragma unroll
-      for (int a = 0; a < 4; ++a) next[a] = (st + 1 < TB_KC / 16) ? crow[a][kg + 16] : 0;
+      const int kk = st * 16 + l;
       float2 w2[4];
 #pragma unroll
       for (int a = 0; a < 4; ++a) {
-        const float w = __fmul_rn((float)code[a], table_scale(T, live[a] ? row0 + a : 0, kg / 32));
+        const uint8_t* sp = srow + a * TB_SPITCH;
+        const float scale = T.scale_f16 ? __half2float(((const __half*)sp)[st >> 1]) : ((const float*)sp)[st >> 1];
+        const float w = __fmul_rn((float)crow[a * TB_CPITCH + kk], scale);
         w2[a] = make_float2(w, w);
       }
       const float2* xr = (const float2*)(xt + kk * PB);
@@ -1054,8 +1074,6 @@ __global__ void __launch_bounds__(256) k_table_rows(DTable T, const float* xn, i
 #pragma unroll
         for (int a = 0; a < 4; ++a) acc[a][p] = fma2(x2, w2[a], acc[a][p]);
       }
-#pragma unroll
-      for (int a = 0; a < 4; ++a) code[a] = next[a];
     }
     __syncthreads();
   }
@@ -1301,8 +1319,8 @@ static cudaError_t configure_tables() {
       cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
       if (r != cudaSuccess) return r;
     }
-    const int rows16 = (int)(((size_t)2 * 16 * TB_KC + (size_t)TB_KC * 18) * 4);
-    const int rows32 = (int)(((size_t)2 * 32 * TB_KC + (size_t)TB_KC * 34) * 4);
+    const int rows16 = (int)table_rows_smem(16);
+    const int rows32 = (int)table_rows_smem(32);
     cudaError_t r = cudaFuncSetAttribute(k_table_rows<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, rows16);
     if (r != cudaSuccess) return r;
     return cudaFuncSetAttribute(k_table_rows<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, rows32);
@@ -1323,7 +1341,7 @@ static cudaError_t table_pass(const DTable& T, const float* xn, int nb, float mu
 template <int B>
 static cudaError_t table_rows_pass(const DTable& T, const float* xn, int nb, float mult, float* logits,
                                    float* best_val, int* best_idx, cudaStream_t s) {
-  size_t smem = ((size_t)2 * B * TB_KC + (size_t)TB_KC * (B + 2)) * 4;
+  size_t smem = table_rows_smem(B);
   cudaError_t e = configure_tables();
   if (e != cudaSuccess) return e;
   int blocks = table_blocks(T.n);

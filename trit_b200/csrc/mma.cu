@@ -521,6 +521,307 @@ __global__ void k_silu_pairs(const float* g, int m, int units, float* h) {
 
 // Bits 2s..2s+1 of byte j of word w hold the code of k = 16 w + 4 s + j
 // (pack_span, src/cpu/kernels.rs:624-628); the int8 value is code - 1.
+// ------------------------------------------ prompt attention, f16 MMA ----
+// The `"exact": false` prompt attention: causal GQA attention of a tile of
+// 128 query rows (128 / qpk consecutive positions of one stream, each with
+// the qpk query heads of one kv head) over the stream's paged f16 keys and
+// values, flash-style on the tensor cores:
+//   S = Q K^T   tcgen05.mma kind::f16 (M 128 rows, N 128 keys, K 128 dims),
+//               f32 in one of two TMEM buffers;
+//   softmax     a thread a row: running max and sum, exp2, P rounded to f16
+//               into shared memory (K-major, 128-byte swizzle), O rescaled
+//               in TMEM when its row's max grows;
+//   O += P V    tcgen05.mma kind::f16 (N 128 dims, K 128 keys), V read
+//               MN-major straight from the cache's layout.
+// Warp 0 loads key/value tiles by TMA (two stages, one 64-row box per cache
+// page and 64-dimension half), warp 1 issues the MMAs, warps 2-5 run the
+// softmax. The sums' order differs from the reference's (the tensor cores'
+// order, per-tile softmax, f16 P), so this path is not bit-exact. Every wait
+// is bounded in time and reports through the status word.
+constexpr int FA_ROWS = 128;                 // query rows a CTA (TMEM lanes)
+constexpr int FA_KEYS = 128;                 // keys a tile (two cache pages of 64)
+constexpr int FA_THREADS = 64 + 128;
+constexpr int FA_TILE = FA_KEYS * 256;       // bytes of a K or V tile (f16, 128 dims)
+constexpr int FA_HALF = FA_KEYS * 128;       // one 64-dimension half of it
+constexpr uint32_t FA_TMEM_COLS = 512;       // S0 | S1 | O (128 columns each)
+constexpr int FA_PAD = 4096;                 // slack after the last tile (shared memory)
+
+struct FaSmem {
+  uint64_t full[2], empty[2], sfull[2], sfree[2], qfull, pfull, ofull, drain;
+  uint32_t tmem;
+  int abort;
+};
+
+__host__ __device__ constexpr uint32_t idesc_f16(bool b_mn_major) {
+  return (1u << 4) | (b_mn_major ? (1u << 16) : 0u) | ((uint32_t)(FA_KEYS >> 3) << 17) | ((uint32_t)(FA_ROWS >> 4) << 24);
+}
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(mask0), "r"(mask1), "r"(mask2), "r"(mask3));
+}
+// MN-major operand with the 128-byte swizzle: 64-element atoms along MN
+// (the leading offset between them), 8-row groups along K 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t addr, uint32_t mn_atom_bytes) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((mn_atom_bytes >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Row r (128 values, f32 -> f16) into a K-major, 128-byte-swizzled tile of
+// 128 rows: values 64h.. of the row in half h, 16-byte chunk c of a row at
+// chunk c ^ (r % 8).
+__device__ __forceinline__ void put_row_f16(uint8_t* tile, int r, const float (&v)[128]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __half2 p = __floats2half2_rn(v[64 * h + 8 * c + 2 * i], v[64 * h + 8 * c + 2 * i + 1]);
+        w[i] = *(const uint32_t*)&p;
+      }
+      *(uint4*)(tile + h * FA_HALF + r * 128 + ((c ^ (r & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+__global__ void __launch_bounds__(FA_THREADS, 1)
+    k_attention_tc(const __grid_constant__ CUtensorMap kvmap, const float* qkv, const int2* tiles, DConfig cfg,
+                   DCache cache, const int* row_stream, const int* row_pos, int layer, float* att, int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* q_s = base;                 // [2 halves][128 rows][128 B]
+  uint8_t* p_s = q_s + 2 * FA_HALF;    // the same layout for P
+  uint8_t* kv_s = p_s + 2 * FA_HALF;   // [2 stages][K tile | V tile]
+  FaSmem* S = (FaSmem*)(kv_s + 2 * 2 * FA_TILE + FA_PAD);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qpk = cfg.heads / cfg.kv_heads, kvh = blockIdx.y;
+  const int2 tile = tiles[blockIdx.x];
+  const int r0 = tile.x, R = tile.y;
+  const int stream = row_stream[r0], p0 = row_pos[r0];
+  const int nt = (p0 + R - 1) / FA_KEYS + 1;  // key tiles: keys [0, last position]
+  volatile int* abort = &S->abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&S->full[s], 1);
+      mbar_init(&S->empty[s], 1);
+      mbar_init(&S->sfull[s], 1);
+      mbar_init(&S->sfree[s], 128);
+    }
+    mbar_init(&S->qfull, 128);
+    mbar_init(&S->pfull, 128);
+    mbar_init(&S->ofull, 1);
+    mbar_init(&S->drain, 1);
+    S->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S->tmem)),
+                 "r"(FA_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = S->tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int j = 0; j < nt; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&S->empty[s], ((j >> 1) & 1) ^ 1, abort)) break;
+        mbar_expect_tx(&S->full[s], 2 * FA_TILE);
+        uint8_t* kt = kv_s + s * 2 * FA_TILE;
+        for (int pp = 0; pp < 2; ++pp) {
+          const int key = j * FA_KEYS + pp * 64, pgi = key / cache.page_tokens, tok = key % cache.page_tokens;
+          int page = pgi < cache.pages_per_stream ? cache.page_table[(size_t)stream * cache.pages_per_stream + pgi] : 0;
+          if (page < 0) page = 0;
+          for (int which = 0; which < 2; ++which) {
+            const int row = (((page * cfg.layers + layer) * 2 + which) * cfg.kv_heads + kvh) * cache.page_tokens + tok;
+            for (int h = 0; h < 2; ++h)
+              tma_load_2d(kt + which * FA_TILE + h * FA_HALF + pp * 64 * 128, &kvmap, &S->full[s], h * 128, row);
+          }
+        }
+        issued = j + 1;
+      }
+      if (*abort) {
+        for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j) {
+          long long t0 = now_ns();
+          while (!mbar_test(&S->full[j & 1], (j >> 1) & 1) && now_ns() - t0 < TC_WAIT_NS) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t qa = smem_u32(q_s), pa = smem_u32(p_s), kva = smem_u32(kv_s);
+      auto pv = [&](int j) -> bool {
+        if (!mbar_wait(&S->pfull, j & 1, abort)) return false;
+        fence_after();
+        const uint32_t va = kva + (j & 1) * 2 * FA_TILE + FA_TILE;
+#pragma unroll
+        for (int i = 0; i < FA_KEYS / 16; ++i)
+          mma_f16(tmem + 256, smem_desc_sw128(pa + (i >> 2) * FA_HALF + (i & 3) * 32),
+                  smem_desc_sw128_mn(va + i * 2048, FA_HALF), idesc_f16(true), (j > 0 || i > 0) ? 1u : 0u);
+        mma_commit(&S->ofull);
+        mma_commit(&S->empty[j & 1]);
+        return true;
+      };
+      bool ok = mbar_wait(&S->qfull, 0, abort);
+      for (int j = 0; j < nt && ok; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&S->full[s], (j >> 1) & 1, abort) || !mbar_wait(&S->sfree[s], ((j >> 1) & 1) ^ 1, abort)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const uint32_t ka = kva + s * 2 * FA_TILE;
+#pragma unroll
+        for (int i = 0; i < 128 / 16; ++i)
+          mma_f16(tmem + s * 128, smem_desc_sw128(qa + (i >> 2) * FA_HALF + (i & 3) * 32),
+                  smem_desc_sw128(ka + (i >> 2) * FA_HALF + (i & 3) * 32), idesc_f16(false), i > 0 ? 1u : 0u);
+        mma_commit(&S->sfull[s]);
+        if (j > 0) ok = pv(j - 1);
+      }
+      if (ok) pv(nt - 1);
+      mma_commit(&S->drain);
+      long long t0 = now_ns();
+      while (!mbar_test(&S->drain, 0) && now_ns() - t0 < TC_WAIT_NS) {
+      }
+    }
+  } else {
+    // Softmax: thread q is query row q (TMEM lane q).
+    // A warp reaches the TMEM lanes of its quarter (warp % 4) only.
+    const int q = (warp & 3) * 32 + lane, i = q / qpk, h = q % qpk;
+    const bool valid = i < R;
+    const int pos = valid ? row_pos[r0 + i] : p0;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const int qd = cfg.heads * 128, stride = qd + 2 * cfg.kv_heads * 128;
+    {
+      float v[128];
+      const float scale = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
+      const float* src = qkv + (size_t)(r0 + (valid ? i : 0)) * stride + (kvh * qpk + h) * 128;
+#pragma unroll
+      for (int d = 0; d < 128; d += 4) {
+        const float4 x = valid ? *(const float4*)(src + d) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        v[d] = __fmul_rn(x.x, scale);
+        v[d + 1] = __fmul_rn(x.y, scale);
+        v[d + 2] = __fmul_rn(x.z, scale);
+        v[d + 3] = __fmul_rn(x.w, scale);
+      }
+      put_row_f16(q_s, q, v);
+    }
+    fence_async_smem();
+    mbar_arrive(&S->qfull);
+    const float log2e = 1.4426950408889634f;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nt && ok; ++j) {
+      const int s = j & 1;
+      // Warp-uniform waits: the TMEM loads and stores below are warp-wide.
+      if (!__all_sync(0xffffffffu, mbar_wait(&S->sfull[s], (j >> 1) & 1, abort))) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      float v[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld<32>(lane_base + s * 128 + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v[32 * c + k] = __uint_as_float(r[k]);
+      }
+      fence_before();
+      mbar_arrive(&S->sfree[s]);
+      // Causal mask, then the tile's max.
+      float mt = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < 128; ++k) {
+        if (j * FA_KEYS + k > pos) v[k] = -INFINITY;
+        mt = fmaxf(mt, v[k]);
+      }
+      const float mn = fmaxf(m, mt);
+      const float alpha = exp2f((m - mn) * log2e);
+      float sum = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 128; ++k) {
+        v[k] = exp2f((v[k] - mn) * log2e);
+        sum += v[k];
+      }
+      l = l * alpha + sum;
+      m = mn;
+      if (j > 0) {
+        // O holds tiles 0..j-1 once PV j-1 is done; it then scales by alpha.
+        if (!__all_sync(0xffffffffu, mbar_wait(&S->ofull, (j - 1) & 1, abort))) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld<32>(lane_base + 256 + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int k = 0; k < 32; ++k) r[k] = __float_as_uint(__uint_as_float(r[k]) * alpha);
+            tmem_st32(lane_base + 256 + c * 32, r);
+          }
+          tmem_wait_st();
+        }
+      }
+      put_row_f16(p_s, q, v);
+      fence_async_smem();
+      fence_before();
+      mbar_arrive(&S->pfull);
+    }
+    if (ok && __all_sync(0xffffffffu, mbar_wait(&S->ofull, (nt - 1) & 1, abort))) {
+      fence_after();
+      const float inv = 1.0f / l;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld<32>(lane_base + 256 + c * 32, r);
+        tmem_wait_ld();
+        if (valid) {
+          float* dst = att + (size_t)(r0 + i) * qd + (kvh * qpk + h) * 128 + c * 32;
+#pragma unroll
+          for (int k = 0; k < 32; k += 4)
+            *(float4*)(dst + k) = make_float4(__uint_as_float(r[k]) * inv, __uint_as_float(r[k + 1]) * inv,
+                                              __uint_as_float(r[k + 2]) * inv, __uint_as_float(r[k + 3]) * inv);
+        }
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(FA_TMEM_COLS) : "memory");
+  }
+  if (threadIdx.x == 0 && S->abort) atomicExch(status, 1);
+}
+
 __global__ void k_expand_ternary(const uint32_t* words, size_t n, int k, int8_t* out) {
   const int wpr = k / 16;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n * wpr; i += (size_t)gridDim.x * blockDim.x) {
@@ -649,6 +950,36 @@ cudaError_t launch_gemm_tc(const TcMap& amap, const TcMap& bmap, const DMat& W, 
   if (tile == 16) return launch_tc_n<16>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
   if (tile == 32) return launch_tc_n<32>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
   return launch_tc_n<64>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
+}
+
+bool attention_tc_supported(const DConfig& cfg, const DCache& cache) {
+  const int qpk = cfg.heads / cfg.kv_heads;
+  return cache.f16 && cfg.hd == 128 && cache.page_tokens % 64 == 0 && (qpk == 1 || qpk == 2 || qpk == 4 || qpk == 8);
+}
+
+int attention_tc_rows(const DConfig& cfg) { return FA_ROWS / (cfg.heads / cfg.kv_heads); }
+
+// The key/value pool as a 2-D byte view for TMA: rows of 256 bytes (one
+// key or value, 128 f16), boxes of 64 rows x 128 bytes (one cache page's
+// rows, one half of the dimensions), 128-byte swizzle.
+cudaError_t make_kv_map(TcMap* out, const void* pool, size_t rows) { return make_tc_map(out, pool, rows, 256, 64); }
+
+cudaError_t launch_attention_tc(const TcMap& kvmap, const float* qkv, const int2* tiles, int ntiles,
+                                const DConfig& cfg, const DCache& cache, const int* row_stream, const int* row_pos,
+                                int layer, float* att, int* status, cudaStream_t s) {
+  if (!attention_tc_supported(cfg, cache) || ntiles <= 0) return cudaErrorInvalidValue;
+  const size_t smem = 1024 + 4 * (size_t)FA_HALF + 4 * (size_t)FA_TILE + FA_PAD + sizeof(FaSmem);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static DeviceOnce once;
+  e = once.run(dev, [smem] {
+    return cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  });
+  if (e != cudaSuccess) return e;
+  k_attention_tc<<<dim3(ntiles, cfg.kv_heads), FA_THREADS, smem, s>>>(*(const CUtensorMap*)&kvmap, qkv, tiles, cfg,
+                                                                       cache, row_stream, row_pos, layer, att, status);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_expand_ternary(const DMat& W, int8_t* out, cudaStream_t s) {
