@@ -49,6 +49,7 @@ def test_tc_prompt_attention_logits_near_oracle(mini_models, name, length):
         assert cos >= TC_MIN_COS, (i, cos)
         if toks[i] != ref["tokens"][i]:
             break
+    print(f"{name} prompt {length}: max |dlogit| {worst:.4g}")
     assert worst <= TC_MAX_ABS, worst
     gaps = [float(np.sort(np.asarray(l))[-1] - np.sort(np.asarray(l))[-2]) for l in ref["logits"]]
     _agree_until_gap(toks, ref["tokens"], gaps, 2 * worst + 1e-6)
