@@ -383,7 +383,7 @@ def measure(w: dict, args, r: dp.Rank, steps: int, warmup: int, decode: str, exa
     fields = {
         "metric": w["metric"], "value": value, "unit": "tok/s", "n_gpus": r.world,
         "steps": steps, "warmup": warmup, "ms_per_step": wall_max * 1e3 / steps,
-        "config": {"workload": w["workload"], "model": w["model"], "global_batch": S * r.world,
+        "config": {"workload": w["workload"], "model": w["model"], "global_batch": S * r.world // tp,
                    "seq_len": prompt_len + w["new"], "parallelism": (f"dp{r.world} (independent streams, no collective)" if tp == 1 else
                                    f"tp{tp} x dp{r.world // tp} (NCCL all-reduce of o/down partials, argmax keys)"),
                    "decode": decode if w["kind"] != "batch" else "batched", "exact": exact, "kv_cache": args.kv,
