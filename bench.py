@@ -324,6 +324,8 @@ def measure(w: dict, args, r: dp.Rank, steps: int, warmup: int, decode: str, exa
         opts.update(max_streams=S, prefill_rows=max(4096, S))
     if args.tc_rows is not None:
         opts.update(tc_rows=args.tc_rows)
+    if getattr(args, "tc_f16", False):
+        opts.update(tc_f16=True)
     if args.prefill_rows is not None:
         opts.update(prefill_rows=args.prefill_rows)
     else:
@@ -582,6 +584,7 @@ def main() -> None:
                     help="the tree-order persistent decode (\"exact\": false) instead of the default exact one")
     ap.add_argument("--no-batch64", action="store_true", help="leave the C5 batch-64 object out of the C1 line")
     ap.add_argument("--tc-rows", type=int, help="rows from which products use the tensor cores (engine option)")
+    ap.add_argument("--tc-f16", action="store_true", help="f16-operand tensor-core products for Q8_0 layers (engine option)")
     ap.add_argument("--prefill-rows", type=int, help="rows a prompt pass (engine option)")
     ap.add_argument("--kv", default="f16")
     ap.add_argument("--tp", type=int, default=1,

@@ -101,6 +101,11 @@ void trit_cuda_free_text(char *text);
  *   "tensor_cores": true (default on sm_100) or false: products of
  *                   "tc_rows" rows or more on the tensor cores
  *   "tc_rows":      rows from which a product uses the tensor cores (64)
+ *   "tc_f16":       false (default) or true: Q8_0 products on the tensor
+ *                   cores take their codes as f16 (exact; the MMA makes the
+ *                   group dots as exact f32), at the cost of an f16 copy of
+ *                   the Q8_0 layers' codes (2 bytes a weight); measured
+ *                   slower than the int8 MMA on C5 (5045 against 5268 tok/s)
  *   "tp_size", "tp_rank", "tp_id": tensor parallelism over tp_size ranks,
  *                   one process (or thread) and GPU each: every rank loads
  *                   with the same tp_id (trit_cuda_tp_id's text, made once
@@ -112,6 +117,10 @@ void trit_cuda_free_text(char *text);
  *                   output rows through NCCL (all-reduce). Greedy steps run
  *                   the layered kernels; logit traces, generate_additive
  *                   and bidirectional_tokens are not available
+ *   "tp_timeout_s": seconds a rank waits for the others (joining, or a call
+ *                   whose collectives they must answer) before it aborts
+ *                   the communicator and the call fails (120); the handle
+ *                   is unusable afterwards
  *   "weight_cache": false (default) or true: keep the weights' device
  *                   layout in a file (in "cache_dir", default
  *                   <model_dir>/.trit_cuda) on the first load and read it

@@ -58,6 +58,9 @@ Options Options::parse(const char* text, bool lenient) {
       o.tp_size = count(1, 64);
     } else if (k == "tp_rank") {
       o.tp_rank = count(0, 63);
+    } else if (k == "tc_f16") {
+      if (v.kind != Json::Bool) throw Error("options: tc_f16 must be true or false");
+      o.tc_f16 = v.b;
     } else if (k == "tp_timeout_s") {
       if (v.kind != Json::Number || v.num <= 0) throw Error("options: tp_timeout_s must be a positive number");
       o.tp_timeout_s = v.num;
@@ -424,6 +427,11 @@ void Lm::release() {
   if (tiles_dev_) cudaFree(tiles_dev_);
   tiles_pinned_ = nullptr;
   tiles_dev_ = nullptr;
+  if (tc_w16_buf_) cudaFree(tc_w16_buf_);
+  if (xq16_) cudaFree(xq16_);
+  tc_w16_buf_ = nullptr;
+  xq16_ = nullptr;
+  tc_f16_ = false;
   void* batch[] = {batch_last_, batch_cur_, batch_step_, batch_tok_, tc_expanded_, gu_, tc_status_, ffn_scales_, audio_,
                    part_, keys_};
   for (void* b : batch)
@@ -858,18 +866,27 @@ void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* runs)
   }
   const bool tc = tc_ready_ && m >= opt_.tc_rows;
   // One product: the tensor-core kernel for enough rows, else the GEMV.
-  auto product = [&](int l, int which, const DMat& W, const TcMap& xmap, int mode, float* y, int ldy, float mult) {
+  // xi: the width of the product's input (0: d, 1: heads * hd, 2: ffn).
+  auto product = [&](int l, int which, const DMat& W, int xi, int mode, float* y, int ldy, float mult) {
     if (!tc) {
       TRIT_CUDA(launch_gemv(W, xq_, xs_, m, mode, y, ldy, mult, s));
       return;
     }
-    const TcMap& wmap = tc_w_[(size_t)l * 4 + which];
+    // Q8_0 layers with an f16 copy of their codes: the frames' codes as f16
+    // too, and the exact f16 MMA.
+    const bool f16 = tc_f16_ && W.kind == kQ8_0;
+    if (f16) {
+      TRIT_CUDA(launch_codes_f16(xq_, (size_t)m * W.k, xq16_, s));
+      timing_.gpu_launches += 1;
+    }
+    const TcMap& wmap = f16 ? tc_w16_[(size_t)l * 4 + which] : tc_w_[(size_t)l * 4 + which];
+    const TcMap& xmap = f16 ? tc_x16_[xi] : tc_x_[xi];
     if (mode == kEpSilu) {
-      TRIT_CUDA(launch_gemm_tc(wmap, xmap, W, xs_, m, kEpOut, gu_, W.n, 1.0f, tc_status_, s));
+      TRIT_CUDA(launch_gemm_tc(wmap, xmap, W, xs_, m, kEpOut, gu_, W.n, 1.0f, tc_status_, s, f16));
       TRIT_CUDA(launch_silu_pairs(gu_, m, W.n / 2, y, s));
       timing_.gpu_launches += 1;
     } else {
-      TRIT_CUDA(launch_gemm_tc(wmap, xmap, W, xs_, m, mode, y, ldy, mult, tc_status_, s));
+      TRIT_CUDA(launch_gemm_tc(wmap, xmap, W, xs_, m, mode, y, ldy, mult, tc_status_, s, f16));
     }
   };
   if (cfg_.embedding_multiplier != 1.0f) TRIT_CUDA(launch_scale(x_, (size_t)m * d, cfg_.embedding_multiplier, s));
@@ -878,7 +895,7 @@ void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* runs)
     clock_.mark("norm+quant", s);
     TRIT_CUDA(launch_norm_quant(x_, m, d, L.norm_attn, cfg_.eps, L.qkv.agroup, L.qkv.half, xq_, xs_, s));
     clock_.mark("qkv", s);
-    product(l, 0, L.qkv, tc_x_[0], kEpOut, qkv_, qd + 2 * kvd, 1.0f);
+    product(l, 0, L.qkv, 0, kEpOut, qkv_, qd + 2 * kvd, 1.0f);
     clock_.mark("qk norm+rope+append", s);
     TRIT_CUDA(launch_qk_rope_append(qkv_, m, cfg_, L.q_norm, L.k_norm, rope_, opt_.max_context, cache_, row_stream_,
                                     row_pos_, l, s));
@@ -897,24 +914,24 @@ void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* runs)
     clock_.mark("o", s);
     if (tp_.size > 1) {
       // A rank's heads give a partial sum of o; the ranks' sum joins x.
-      product(l, 1, L.out, tc_x_[1], kEpOut, part_, d, 1.0f);
+      product(l, 1, L.out, 1, kEpOut, part_, d, 1.0f);
       reduce_into_x(m);
     } else {
-      product(l, 1, L.out, tc_x_[1], kEpResid, x_, d, cfg_.residual_multiplier);
+      product(l, 1, L.out, 1, kEpResid, x_, d, cfg_.residual_multiplier);
     }
     clock_.mark("norm+quant", s);
     TRIT_CUDA(launch_norm_quant(x_, m, d, L.norm_mlp, cfg_.eps, L.gate_up.agroup, L.gate_up.half, xq_, xs_, s,
                                 L.ffn_scale));
     clock_.mark("gate_up", s);
-    product(l, 2, L.gate_up, tc_x_[0], kEpSilu, h_, cfg_.ffn, 1.0f);
+    product(l, 2, L.gate_up, 0, kEpSilu, h_, cfg_.ffn, 1.0f);
     clock_.mark("norm+quant", s);
     TRIT_CUDA(launch_norm_quant(h_, m, cfg_.ffn, nullptr, cfg_.eps, L.down.agroup, L.down.half, xq_, xs_, s));
     clock_.mark("down", s);
     if (tp_.size > 1) {
-      product(l, 3, L.down, tc_x_[2], kEpOut, part_, d, 1.0f);
+      product(l, 3, L.down, 2, kEpOut, part_, d, 1.0f);
       reduce_into_x(m);
     } else {
-      product(l, 3, L.down, tc_x_[2], kEpResid, x_, d, cfg_.residual_multiplier);
+      product(l, 3, L.down, 2, kEpResid, x_, d, cfg_.residual_multiplier);
     }
     clock_.mark(nullptr, s);
   }
@@ -1110,6 +1127,35 @@ void Lm::setup_tensor_cores() {
   const size_t rows8 = (size_t)(rows_cap_ + 63) / 64 * 64;
   const int widths[3] = {d, qd, cfg_.ffn};
   for (int i = 0; i < 3; ++i) TRIT_CUDA(make_tc_frame_map(&tc_x_[i], xq_, rows8, (size_t)widths[i]));
+  // The f16 form of the Q8_0 products (exact f32 dots from the tensor cores,
+  // no integer bias in the fold): an f16 copy of each Q8_0 layer's codes,
+  // and an f16 buffer for the frames' codes.
+  if (opt_.tc_f16) {
+    size_t bytes = 0;
+    for (const DLayer& L : layers_)
+      for (const DMat* W : {&L.qkv, &L.out, &L.gate_up, &L.down})
+        if (W->kind == kQ8_0) bytes += (size_t)W->n * W->k * 2;
+    if (bytes) {
+      TRIT_CUDA(cudaMalloc(&tc_w16_buf_, bytes));
+      tc_w16_.assign((size_t)cfg_.layers * 4, TcMap{});
+      size_t at16 = 0;
+      for (int l = 0; l < cfg_.layers; ++l) {
+        const DLayer& L = layers_[l];
+        const DMat* mats[4] = {&L.qkv, &L.out, &L.gate_up, &L.down};
+        for (int i = 0; i < 4; ++i) {
+          if (mats[i]->kind != kQ8_0) continue;
+          char* dst = (char*)tc_w16_buf_ + at16;
+          TRIT_CUDA(launch_codes_f16((const int8_t*)mats[i]->codes, (size_t)mats[i]->n * mats[i]->k, dst, stream_));
+          TRIT_CUDA(make_tc_map_f16(&tc_w16_[(size_t)l * 4 + i], dst, (size_t)mats[i]->n, (size_t)mats[i]->k, 128));
+          at16 += (size_t)mats[i]->n * mats[i]->k * 2;
+        }
+      }
+      const int kmax = std::max(std::max(d, qd), cfg_.ffn);
+      TRIT_CUDA(cudaMalloc(&xq16_, rows8 * kmax * 2));
+      for (int i = 0; i < 3; ++i) TRIT_CUDA(make_tc_map_f16(&tc_x16_[i], xq16_, rows8, (size_t)widths[i], 16));
+      tc_f16_ = true;
+    }
+  }
   TRIT_CUDA(cudaMalloc(&gu_, (size_t)rows_cap_ * 2 * cfg_.ffn * 4));
   TRIT_CUDA(cudaMalloc(&tc_status_, 4));
   TRIT_CUDA(cudaMemset(tc_status_, 0, 4));

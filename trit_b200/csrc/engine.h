@@ -28,6 +28,11 @@ struct Options {
   std::string decode = "persistent";  // "persistent" (one kernel per generation) or "layered"
   bool tensor_cores = true;      // tcgen05 products for prefill and batches of >= tc_rows rows
   int tc_rows = 64;
+  // The f16 form of the Q8_0 tensor-core products (codes as f16, exact f32
+  // dots, a fold without the integer bias); costs an f16 copy of the Q8_0
+  // layers' codes. Measured slower on C5 (two 32-value groups a stage
+  // instead of four: twice the stages and hand-offs), so off by default.
+  bool tc_f16 = false;
   // true (default): every floating-point step in the reference's order
   // (logits bit for bit those of the CPU decoder). false: the batch-1
   // decode sums in tree order (decode_fast.cu); tokens stay the reference's
@@ -253,6 +258,11 @@ class Lm {
   std::vector<TcMap> tc_w_;     // [layer][qkv, out, gate_up, down]
   TcMap tc_x_[3] = {};          // quantized frames of width d, heads * hd, ffn
   TcMap kv_map_{};              // the KV pool for the tensor-core prompt attention
+  std::vector<TcMap> tc_w16_;   // f16 codes of the Q8_0 layers, [layer][qkv, out, gate_up, down]
+  TcMap tc_x16_[3] = {};        // the frames' codes as f16, widths d, heads * hd, ffn
+  void* tc_w16_buf_ = nullptr;
+  void* xq16_ = nullptr;
+  bool tc_f16_ = false;
   bool attention_tc_ = false;   // "exact": false prompt attention on the tensor cores
   size_t pool_pages_ = 0;
   int8_t* tc_expanded_ = nullptr;  // int8 codes of ternary layers

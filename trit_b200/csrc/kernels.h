@@ -76,6 +76,10 @@ struct alignas(64) TcMap {
 int tc_frames();  // frames (rows of x) per CTA: the frame map's row multiple
 cudaError_t make_tc_weight_map(TcMap* out, const DMat& W, const void* codes8);
 cudaError_t make_tc_frame_map(TcMap* out, const int8_t* xq, size_t rows_cap, size_t k);
+// The f16 form of the Q8_0 products: codes as f16 (exact), so the tensor
+// cores make exact f32 group dots and the fold needs no integer bias.
+cudaError_t make_tc_map_f16(TcMap* out, const void* codes16, size_t rows, size_t k, int box_rows);
+cudaError_t launch_codes_f16(const int8_t* in, size_t n, void* out, cudaStream_t s);
 // y (m x ldy) from W times the quantized frames (xq via bmap, scales xs):
 // kEpOut stores, kEpResid adds (times resid_mult). *status is set when a
 // wait inside the kernel ran out.
@@ -89,7 +93,7 @@ cudaError_t launch_attention_tc(const TcMap& kvmap, const float* qkv, const int2
                                 const DConfig& cfg, const DCache& cache, const int* row_stream, const int* row_pos,
                                 int layer, float* att, int* status, cudaStream_t s);
 cudaError_t launch_gemm_tc(const TcMap& amap, const TcMap& bmap, const DMat& W, const float* xs, int m, int mode,
-                           float* y, int ldy, float resid_mult, int* status, cudaStream_t s);
+                           float* y, int ldy, float resid_mult, int* status, cudaStream_t s, bool f16 = false);
 // h[m][units] = silu(g[.][u]) * g[.][units + u] for g = [m][2 units].
 cudaError_t launch_silu_pairs(const float* g, int m, int units, float* h, cudaStream_t s);
 // Ternary 2-bit words [n][k/16] -> int8 codes c - 1 in {-1, 0, 1}, [n][k].

@@ -34,6 +34,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <mutex>
 
@@ -56,13 +57,19 @@ constexpr long long TC_WAIT_NS = 2000000000ll;  // 2 s
 
 // A CTA's frame tile: N frames (the MMA's N). A TMEM buffer holds one
 // stage's group accumulators side by side (TC_GPS x N columns).
-template <int N>
+// F16: the codes as f16 (exact: |code| <= 128), so a stage's 128 bytes
+// hold 64 values, two 32-value groups, and the MMA (kind::f16, f32
+// accumulators) makes each group's dot as an exact f32 (every partial sum
+// is an integer below 2^24).
+template <int N, bool F16 = false>
 struct TcShape {
   static_assert(N == 16 || N == 32 || N == 64, "frame tiles of 16, 32 or 64");
   static constexpr int B_STAGE = N * TC_KT;
-  static constexpr int BUF_COLS = TC_GPS * N;
-  static constexpr int BUFS = N == 16 ? 4 : 2;
+  static constexpr int GPS = F16 ? 2 : TC_GPS;       // 32-value groups a stage
+  static constexpr int BUF_COLS = GPS * N;
+  static constexpr int BUFS = F16 ? (N == 16 ? 8 : 4) : (N == 16 ? 4 : 2);
   static constexpr int TMEM_COLS = BUFS * BUF_COLS;  // 512, 256, 256: powers of two
+  static_assert(BUFS <= 8, "TcSmem holds 8 buffer barriers");
   static constexpr int CW = N / 2;                   // columns an epilogue warp folds
   static constexpr int CTAS = N == 64 ? 1 : 2;       // CTAs an SM holds (TMEM, shared memory)
 };
@@ -138,7 +145,22 @@ __host__ __device__ constexpr uint32_t idesc_i8(int n) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
 }
 
+// Instruction descriptor of kind::f16: D f32 (bits 4-5 = 1), A and B f16
+// (bits 7-9, 10-12 = 0), A K-major, B K-major or MN-major (bit 16), N >> 3
+// at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t idesc_f16n(int n, bool b_mn_major = false) {
+  return (1u << 4) | (b_mn_major ? (1u << 16) : 0u) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
+}
+
 // D = A B (+ D when `accumulate`).
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(mask0), "r"(mask1), "r"(mask2), "r"(mask3));
+}
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
   uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0;
   asm volatile(
@@ -244,26 +266,26 @@ __device__ __forceinline__ Ws8 load_ws8(const DMat& W, int row, bool live, int g
 }
 
 struct TcSmem {
-  uint64_t full[TC_STAGES], empty[TC_STAGES], tfull[4], tempty[4], drain;
+  uint64_t full[TC_STAGES], empty[TC_STAGES], tfull[8], tempty[8], drain;  // up to 8 TMEM buffers
   uint32_t tmem;
   int abort;
 };
 
 // y (m x ldy) <- the product of W (rows [0, n)) and the quantized frames
 // xq / xs (m rows). mode kEpOut: y = acc; kEpResid: y += acc (times mult).
-template <int N>
-__global__ void __launch_bounds__(TC_THREADS, TcShape<N>::CTAS)
+template <int N, bool F16>
+__global__ void __launch_bounds__(TC_THREADS, TcShape<N, F16>::CTAS)
     k_gemm_tc(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, DMat W,
               const float* xs, int m, int mode, float* y, int ldy, float resid_mult, int* status) {
-  using T = TcShape<N>;
+  using T = TcShape<N, F16>;
   constexpr int CW = T::CW;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* a_st = base;
   uint8_t* b_st = a_st + TC_STAGES * A_STAGE;
   const int G = W.agroup, groups = W.k / G;
-  // A stage holds 4 groups of 32 (Q8_0) or one of 128.
-  const int gshift = (G == 32) ? 2 : 0, gmask = (1 << gshift) - 1;
+  // A stage holds 4 groups of 32 (Q8_0) or one of 128; as f16, 2 of 32.
+  const int gshift = (G == 32) ? (F16 ? 1 : 2) : 0, gmask = (1 << gshift) - 1;
   // 128-value groups with a multiple of 4 of them: four consecutive stages
   // (one group each) share a TMEM buffer, as a Q8_0 stage's four groups do.
   const bool quad128 = G == 128 && groups % 4 == 0;
@@ -272,7 +294,7 @@ __global__ void __launch_bounds__(TC_THREADS, TcShape<N>::CTAS)
   TcSmem* S = (TcSmem*)(xs_s + XP * groups);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * TC_M, f0 = blockIdx.y * N;
-  const int ktiles = W.k / TC_KT;
+  const int ktiles = W.k * (F16 ? 2 : 1) / TC_KT;
   volatile int* abort = &S->abort;
 
   if (threadIdx.x == 0) {
@@ -335,10 +357,15 @@ __global__ void __launch_bounds__(TC_THREADS, TcShape<N>::CTAS)
         fence_after();
 #pragma unroll
         for (int j = 0; j < TC_KT / 32; ++j) {
-          const int gi = slot + (j * 32) / G;  // the group within the buffer
           const uint64_t ad = smem_desc_sw128(a0 + s * A_STAGE + j * 32);
           const uint64_t bd = smem_desc_sw128(b0 + s * T::B_STAGE + j * 32);
-          mma_i8(tmem + b * T::BUF_COLS + gi * N, ad, bd, idesc_i8(N), (j * 32) % G ? 1u : 0u);
+          if (F16) {
+            // K = 16 values a step: two steps a 32-value group.
+            mma_f16(tmem + b * T::BUF_COLS + (j >> 1) * N, ad, bd, idesc_f16n(N), (uint32_t)(j & 1));
+          } else {
+            const int gi = slot + (j * 32) / G;  // the group within the buffer
+            mma_i8(tmem + b * T::BUF_COLS + gi * N, ad, bd, idesc_i8(N), (j * 32) % G ? 1u : 0u);
+          }
         }
         if (slot == 3 || !quad128) mma_commit(&S->tfull[b]);
         mma_commit(&S->empty[s]);
@@ -407,9 +434,12 @@ __global__ void __launch_bounds__(TC_THREADS, TcShape<N>::CTAS)
 #pragma unroll
       for (int q = 0; q < CW / 4; ++q) {
         const float4 xv = xg[q];
-        acc[2 * q] = fma2(dots_to_float2(rc[4 * q], rc[4 * q + 1]), mul2(ws2, make_float2(xv.x, xv.y)), acc[2 * q]);
-        acc[2 * q + 1] =
-            fma2(dots_to_float2(rc[4 * q + 2], rc[4 * q + 3]), mul2(ws2, make_float2(xv.z, xv.w)), acc[2 * q + 1]);
+        const float2 d01 = F16 ? make_float2(__uint_as_float(rc[4 * q]), __uint_as_float(rc[4 * q + 1]))
+                               : dots_to_float2(rc[4 * q], rc[4 * q + 1]);
+        const float2 d23 = F16 ? make_float2(__uint_as_float(rc[4 * q + 2]), __uint_as_float(rc[4 * q + 3]))
+                               : dots_to_float2(rc[4 * q + 2], rc[4 * q + 3]);
+        acc[2 * q] = fma2(d01, mul2(ws2, make_float2(xv.x, xv.y)), acc[2 * q]);
+        acc[2 * q + 1] = fma2(d23, mul2(ws2, make_float2(xv.z, xv.w)), acc[2 * q + 1]);
       }
     };
     bool ok = true;
@@ -417,27 +447,28 @@ __global__ void __launch_bounds__(TC_THREADS, TcShape<N>::CTAS)
       // Four groups a buffer (a Q8_0 stage, or four 128-value stages):
       // the four accumulators load GB at a time (one TMEM wait
       // per batch and one hand-off per stage), then fold in order.
-      constexpr int GB = CW <= 8 ? 4 : 2;
+      constexpr int GPS = T::GPS;  // groups a buffer: 4 (int8 stage or quad128) or 2 (f16 stage)
+      constexpr int GB = (CW <= 8 ? 4 : 2) < GPS ? (CW <= 8 ? 4 : 2) : GPS;
       auto chunk = [&](int gc, int c) -> bool {
         wq[(c + 3) & 3] = load_ws8(W, row, live, gc + 24, groups, wvec);
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const int g0 = gc + 4 * h2, st = g0 >> 2;
+        for (int h2 = 0; h2 < 8 / GPS; ++h2) {
+          const int g0 = gc + GPS * h2, st = g0 / GPS;
           if (g0 >= groups) return true;
           if (!stage_ready(st)) return false;
           const uint32_t base = tl + (st % T::BUFS) * T::BUF_COLS;
 #pragma unroll
-          for (int b0 = 0; b0 < 4; b0 += GB) {
+          for (int b0 = 0; b0 < GPS; b0 += GB) {
             uint32_t rs[GB][CW];
 #pragma unroll
             for (int gi = 0; gi < GB; ++gi) tmem_ld<CW>(base + (b0 + gi) * N, rs[gi]);
             tmem_wait_ld();
-            if (b0 + GB == 4) {
+            if (b0 + GB == GPS) {
               fence_before();
               mbar_arrive(&S->tempty[st % T::BUFS]);
             }
 #pragma unroll
-            for (int gi = 0; gi < GB; ++gi) fold(g0 + b0 + gi, wq[c].get(W, 4 * h2 + b0 + gi), rs[gi]);
+            for (int gi = 0; gi < GB; ++gi) fold(g0 + b0 + gi, wq[c].get(W, GPS * h2 + b0 + gi), rs[gi]);
           }
         }
         return true;
@@ -552,17 +583,8 @@ struct FaSmem {
   int abort;
 };
 
-__host__ __device__ constexpr uint32_t idesc_f16(bool b_mn_major) {
-  return (1u << 4) | (b_mn_major ? (1u << 16) : 0u) | ((uint32_t)(FA_KEYS >> 3) << 17) | ((uint32_t)(FA_ROWS >> 4) << 24);
-}
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
-  uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(mask0), "r"(mask1), "r"(mask2), "r"(mask3));
-}
+static_assert(FA_ROWS == TC_M, "the attention MMA's M is the products' M");
+__host__ __device__ constexpr uint32_t idesc_f16(bool b_mn_major) { return idesc_f16n(FA_KEYS, b_mn_major); }
 // MN-major operand with the 128-byte swizzle: 64-element atoms along MN
 // (the leading offset between them), 8-row groups along K 1024 bytes apart.
 __device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t addr, uint32_t mn_atom_bytes) {
@@ -915,14 +937,18 @@ int tc_frame_tile(int n, int m, int sms) {
 static cudaError_t configure_gemm_tc(int dev) {
   static DeviceOnce once;
   return once.run(dev, [] {
-    cudaError_t r = cudaFuncSetAttribute(k_gemm_tc<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (r == cudaSuccess) r = cudaFuncSetAttribute(k_gemm_tc<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (r == cudaSuccess) r = cudaFuncSetAttribute(k_gemm_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    return r;
+    const void* fns[] = {(const void*)k_gemm_tc<16, false>, (const void*)k_gemm_tc<32, false>,
+                         (const void*)k_gemm_tc<64, false>, (const void*)k_gemm_tc<16, true>,
+                         (const void*)k_gemm_tc<32, true>, (const void*)k_gemm_tc<64, true>};
+    for (const void* f : fns) {
+      cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      if (r != cudaSuccess) return r;
+    }
+    return cudaSuccess;
   });
 }
 
-template <int N>
+template <int N, bool F16>
 cudaError_t launch_tc_n(const TcMap& amap, const TcMap& bmap, const DMat& W, const float* xs, int m, int mode,
                         float* y, int ldy, float resid_mult, int* status, cudaStream_t s, int dev) {
   size_t smem = tc_smem_bytes(W, N);
@@ -930,14 +956,45 @@ cudaError_t launch_tc_n(const TcMap& amap, const TcMap& bmap, const DMat& W, con
   cudaError_t e = configure_gemm_tc(dev);
   if (e != cudaSuccess) return e;
   dim3 grid((W.n + TC_M - 1) / TC_M, (m + N - 1) / N);
-  k_gemm_tc<N><<<grid, TC_THREADS, smem, s>>>(*(const CUtensorMap*)&amap, *(const CUtensorMap*)&bmap, W, xs, m, mode,
-                                               y, ldy, resid_mult, status);
+  k_gemm_tc<N, F16><<<grid, TC_THREADS, smem, s>>>(*(const CUtensorMap*)&amap, *(const CUtensorMap*)&bmap, W, xs, m,
+                                                    mode, y, ldy, resid_mult, status);
   return cudaGetLastError();
 }
 
+// int8 codes as f16 (exact), for the f16 form of the products.
+__global__ void k_codes_f16(const int8_t* in, size_t n, __half* out) {
+  for (size_t i = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) * 8; i < n; i += (size_t)gridDim.x * blockDim.x * 8) {
+    if (i + 8 <= n) {
+      const int2 c = *(const int2*)(in + i);
+      const int8_t* b = (const int8_t*)&c;
+      __half2 h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[j] = __halves2half2(__int2half_rn(b[2 * j]), __int2half_rn(b[2 * j + 1]));
+      *(uint4*)(out + i) = *(const uint4*)h;
+    } else {
+      for (size_t j = i; j < n; ++j) out[j] = __int2half_rn(in[j]);
+    }
+  }
+}
+
+cudaError_t launch_codes_f16(const int8_t* in, size_t n, void* out, cudaStream_t s) {
+  if (((uintptr_t)in & 7) || ((uintptr_t)out & 15)) return cudaErrorInvalidValue;
+  const size_t threads = (n + 7) / 8;
+  const int blocks = (int)std::min<size_t>((threads + 255) / 256, 148 * 16);
+  k_codes_f16<<<std::max(blocks, 1), 256, 0, s>>>(in, n, (__half*)out);
+  return cudaGetLastError();
+}
+
+// f16 codes of a [rows][k] matrix as a 2-D byte view (2k bytes a row) for
+// the f16 products: boxes of 64 values (128 bytes) x box_rows.
+cudaError_t make_tc_map_f16(TcMap* out, const void* codes16, size_t rows, size_t k, int box_rows) {
+  return make_tc_map(out, codes16, rows, 2 * k, box_rows);
+}
+
 cudaError_t launch_gemm_tc(const TcMap& amap, const TcMap& bmap, const DMat& W, const float* xs, int m, int mode,
-                           float* y, int ldy, float resid_mult, int* status, cudaStream_t s) {
+                           float* y, int ldy, float resid_mult, int* status, cudaStream_t s, bool f16) {
   if (W.k % TC_KT || (W.agroup != 32 && W.agroup != 128) || m <= 0) return cudaErrorInvalidValue;
+  if (f16 && W.agroup != 32) return cudaErrorInvalidValue;
   int dev = 0;
   cudaGetDevice(&dev);
   // TRIT_TC_FRAMES=16, 32 or 64 fixes the frame tile (tests, tuning).
@@ -947,9 +1004,14 @@ cudaError_t launch_gemm_tc(const TcMap& amap, const TcMap& bmap, const DMat& W, 
     return (v == 16 || v == 32 || v == 64) ? v : 0;
   }();
   const int tile = forced ? forced : tc_frame_tile(W.n, m, current_sm_count());
-  if (tile == 16) return launch_tc_n<16>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
-  if (tile == 32) return launch_tc_n<32>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
-  return launch_tc_n<64>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
+  if (f16) {
+    if (tile == 16) return launch_tc_n<16, true>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
+    if (tile == 32) return launch_tc_n<32, true>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
+    return launch_tc_n<64, true>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
+  }
+  if (tile == 16) return launch_tc_n<16, false>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
+  if (tile == 32) return launch_tc_n<32, false>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
+  return launch_tc_n<64, false>(amap, bmap, W, xs, m, mode, y, ldy, resid_mult, status, s, dev);
 }
 
 bool attention_tc_supported(const DConfig& cfg, const DCache& cache) {
