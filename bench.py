@@ -313,6 +313,8 @@ def measure(w: dict, args, r: dp.Rank, steps: int, warmup: int, decode: str, exa
     info = lmmod.inspect(model_dir)
     S = w["streams"]
     prompt_len = w["prompt"] + w.get("rows", 0)
+    tc_attention = bool(getattr(args, "tc_attention", False))
+    exact = exact and not tc_attention
     opts = {"device": r.local, "kv": args.kv, "max_context": prompt_len + w["new"] + 8, "exact": exact}
     tp = max(1, getattr(args, "tp", 1) or 1)
     group = r.rank // tp  # ranks of one tensor-parallel group serve the same streams
@@ -326,6 +328,8 @@ def measure(w: dict, args, r: dp.Rank, steps: int, warmup: int, decode: str, exa
         opts.update(tc_rows=args.tc_rows)
     if getattr(args, "tc_f16", False):
         opts.update(tc_f16=True)
+    if tc_attention:
+        opts.update(tc_attention=True)
     if args.prefill_rows is not None:
         opts.update(prefill_rows=args.prefill_rows)
     else:
@@ -388,7 +392,8 @@ def measure(w: dict, args, r: dp.Rank, steps: int, warmup: int, decode: str, exa
         "config": {"workload": w["workload"], "model": w["model"], "global_batch": S * r.world // tp,
                    "seq_len": prompt_len + w["new"], "parallelism": (f"dp{r.world} (independent streams, no collective)" if tp == 1 else
                                    f"tp{tp} x dp{r.world // tp} (NCCL all-reduce of o/down partials, argmax keys)"),
-                   "decode": decode if w["kind"] != "batch" else "batched", "exact": exact, "kv_cache": args.kv,
+                   "decode": decode if w["kind"] != "batch" else "batched", "exact": exact,
+                   "prompt_attention": "tensor cores (f16)" if tc_attention else "exact", "kv_cache": args.kv,
                    "l2": f"weights {alg['weights'] / 1e6:.0f} MB > 126 MB L2; no flush"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": S * w["new"] * 4},
         "gpu_launches": launches,
@@ -585,6 +590,8 @@ def main() -> None:
     ap.add_argument("--no-batch64", action="store_true", help="leave the C5 batch-64 object out of the C1 line")
     ap.add_argument("--tc-rows", type=int, help="rows from which products use the tensor cores (engine option)")
     ap.add_argument("--tc-f16", action="store_true", help="f16-operand tensor-core products for Q8_0 layers (engine option)")
+    ap.add_argument("--tc-attention", action="store_true",
+                    help="prompt attention on the tensor cores (f16 flash attention; not bit-exact)")
     ap.add_argument("--prefill-rows", type=int, help="rows a prompt pass (engine option)")
     ap.add_argument("--kv", default="f16")
     ap.add_argument("--tp", type=int, default=1,

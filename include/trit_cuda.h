@@ -133,14 +133,18 @@ void trit_cuda_free_text(char *text);
  *                   step in the order of the reference's CPU decoder, so
  *                   logits equal its logits bit for bit. false: the batch-1
  *                   decode sums in tree order and splits attention and
- *                   o_proj by kv head, and prompt attention runs on the
- *                   tensor cores (f16 flash attention; f16 cache, pages of
- *                   a multiple of 64 positions); the int8 activation codes can then
+ *                   o_proj by kv head; the int8 activation codes can then
  *                   move where a value sits on a rounding boundary, so
  *                   logits drift (measured up to 5e-2 max-abs, cosine
  *                   >= 0.9999; the reference restatement with only its
  *                   RmsNorm sum reordered drifts as much) while tokens
  *                   stayed the reference's on every tested config
+ *   "tc_attention": false (default) or true (with "exact": false): prompt
+ *                   attention as f16 flash attention on the tensor cores
+ *                   (f16 cache, pages of a multiple of 64 positions); its
+ *                   sums are not the reference's, so logits drift and a
+ *                   token can differ where the reference's top two logits
+ *                   are close
  *   "config_at":    key path of the decoder settings in config.json ("";
  *                   "thinker_config.text_config." in Qwen3-ASR)
  *   "prefix":       start of every tensor name ("", "thinker.", "llm.")

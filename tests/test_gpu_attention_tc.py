@@ -1,4 +1,5 @@
-"""The tensor-core prompt attention of `"exact": false` (tcgen05 kind::f16,
+"""The tensor-core prompt attention (`"tc_attention": true`, with `"exact":
+false`; tcgen05 kind::f16,
 flash-style, mma.cu k_attention_tc) against the oracle. The prompt's
 attention runs in another order than the reference's (the tensor cores'
 sums, per-tile softmax, probabilities rounded to f16), so logits are not
@@ -38,7 +39,7 @@ def test_tc_prompt_attention_logits_near_oracle(mini_models, name, length):
     oracle = O.Oracle(path, kv_f16=True)
     prompt = np.random.default_rng(61).integers(0, oracle.vocab, size=length).tolist()
     ref = oracle.generate(prompt, 8, trace=True)
-    with CausalLm.load(path, kv="f16", decode="layered", exact=False, max_context=length + 64) as lm:
+    with CausalLm.load(path, kv="f16", decode="layered", exact=False, tc_attention=True, max_context=length + 64) as lm:
         toks, logits = lm.generate_traced(prompt, max_new=8)
     n = min(len(toks), len(ref["tokens"]))
     worst = 0.0
@@ -63,7 +64,7 @@ def test_tc_prompt_attention_batch_equals_single(mini_models):
     path = mini_models["mini_qwen3_q8_0"]
     rng = np.random.default_rng(62)
     prompts = [rng.integers(0, 4096, size=n).tolist() for n in (5, 140, 260, 33)]
-    with CausalLm.load(path, kv="f16", decode="layered", exact=False, max_context=400, max_streams=4,
+    with CausalLm.load(path, kv="f16", decode="layered", exact=False, tc_attention=True, max_context=400, max_streams=4,
                        prefill_rows=256) as lm:
         got = lm.generate_batch(prompts, max_new=6)
         single = [lm.generate(p, max_new=6) for p in prompts]

@@ -131,7 +131,7 @@ def test_c5_two_of_64_streams():
     batch_against_oracle("c5", "c5_ministral_3b_q8_0", 64, 64, 32, [0, 63])
 
 
-# The tensor-core prompt attention of `"exact": false` (f16 operands, the
+# The tensor-core prompt attention (`"tc_attention": true`: f16 operands, the
 # tensor cores' sums, a per-tile softmax) is not the reference's arithmetic:
 # its logits drift, and where the oracle's top-1/top-2 gap is small a token
 # can flip (C5 stream 0 flips at step 12). These tests record the drift up
@@ -156,23 +156,23 @@ def drift_until_divergence(name: str, toks, logits, want: dict) -> None:
 
 
 def test_c5_tensor_core_prompt_attention_drift():
-    """`"exact": false` on C5 (stream 0's 64-id prompt of the batch test):
+    """`"tc_attention": true` on C5 (stream 0's 64-id prompt of the batch test):
     the prompt's attention on the tensor cores, the decode steps exact."""
     path = presets.model_path("c5_ministral_3b_q8_0")
     rng = np.random.default_rng(sum(map(ord, "c5")))
     prompt = rng.integers(0, presets.CONFIGS["c5_ministral_3b_q8_0"][0]["vocab_size"], size=64).tolist()
     want = O.Oracle(path, kv_f16=True).generate(prompt, 32, trace=True)
-    with CausalLm.load(path, kv="f16", decode="layered", exact=False, max_context=128) as lm:
+    with CausalLm.load(path, kv="f16", decode="layered", exact=False, tc_attention=True, max_context=128) as lm:
         toks, logits = lm.generate_traced(prompt, max_new=32)
     drift_until_divergence("c5_tc_prompt", toks, logits, want)
 
 
 def test_c1_tensor_core_prompt_attention_drift():
-    """`"exact": false` with layered decode on C1: only the prompt's attention
+    """`"tc_attention": true` with layered decode on C1: only the prompt's attention
     (300 ids, three 128-key tiles) runs in another order."""
     path = presets.model_path("c1_qwen3_0.6b_q8_0")
     prompt = np.random.default_rng(5).integers(0, 151936, size=300).tolist()
     want = O.Oracle(path, kv_f16=True).generate(prompt, 32, trace=True)
-    with CausalLm.load(path, kv="f16", decode="layered", exact=False, max_context=400) as lm:
+    with CausalLm.load(path, kv="f16", decode="layered", exact=False, tc_attention=True, max_context=400) as lm:
         toks, logits = lm.generate_traced(prompt, max_new=32)
     drift_until_divergence("c1_tc_prompt", toks, logits, want)

@@ -58,6 +58,9 @@ Options Options::parse(const char* text, bool lenient) {
       o.tp_size = count(1, 64);
     } else if (k == "tp_rank") {
       o.tp_rank = count(0, 63);
+    } else if (k == "tc_attention") {
+      if (v.kind != Json::Bool) throw Error("options: tc_attention must be true or false");
+      o.tc_attention = v.b;
     } else if (k == "tc_f16") {
       if (v.kind != Json::Bool) throw Error("options: tc_f16 must be true or false");
       o.tc_f16 = v.b;
@@ -83,6 +86,7 @@ Options Options::parse(const char* text, bool lenient) {
       throw Error("options: unknown key " + k);
     }
   }
+  if (o.tc_attention && o.exact) throw Error("options: tc_attention needs \"exact\": false (it is not the reference's arithmetic)");
   return o;
 }
 
@@ -1161,7 +1165,7 @@ void Lm::setup_tensor_cores() {
   TRIT_CUDA(cudaMemset(tc_status_, 0, 4));
   // "exact": false: prompt attention on the tensor cores (f16 cache, pages
   // of a multiple of 64 positions), over a TMA view of the whole pool.
-  if (!opt_.exact && attention_tc_supported(cfg_, cache_)) {
+  if (opt_.tc_attention && attention_tc_supported(cfg_, cache_)) {
     const size_t rows = pool_pages_ * (size_t)cfg_.layers * 2 * cfg_.kv_heads * cache_.page_tokens;
     TRIT_CUDA(make_kv_map(&kv_map_, pool_, rows));
     attention_tc_ = true;

@@ -39,6 +39,10 @@ struct Options {
   // but, since a reordered sum can move an int8 activation code, logits
   // drift by up to ~5e-2.
   bool exact = true;
+  // Prompt attention as f16 flash attention on the tensor cores (not the
+  // reference's arithmetic; needs exact false, an f16 cache and pages of a
+  // multiple of 64 positions).
+  bool tc_attention = false;
   // Keep the weights' device layout in a cache file and read it on later
   // loads (cache_dir, default <model folder>/.trit_cuda).
   bool weight_cache = false;

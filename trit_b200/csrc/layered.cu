@@ -821,6 +821,213 @@ static StepFn step_kernel(int qpk, int tmax) {
   }
 }
 
+// ------------------------------------------ attention of prompt tiles ----
+// k_attention_rows' work for tiles of 16 or more query heads on an f16
+// cache with an even number of query heads a kv head, with the same
+// operations in the same order, laid out so that each staged key or value
+// is converted to f32 once for the whole tile and two chains share one
+// packed f32x2 fma (each lane rounded as the scalar fma):
+//   staging: a tile's keys (then values) are loaded into registers while
+//            the tile before is used, and stored to shared memory as f32;
+//   scores:  a thread keeps 4 query heads (two pairs, q interleaved by
+//            pair in shared memory) x 4 keys; per dimension one packed fma
+//            updates a pair's chains with the key duplicated;
+//   values:  a thread keeps two query heads of one row (the same visible
+//            keys) x 8 dimensions (4 and 4, 64 apart: conflict-free reads),
+//            one packed fma per pair of dimensions and head.
+constexpr int AT_PITCH = 132;  // floats a staged f32 row (16-byte aligned, rows 4 banks apart)
+constexpr int AT_VI = 2;       // value items a thread at most (64 query heads)
+
+__global__ void __launch_bounds__(256) k_attention_tile(const float* qkv, const int2* tiles, DConfig cfg, DCache cache,
+                                                        const int* row_stream, const int* row_pos, int layer, int tmax,
+                                                        int all_keys, float* att) {
+  extern __shared__ __align__(16) float sm[];
+  const int kvh = blockIdx.y, t = threadIdx.x;
+  const int2 tile = tiles[blockIdx.x];
+  const int r0 = tile.x, R = tile.y;
+  const int qpk = cfg.heads / cfg.kv_heads, qd = cfg.heads * 128, stride = qd + 2 * cfg.kv_heads * 128;
+  const int RQ = R * qpk;                // a multiple of 4 (qpk even, quad tiles)
+  float* qp = sm;                        // [RQ / 2][128][2]: q of heads 2i and 2i + 1 per dimension
+  float* sc = qp + (size_t)RQ * 128;     // [RQ][tmax]
+  float* kv = sc + (size_t)RQ * tmax;    // [AR_KT][AT_PITCH]
+  float* inv = kv + AR_KT * AT_PITCH;    // [RQ]
+  const int stream = row_stream[r0], p0 = row_pos[r0];
+  const int T = all_keys > 0 ? all_keys : p0 + R;
+  auto visible = [&](int qh) { return all_keys > 0 ? all_keys : p0 + qh / qpk + 1; };
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
+  for (int i = t; i < RQ * 128; i += 256) {
+    const int qh = i / 128, e = i % 128, r = qh / qpk, h = qh % qpk;
+    qp[((qh >> 1) * 128 + e) * 2 + (qh & 1)] = __fmul_rn(qkv[(size_t)(r0 + r) * stride + (kvh * qpk + h) * 128 + e], scale);
+  }
+  // Chunk u of a tile for this thread: chunk t + 256 u, row (t + 256 u) / 16
+  // (rows 16 apart), 16 bytes = 8 values; neighbouring threads read a row's
+  // neighbouring chunks.
+  const int ntile = (T + AR_KT - 1) / AR_KT;
+  uint4 pre[8];
+  auto fetch = [&](int i) {
+    const int which = i < ntile ? 0 : 1, j0 = (i % ntile) * AR_KT, n = min(AR_KT, T - j0);
+    int pg_end = -1, pg_start = 0;
+    const __half* base = nullptr;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int jj = (t >> 4) + 16 * u, cc = t & 15, j = j0 + jj;
+      pre[u] = make_uint4(0, 0, 0, 0);
+      if (jj < n) {
+        if (j >= pg_end) {
+          const int pgi = j / cache.page_tokens;
+          pg_start = pgi * cache.page_tokens;
+          pg_end = pg_start + cache.page_tokens;
+          const int page = cache.page_table[(size_t)stream * cache.pages_per_stream + pgi];
+          base = (const __half*)cache.pool + kv_offset(cache, cfg, page, layer, which, kvh, 0);
+        }
+        pre[u] = *(const uint4*)(base + (size_t)(j - pg_start) * 128 + cc * 8);
+      }
+    }
+  };
+  auto store = [&]() {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int jj = (t >> 4) + 16 * u, cc = t & 15;
+      const __half2* h = (const __half2*)&pre[u];
+      const float2 a = __half22float2(h[0]), b = __half22float2(h[1]), c = __half22float2(h[2]),
+                   d = __half22float2(h[3]);
+      *(float4*)(kv + jj * AT_PITCH + cc * 8) = make_float4(a.x, a.y, b.x, b.y);
+      *(float4*)(kv + jj * AT_PITCH + cc * 8 + 4) = make_float4(c.x, c.y, d.x, d.y);
+    }
+  };
+  const int warp = t >> 5, lane = t & 31;
+  float2 vacc[AT_VI][2][4];
+#pragma unroll
+  for (int u = 0; u < AT_VI; ++u)
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) vacc[u][h][k] = make_float2(0.0f, 0.0f);
+  const int vitems = (RQ / 2) * 16;
+  fetch(0);
+  for (int i = 0; i < 2 * ntile; ++i) {
+    __syncthreads();  // the tile before is used up
+    store();
+    __syncthreads();
+    if (i + 1 < 2 * ntile) fetch(i + 1);  // in flight while this tile is used
+    const int j0 = (i % ntile) * AR_KT, n = min(AR_KT, T - j0);
+    if (i < ntile) {
+      // Scores: 4 query heads x keys jb, jb + kg, jb + 2 kg, jb + 3 kg.
+      // (The last group of a tile may hold one pair: RQ is even; the other
+      // pair's q reads stay inside shared memory and its chains are dropped.)
+      const int kg = (n + 3) / 4, items = ((RQ + 3) / 4) * kg;
+      for (int it = t; it < items; it += 256) {
+        const int qb = it / kg, jb = it % kg;
+        float2 acc[2][4];
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+#pragma unroll
+          for (int b = 0; b < 4; ++b) acc[p][b] = make_float2(0.0f, 0.0f);
+        const float* kr[4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) kr[b] = kv + min(jb + b * kg, n - 1) * AT_PITCH;
+        const float* qa = qp + (size_t)(2 * qb) * 256;
+        const float* qb2 = qa + 256;
+#pragma unroll 2
+        for (int e = 0; e < 128; e += 4) {
+          float4 kk[4];
+#pragma unroll
+          for (int b = 0; b < 4; ++b) kk[b] = *(const float4*)(kr[b] + e);
+          const float4 a0 = *(const float4*)(qa + 2 * e), a1 = *(const float4*)(qa + 2 * e + 4);
+          const float4 c0 = *(const float4*)(qb2 + 2 * e), c1 = *(const float4*)(qb2 + 2 * e + 4);
+          const float2 qx[2][4] = {{make_float2(a0.x, a0.y), make_float2(a0.z, a0.w), make_float2(a1.x, a1.y),
+                                    make_float2(a1.z, a1.w)},
+                                   {make_float2(c0.x, c0.y), make_float2(c0.z, c0.w), make_float2(c1.x, c1.y),
+                                    make_float2(c1.z, c1.w)}};
+#pragma unroll
+          for (int d = 0; d < 4; ++d)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const float kd = d == 0 ? kk[b].x : d == 1 ? kk[b].y : d == 2 ? kk[b].z : kk[b].w;
+              const float2 k2 = make_float2(kd, kd);
+              acc[0][b] = fma2(qx[0][d], k2, acc[0][b]);
+              acc[1][b] = fma2(qx[1][d], k2, acc[1][b]);
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int qh = 4 * qb + 2 * p + c;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const int jj = jb + b * kg, j = j0 + jj;
+              if (qh < RQ && jj < n && j < visible(qh)) sc[(size_t)qh * tmax + j] = c ? acc[p][b].y : acc[p][b].x;
+            }
+          }
+      }
+      if (i == ntile - 1) {
+        // Softmax: max and exp a warp per query head; the sums in key order,
+        // one thread per query head, its loads ahead of the adds.
+        __syncthreads();
+        for (int qh = warp; qh < RQ; qh += 8) {
+          const int vis = visible(qh);
+          float* srow = sc + (size_t)qh * tmax;
+          float mx = -INFINITY;
+          for (int j = lane; j < vis; j += 32) mx = fmaxf(mx, srow[j]);
+          mx = warp_max(mx);
+          for (int j = lane; j < vis; j += 32) srow[j] = cephes_exp(__fsub_rn(srow[j], mx));
+        }
+        __syncthreads();
+        if (t < RQ) inv[t] = __fdiv_rn(1.0f, seq_sum_ahead(sc + (size_t)t * tmax, visible(t)));
+        __syncthreads();
+        for (int qh = warp; qh < RQ; qh += 8) {
+          const int vis = visible(qh);
+          float* srow = sc + (size_t)qh * tmax;
+          const float iv = inv[qh];
+          for (int j = lane; j < vis; j += 32) srow[j] = __fmul_rn(srow[j], iv);
+        }
+      }
+    } else {
+      // Values: heads 2 pp and 2 pp + 1 (one row) x dimensions 4 dg.. and
+      // 64 + 4 dg.., keys in order.
+#pragma unroll
+      for (int u = 0; u < AT_VI; ++u) {
+        const int it = t + 256 * u;
+        if (it < vitems) {
+          const int pp = it >> 4, dg = it & 15, qh0 = 2 * pp;
+          const int lim = min(n, visible(qh0) - j0);
+          const float* pr0 = sc + (size_t)qh0 * tmax + j0;
+          const float* pr1 = pr0 + tmax;
+          const float* vr = kv + 4 * dg;
+#pragma unroll 4
+          for (int jj = 0; jj < lim; ++jj) {
+            const float pa = pr0[jj], pb = pr1[jj];
+            const float4 v0 = *(const float4*)(vr + jj * AT_PITCH), v1 = *(const float4*)(vr + jj * AT_PITCH + 64);
+            const float2 vv[4] = {make_float2(v0.x, v0.y), make_float2(v0.z, v0.w), make_float2(v1.x, v1.y),
+                                  make_float2(v1.z, v1.w)};
+            const float2 p2a = make_float2(pa, pa), p2b = make_float2(pb, pb);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              vacc[u][0][k] = fma2(p2a, vv[k], vacc[u][0][k]);
+              vacc[u][1][k] = fma2(p2b, vv[k], vacc[u][1][k]);
+            }
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < AT_VI; ++u) {
+    const int it = t + 256 * u;
+    if (it < vitems) {
+      const int pp = it >> 4, dg = it & 15;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int qh = 2 * pp + c, r = qh / qpk, h = qh % qpk;
+        float* dst = att + (size_t)(r0 + r) * qd + (kvh * qpk + h) * 128;
+        *(float4*)(dst + 4 * dg) = make_float4(vacc[u][c][0].x, vacc[u][c][0].y, vacc[u][c][1].x, vacc[u][c][1].y);
+        *(float4*)(dst + 64 + 4 * dg) = make_float4(vacc[u][c][2].x, vacc[u][c][2].y, vacc[u][c][3].x, vacc[u][c][3].y);
+      }
+    }
+  }
+}
+
 int attention_tile_rows(const DConfig& cfg, int tmax, int f16) {
   // A block's shared memory (220 KB): two staged K/V tiles, and for every
   // query head of the tile its q row and its scores; at most 16 rows and
@@ -850,6 +1057,23 @@ cudaError_t launch_attention_rows(const float* qkv, const int2* tiles, int ntile
   if (smem > 220 * 1024) return cudaErrorInvalidValue;
   // Blocks of 4 query heads for tiles of 16 or more query heads.
   const bool quad = tiles && RQ >= 16;
+  static const bool legacy_tile = getenv("TRIT_ATTENTION_ROWS") != nullptr;
+  if (quad && cache.f16 && qpk % 2 == 0 && !legacy_tile) {
+    const size_t tsmem = ((size_t)RQ * 128 + (size_t)RQ * tmax + (size_t)AR_KT * AT_PITCH + RQ) * 4;
+    static DeviceOnce tonce;
+    int tdev = 0;
+    cudaError_t te = cudaGetDevice(&tdev);
+    if (te != cudaSuccess) return te;
+    te = tonce.run(tdev, [] {
+      return cudaFuncSetAttribute(k_attention_tile, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+    });
+    if (te != cudaSuccess) return te;
+    if (tsmem <= 220 * 1024) {
+      k_attention_tile<<<dim3(ntiles, cfg.kv_heads), 256, tsmem, s>>>(qkv, tiles, cfg, cache, row_stream, row_pos,
+                                                                      layer, tmax, all_keys, att);
+      return cudaGetLastError();
+    }
+  }
   static DeviceOnce once;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
