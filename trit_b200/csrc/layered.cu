@@ -1543,11 +1543,8 @@ static cudaError_t configure_tables() {
       cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
       if (r != cudaSuccess) return r;
     }
-    const int rows16 = (int)table_rows_smem(16);
-    const int rows32 = (int)table_rows_smem(32);
-    cudaError_t r = cudaFuncSetAttribute(k_table_rows<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, rows16);
-    if (r != cudaSuccess) return r;
-    return cudaFuncSetAttribute(k_table_rows<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, rows32);
+    return cudaFuncSetAttribute(k_table_rows<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)table_rows_smem(16));
   });
 }
 
@@ -1612,8 +1609,7 @@ cudaError_t launch_table(const DTable& T, const float* xn, int nb, float mult, f
     if (n == 1) e = table_pass<1>(T, xb, n, mult, lg, bv, bi, s);
     else if (n <= 4) e = table_pass<4>(T, xb, n, mult, lg, bv, bi, s);
     else if (T.k % TB_KC) e = table_pass<16>(T, xb, n, mult, lg, bv, bi, s);
-    else if (n <= 16) e = table_rows_pass<16>(T, xb, n, mult, lg, bv, bi, s);
-    else e = table_rows_pass<32>(T, xb, n, mult, lg, bv, bi, s);
+    else e = table_rows_pass<16>(T, xb, n, mult, lg, bv, bi, s);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
