@@ -871,6 +871,7 @@ void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* runs)
   const bool tc = tc_ready_ && m >= opt_.tc_rows;
   // One product: the tensor-core kernel for enough rows, else the GEMV.
   // xi: the width of the product's input (0: d, 1: heads * hd, 2: ffn).
+  bool h_quantized = false;  // the tensor-core gate_up quantized h for the down product already
   auto product = [&](int l, int which, const DMat& W, int xi, int mode, float* y, int ldy, float mult) {
     if (!tc) {
       TRIT_CUDA(launch_gemv(W, xq_, xs_, m, mode, y, ldy, mult, s));
@@ -886,9 +887,13 @@ void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* runs)
     const TcMap& wmap = f16 ? tc_w16_[(size_t)l * 4 + which] : tc_w_[(size_t)l * 4 + which];
     const TcMap& xmap = f16 ? tc_x16_[xi] : tc_x_[xi];
     if (mode == kEpSilu) {
+      // h = silu(gate) * up, quantized straight into the down product's
+      // input (h itself is needed by nothing else).
       TRIT_CUDA(launch_gemm_tc(wmap, xmap, W, xs_, m, kEpOut, gu_, W.n, 1.0f, tc_status_, s, f16));
-      TRIT_CUDA(launch_silu_pairs(gu_, m, W.n / 2, y, s));
+      const DMat& D = layers_[l].down;
+      TRIT_CUDA(launch_silu_quant(gu_, m, W.n / 2, D.agroup, D.half, xq_, xs_, s));
       timing_.gpu_launches += 1;
+      h_quantized = true;
     } else {
       TRIT_CUDA(launch_gemm_tc(wmap, xmap, W, xs_, m, mode, y, ldy, mult, tc_status_, s, f16));
     }
@@ -927,9 +932,11 @@ void Lm::hidden(int m, int max_tk, const std::vector<std::pair<int, int>>* runs)
     TRIT_CUDA(launch_norm_quant(x_, m, d, L.norm_mlp, cfg_.eps, L.gate_up.agroup, L.gate_up.half, xq_, xs_, s,
                                 L.ffn_scale));
     clock_.mark("gate_up", s);
+    h_quantized = false;
     product(l, 2, L.gate_up, 0, kEpSilu, h_, cfg_.ffn, 1.0f);
     clock_.mark("norm+quant", s);
-    TRIT_CUDA(launch_norm_quant(h_, m, cfg_.ffn, nullptr, cfg_.eps, L.down.agroup, L.down.half, xq_, xs_, s));
+    if (!h_quantized)
+      TRIT_CUDA(launch_norm_quant(h_, m, cfg_.ffn, nullptr, cfg_.eps, L.down.agroup, L.down.half, xq_, xs_, s));
     clock_.mark("down", s);
     if (tp_.size > 1) {
       product(l, 3, L.down, 2, kEpOut, part_, d, 1.0f);

@@ -95,7 +95,10 @@ cudaError_t launch_attention_tc(const TcMap& kvmap, const float* qkv, const int2
 cudaError_t launch_gemm_tc(const TcMap& amap, const TcMap& bmap, const DMat& W, const float* xs, int m, int mode,
                            float* y, int ldy, float resid_mult, int* status, cudaStream_t s, bool f16 = false);
 // h[m][units] = silu(g[.][u]) * g[.][units + u] for g = [m][2 units].
-cudaError_t launch_silu_pairs(const float* g, int m, int units, float* h, cudaStream_t s);
+// silu(gate) * up of a stacked gate|up product, quantized in groups for the
+// down product (the tensor-core path's h, never stored in f32).
+cudaError_t launch_silu_quant(const float* g, int m, int units, int group, int half, int8_t* xq, float* xs,
+                              cudaStream_t s);
 // Ternary 2-bit words [n][k/16] -> int8 codes c - 1 in {-1, 0, 1}, [n][k].
 cudaError_t launch_expand_ternary(const DMat& W, int8_t* out, cudaStream_t s);
 

@@ -37,16 +37,25 @@ __global__ void k_scale(float* x, size_t n, float mult) {
 // (src/cpu/kernels.rs:661-737) of the normed row. One block per row; one
 // thread sums the squares in order, as the reference does, so the result
 // is the reference's to the bit.
+// With `squares`, the squares are formed by all threads into shared memory
+// first (each rounded, as the reference rounds them), so the one thread's
+// chain is adds only.
 template <int G>
 __global__ void __launch_bounds__(256) k_norm_quant(const float* x, int d, const float* w, float eps, int half,
-                                                    int8_t* xq, float* xs, const float* sc) {
-  extern __shared__ __align__(16) float rowv[];  // [d]
+                                                    int8_t* xq, float* xs, const float* sc, int squares) {
+  extern __shared__ __align__(16) float rowv[];  // [d], then [d] squares
+  float* sq = rowv + d;
   int r = blockIdx.x;
   const float* row = x + (size_t)r * d;
   __shared__ float s_inv;
-  for (int i = threadIdx.x; i < d; i += 256) rowv[i] = row[i];
+  for (int i = threadIdx.x; i < d; i += 256) {
+    const float v = row[i];
+    rowv[i] = v;
+    if (squares) sq[i] = __fmul_rn(v, v);
+  }
   __syncthreads();
-  if (threadIdx.x == 0) s_inv = w ? rms_inv(seq_sum_squares_ahead(rowv, d), d, eps) : 1.0f;
+  if (threadIdx.x == 0)
+    s_inv = !w ? 1.0f : rms_inv(squares ? seq_sum_ahead(sq, d) : seq_sum_squares_ahead(rowv, d), d, eps);
   __syncthreads();
   float inv = s_inv;
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1438,12 +1447,76 @@ cudaError_t launch_scale(float* x, size_t n, float mult, cudaStream_t s) {
   return cudaSuccess;
 }
 
+// Quantized::grouped of rows with no norm and no scale (the attention
+// output, h): the groups of a row are independent, so a row's groups spread
+// over `gridDim.y` blocks (a warp a group, as k_norm_quant quantizes them).
+template <int G>
+__global__ void __launch_bounds__(256) k_quant_rows(const float* x, int d, int half, int8_t* xq, float* xs) {
+  const int r = blockIdx.x, groups = d / G;
+  const int per = (groups + gridDim.y - 1) / gridDim.y;
+  const int g0 = blockIdx.y * per, g1 = min(groups, g0 + per);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* row = x + (size_t)r * d;
+  for (int g = g0 + warp; g < g1; g += 8) {
+    float v[G / 32];
+#pragma unroll
+    for (int i = 0; i < G / 32; ++i) v[i] = row[g * G + lane * (G / 32) + i];
+    const float scale = warp_quantize_group<G>(v, xq + (size_t)r * d + g * G, half);
+    if (lane == 0) xs[(size_t)r * groups + g] = scale;
+  }
+}
+
+// h = silu(gate) * up of a stacked gate|up product (causal_lm.rs:464-474;
+// g = [m][2 * units]), quantized as k_quant_rows quantizes h.
+template <int G>
+__global__ void __launch_bounds__(256) k_silu_quant(const float* g, int units, int half, int8_t* xq, float* xs) {
+  const int r = blockIdx.x, groups = units / G;
+  const int per = (groups + gridDim.y - 1) / gridDim.y;
+  const int g0 = blockIdx.y * per, g1 = min(groups, g0 + per);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* row = g + (size_t)r * 2 * units;
+  for (int gi = g0 + warp; gi < g1; gi += 8) {
+    float v[G / 32];
+#pragma unroll
+    for (int i = 0; i < G / 32; ++i) {
+      const int u = gi * G + lane * (G / 32) + i;
+      v[i] = __fmul_rn(silu(row[u]), row[units + u]);
+    }
+    const float scale = warp_quantize_group<G>(v, xq + (size_t)r * units + gi * G, half);
+    if (lane == 0) xs[(size_t)r * groups + gi] = scale;
+  }
+}
+
+static int quant_splits(int m, int groups) {
+  // Enough blocks for two an SM when the rows are few (decode batches).
+  return std::max(1, std::min((groups + 7) / 8, (2 * current_sm_count() + m - 1) / m));
+}
+
+cudaError_t launch_silu_quant(const float* g, int m, int units, int group, int half, int8_t* xq, float* xs,
+                              cudaStream_t s) {
+  if (units % group) return cudaErrorInvalidValue;
+  const int splits = quant_splits(m, units / group);
+  if (group == 32) k_silu_quant<32><<<dim3(m, splits), 256, 0, s>>>(g, units, half, xq, xs);
+  else k_silu_quant<128><<<dim3(m, splits), 256, 0, s>>>(g, units, half, xq, xs);
+  LAUNCH_CHECK();
+  return cudaSuccess;
+}
+
 cudaError_t launch_norm_quant(const float* x, int m, int d, const float* w, float eps, int group, int half,
                               int8_t* xq, float* xs, cudaStream_t s, const float* scale) {
+  if (!w && !scale) {
+    const int splits = quant_splits(m, d / group);
+    if (group == 32) k_quant_rows<32><<<dim3(m, splits), 256, 0, s>>>(x, d, half, xq, xs);
+    else k_quant_rows<128><<<dim3(m, splits), 256, 0, s>>>(x, d, half, xq, xs);
+    LAUNCH_CHECK();
+    return cudaSuccess;
+  }
   size_t smem = (size_t)d * 4;
   if (smem > 48 * 1024) return cudaErrorInvalidValue;  // d <= 12288
-  if (group == 32) k_norm_quant<32><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs, scale);
-  else k_norm_quant<128><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs, scale);
+  const int squares = 2 * smem <= 48 * 1024;          // room for the squares (d <= 6144)
+  if (squares) smem *= 2;
+  if (group == 32) k_norm_quant<32><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs, scale, squares);
+  else k_norm_quant<128><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs, scale, squares);
   LAUNCH_CHECK();
   return cudaSuccess;
 }
@@ -1518,14 +1591,19 @@ cudaError_t launch_qk_rope_append(float* qkv, int m, const DConfig& cfg, const f
 // Final RmsNorm of `nb` rows (row stride `ldx`), then the table and the
 // argmax of every row: token[b].
 __global__ void __launch_bounds__(256) k_final_norm_rows(const float* x, int ldx, int d, const float* w, float eps,
-                                                         float* xn) {
-  extern __shared__ __align__(16) float rowv[];  // [d]
+                                                         float* xn, int squares) {
+  extern __shared__ __align__(16) float rowv[];  // [d], then [d] squares (as k_norm_quant)
+  float* sq = rowv + d;
   const float* row = x + (size_t)blockIdx.x * ldx;
   float* out = xn + (size_t)blockIdx.x * d;
   __shared__ float s_inv;
-  for (int i = threadIdx.x; i < d; i += 256) rowv[i] = row[i];
+  for (int i = threadIdx.x; i < d; i += 256) {
+    const float v = row[i];
+    rowv[i] = v;
+    if (squares) sq[i] = __fmul_rn(v, v);
+  }
   __syncthreads();
-  if (threadIdx.x == 0) s_inv = rms_inv(seq_sum_squares_ahead(rowv, d), d, eps);
+  if (threadIdx.x == 0) s_inv = rms_inv(squares ? seq_sum_ahead(sq, d) : seq_sum_squares_ahead(rowv, d), d, eps);
   __syncthreads();
   for (int i = threadIdx.x; i < d; i += 256) out[i] = __fmul_rn(rowv[i], __fmul_rn(s_inv, w[i]));
 }
@@ -1579,7 +1657,8 @@ cudaError_t launch_key_tokens(const unsigned long long* keys, int nb, int* token
 cudaError_t launch_final(const float* x, int ldx, int nb, const float* norm_w, const DConfig& cfg, const DTable& T,
                          float* xn, float* logits, float* best_val, int* best_idx, int* token, cudaStream_t s,
                          unsigned long long* keys, int v0) {
-  k_final_norm_rows<<<nb, 256, (size_t)cfg.d * 4, s>>>(x, ldx, cfg.d, norm_w, cfg.eps, xn);
+  const int squares = (size_t)cfg.d * 8 <= 48 * 1024;  // room for the squares (hidden size <= 6144)
+  k_final_norm_rows<<<nb, 256, (size_t)cfg.d * (squares ? 8 : 4), s>>>(x, ldx, cfg.d, norm_w, cfg.eps, xn, squares);
   LAUNCH_CHECK();
   float mult = (cfg.logits_scaling == 1.0f) ? 1.0f : 1.0f / cfg.logits_scaling;
   int blocks = table_blocks(T.n);

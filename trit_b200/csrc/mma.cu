@@ -539,21 +539,8 @@ __global__ void __launch_bounds__(TC_THREADS, TcShape<N, F16>::CTAS)
   if (threadIdx.x == 0 && S->abort) atomicExch(status, 1);
 }
 
-// silu(gate) * up of a stacked gate|up product (causal_lm.rs:464-474):
-// g = [m][2 * units], h = [m][units].
-__global__ void k_silu_pairs(const float* g, int m, int units, float* h) {
-  size_t total = (size_t)m * units;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    size_t r = i / units, u = i % units;
-    const float* row = g + r * 2 * units;
-    h[i] = __fmul_rn(silu(row[u]), row[units + u]);
-  }
-}
-
-// Bits 2s..2s+1 of byte j of word w hold the code of k = 16 w + 4 s + j
-// (pack_span, src/cpu/kernels.rs:624-628); the int8 value is code - 1.
 // ------------------------------------------ prompt attention, f16 MMA ----
-// The `"exact": false` prompt attention: causal GQA attention of a tile of
+// The `"tc_attention": true` prompt attention: causal GQA attention of a tile of
 // 128 query rows (128 / qpk consecutive positions of one stream, each with
 // the qpk query heads of one kv head) over the stream's paged f16 keys and
 // values, flash-style on the tensor cores:
@@ -844,6 +831,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   if (threadIdx.x == 0 && S->abort) atomicExch(status, 1);
 }
 
+// Bits 2s..2s+1 of byte j of word w hold the code of k = 16 w + 4 s + j
+// (pack_span, src/cpu/kernels.rs:624-628); the int8 value is code - 1.
 __global__ void k_expand_ternary(const uint32_t* words, size_t n, int k, int8_t* out) {
   const int wpr = k / 16;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n * wpr; i += (size_t)gridDim.x * blockDim.x) {
@@ -1050,11 +1039,5 @@ cudaError_t launch_expand_ternary(const DMat& W, int8_t* out, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_silu_pairs(const float* g, int m, int units, float* h, cudaStream_t s) {
-  size_t total = (size_t)m * units;
-  int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 16);
-  k_silu_pairs<<<blocks, 256, 0, s>>>(g, m, units, h);
-  return cudaGetLastError();
-}
 
 }  // namespace trit
