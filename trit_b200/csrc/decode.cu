@@ -93,6 +93,7 @@ struct Shared {
   float* xs;       // [kmax / 32]
   float* own;      // [512]: the residual rows this block owns
   float* out;      // [512]
+  float* nw;       // [d]: the phase's RmsNorm weights, staged while the block waits
   float* red;      // [64]
   int* part;       // union: GEMV group dots ...
   float* att;      // ... attention scratch ...
@@ -144,6 +145,16 @@ __device__ void norm_quant(int d, const float* w, float eps, int G, bool half, S
     }
   }
   __syncthreads();
+}
+
+// The layer's RmsNorm weights (d floats) into S.nw by cp.async, one commit
+// group, issued before the product's first weight batch so that both travel
+// while the block waits for its input; the norm waits for this group
+// (cp_wait<1>: all but the batch after it). w and d * 4 are 16-byte
+// multiples (arena vectors).
+__device__ __forceinline__ void stage_norm(const float* w, int d, Shared& S) {
+  for (int i = 4 * threadIdx.x; i < d; i += 4 * DT) cp_async16(S.nw + i, w + i);
+  cp_commit();
 }
 
 // ------------------------------------------------------------- products --
@@ -558,6 +569,7 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
   S.xs = (float*)p; p += (size_t)(kmax / 32) * 4;
   S.own = (float*)p; p += 512 * 4;
   S.out = (float*)p; p += 512 * 4;
+  S.nw = (float*)p; p += (size_t)cfg.d * 4;
   S.gmax = kmax / 32;
   S.part = (int*)p;  // union with the attention and table scratch
   S.att = (float*)p;
@@ -606,12 +618,14 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
       const uint32_t t_qkv = base + 5 * l, t_att = t_qkv + 1, t_xa = t_qkv + 2, t_h = t_qkv + 3, t_xb = t_qkv + 4;
       const uint32_t t_x_in = t_qkv - 1;  // xb of the layer before
       // P1: qkv. Input: x (the embedding, or xb of the layer before).
+      stage_norm(Lw.norm_attn, cfg.d, S);
       bool ok = gemv(Lw.qkv, q1 - q0, [&](int lr) { return q0 + lr; }, S, [&]() {
         if (l > 0 && !ll_wait(a.ll + ll.xb, cfg.d, t_x_in, a.status,
                               [&](int k, uint32_t v) { S.xf[k] = __uint_as_float(v); }))
           return false;
         ev(1);
-        norm_quant(cfg.d, Lw.norm_attn, cfg.eps, Lw.qkv.agroup, Lw.qkv.half, S);
+        cp_wait<1>();  // the norm weights (the group before the product's first weight batch)
+        norm_quant(cfg.d, S.nw, cfg.eps, Lw.qkv.agroup, Lw.qkv.half, S);
         ev(2);
         return true;
       }, ev, 16);
@@ -649,11 +663,13 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
         ll_put(a.ll + ll.xa + r0 + lr, __float_as_uint(xv), t_xa);
       }
       // P4: gate_up, h = silu(gate) * up. Input: xa.
+      stage_norm(Lw.norm_mlp, cfg.d, S);
       ok = gemv(Lw.gate_up, 2 * nu, [&](int lr) { return lr < nu ? u0 + lr : cfg.ffn + u0 + lr - nu; }, S, [&]() {
         if (!ll_wait(a.ll + ll.xa, cfg.d, t_xa, a.status, [&](int k, uint32_t v) { S.xf[k] = __uint_as_float(v); }))
           return false;
         ev(10);
-        norm_quant(cfg.d, Lw.norm_mlp, cfg.eps, Lw.gate_up.agroup, Lw.gate_up.half, S, Lw.ffn_scale);
+        cp_wait<1>();
+        norm_quant(cfg.d, S.nw, cfg.eps, Lw.gate_up.agroup, Lw.gate_up.half, S, Lw.ffn_scale);
         ev(11);
         return true;
       }, ev, 22);
@@ -738,7 +754,7 @@ __global__ void __launch_bounds__(DT, 1) k_decode(DecodeArgs a) {
 size_t head_smem(const DConfig& cfg) {
   const int qd = cfg.heads * 128;
   const int kmax = std::max(std::max(cfg.d, qd), cfg.ffn);
-  return 64 + 64 * 4 + (size_t)kmax * 8 + kmax + (size_t)(kmax / 32) * 4 + 512 * 4 + 512 * 4;
+  return 64 + 64 * 4 + (size_t)kmax * 8 + kmax + (size_t)(kmax / 32) * 4 + 512 * 4 + 512 * 4 + (size_t)cfg.d * 4;
 }
 
 // The union region: the largest of the GEMV group dots and scales, the

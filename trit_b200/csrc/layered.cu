@@ -39,13 +39,20 @@ __global__ void k_scale(float* x, size_t n, float mult) {
 // is the reference's to the bit.
 // With `squares`, the squares are formed by all threads into shared memory
 // first (each rounded, as the reference rounds them), so the one thread's
-// chain is adds only.
+// chain is adds only. A row's groups spread over `gridDim.y` blocks (decode
+// batches: few rows); each block sums the whole row (the same chain, so the
+// same inv) and quantizes its own groups. With `wstage`, the block's slice
+// of the norm weights loads with the row, so its latency hides behind the
+// sum.
 template <int G>
 __global__ void __launch_bounds__(256) k_norm_quant(const float* x, int d, const float* w, float eps, int half,
-                                                    int8_t* xq, float* xs, const float* sc, int squares) {
-  extern __shared__ __align__(16) float rowv[];  // [d], then [d] squares
+                                                    int8_t* xq, float* xs, const float* sc, int squares, int wstage) {
+  extern __shared__ __align__(16) float rowv[];  // [d], then [d] squares, then the weights of the block's groups
   float* sq = rowv + d;
-  int r = blockIdx.x;
+  float* wv = sq + (squares ? d : 0);
+  const int r = blockIdx.x, groups = d / G;
+  const int per = (groups + gridDim.y - 1) / gridDim.y;
+  const int g0 = blockIdx.y * per, g1 = min(groups, g0 + per);
   const float* row = x + (size_t)r * d;
   __shared__ float s_inv;
   for (int i = threadIdx.x; i < d; i += 256) {
@@ -53,19 +60,21 @@ __global__ void __launch_bounds__(256) k_norm_quant(const float* x, int d, const
     rowv[i] = v;
     if (squares) sq[i] = __fmul_rn(v, v);
   }
+  if (w && wstage)
+    for (int i = g0 * G + threadIdx.x; i < g1 * G; i += 256) wv[i - g0 * G] = w[i];
   __syncthreads();
   if (threadIdx.x == 0)
     s_inv = !w ? 1.0f : rms_inv(squares ? seq_sum_ahead(sq, d) : seq_sum_squares_ahead(rowv, d), d, eps);
   __syncthreads();
   float inv = s_inv;
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int groups = d / G;
-  for (int g = warp; g < groups; g += 8) {
+  const float* wg = wstage ? wv - g0 * G : w;  // weight kk at wg[kk]
+  for (int g = g0 + warp; g < g1; g += 8) {
     float v[G / 32];
 #pragma unroll
     for (int i = 0; i < G / 32; ++i) {
       int kk = g * G + lane * (G / 32) + i;
-      v[i] = w ? __fmul_rn(rowv[kk], __fmul_rn(inv, w[kk])) : rowv[kk];
+      v[i] = w ? __fmul_rn(rowv[kk], __fmul_rn(inv, wg[kk])) : rowv[kk];
       if (sc) v[i] = __fmul_rn(v[i], sc[kk]);
     }
     float scale = warp_quantize_group<G>(v, xq + (size_t)r * d + g * G, half);
@@ -775,8 +784,21 @@ __global__ void __launch_bounds__(256, 2) k_attention_step(const float* qkv, DCo
         const int h = it / 64, d = it % 64;
         const float* pr = sc + (size_t)h * tmax + j0;
         float2 a = acc[u];
-#pragma unroll 8
-        for (int jj = 0; jj < n; ++jj) {
+        // Four probabilities a load (pr is 16-byte aligned: tmax and the
+        // tile's first key are multiples of 4); the fmas stay in key order.
+        int jj = 0;
+#pragma unroll 2
+        for (; jj + 4 <= n; jj += 4) {
+          const float4 p4 = *(const float4*)(pr + jj);
+          const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 v = F16 ? __half22float2(*((const __half2*)(kv + (jj + i) * PITCH) + d))
+                                 : *(const float2*)(kv + (jj + i) * PITCH + 2 * d);
+            a = fma2(make_float2(pv[i], pv[i]), v, a);
+          }
+        }
+        for (; jj < n; ++jj) {
           const float p = pr[jj];
           const float2 v = F16 ? __half22float2(*((const __half2*)(kv + jj * PITCH) + d))
                                : *(const float2*)(kv + jj * PITCH + 2 * d);
@@ -1511,12 +1533,16 @@ cudaError_t launch_norm_quant(const float* x, int m, int d, const float* w, floa
     LAUNCH_CHECK();
     return cudaSuccess;
   }
-  size_t smem = (size_t)d * 4;
-  if (smem > 48 * 1024) return cudaErrorInvalidValue;  // d <= 12288
-  const int squares = 2 * smem <= 48 * 1024;          // room for the squares (d <= 6144)
-  if (squares) smem *= 2;
-  if (group == 32) k_norm_quant<32><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs, scale, squares);
-  else k_norm_quant<128><<<m, 256, smem, s>>>(x, d, w, eps, half, xq, xs, scale, squares);
+  const int groups = d / group, splits = quant_splits(m, groups), per = (groups + splits - 1) / splits;
+  const size_t row = (size_t)d * 4, wslice = w ? (size_t)per * group * 4 : 0;
+  if (row > 48 * 1024) return cudaErrorInvalidValue;          // d <= 12288
+  const int wstage = row + wslice <= 48 * 1024;                // room for the block's norm weights
+  const size_t base = row + (wstage ? wslice : 0);
+  const int squares = base + row <= 48 * 1024;                 // room for the squares as well
+  const size_t smem = base + (squares ? row : 0);
+  const dim3 grid(m, splits);
+  if (group == 32) k_norm_quant<32><<<grid, 256, smem, s>>>(x, d, w, eps, half, xq, xs, scale, squares, wstage);
+  else k_norm_quant<128><<<grid, 256, smem, s>>>(x, d, w, eps, half, xq, xs, scale, squares, wstage);
   LAUNCH_CHECK();
   return cudaSuccess;
 }
