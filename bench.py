@@ -451,7 +451,7 @@ def run_decode(args, r: dp.Rank) -> None:
 TRAFFIC: dict = {}
 # C1: a 15-step capture (read + write per step) plus the KV bytes of the
 # bench's 56 more positions on average (profiles/k_decode_c1.md).
-TRAFFIC_EXACT: dict = {"c1": (9.629315e9 + 11.049728e6) / 15 + 56 * 114688}
+TRAFFIC_EXACT: dict = {"c1": (9.629856e9 + 8.017664e6) / 15 + 56 * 114688}
 # The batch-64 object of the default line: generations timed (C5 takes
 # ~8 s a generation on one B200).
 BATCH64_STEPS = 2
