@@ -34,9 +34,9 @@ __global__ void k_scale(float* x, size_t n, float mult) {
 
 // ------------------------------------------------- norm + quantize ----
 // RmsNorm::apply (src/layers.rs:135-153) then Quantized::grouped
-// (src/cpu/kernels.rs:661-737) of the normed row. One block per row; one
-// thread sums the squares in order, as the reference does, so the result
-// is the reference's to the bit.
+// (src/cpu/kernels.rs:661-737) of the normed row. One thread of a block
+// sums the row's squares in order, as the reference does, so the result is
+// the reference's to the bit.
 // With `squares`, the squares are formed by all threads into shared memory
 // first (each rounded, as the reference rounds them), so the one thread's
 // chain is adds only. A row's groups spread over `gridDim.y` blocks (decode
@@ -68,13 +68,12 @@ __global__ void __launch_bounds__(256) k_norm_quant(const float* x, int d, const
   __syncthreads();
   float inv = s_inv;
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float* wg = wstage ? wv - g0 * G : w;  // weight kk at wg[kk]
   for (int g = g0 + warp; g < g1; g += 8) {
     float v[G / 32];
 #pragma unroll
     for (int i = 0; i < G / 32; ++i) {
       int kk = g * G + lane * (G / 32) + i;
-      v[i] = w ? __fmul_rn(rowv[kk], __fmul_rn(inv, wg[kk])) : rowv[kk];
+      v[i] = w ? __fmul_rn(rowv[kk], __fmul_rn(inv, wstage ? wv[kk - g0 * G] : w[kk])) : rowv[kk];
       if (sc) v[i] = __fmul_rn(v[i], sc[kk]);
     }
     float scale = warp_quantize_group<G>(v, xq + (size_t)r * d + g * G, half);
