@@ -33,6 +33,10 @@ __global__ void k_scale(float* x, size_t n, float mult) {
 }
 
 // ------------------------------------------------- norm + quantize ----
+// Dynamic shared memory of the norm kernels: the 48 KB a launch may take
+// without an opt-in, less room for their static shared variables.
+constexpr size_t kNormSmem = 48 * 1024 - 256;
+
 // RmsNorm::apply (src/layers.rs:135-153) then Quantized::grouped
 // (src/cpu/kernels.rs:661-737) of the normed row. One thread of a block
 // sums the row's squares in order, as the reference does, so the result is
@@ -1534,10 +1538,10 @@ cudaError_t launch_norm_quant(const float* x, int m, int d, const float* w, floa
   }
   const int groups = d / group, splits = quant_splits(m, groups), per = (groups + splits - 1) / splits;
   const size_t row = (size_t)d * 4, wslice = w ? (size_t)per * group * 4 : 0;
-  if (row > 48 * 1024) return cudaErrorInvalidValue;          // d <= 12288
-  const int wstage = row + wslice <= 48 * 1024;                // room for the block's norm weights
+  if (row > kNormSmem) return cudaErrorInvalidValue;           // d <= 12224
+  const int wstage = row + wslice <= kNormSmem;                // room for the block's norm weights
   const size_t base = row + (wstage ? wslice : 0);
-  const int squares = base + row <= 48 * 1024;                 // room for the squares as well
+  const int squares = base + row <= kNormSmem;                 // room for the squares as well
   const size_t smem = base + (squares ? row : 0);
   const dim3 grid(m, splits);
   if (group == 32) k_norm_quant<32><<<grid, 256, smem, s>>>(x, d, w, eps, half, xq, xs, scale, squares, wstage);
@@ -1682,7 +1686,7 @@ cudaError_t launch_key_tokens(const unsigned long long* keys, int nb, int* token
 cudaError_t launch_final(const float* x, int ldx, int nb, const float* norm_w, const DConfig& cfg, const DTable& T,
                          float* xn, float* logits, float* best_val, int* best_idx, int* token, cudaStream_t s,
                          unsigned long long* keys, int v0) {
-  const int squares = (size_t)cfg.d * 8 <= 48 * 1024;  // room for the squares (hidden size <= 6144)
+  const int squares = (size_t)cfg.d * 8 <= kNormSmem;  // room for the squares (hidden size < 6144)
   k_final_norm_rows<<<nb, 256, (size_t)cfg.d * (squares ? 8 : 4), s>>>(x, ldx, cfg.d, norm_w, cfg.eps, xn, squares);
   LAUNCH_CHECK();
   float mult = (cfg.logits_scaling == 1.0f) ? 1.0f : 1.0f / cfg.logits_scaling;
