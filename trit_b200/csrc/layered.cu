@@ -1513,14 +1513,22 @@ __global__ void __launch_bounds__(256) k_silu_quant(const float* g, int units, i
 }
 
 static int quant_splits(int m, int groups) {
-  // Enough blocks for two an SM when the rows are few (decode batches).
+  // Enough blocks for two an SM when the rows are few (decode batches):
+  // each block of k_norm_quant runs the row's whole sum of squares.
   return std::max(1, std::min((groups + 7) / 8, (2 * current_sm_count() + m - 1) / m));
+}
+
+// Splits of the norm-free quantizers (k_quant_rows, k_silu_quant): a warp
+// waits on its group's loads before it can quantize, so a block takes few
+// groups a warp (up to eight blocks an SM when the rows are few).
+static int free_quant_splits(int m, int groups) {
+  return std::max(1, std::min((groups + 7) / 8, (8 * current_sm_count() + m - 1) / m));
 }
 
 cudaError_t launch_silu_quant(const float* g, int m, int units, int group, int half, int8_t* xq, float* xs,
                               cudaStream_t s) {
   if (units % group) return cudaErrorInvalidValue;
-  const int splits = quant_splits(m, units / group);
+  const int splits = free_quant_splits(m, units / group);
   if (group == 32) k_silu_quant<32><<<dim3(m, splits), 256, 0, s>>>(g, units, half, xq, xs);
   else k_silu_quant<128><<<dim3(m, splits), 256, 0, s>>>(g, units, half, xq, xs);
   LAUNCH_CHECK();
@@ -1530,7 +1538,7 @@ cudaError_t launch_silu_quant(const float* g, int m, int units, int group, int h
 cudaError_t launch_norm_quant(const float* x, int m, int d, const float* w, float eps, int group, int half,
                               int8_t* xq, float* xs, cudaStream_t s, const float* scale) {
   if (!w && !scale) {
-    const int splits = quant_splits(m, d / group);
+    const int splits = free_quant_splits(m, d / group);
     if (group == 32) k_quant_rows<32><<<dim3(m, splits), 256, 0, s>>>(x, d, half, xq, xs);
     else k_quant_rows<128><<<dim3(m, splits), 256, 0, s>>>(x, d, half, xq, xs);
     LAUNCH_CHECK();
